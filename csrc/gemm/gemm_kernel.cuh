@@ -1,0 +1,429 @@
+// Persistent warp-specialized tcgen05/TMEM GEMM for sm_100a with fused epilogues.
+//
+// Replaces every cuBLAS GEMM of the reference step (bench_train.py:121-162 nn.Linear under
+// autocast, kernels/triton_ops.py:383-390 lm-head chunks): forward y = x W^T, dgrad
+// dx = dy W, wgrad dW = dy^T x, with fp32 accumulation in tensor memory.
+//
+//   D[M, N] (+)= A'[M, K] * B'[K, N]
+//   A' = a (K-major) or a^T (MN-major); B' = b^T (K-major) or b (MN-major), all row-major
+//   PyTorch tensors, so fwd/dgrad/wgrad never need a transposed copy.
+//
+// CTA = 6 warps, one CTA per SM, persistent over output tiles (BM = 128, BN = 128|256, BK = 64):
+//   warp 0    TMA producer: STAGES-deep ring of A/B tiles in 128B-swizzled shared memory
+//   warp 1    TMEM allocator + single-thread tcgen05.mma issuer (4 x K=16 per stage)
+//   warps 2-5 epilogue: tcgen05.ld 32x32b of the accumulator, fused math, global stores
+// Two accumulators live in TMEM (2 x BN fp32 columns) so the epilogue of tile i overlaps the
+// MMAs of tile i+1. No TMA multicast is used (the kernel also runs in multi-GPU jobs).
+//
+// Epilogues:
+//   BF16       out = bf16(acc)
+//   F32        out = acc (+ out when accumulating: fp32 main-grad accumulation)
+//   SWIGLU     merged w1||w3 GEMM: the B tile holds BN/2 rows of W1 and the same BN/2 rows
+//              of W3 (two TMA boxes), so acc = [g | u] for the same h columns;
+//              writes h = silu(g) * u plus g and u (needed by the backward)
+//   SWIGLU_BWD w2 dgrad: acc = dh; reads g, u and writes dg, du (reference triton_ops.py:182-194)
+//   ROPE       qkv GEMM: rotate-half RoPE on q/k columns while storing the packed qkv rows
+//   CE_FWD     lm head: per-row partial max / sum-exp over the tile's vocab columns and the
+//              target logit; logits are never written (reference triton_ops.py:338-364)
+//   CE_BWD     lm head recompute: dlogits = (exp(acc - lse) - onehot) * grad_out * alpha
+#pragma once
+#include "../common/common.cuh"
+#include "../common/sm100.cuh"
+#include "../common/tma.h"
+
+namespace llmt {
+
+enum EpiKind : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_ROPE = 4, EPI_CE_FWD = 5, EPI_CE_BWD = 6 };
+
+struct GemmArgs {
+  int M, N, K;
+  int m_blocks, n_blocks, k_blocks;
+  void* out;
+  int64_t ldo;
+  int accumulate;
+  int split;  // SWIGLU: row offset of W3 inside W13 (= ffn); SWIGLU_BWD: column offset of u in gu (= ffn)
+  const void* aux;
+  int64_t ld_aux;
+  void* out2;
+  int64_t ldo2;
+  const float* cos_t;
+  const float* sin_t;
+  int T, hd, rot_cols;
+  const int64_t* tgt;
+  const float* lse;
+  const float* grad_out;
+  float* part;    // CE_FWD partials (M, n_blocks, 2)
+  float* tlogit;  // CE_FWD target logits (M)
+  float alpha;
+  int* err;
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+// Host launchers, one translation unit per operand layout (keeps build parallel).
+void gemm_launch_kk(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // fwd
+void gemm_launch_km(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // dgrad
+void gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // wgrad
+int* gemm_err_word();
+
+namespace gemm_detail {
+
+using namespace sm100;
+
+__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+
+__device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v, int col0, int N) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (col0 + q * 8 < N) *reinterpret_cast<BF16x8*>(dst + q * 8) = float_to_bf16x8(v + q * 8);
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const bf16* src, float* v, int col0, int N) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (col0 + q * 8 < N) {
+      bf16x8_to_float(*reinterpret_cast<const BF16x8*>(src + q * 8), v + q * 8);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q * 8 + j] = 0.f;
+    }
+  }
+}
+
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, const GemmArgs& a) {
+  const bool rv = row < a.M;
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_CE_BWD) {
+    float l = 0.f, scale = 0.f;
+    int64_t t = -1;
+    if constexpr (EPI == EPI_CE_BWD) {
+      if (rv) {
+        l = a.lse[row];
+        t = a.tgt[row];
+      }
+      scale = a.alpha * (a.grad_out ? *a.grad_out : 1.f);
+    }
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col0 = nb * BN + c * 32;
+      if (!rv || col0 >= a.N) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+      if constexpr (EPI == EPI_BF16) {
+        store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, v, col0, a.N);
+      } else if constexpr (EPI == EPI_CE_BWD) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (__expf(v[j] - l) - ((int64_t)(col0 + j) == t ? 1.f : 0.f)) * scale;
+        store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, v, col0, a.N);
+      } else {
+        float* o = reinterpret_cast<float*>(a.out) + (int64_t)row * a.ldo + col0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (col0 + q * 4 < a.N) {
+            float4 x = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            if (a.accumulate) {
+              const float4 y = *reinterpret_cast<const float4*>(o + 4 * q);
+              x.x += y.x;
+              x.y += y.y;
+              x.z += y.z;
+              x.w += y.w;
+            }
+            *reinterpret_cast<float4*>(o + 4 * q) = x;
+          }
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    const int F = a.split;
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c * 32, rg);
+      tmem_ld32(taddr + BN / 2 + c * 32, ru);
+      tmem_wait_ld();
+      const int col0 = nb * (BN / 2) + c * 32;
+      if (!rv || col0 >= F) continue;
+      float g[32], u[32], h[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        g[j] = u2f(rg[j]);
+        u[j] = u2f(ru[j]);
+        h[j] = g[j] * sigm(g[j]) * u[j];
+      }
+      store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, h, col0, F);
+      bf16* gu = reinterpret_cast<bf16*>(const_cast<void*>(a.aux)) + (int64_t)row * a.ld_aux;
+      store_bf16x32(gu + col0, g, col0, F);
+      store_bf16x32(gu + F + col0, u, col0, F);
+    }
+  } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+    const int F = a.split;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col0 = nb * BN + c * 32;
+      if (!rv || col0 >= a.N) continue;
+      const bf16* gu = reinterpret_cast<const bf16*>(a.aux) + (int64_t)row * a.ld_aux;
+      float g[32], u[32], dg[32], du[32];
+      load_bf16x32(gu + col0, g, col0, F);
+      load_bf16x32(gu + F + col0, u, col0, F);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float d = u2f(r[j]);
+        const float sg = sigm(g[j]);
+        dg[j] = d * u[j] * sg * (1.f + g[j] * (1.f - sg));
+        du[j] = d * g[j] * sg;
+      }
+      bf16* o = reinterpret_cast<bf16*>(a.out2) + (int64_t)row * a.ldo2;
+      store_bf16x32(o + col0, dg, col0, F);
+      store_bf16x32(o + F + col0, du, col0, F);
+    }
+  } else if constexpr (EPI == EPI_ROPE) {
+    const int hd = a.hd, half = hd / 2;
+    const int tpos = rv ? row % a.T : 0;
+    const float* cr = a.cos_t + (int64_t)tpos * hd;
+    const float* sr = a.sin_t + (int64_t)tpos * hd;
+#pragma unroll 1
+    for (int hl = 0; hl < BN / hd; ++hl) {
+#pragma unroll 1
+      for (int j = 0; j < half / 32; ++j) {
+        const int c1 = hl * hd + j * 32;
+        uint32_t r1[32], r2[32];
+        tmem_ld32(taddr + c1, r1);
+        tmem_ld32(taddr + c1 + half, r2);
+        tmem_wait_ld();
+        const int col1 = nb * BN + c1;
+        if (!rv || col1 >= a.N) continue;
+        float x1[32], x2[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          x1[e] = u2f(r1[e]);
+          x2[e] = u2f(r2[e]);
+        }
+        if (col1 < a.rot_cols) {
+          const int f1 = j * 32, f2 = half + j * 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float c1v = cr[f1 + e], s1v = sr[f1 + e], c2v = cr[f2 + e], s2v = sr[f2 + e];
+            const float y1 = x1[e] * c1v - x2[e] * s1v;
+            const float y2 = x2[e] * c2v + x1[e] * s2v;
+            x1[e] = y1;
+            x2[e] = y2;
+          }
+        }
+        bf16* o = reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo;
+        store_bf16x32(o + col1, x1, col1, a.N);
+        store_bf16x32(o + col1 + half, x2, col1 + half, a.N);
+      }
+    }
+  } else if constexpr (EPI == EPI_CE_FWD) {
+    const int64_t t = rv ? a.tgt[row] : -1;
+    float m = -INFINITY, s = 0.f, tl = 0.f;
+    bool has_t = false;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col0 = nb * BN + c * 32;
+      float cm = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = u2f(r[j]);
+        if (col0 + j < a.N) cm = fmaxf(cm, x);
+        if ((int64_t)(col0 + j) == t) {
+          tl = x;
+          has_t = true;
+        }
+      }
+      if (cm == -INFINITY) continue;
+      float cs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < a.N) cs += __expf(u2f(r[j]) - cm);
+      const float nm = fmaxf(m, cm);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + cs * __expf(cm - nm);
+      m = nm;
+    }
+    if (rv) {
+      float* p = a.part + ((int64_t)row * a.n_blocks + nb) * 2;
+      p[0] = m;
+      p[1] = s;
+      if (has_t) a.tlogit[row] = tl;
+    }
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  constexpr int BM = kGemmBM, BK = kGemmBK;
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  int* err = args.err;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&tfull[b], 1);
+      bar_init(&tempty[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = args.m_blocks * args.n_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % args.m_blocks, nb = tile / args.m_blocks;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!wait_bar(&empty[stage], phase ^ 1, err, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          bar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(sa, &tmA, &full[stage], k0, mb * BM);
+          } else {
+            tma_load_2d(sa, &tmA, &full[stage], mb * BM, k0);
+            tma_load_2d(sa + 8192, &tmA, &full[stage], mb * BM + 64, k0);
+          }
+          if constexpr (!B_MN) {
+            if constexpr (EPI == EPI_SWIGLU) {
+              tma_load_2d(sb, &tmB, &full[stage], k0, nb * (BN / 2));
+              tma_load_2d(sb + (BN / 2) * 128, &tmB, &full[stage], k0, args.split + nb * (BN / 2));
+            } else {
+              tma_load_2d(sb, &tmB, &full[stage], k0, nb * BN);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[stage], nb * BN + j * 64, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0, buf = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!wait_bar(&tempty[buf], aphase ^ 1, err, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!wait_bar(&full[stage], phase, err, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad =
+                A_MN ? make_sw128_desc(sa + k * 2048, 8192, 1024) : make_sw128_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd =
+                B_MN ? make_sw128_desc(sb + k * 2048, 8192, 1024) : make_sw128_desc(sb + k * 32, 16, 1024);
+            mma_f16(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+        buf ^= 1;
+        if (buf == 0) aphase ^= 1;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int buf = 0;
+    uint32_t aphase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mb = tile % args.m_blocks, nb = tile / args.m_blocks;
+      if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
+      epilogue_tile<EPI, BN>(taddr, mb * BM + row_in_tile, nb, args);
+      tc_fence_before();
+      bar_arrive(&tempty[buf]);
+      buf ^= 1;
+      if (buf == 0) aphase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<TMEM_COLS>(tmem_base);
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args) {
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  const int tiles = args.m_blocks * args.n_blocks;
+  const int grid = std::min(tiles, sm_count());
+  kern<<<grid, kGemmThreads, smem, cur_stream()>>>(ta, tb, args);
+  LLMT_LAUNCH_CHECK();
+}
+
+template <int BN>
+constexpr int stages_for() {
+  return BN == 256 ? 4 : 6;
+}
+
+}  // namespace gemm_detail
+}  // namespace llmt

@@ -1,0 +1,303 @@
+// Fused residual-add + RMSNorm, forward and backward (sm_100a).
+//
+// Contract (same math as the reference's add+RMSNorm, kernels/cuda_ext/add_rmsnorm.cu:78-178
+// and kernels/triton_ops.py:38-86):
+//   forward   s = r + a (a optional), rstd = 1/sqrt(mean(s^2) + eps), y = s * rstd * w
+//   backward  g = dy * w, c = mean(g * s), ds = rstd * g - s * rstd^3 * c + ds_in,
+//             dw = sum_rows dy * s * rstd
+// Dtypes on the native path: a bf16 (a GEMM output), r/s fp32 (the residual stream),
+// w fp32 (master weight), y bf16 (the next GEMM's operand), ds fp32 + a bf16 copy.
+//
+// Layout: TPR threads per row (a power of two, 32..256), each owning up to 4 chunks of 8
+// consecutive elements, 256 threads per CTA (256/TPR rows per CTA). The backward is
+// persistent; every CTA keeps its dw partial in registers, writes one (D) partial row and
+// the last CTA to finish (atomic ticket) sums the partials in a fixed order, so dw is
+// deterministic and needs no extra launch (the reference sums its (P, D) partials with a
+// separate host-side dwp.sum(0), add_rmsnorm_ext.py:70).
+#include "../common/common.cuh"
+
+namespace llmt {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxChunks = 4;
+
+template <int TPR>
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  v = warp_sum(v);
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    constexpr int WPR = TPR / 32;  // warps per row
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row_in_cta = threadIdx.x / TPR;
+    __syncthreads();  // protect red[] from the previous use
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < WPR; ++i) t += red[row_in_cta * WPR + i];
+    return t;
+  }
+}
+
+template <int TPR, bool HAS_A, bool WRITE_S>
+__global__ void __launch_bounds__(kThreads)
+add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, const float* __restrict__ w,
+                       bf16* __restrict__ y, float* __restrict__ s_out, float* __restrict__ rstd_out,
+                       int64_t N, int D, float eps) {
+  __shared__ float red[kThreads / 32];
+  constexpr int RPC = kThreads / TPR;
+  const int t = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * RPC + threadIdx.x / TPR;
+  const bool valid = row < N;
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int e = (c * TPR + t) * 8;
+    if (valid && e < D) {
+      const int64_t off = row * D + e;
+      float4 r0 = ld_f4(r + off), r1 = ld_f4(r + off + 4);
+      v[c][0] = r0.x; v[c][1] = r0.y; v[c][2] = r0.z; v[c][3] = r0.w;
+      v[c][4] = r1.x; v[c][5] = r1.y; v[c][6] = r1.z; v[c][7] = r1.w;
+      if constexpr (HAS_A) {
+        float af[8];
+        bf16x8_to_float(*reinterpret_cast<const BF16x8*>(a + off), af);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c][j] += af[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+    }
+  }
+  ss = row_sum<TPR>(ss, red);
+  const float rstd = rsqrtf(ss / (float)D + eps);
+  if (!valid) return;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int e = (c * TPR + t) * 8;
+    if (e < D) {
+      const int64_t off = row * D + e;
+      if constexpr (WRITE_S) {
+        st_f4(s_out + off, make_float4(v[c][0], v[c][1], v[c][2], v[c][3]));
+        st_f4(s_out + off + 4, make_float4(v[c][4], v[c][5], v[c][6], v[c][7]));
+      }
+      float4 w0 = ld_f4(w + e), w1 = ld_f4(w + e + 4);
+      float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[c][j] * rstd * ww[j];
+      *reinterpret_cast<BF16x8*>(y + off) = float_to_bf16x8(o);
+    }
+  }
+  if (t == 0) rstd_out[row] = rstd;
+}
+
+// dy bf16, s fp32, ds_in fp32 (optional); ds fp32 and ds16 bf16 (optional) out.
+template <int TPR, bool HAS_DSIN, bool WRITE_DS16>
+__global__ void __launch_bounds__(kThreads)
+rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, const float* __restrict__ w,
+                   const float* __restrict__ rstd_in, const float* __restrict__ ds_in,
+                   float* __restrict__ ds, bf16* __restrict__ ds16, float* __restrict__ dw_part,
+                   float* __restrict__ dw, unsigned int* __restrict__ ticket, int64_t N, int D,
+                   int accumulate) {
+  __shared__ float red[kThreads / 32];
+  __shared__ bool is_last;
+  constexpr int RPC = kThreads / TPR;
+  const int t = threadIdx.x % TPR;
+  const int rgroup = threadIdx.x / TPR;
+  float wv[kMaxChunks][8];
+  float dwacc[kMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int e = (c * TPR + t) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { dwacc[c][j] = 0.f; wv[c][j] = (e < D) ? w[e + j] : 0.f; }
+  }
+  const int64_t stride = (int64_t)gridDim.x * RPC;
+  // Every row group runs the same number of iterations so the block-wide barriers in
+  // row_sum line up; rows past N are masked.
+  const int64_t iters = cdiv(N, stride);
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t row = it * stride + (int64_t)blockIdx.x * RPC + rgroup;
+    const bool valid = row < N;
+    float g[kMaxChunks][8], sv[kMaxChunks][8];
+    float dot = 0.f;
+    const float rs = valid ? rstd_in[row] : 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int e = (c * TPR + t) * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { g[c][j] = 0.f; sv[c][j] = 0.f; }
+      if (valid && e < D) {
+        const int64_t off = row * D + e;
+        float dyf[8];
+        bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dy + off), dyf);
+        float4 s0 = ld_f4(s + off), s1 = ld_f4(s + off + 4);
+        sv[c][0] = s0.x; sv[c][1] = s0.y; sv[c][2] = s0.z; sv[c][3] = s0.w;
+        sv[c][4] = s1.x; sv[c][5] = s1.y; sv[c][6] = s1.z; sv[c][7] = s1.w;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          g[c][j] = dyf[j] * wv[c][j];
+          dot += g[c][j] * sv[c][j];
+          dwacc[c][j] += dyf[j] * sv[c][j] * rs;
+        }
+      }
+    }
+    dot = row_sum<TPR>(dot, red);
+    const float cc = dot / (float)D;
+    const float rs3 = rs * rs * rs;
+    if (valid) {
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int e = (c * TPR + t) * 8;
+        if (e < D) {
+          const int64_t off = row * D + e;
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = rs * g[c][j] - sv[c][j] * rs3 * cc;
+          if constexpr (HAS_DSIN) {
+            float4 d0 = ld_f4(ds_in + off), d1 = ld_f4(ds_in + off + 4);
+            o[0] += d0.x; o[1] += d0.y; o[2] += d0.z; o[3] += d0.w;
+            o[4] += d1.x; o[5] += d1.y; o[6] += d1.z; o[7] += d1.w;
+          }
+          st_f4(ds + off, make_float4(o[0], o[1], o[2], o[3]));
+          st_f4(ds + off + 4, make_float4(o[4], o[5], o[6], o[7]));
+          if constexpr (WRITE_DS16) *reinterpret_cast<BF16x8*>(ds16 + off) = float_to_bf16x8(o);
+        }
+      }
+    }
+  }
+  // CTA-level reduction of dw over the row groups, through shared memory (D floats).
+  extern __shared__ float sdw[];
+  for (int i = threadIdx.x; i < D; i += kThreads) sdw[i] = 0.f;
+  __syncthreads();
+  for (int rg = 0; rg < RPC; ++rg) {
+    if (rgroup == rg) {
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int e = (c * TPR + t) * 8;
+        if (e < D) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sdw[e + j] += dwacc[c][j];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < D; i += kThreads) dw_part[(int64_t)blockIdx.x * D + i] = sdw[i];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int prev = atomicAdd(ticket, 1u);
+    is_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < D; i += kThreads) {
+    float acc = 0.f;
+    for (int p = 0; p < (int)gridDim.x; ++p) acc += __ldcg(dw_part + (int64_t)p * D + i);
+    dw[i] = accumulate ? dw[i] + acc : acc;
+  }
+  if (threadIdx.x == 0) *ticket = 0u;  // re-arm for the next call
+}
+
+template <typename F>
+void dispatch_tpr(int D, F&& f) {
+  LLMT_CHECK(D % 8 == 0, "RMSNorm width must be a multiple of 8, got ", D);
+  if (D <= 32 * 8 * kMaxChunks) f(std::integral_constant<int, 32>{});
+  else if (D <= 64 * 8 * kMaxChunks) f(std::integral_constant<int, 64>{});
+  else if (D <= 128 * 8 * kMaxChunks) f(std::integral_constant<int, 128>{});
+  else if (D <= 256 * 8 * kMaxChunks) f(std::integral_constant<int, 256>{});
+  else LLMT_CHECK(false, "RMSNorm width ", D, " exceeds 8192");
+}
+
+}  // namespace
+
+// y = rmsnorm(r + a) * w.  Returns (y bf16, s fp32 or undefined, rstd fp32).
+std::vector<at::Tensor> add_rmsnorm_fwd(c10::optional<at::Tensor> a, at::Tensor r, at::Tensor w, double eps,
+                                        bool write_s) {
+  LLMT_CHECK_CUDA(r);
+  LLMT_CHECK_CONTIG(r);
+  LLMT_CHECK_DTYPE(r, at::kFloat);
+  LLMT_CHECK_DTYPE(w, at::kFloat);
+  const int D = r.size(-1);
+  const int64_t N = r.numel() / D;
+  auto y = at::empty(r.sizes(), r.options().dtype(at::kBFloat16));
+  auto rstd = at::empty({N}, r.options());
+  at::Tensor s;
+  const bool has_a = a.has_value() && a->defined();
+  if (has_a) {
+    LLMT_CHECK_DTYPE((*a), at::kBFloat16);
+    LLMT_CHECK_CONTIG((*a));
+    LLMT_CHECK(a->numel() == r.numel(), "a and r differ in size");
+  }
+  if (write_s) s = at::empty_like(r);
+  if (N == 0) return {y, s, rstd};
+  dispatch_tpr(D, [&](auto tpr) {
+    constexpr int TPR = decltype(tpr)::value;
+    constexpr int RPC = kThreads / TPR;
+    dim3 grid(cdiv(N, RPC));
+    const bf16* ap = has_a ? reinterpret_cast<const bf16*>(a->data_ptr()) : nullptr;
+    auto launch = [&](auto kern) {
+      kern<<<grid, kThreads, 0, cur_stream()>>>(ap, r.data_ptr<float>(), w.data_ptr<float>(),
+                                                 reinterpret_cast<bf16*>(y.data_ptr()),
+                                                 write_s ? s.data_ptr<float>() : nullptr, rstd.data_ptr<float>(),
+                                                 N, D, (float)eps);
+    };
+    if (has_a && write_s) launch(add_rmsnorm_fwd_kernel<TPR, true, true>);
+    else if (has_a) launch(add_rmsnorm_fwd_kernel<TPR, true, false>);
+    else if (write_s) launch(add_rmsnorm_fwd_kernel<TPR, false, true>);
+    else launch(add_rmsnorm_fwd_kernel<TPR, false, false>);
+    LLMT_LAUNCH_CHECK();
+  });
+  return {y, s, rstd};
+}
+
+// Returns (ds fp32, ds16 bf16 or undefined). dw (fp32, D) is written or accumulated in place.
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor s, at::Tensor w, at::Tensor rstd,
+                                    c10::optional<at::Tensor> ds_in, at::Tensor dw, at::Tensor ticket,
+                                    bool write_ds16, bool accumulate) {
+  LLMT_CHECK_DTYPE(dy, at::kBFloat16);
+  LLMT_CHECK_DTYPE(s, at::kFloat);
+  LLMT_CHECK_DTYPE(dw, at::kFloat);
+  LLMT_CHECK_DTYPE(ticket, at::kInt);
+  LLMT_CHECK_CONTIG(dy);
+  LLMT_CHECK_CONTIG(s);
+  const int D = s.size(-1);
+  const int64_t N = s.numel() / D;
+  LLMT_CHECK(dy.numel() == s.numel(), "dy and s differ in size");
+  auto ds = at::empty_like(s);
+  at::Tensor ds16;
+  if (write_ds16) ds16 = at::empty(s.sizes(), s.options().dtype(at::kBFloat16));
+  const bool has_dsin = ds_in.has_value() && ds_in->defined();
+  if (has_dsin) {
+    LLMT_CHECK_DTYPE((*ds_in), at::kFloat);
+    LLMT_CHECK_CONTIG((*ds_in));
+  }
+  if (N == 0) return {ds, ds16};
+  dispatch_tpr(D, [&](auto tpr) {
+    constexpr int TPR = decltype(tpr)::value;
+    constexpr int RPC = kThreads / TPR;
+    int grid = (int)std::min<int64_t>(cdiv(N, RPC), 2 * sm_count());
+    auto part = at::empty({grid, D}, s.options());
+    const size_t smem = D * sizeof(float);
+    auto launch = [&](auto kern) {
+      kern<<<grid, kThreads, smem, cur_stream()>>>(
+          reinterpret_cast<const bf16*>(dy.data_ptr()), s.data_ptr<float>(), w.data_ptr<float>(),
+          rstd.data_ptr<float>(), has_dsin ? ds_in->data_ptr<float>() : nullptr, ds.data_ptr<float>(),
+          write_ds16 ? reinterpret_cast<bf16*>(ds16.data_ptr()) : nullptr, part.data_ptr<float>(),
+          dw.data_ptr<float>(), reinterpret_cast<unsigned int*>(ticket.data_ptr<int>()), N, D, accumulate ? 1 : 0);
+    };
+    if (has_dsin && write_ds16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
+    else if (has_dsin) launch(rmsnorm_bwd_kernel<TPR, true, false>);
+    else if (write_ds16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
+    else launch(rmsnorm_bwd_kernel<TPR, false, false>);
+    LLMT_LAUNCH_CHECK();
+  });
+  return {ds, ds16};
+}
+
+}  // namespace llmt

@@ -1,0 +1,192 @@
+"""Thin Python wrappers over the sm_100a extension `llmt._C`.
+
+Every wrapper launches on the current CUDA stream and allocates its outputs through the
+PyTorch caching allocator, so the whole training step can be captured in one CUDA graph.
+The extension is required: importing a wrapper without the built extension raises instead
+of silently falling back to PyTorch.
+"""
+from __future__ import annotations
+
+import torch
+
+_C = None
+
+EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD = range(7)
+
+
+def ext():
+    """The compiled extension; raises with build instructions when it is missing."""
+    global _C
+    if _C is None:
+        try:
+            from llmt import _C as c  # noqa: PLC0415
+        except ImportError as e:  # pragma: no cover - depends on the build
+            raise RuntimeError(
+                "llmt native extension is not built; run `python setup.py build_ext --inplace` "
+                "(or __graft_entry__.build())") from e
+        _C = c
+    return _C
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+_tickets: dict[int, torch.Tensor] = {}
+
+
+def _ticket(device) -> torch.Tensor:
+    """Per-device int32 word used by the norm backward's last-CTA-done reduction (self re-arming)."""
+    idx = torch.device(device).index or 0
+    t = _tickets.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _tickets[idx] = t
+    return t
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    return t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and (t.stride(0) * t.element_size()) % 16 == 0
+
+
+# ---------------------------------------------------------------- norms
+def add_rmsnorm_fwd(a, r, w, eps, write_s=True):
+    """y = rmsnorm(r + a) * w. a bf16 or None, r fp32, w fp32 -> (y bf16, s fp32 | None, rstd fp32)."""
+    y, s, rstd = ext().add_rmsnorm_fwd(a, r, w, float(eps), bool(write_s))
+    return y, (s if write_s else None), rstd
+
+
+def rmsnorm_bwd(dy, s, w, rstd, ds_in, dw, accumulate, write_ds16=True):
+    """Returns (ds fp32, ds bf16 | None); writes or accumulates dw (fp32) in place."""
+    ds, ds16 = ext().rmsnorm_bwd(dy, s, w, rstd, ds_in, dw, _ticket(s.device), bool(write_ds16), bool(accumulate))
+    return ds, (ds16 if write_ds16 else None)
+
+
+# ---------------------------------------------------------------- GEMM
+def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate=False, bn=0):
+    """out = op(a) @ op(b) on the tcgen05 GEMM (bf16 operands, fp32 accumulation).
+
+    ta=False, tb=True  : forward   y  = x  @ W^T
+    ta=False, tb=False : dgrad     dx = dy @ W
+    ta=True,  tb=False : wgrad     dW = dy^T @ x   (fp32 out, optional accumulate)
+    Operands need 16-byte aligned bases and row pitches (TMA); the caller pads otherwise.
+    """
+    if not (_tma_ok(a) and _tma_ok(b)):
+        raise ValueError("gemm operands need 16-byte aligned bases and row pitches (TMA)")
+    M = a.shape[1] if ta else a.shape[0]
+    N = b.shape[0] if tb else b.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
+    ext().gemm(a, b, ta, tb, epi, out, accumulate=accumulate, bn=bn)
+    return out
+
+
+def gemm_swiglu(x, w13, ffn, h=None, gu=None, bn=0):
+    """Merged gate/up GEMM with the SwiGLU epilogue: h = silu(x W1^T) * (x W3^T); also saves [g | u]."""
+    M = x.shape[0]
+    if h is None:
+        h = torch.empty((M, ffn), dtype=torch.bfloat16, device=x.device)
+    if gu is None:
+        gu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=x.device)
+    ext().gemm(x, w13, False, True, EPI_SWIGLU, h, aux=gu, split=ffn, bn=bn)
+    return h, gu
+
+
+def gemm_swiglu_bwd(dm, w2, gu, ffn, dgu=None, bn=0):
+    """w2 dgrad with the SwiGLU backward epilogue: dh = dm @ W2, then [dg | du] from the saved [g | u]."""
+    M = dm.shape[0]
+    if dgu is None:
+        dgu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=dm.device)
+    ext().gemm(dm, w2, False, False, EPI_SWIGLU_BWD, dgu, aux=gu, out2=dgu, split=ffn, bn=bn)
+    return dgu
+
+
+def gemm_rope(x, wqkv, cos, sin, T, hd, rot_cols, out=None, bn=0):
+    """qkv GEMM with RoPE applied to the first rot_cols (q and k) columns in the epilogue."""
+    M, N = x.shape[0], wqkv.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    ext().gemm(x, wqkv, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols, bn=bn)
+    return out
+
+
+def gemm_ce_fwd(h, w, targets, bn=256):
+    """Logit tiles reduced in the epilogue: returns (lse fp32 (M,), loss fp32 (M,)); no logits written."""
+    M, V = h.shape[0], w.shape[0]
+    nblk = -(-V // bn)
+    part = torch.empty((M, nblk, 2), dtype=torch.float32, device=h.device)
+    tl = torch.zeros((M,), dtype=torch.float32, device=h.device)
+    dummy = torch.empty((M, 8), dtype=torch.bfloat16, device=h.device)
+    ext().gemm(h, w, False, True, EPI_CE_FWD, dummy, tgt=targets, part=part, tlogit=tl, bn=bn)
+    lse = torch.empty((M,), dtype=torch.float32, device=h.device)
+    loss = torch.empty((M,), dtype=torch.float32, device=h.device)
+    ext().ce_combine(part, tl, targets, lse, loss, nblk, V)
+    return lse, loss
+
+
+def gemm_ce_bwd(h, w, targets, lse, grad_out, scale, out=None, bn=0):
+    """Recomputed logit tiles -> dlogits = (softmax - onehot) * grad_out * scale, bf16 (M, V)."""
+    M, V = h.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty((M, V), dtype=torch.bfloat16, device=h.device)
+    ext().gemm(h, w, False, True, EPI_CE_BWD, out, tgt=targets, lse=lse, grad_out=grad_out, alpha=scale, bn=bn)
+    return out
+
+
+def gemm_error_code(reset=False) -> int:
+    """Sticky code of the first bounded-wait timeout any GEMM launch hit (0 = none)."""
+    return ext().gemm_error_code(reset)
+
+
+# ---------------------------------------------------------------- elementwise
+def swiglu_fwd(g, u, h=None):
+    if h is None:
+        h = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
+    ext().swiglu_fwd(g, u, h)
+    return h
+
+
+def swiglu_bwd(dh, g, u, dg=None, du=None):
+    if dg is None:
+        dg = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
+    if du is None:
+        du = torch.empty(u.shape, dtype=torch.bfloat16, device=u.device)
+    ext().swiglu_bwd(dh, g, u, dg, du)
+    return dg, du
+
+
+def rope_inplace(qkv2d, cos, sin, T, n_rot_heads, hd, backward=False):
+    ext().rope_inplace(qkv2d, cos, sin, int(T), int(n_rot_heads), int(hd), bool(backward))
+    return qkv2d
+
+
+def embedding_fwd(idx, W, out=None):
+    if out is None:
+        out = torch.empty((idx.numel(), W.shape[1]), dtype=torch.float32, device=W.device)
+    ext().embedding_fwd(idx.reshape(-1), W, out, None)
+    return out
+
+
+def embedding_bwd(idx, dx, dW):
+    ext().embedding_bwd(idx.reshape(-1), dx, dW)
+
+
+def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0):
+    ext().adamw_step(p, g, m, v, p16, lr, step, float(b1), float(b2), float(eps), float(wd), float(grad_scale))
+
+
+def cast_bf16(x, y):
+    ext().cast_bf16(x, y)
+
+
+def ce_fwd_rows(logits, targets, lse, loss):
+    ext().ce_fwd_rows(logits, targets, lse, loss)
+
+
+def ce_bwd_rows(logits, targets, lse, grad_out, scale):
+    ext().ce_bwd_rows(logits, targets, lse, grad_out, float(scale))
