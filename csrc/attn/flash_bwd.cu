@@ -1,0 +1,453 @@
+// Causal flash attention backward on tcgen05 tensor cores (sm_100a), with the RoPE backward
+// and the packed-dqkv write fused into its epilogues.
+//
+// Replaces the backward of the reference's SDPA (autograd of bench_train.py:141-142, three
+// launches, perf_model/roofline.py:234-236) and its RoPE backward kernel
+// (kernels/triton_ops.py:256-287): the result is written straight into the packed
+// dqkv rows (B*T, (H + 2*KV) * hd) that the qkv dgrad/wgrad GEMMs read.
+//
+// FlashAttention-2 style split (Dao 2023): one CTA per (batch, kv head, 128-key block) owns
+// dK/dV in TMEM and walks every query block at or after its keys (causal) of every query
+// head in its GQA group. Per step, with S^T, dP^T and the accumulators in TMEM:
+//   S^T  = K Q^T,  dP^T = V dO^T                 (M = 128 keys)
+//   P^T  = exp(scale S^T - lse),  dS^T = P^T (dP^T - D)   (one thread per key row)
+//   dV  += P^T dO,  dK += dS^T Q                  (P^T, dS^T staged in swizzled smem)
+//   dQ   = dS K  (dS^T read as an MN-major A operand) -> fp32 atomics into dq_acc
+// D = rowsum(dO * O) comes from a small pre-pass; a post-pass turns dq_acc into bf16 with
+// the RoPE backward applied. dK gets its RoPE backward in this kernel's epilogue.
+#include "../common/common.cuh"
+#include "../common/sm100.cuh"
+#include "../common/tma.h"
+
+namespace llmt {
+int* attn_err_word();
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;  // keys per CTA
+constexpr int kBN = 128;  // queries per step
+constexpr int kBwdThreads = 192;
+
+struct AttnBwdArgs {
+  const float* lse;   // (B, H, T) natural log
+  const float* dsum;  // (B, H, T) rowsum(dO * O)
+  float* dq_acc;      // (B*T, H*hd) fp32, pre-zeroed
+  bf16* dqkv;         // (B*T, (H + 2*KV) * hd)
+  const float* cos_t;
+  const float* sin_t;
+  int B, T, H, KV, ld_qkv, ld_dq;
+  float scale, scale_log2;
+  int causal;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t sw_unit(int r, int u) {
+  return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void named_bar_compute() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int HD>
+struct BwdSmem {
+  static constexpr int STAGES = HD == 64 ? 2 : 1;
+  static constexpr uint32_t T_BYTES = 128 * HD * 2;  // one 128-row tile
+  static constexpr uint32_t K_OFF = 0;
+  static constexpr uint32_t V_OFF = K_OFF + T_BYTES;
+  static constexpr uint32_t Q_OFF = V_OFF + T_BYTES;
+  static constexpr uint32_t DO_OFF = Q_OFF + STAGES * T_BYTES;
+  static constexpr uint32_t P_OFF = DO_OFF + STAGES * T_BYTES;
+  static constexpr uint32_t DS_OFF = P_OFF + 128 * 128 * 2;
+  static constexpr uint32_t VEC_OFF = DS_OFF + 128 * 128 * 2;  // lse (128) + D (128) floats
+  static constexpr uint32_t BAR_OFF = VEC_OFF + 1024;
+  static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                 const AttnBwdArgs a) {
+  using L = BwdSmem<HD>;
+  constexpr int ST = L::STAGES;
+  constexpr int TMEM_COLS = 512;
+  constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + HD;
+  constexpr uint32_t C_DQ = HD == 64 ? 384 : 0;  // HD=128: dQ reuses S^T's columns
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;     // [ST]
+  uint64_t* q_empty = bars + 3;    // [ST]
+  uint64_t* s_full = bars + 5;
+  uint64_t* pds_full = bars + 6;   // 128 arrivals
+  uint64_t* pds_empty = bars + 7;
+  uint64_t* dq_full = bars + 8;
+  uint64_t* tm_free = bars + 9;    // 128 arrivals: S/dP/dQ columns free again
+  uint64_t* dkv_full = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  float* lse_s = reinterpret_cast<float*>(smem + L::VEC_OFF);
+  float* d_s = lse_s + 128;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kb = blockIdx.x;             // key block
+  const int bk = blockIdx.y;             // b * KV + kv head
+  const int b = bk / a.KV, kvh = bk % a.KV;
+  const int group = a.H / a.KV;
+  const int nqb = (int)cdiv(a.T, kBN);
+  const int i_start = a.causal ? kb : 0;
+  const int n_i = nqb - i_start;
+  const int n_items = group * n_i;
+  const int row0 = b * a.T;
+  const int k0 = kb * kBM;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    bar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      bar_init(&q_full[s], 1);
+      bar_init(&q_empty[s], 1);
+    }
+    bar_init(s_full, 1);
+    bar_init(pds_full, 128);
+    bar_init(pds_empty, 1);
+    bar_init(dq_full, 1);
+    bar_init(tm_free, 128);
+    bar_init(dkv_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_qkv);
+      prefetch_tmap(&tm_do);
+      const int kcol = (a.H + kvh) * HD, vcol = (a.H + a.KV + kvh) * HD;
+      bar_arrive_expect_tx(kv_full, 2 * L::T_BYTES);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        tma_load_2d(smem + L::K_OFF + c * 16384, &tm_qkv, kv_full, kcol + c * 64, row0 + k0);
+        tma_load_2d(smem + L::V_OFF + c * 16384, &tm_qkv, kv_full, vcol + c * 64, row0 + k0);
+      }
+      for (int n = 0; n < n_items; ++n) {
+        const int s = n % ST;
+        const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
+        if (!wait_bar(&q_empty[s], ((n / ST) & 1) ^ 1, err, 31)) break;
+        bar_arrive_expect_tx(&q_full[s], 2 * L::T_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_2d(smem + L::Q_OFF + s * L::T_BYTES + c * 16384, &tm_qkv, &q_full[s], hq * HD + c * 64,
+                      row0 + i * kBN);
+          tma_load_2d(smem + L::DO_OFF + s * L::T_BYTES + c * 16384, &tm_do, &q_full[s], hq * HD + c * 64,
+                      row0 + i * kBN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = make_idesc_bf16(kBM, kBN, false, false);   // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_bf16(kBM, HD, false, true);   // dV, dK (B MN-major)
+      constexpr uint32_t id_q = make_idesc_bf16(kBN, HD, true, true);     // dQ (A = dS MN-major)
+      const uint32_t k_addr = smem_u32(smem + L::K_OFF), v_addr = smem_u32(smem + L::V_OFF);
+      const uint32_t p_addr = smem_u32(smem + L::P_OFF), ds_addr = smem_u32(smem + L::DS_OFF);
+      bool ok = wait_bar(kv_full, 0, err, 32);
+      for (int n = 0; n < n_items && ok; ++n) {
+        const int s = n % ST;
+        if (!wait_bar(&q_full[s], (n / ST) & 1, err, 33)) { ok = false; break; }
+        if (!wait_bar(tm_free, (n & 1) ^ 1, err, 34)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::T_BYTES);
+        const uint32_t do_addr = smem_u32(smem + L::DO_OFF + s * L::T_BYTES);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          mma_f16(tmem + C_S, make_sw128_desc(k_addr + off, 16, 1024), make_sw128_desc(q_addr + off, 16, 1024), id_s,
+                  k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          mma_f16(tmem + C_DP, make_sw128_desc(v_addr + off, 16, 1024), make_sw128_desc(do_addr + off, 16, 1024), id_s,
+                  k > 0);
+        }
+        mma_commit(s_full);
+        if (!wait_bar(pds_full, n & 1, err, 35)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          const uint32_t offk = (k >> 2) * 16384 + (k & 3) * 32;  // K-major step over queries
+          const uint32_t offm = k * 2048;                          // MN-major step over queries
+          mma_f16(tmem + C_DV, make_sw128_desc(p_addr + offk, 16, 1024), make_sw128_desc(do_addr + offm, 16384, 1024),
+                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
+          mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024), make_sw128_desc(q_addr + offm, 16384, 1024),
+                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < kBM / 16; ++k) {  // contraction over keys
+          mma_f16(tmem + C_DQ, make_sw128_desc(ds_addr + k * 2048, 16384, 1024),
+                  make_sw128_desc(k_addr + k * 2048, 16384, 1024), id_q, k > 0);
+        }
+        mma_commit(dq_full);
+        mma_commit(pds_empty);
+        mma_commit(&q_empty[s]);
+      }
+      if (ok) mma_commit(dkv_full);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
+    bool ok = true;
+    for (int n = 0; n < n_items; ++n) {
+      const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
+      const int qbase = i * kBN;
+      named_bar_compute();
+      {
+        const int qq = qbase + r;
+        const int64_t vi = ((int64_t)b * a.H + hq) * a.T + qq;
+        lse_s[r] = qq < a.T ? a.lse[vi] * 1.4426950408889634f : INFINITY;
+        d_s[r] = qq < a.T ? a.dsum[vi] : 0.f;
+      }
+      named_bar_compute();
+      if (!wait_bar(s_full, n & 1, err, 36)) { ok = false; break; }
+      if (!wait_bar(pds_empty, (n & 1) ^ 1, err, 37)) { ok = false; break; }
+      tc_fence_after();
+      uint8_t* pt = smem + L::P_OFF;
+      uint8_t* dst = smem + L::DS_OFF;
+      const bool diag = a.causal && (qbase < k0 + kBM);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
+        tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
+        tmem_wait_ld();
+        float p[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qi = c * 32 + e;
+          const int qq = qbase + qi;
+          const bool valid = (kk < a.T) && (!diag || qq >= kk);
+          const float pe = valid ? exp2f(__uint_as_float(sv[e]) * a.scale_log2 - lse_s[qi]) : 0.f;
+          p[e] = pe;
+          ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          *reinterpret_cast<BF16x8*>(pt + sw_unit(r, c * 4 + u)) = float_to_bf16x8(p + u * 8);
+          *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      bar_arrive(pds_full);
+      // dQ rows (thread = query row of this block)
+      if (!wait_bar(dq_full, n & 1, err, 38)) { ok = false; break; }
+      tc_fence_after();
+      const int qq = qbase + r;
+      float* dqrow = a.dq_acc + (int64_t)(row0 + qq) * a.ld_dq + hq * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + C_DQ + c * 32, v);
+        tmem_wait_ld();
+        if (qq < a.T) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 t = make_float4(__uint_as_float(v[e]) * a.scale, __uint_as_float(v[e + 1]) * a.scale,
+                                   __uint_as_float(v[e + 2]) * a.scale, __uint_as_float(v[e + 3]) * a.scale);
+            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + e), t);
+          }
+        }
+      }
+      tc_fence_before();
+      bar_arrive(tm_free);
+    }
+    // dK (scaled, RoPE backward) and dV rows -> packed dqkv
+    if (ok && wait_bar(dkv_full, 0, err, 39)) {
+      tc_fence_after();
+      float x[HD];
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + C_DK + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * a.scale;
+      }
+      if (kk < a.T) {
+        const float* cr = a.cos_t + (int64_t)kk * HD;
+        const float* sr = a.sin_t + (int64_t)kk * HD;
+        float y[HD];
+#pragma unroll
+        for (int e = 0; e < HD / 2; ++e) {
+          y[e] = x[e] * cr[e] + x[e + HD / 2] * sr[e + HD / 2];
+          y[e + HD / 2] = x[e + HD / 2] * cr[e + HD / 2] - x[e] * sr[e];
+        }
+        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (a.H + kvh) * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(y + c * 8);
+      }
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + C_DV + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]);
+      }
+      if (kk < a.T) {
+        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (a.H + a.KV + kvh) * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(x + c * 8);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<TMEM_COLS>(tmem);
+  }
+}
+
+// D = rowsum(dO * O) per (b, h, t); also zeroes the fp32 dQ accumulator row slice.
+template <int HD>
+__global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dO, float* __restrict__ dsum,
+                                    float* __restrict__ dq_acc, int BT, int T, int H) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // (row, head)
+  if (idx >= (int64_t)BT * H) return;
+  const int64_t row = idx / H;
+  const int h = (int)(idx % H);
+  const bf16* op = o + row * (int64_t)H * HD + h * HD;
+  const bf16* dp = dO + row * (int64_t)H * HD + h * HD;
+  float* dq = dq_acc + row * (int64_t)H * HD + h * HD;
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD / 8; ++c) {
+    float x[8], y[8];
+    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(op + c * 8), x);
+    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dp + c * 8), y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += x[e] * y[e];
+    st_f4(dq + c * 8, make_float4(0.f, 0.f, 0.f, 0.f));
+    st_f4(dq + c * 8 + 4, make_float4(0.f, 0.f, 0.f, 0.f));
+  }
+  const int b = (int)(row / T), t = (int)(row % T);
+  dsum[((int64_t)b * H + h) * T + t] = acc;
+}
+
+// dq (bf16, RoPE backward) <- dq_acc (fp32), into the q columns of the packed dqkv rows.
+template <int HD>
+__global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, bf16* __restrict__ dqkv,
+                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int BT, int T,
+                                     int H, int ld_qkv) {
+  constexpr int HALF = HD / 2;
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // (row, head, 8-chunk of half)
+  constexpr int CH = HALF / 8;
+  if (idx >= (int64_t)BT * H * CH) return;
+  const int c = (int)(idx % CH) * 8;
+  const int64_t rest = idx / CH;
+  const int h = (int)(rest % H);
+  const int64_t row = rest / H;
+  const int t = (int)(row % T);
+  const float* src = dq_acc + row * (int64_t)H * HD + h * HD;
+  float x1[8], x2[8], y1[8], y2[8];
+  float4 a0 = ld_f4(src + c), a1 = ld_f4(src + c + 4), b0 = ld_f4(src + HALF + c), b1 = ld_f4(src + HALF + c + 4);
+  x1[0] = a0.x; x1[1] = a0.y; x1[2] = a0.z; x1[3] = a0.w; x1[4] = a1.x; x1[5] = a1.y; x1[6] = a1.z; x1[7] = a1.w;
+  x2[0] = b0.x; x2[1] = b0.y; x2[2] = b0.z; x2[3] = b0.w; x2[4] = b1.x; x2[5] = b1.y; x2[6] = b1.z; x2[7] = b1.w;
+  const float* cr = cos_t + (int64_t)t * HD;
+  const float* sr = sin_t + (int64_t)t * HD;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    y1[e] = x1[e] * cr[c + e] + x2[e] * sr[HALF + c + e];
+    y2[e] = x2[e] * cr[HALF + c + e] - x1[e] * sr[c + e];
+  }
+  bf16* dst = dqkv + row * (int64_t)ld_qkv + h * HD;
+  *reinterpret_cast<BF16x8*>(dst + c) = float_to_bf16x8(y1);
+  *reinterpret_cast<BF16x8*>(dst + HALF + c) = float_to_bf16x8(y2);
+}
+
+template <int HD>
+void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args) {
+  auto kern = flash_bwd_kernel<HD>;
+  constexpr size_t smem = BwdSmem<HD>::TOTAL;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  dim3 grid((int)cdiv(args.T, kBM), args.B * args.KV);
+  kern<<<grid, kBwdThreads, smem, cur_stream()>>>(tq, tdo, args);
+  LLMT_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+// Returns dqkv (B*T, (H + 2*KV) * hd) bf16 with the RoPE backward applied to the q and k parts.
+at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor cos_t,
+                          at::Tensor sin_t, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, bool causal,
+                          double scale) {
+  LLMT_CHECK_DTYPE(dO, at::kBFloat16);
+  LLMT_CHECK_DTYPE(qkv, at::kBFloat16);
+  LLMT_CHECK_DTYPE(o, at::kBFloat16);
+  LLMT_CHECK_DTYPE(lse, at::kFloat);
+  LLMT_CHECK(hd == 64 || hd == 128, "flash_attn_bwd: head dim must be 64 or 128");
+  LLMT_CHECK(dO.is_contiguous() && o.is_contiguous() && qkv.is_contiguous() && lse.is_contiguous(),
+             "flash_attn_bwd: operands must be contiguous");
+  LLMT_CHECK(dO.numel() == B * T * H * hd && o.numel() == dO.numel(), "flash_attn_bwd: dO/o shape");
+  LLMT_CHECK(qkv.size(0) == B * T && qkv.size(1) == (H + 2 * KV) * hd, "flash_attn_bwd: qkv shape");
+  LLMT_CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd && cos_t.is_contiguous() && sin_t.is_contiguous(),
+             "flash_attn_bwd: rope tables");
+  LLMT_CHECK(tma_ok(qkv.data_ptr(), qkv.stride(0), 2) && tma_ok(dO.data_ptr(), H * hd, 2),
+             "flash_attn_bwd: TMA alignment");
+  auto dqkv = at::empty_like(qkv);
+  auto dsum = at::empty({B, H, T}, lse.options());
+  auto dq_acc = at::empty({B * T, H * hd}, lse.options());
+  const int64_t rows = B * T;
+  {
+    const int64_t n = rows * H;
+    auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
+    k<<<cdiv(n, 256), 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
+                                              reinterpret_cast<const bf16*>(dO.data_ptr()), dsum.data_ptr<float>(),
+                                              dq_acc.data_ptr<float>(), (int)rows, (int)T, (int)H);
+    LLMT_LAUNCH_CHECK();
+  }
+  AttnBwdArgs args{};
+  args.lse = lse.data_ptr<float>();
+  args.dsum = dsum.data_ptr<float>();
+  args.dq_acc = dq_acc.data_ptr<float>();
+  args.dqkv = reinterpret_cast<bf16*>(dqkv.data_ptr());
+  args.cos_t = cos_t.data_ptr<float>();
+  args.sin_t = sin_t.data_ptr<float>();
+  args.B = (int)B;
+  args.T = (int)T;
+  args.H = (int)H;
+  args.KV = (int)KV;
+  args.ld_qkv = (int)qkv.size(1);
+  args.ld_dq = (int)(H * hd);
+  args.scale = (float)scale;
+  args.scale_log2 = (float)(scale * 1.4426950408889634);
+  args.causal = causal ? 1 : 0;
+  args.err = attn_err_word();
+  alignas(64) CUtensorMap tq, tdo;
+  make_tmap_2d(&tq, qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.size(1), rows, qkv.stride(0), 64, 128);
+  make_tmap_2d(&tdo, dO.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H * hd, rows, H * hd, 64, 128);
+  if (hd == 64) launch_bwd<64>(tq, tdo, args);
+  else launch_bwd<128>(tq, tdo, args);
+  {
+    const int64_t n = rows * H * (hd / 16);
+    auto k = hd == 64 ? attn_bwd_post_kernel<64> : attn_bwd_post_kernel<128>;
+    k<<<cdiv(n, 256), 256, 0, cur_stream()>>>(dq_acc.data_ptr<float>(), reinterpret_cast<bf16*>(dqkv.data_ptr()),
+                                              cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)rows, (int)T,
+                                              (int)H, (int)qkv.size(1));
+    LLMT_LAUNCH_CHECK();
+  }
+  return dqkv;
+}
+
+}  // namespace llmt

@@ -27,6 +27,12 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
 int gemm_error_code(bool reset);
 void ce_combine(at::Tensor part, at::Tensor tlogit, at::Tensor tgt, at::Tensor lse, at::Tensor loss, int64_t nblk,
                 int64_t V);
+std::vector<at::Tensor> flash_attn_fwd(at::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
+                                       bool causal, double scale);
+at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor cos_t,
+                          at::Tensor sin_t, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, bool causal,
+                          double scale);
+int attn_error_code(bool reset);
 }  // namespace llmt
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -51,4 +57,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "grad_out"_a = py::none(), "part"_a = py::none(), "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
   m.def("ce_combine", &llmt::ce_combine);
+  m.def("flash_attn_fwd", &llmt::flash_attn_fwd);
+  m.def("flash_attn_bwd", &llmt::flash_attn_bwd);
+  m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
 }

@@ -1,0 +1,122 @@
+"""Native (sm_100a) execution of the reference-layout LlamaModel.
+
+`NativeLlama(model)` keeps the model's nn.Parameters (so state_dict keys and values are
+unchanged) but re-points every parameter at a view of one flat fp32 master buffer, with
+matching views into a flat fp32 gradient buffer (`p.main_grad`) and a flat bf16 shadow
+buffer (`p.w16`) that the GEMMs read and the fused AdamW rewrites every step. Packing
+order puts each block's w1 directly before w3, so the merged gate/up GEMM reads one
+(2*ffn, d) weight and writes one (2*ffn, d) gradient without any copy. The flat buffers
+are also what the data-parallel engine shards (ZeRO-1) and reduce-scatters.
+
+The reference builds the same network from nn.Linear under bf16 autocast with fp32 master
+weights (bench_train.py:458-492); this path keeps fp32 masters and the fp32 residual stream,
+runs every GEMM in bf16 with fp32 accumulation, and never materializes logits.
+"""
+from __future__ import annotations
+
+import torch
+
+from llmt.models.llama import LlamaModel
+from llmt.ops import functions as Fn
+from llmt.ops import native as N
+
+ALIGN = 64  # elements; keeps every view 256-byte (fp32) / 128-byte (bf16) aligned
+
+
+def param_order(model: LlamaModel):
+    """(name, parameter) in flat-buffer order: per block qkv, wo, w1, w3, w2, norms; then emb, norm_f, head."""
+    out = []
+    for i, blk in enumerate(model.blocks):
+        p = f"blocks.{i}."
+        out += [(p + "attn.qkv.weight", blk.attn.qkv.weight), (p + "attn.wo.weight", blk.attn.wo.weight),
+                (p + "mlp.w1.weight", blk.mlp.w1.weight), (p + "mlp.w3.weight", blk.mlp.w3.weight),
+                (p + "mlp.w2.weight", blk.mlp.w2.weight), (p + "norm1.weight", blk.norm1.weight),
+                (p + "norm2.weight", blk.norm2.weight)]
+    out += [("emb.weight", model.emb.weight), ("norm_f.weight", model.norm_f.weight), ("head.weight", model.head.weight)]
+    return out
+
+
+class FlatParams:
+    """Flat fp32 master / fp32 grad / bf16 shadow storage behind a model's parameters."""
+
+    def __init__(self, model: LlamaModel, device, pad_to: int = 1):
+        self.names = []
+        self.params = []
+        self.offsets = []
+        off = 0
+        for name, p in param_order(model):
+            if off % ALIGN:
+                off += ALIGN - off % ALIGN
+            self.names.append(name)
+            self.params.append(p)
+            self.offsets.append(off)
+            off += p.numel()
+        if off % (ALIGN * pad_to):
+            off += ALIGN * pad_to - off % (ALIGN * pad_to)
+        self.numel = off
+        dev = torch.device(device)
+        self.master = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.grad = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.shadow = torch.zeros(off, dtype=torch.bfloat16, device=dev)
+        with torch.no_grad():
+            for p, o in zip(self.params, self.offsets):
+                n = p.numel()
+                self.master[o:o + n].copy_(p.detach().reshape(-1).to(dev, torch.float32))
+                p.data = self.master[o:o + n].view(p.shape)
+                p.main_grad = self.grad[o:o + n].view(p.shape)
+                p.w16 = self.shadow[o:o + n].view(p.shape)
+        for blk in model.blocks:
+            w1, w3 = blk.mlp.w1.weight, blk.mlp.w3.weight
+            o1 = self.offsets[self.params.index(w1)]
+            o3 = self.offsets[self.params.index(w3)]
+            if o3 != o1 + w1.numel():
+                raise RuntimeError("w1 and w3 must be adjacent in the flat buffer (ffn*d must be a multiple of 64)")
+            ffn, d = w1.shape
+            w1.w13_16 = self.shadow[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
+            w1.w13_grad = self.grad[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
+            w1.w3_param = w3
+        self.refresh_shadow()
+
+    def refresh_shadow(self):
+        """bf16 shadow := master (after init or a checkpoint load)."""
+        N.cast_bf16(self.master, self.shadow)
+
+    def zero_grad(self):
+        self.grad.zero_()
+
+
+class NativeLlama:
+    """Runs `model` on the native kernels. forward(idx, targets) -> mean loss (like the reference).
+
+    A plain wrapper (not an nn.Module), so model.state_dict() keeps the reference keys."""
+
+    def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1):
+        self.model = model
+        self.cfg = model.cfg
+        dev = model.emb.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("the native path runs on CUDA (sm_100a) only")
+        self.flat = FlatParams(model, dev, pad_to=pad_to)
+        self.ce_chunk = ce_chunk
+
+    def forward(self, idx, targets):
+        cfg, m = self.cfg, self.model
+        B, T = idx.shape
+        cos = m.rope_cos[:T].contiguous()
+        sin = m.rope_sin[:T].contiguous()
+        x = Fn.Embed.apply(idx.reshape(-1), m.emb.weight)
+        a, r = None, x
+        for blk in m.blocks:
+            if a is None:
+                n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
+            else:
+                n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+            o = Fn.QKVAttention.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
+            att = Fn.Linear.apply(o, blk.attn.wo.weight)
+            n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+            a = Fn.SwiGLUMLP.apply(n2, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn)
+            r = s2
+        h = Fn.FinalNormFn.apply(a, r, m.norm_f.weight, cfg.eps)
+        return Fn.HeadCE.apply(h, m.head.weight, targets.reshape(-1), self.ce_chunk)
+
+    __call__ = forward

@@ -1,0 +1,213 @@
+"""Autograd Functions of the native training path.
+
+Each Function covers one fused region of the step and calls only sm_100a kernels of
+llmt._C. Weight gradients never go through autograd: every backward writes its fp32 weight
+gradient straight into the parameter's `main_grad` view of the flat gradient buffer
+(overwrite on the first micro-batch, accumulate afterwards; see GradFlags), so the
+optimizer and the data-parallel reduce-scatter read one contiguous buffer.
+
+Regions (reference equivalents in bench_train.py / kernels/triton_ops.py):
+  Embed          emb(idx)                                        bench_train.py:213
+  RMSNormFn      rmsnorm on the fp32 residual                    triton_ops.py:113-128
+  AddRMSNormFn   s = r + a; y = rmsnorm(s)                       triton_ops.py:131-151
+  QKVAttention   qkv GEMM (+RoPE epilogue) -> causal flash attn  bench_train.py:130-149
+  Linear         y = x W^T (wo)                                  bench_train.py:150
+  SwiGLUMLP      w1||w3 GEMM (+SwiGLU epilogue) -> w2 GEMM       bench_train.py:153-163
+  HeadCE         lm head + cross entropy, logits never written   triton_ops.py:367-405
+"""
+from __future__ import annotations
+
+import torch
+
+from llmt.ops import native as N
+
+
+class GradFlags:
+    """Tracks which parameters already hold a gradient in this step (write vs accumulate)."""
+
+    def __init__(self):
+        self._written: set[int] = set()
+
+    def reset(self):
+        self._written.clear()
+
+    def accumulate(self, p) -> bool:
+        """True if p's main_grad already holds this step's gradient; marks it as written."""
+        key = id(p)
+        acc = key in self._written
+        self._written.add(key)
+        return acc
+
+
+FLAGS = GradFlags()
+
+
+class Embed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, idx, w):
+        ctx.save_for_backward(idx)
+        ctx.w = w
+        return N.embedding_fwd(idx, w)
+
+    @staticmethod
+    def backward(ctx, dx):
+        (idx,) = ctx.saved_tensors
+        w = ctx.w
+        if not FLAGS.accumulate(w):
+            w.main_grad.zero_()
+        N.embedding_bwd(idx, dx.contiguous(), w.main_grad)
+        return None, None
+
+
+class RMSNormFn(torch.autograd.Function):
+    """y = rmsnorm(x) * w on the fp32 residual x (no add); y bf16."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        y, _, rstd = N.add_rmsnorm_fwd(None, x, w, eps, write_s=False)
+        ctx.save_for_backward(x, rstd)
+        ctx.w = w
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rstd = ctx.saved_tensors
+        w = ctx.w
+        ds, _ = N.rmsnorm_bwd(dy.contiguous(), x, w, rstd, None, w.main_grad, FLAGS.accumulate(w), write_ds16=False)
+        return ds, None, None
+
+
+class AddRMSNormFn(torch.autograd.Function):
+    """s = r + a (fp32 residual + bf16 branch output), y = rmsnorm(s) * w. Returns (y, s)."""
+
+    @staticmethod
+    def forward(ctx, a, r, w, eps):
+        y, s, rstd = N.add_rmsnorm_fwd(a, r, w, eps, write_s=True)
+        ctx.save_for_backward(s, rstd)
+        ctx.w = w
+        return y, s
+
+    @staticmethod
+    def backward(ctx, dy, ds_in):
+        s, rstd = ctx.saved_tensors
+        w = ctx.w
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, ds_in, w.main_grad, FLAGS.accumulate(w), write_ds16=True)
+        return ds16, ds, None, None
+
+
+class FinalNormFn(torch.autograd.Function):
+    """Final norm: y = rmsnorm(r + a) * w without keeping s as an output."""
+
+    @staticmethod
+    def forward(ctx, a, r, w, eps):
+        y, s, rstd = N.add_rmsnorm_fwd(a, r, w, eps, write_s=True)
+        ctx.save_for_backward(s, rstd)
+        ctx.w = w
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        s, rstd = ctx.saved_tensors
+        w = ctx.w
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, None, w.main_grad, FLAGS.accumulate(w), write_ds16=True)
+        return ds16, ds, None, None
+
+
+def _wgrad(dy, x, p):
+    """p.main_grad (out, in) (+)= dy^T x, fp32, on the tcgen05 GEMM."""
+    N.gemm(dy, x, ta=True, tb=False, out=p.main_grad, accumulate=FLAGS.accumulate(p))
+
+
+class QKVAttention(torch.autograd.Function):
+    """o = attention(rope(x Wqkv^T)); x (B*T, d) bf16 -> o (B*T, H*hd) bf16."""
+
+    @staticmethod
+    def forward(ctx, x, w, cos, sin, B, T, H, KV, hd):
+        qkv = N.gemm_rope(x, w.w16, cos, sin, T, hd, (H + KV) * hd)
+        o, lse = N.flash_attn_fwd(qkv, B, T, H, KV, hd, causal=True)
+        ctx.save_for_backward(x, qkv, o, lse, cos, sin)
+        ctx.w = w
+        ctx.dims = (B, T, H, KV, hd)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        x, qkv, o, lse, cos, sin = ctx.saved_tensors
+        B, T, H, KV, hd = ctx.dims
+        w = ctx.w
+        dqkv = N.flash_attn_bwd(do.contiguous(), qkv, o, lse, cos, sin, B, T, H, KV, hd, causal=True)
+        dx = N.gemm(dqkv, w.w16, ta=False, tb=False)
+        _wgrad(dqkv, x, w)
+        return dx, None, None, None, None, None, None, None, None
+
+
+class Linear(torch.autograd.Function):
+    """y = x W^T with bf16 operands; W's fp32 gradient goes to W.main_grad."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.save_for_backward(x)
+        ctx.w = w
+        return N.gemm(x, w.w16, ta=False, tb=True)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        w = ctx.w
+        dy = dy.contiguous()
+        dx = N.gemm(dy, w.w16, ta=False, tb=False)
+        _wgrad(dy, x, w)
+        return dx, None
+
+
+class SwiGLUMLP(torch.autograd.Function):
+    """m = (silu(x W1^T) * (x W3^T)) W2^T with W1, W3 packed adjacently (one merged GEMM)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, ffn):
+        h, gu = N.gemm_swiglu(x, w1.w13_16, ffn)
+        m = N.gemm(h, w2.w16, ta=False, tb=True)
+        ctx.save_for_backward(x, h, gu)
+        ctx.w1, ctx.w2, ctx.ffn = w1, w2, ffn
+        return m
+
+    @staticmethod
+    def backward(ctx, dm):
+        x, h, gu = ctx.saved_tensors
+        w1, w2, ffn = ctx.w1, ctx.w2, ctx.ffn
+        dm = dm.contiguous()
+        dgu = N.gemm_swiglu_bwd(dm, w2.w16, gu, ffn)
+        _wgrad(dm, h, w2)
+        dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
+        acc = FLAGS.accumulate(w1)
+        FLAGS.accumulate(w1.w3_param)
+        N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=acc)
+        return dx, None, None, None
+
+
+class HeadCE(torch.autograd.Function):
+    """Mean cross entropy of the lm head; logits are never written (forward), and are
+    recomputed tile by tile into bf16 dlogits chunks of at most `chunk` rows (backward)."""
+
+    @staticmethod
+    def forward(ctx, h, w, targets, chunk):
+        lse, loss_rows = N.gemm_ce_fwd(h, w.w16, targets)
+        ctx.save_for_backward(h, targets, lse)
+        ctx.w, ctx.chunk = w, chunk
+        return loss_rows.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        h, targets, lse = ctx.saved_tensors
+        w, chunk = ctx.w, ctx.chunk
+        n = h.shape[0]
+        g = g.reshape(1).float().contiguous()
+        dh = torch.empty_like(h)
+        acc = FLAGS.accumulate(w)
+        for i, c0 in enumerate(range(0, n, chunk)):
+            c1 = min(n, c0 + chunk)
+            hc = h[c0:c1]
+            dl = N.gemm_ce_bwd(hc, w.w16, targets[c0:c1], lse[c0:c1], g, 1.0 / n)
+            N.gemm(dl, w.w16, ta=False, tb=False, out=dh[c0:c1])
+            N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=acc or i > 0)
+        return dh, None, None, None

@@ -14,6 +14,45 @@ _C = None
 EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD = range(7)
 
 
+# Kernels launched per call of an extension entry point (1 unless listed).
+_KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0}
+
+
+class LaunchCounter:
+    """Counts this library's kernel launches issued from Python (captured graphs replay them)."""
+
+    def __init__(self):
+        self.count = 0
+        self.bodies = 0
+
+    def reset(self):
+        self.count = 0
+        self.bodies = 0
+
+    def per_step(self, trainer=None) -> int:
+        bodies = trainer.body_calls if trainer is not None else self.bodies
+        return int(round(self.count / max(1, bodies)))
+
+
+LAUNCHES = LaunchCounter()
+
+
+class _Counted:
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        k = _KERNELS_PER_CALL.get(name, 1)
+
+        def call(*a, **kw):
+            LAUNCHES.count += k
+            return fn(*a, **kw)
+        return call
+
+
 def ext():
     """The compiled extension; raises with build instructions when it is missing."""
     global _C
@@ -24,7 +63,7 @@ def ext():
             raise RuntimeError(
                 "llmt native extension is not built; run `python setup.py build_ext --inplace` "
                 "(or __graft_entry__.build())") from e
-        _C = c
+        _C = _Counted(c)
     return _C
 
 
@@ -190,3 +229,22 @@ def ce_fwd_rows(logits, targets, lse, loss):
 
 def ce_bwd_rows(logits, targets, lse, grad_out, scale):
     ext().ce_bwd_rows(logits, targets, lse, grad_out, float(scale))
+
+
+# ---------------------------------------------------------------- attention
+def flash_attn_fwd(qkv, B, T, H, KV, hd, causal=True, scale=None):
+    """Causal flash attention over the packed post-RoPE qkv rows -> (o (B*T, H*hd) bf16, lse (B, H, T))."""
+    scale = (1.0 / hd ** 0.5) if scale is None else scale
+    o, lse = ext().flash_attn_fwd(qkv, int(B), int(T), int(H), int(KV), int(hd), bool(causal), float(scale))
+    return o, lse
+
+
+def flash_attn_bwd(do, qkv, o, lse, cos, sin, B, T, H, KV, hd, causal=True, scale=None):
+    """Gradient w.r.t. the packed *pre-RoPE* qkv rows (the RoPE backward is fused in)."""
+    scale = (1.0 / hd ** 0.5) if scale is None else scale
+    return ext().flash_attn_bwd(do, qkv, o, lse, cos, sin, int(B), int(T), int(H), int(KV), int(hd), bool(causal),
+                                float(scale))
+
+
+def attn_error_code(reset=False) -> int:
+    return ext().attn_error_code(reset)

@@ -1,0 +1,99 @@
+"""Training engine: model + fused optimizer + (optionally) one CUDA graph per step.
+
+`Trainer` is the public API of the native path:
+
+    tr = Trainer(get_config("medium"), batch=4, seq=1024)
+    loss = tr.train_step(idx, targets)      # idx/targets on the host (pinned) or device
+
+One step = forward + backward + AdamW over every parameter, exactly the reference's step()
+(bench_train.py:474-490). With cuda_graph=True the whole step (all kernels, including the
+optimizer and the data-parallel collectives) is captured once after warm-up and replayed,
+which removes the per-kernel launch cost the reference pays from Python (its profile shows
+1177-4033 launches per step, README.md:53-62, :117-125). Inputs are copied into static
+device buffers before each replay.
+"""
+from __future__ import annotations
+
+import torch
+
+from llmt.config import ModelConfig
+from llmt.models.llama import build_model
+from llmt.models.native import NativeLlama
+from llmt.ops import functions as Fn
+from llmt.optim.adamw import FusedAdamW
+
+
+class Trainer:
+    def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
+                 cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192):
+        self.cfg, self.batch, self.seq = cfg, batch, seq
+        self.device = torch.device(device)
+        self.microbatches = microbatches
+        self.dp = dp
+        self.model = build_model(cfg, seq, seed=seed, device=self.device)
+        pad_to = dp.world_size if dp is not None else 1
+        self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to)
+        flat = self.net.flat
+        if dp is not None:
+            self.opt = dp.make_optimizer(flat, lr=lr)
+        else:
+            self.opt = FusedAdamW(flat.master, flat.grad, flat.shadow, lr=lr)
+        mb = batch // microbatches
+        if mb * microbatches != batch:
+            raise ValueError("batch must be a multiple of microbatches")
+        self.idx = torch.zeros((microbatches, mb, seq), dtype=torch.long, device=self.device)
+        self.tgt = torch.zeros((microbatches, mb, seq), dtype=torch.long, device=self.device)
+        self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
+        self.use_graph = cuda_graph
+        self.graph = None
+        self.body_calls = 0
+
+    # ------------------------------------------------------------------ step body
+    def _body(self):
+        self.body_calls += 1
+        Fn.FLAGS.reset()
+        total = None
+        for i in range(self.microbatches):
+            loss = self.net(self.idx[i], self.tgt[i])
+            (loss / self.microbatches).backward()
+            total = loss.detach() if total is None else total + loss.detach()
+        if self.dp is not None:
+            self.dp.reduce_and_step(self.opt)
+        else:
+            self.opt.step()
+        self.loss.copy_(total / self.microbatches)
+
+    def _capture(self, warmup=2):
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._body()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._body()
+        self.graph = g
+
+    def set_batch(self, idx, tgt):
+        """Copy one step's tokens (B, T) into the static device buffers (async from pinned memory)."""
+        self.idx.copy_(idx.view(self.idx.shape), non_blocking=True)
+        self.tgt.copy_(tgt.view(self.tgt.shape), non_blocking=True)
+
+    def run_step(self):
+        """One training step on the current static batch (device-side; no host sync)."""
+        if not self.use_graph:
+            self._body()
+            return
+        if self.graph is None:
+            self._capture()
+        self.graph.replay()
+
+    def train_step(self, idx, tgt) -> float:
+        """Public API: H2D copy of the batch, one step, D2H read of the loss."""
+        self.set_batch(idx, tgt)
+        self.run_step()
+        return float(self.loss.item())
+
+    def release(self):
+        self.graph = None

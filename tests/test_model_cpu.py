@@ -1,0 +1,97 @@
+"""CPU oracle tests of the reference-layout model (tiny256, fp32) and its state_dict layout."""
+import os
+import sys
+
+import pytest
+import torch
+
+from llmt.config import SIZES, count_params, get_config, model_flops_per_token
+from llmt.models.llama import LlamaModel, build_model, make_batch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _ref_module():
+    if not os.path.isfile(os.path.join(REF, "bench_train.py")):
+        pytest.skip("reference not installed under baseline/_ref")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import bench_train
+    return bench_train
+
+
+def test_state_dict_keys_match_reference_layout():
+    m = build_model(get_config("tiny256"), 128)
+    keys = list(m.state_dict().keys())
+    L = m.cfg.L
+    expect = ["emb.weight"]
+    for i in range(L):
+        expect += [f"blocks.{i}.norm1.weight", f"blocks.{i}.attn.qkv.weight", f"blocks.{i}.attn.wo.weight",
+                   f"blocks.{i}.norm2.weight", f"blocks.{i}.mlp.w1.weight", f"blocks.{i}.mlp.w3.weight",
+                   f"blocks.{i}.mlp.w2.weight"]
+    expect += ["norm_f.weight", "head.weight"]
+    assert keys == expect
+    assert "rope_cos" not in keys and "rope_sin" not in keys
+
+
+def test_param_count_and_flops_match_reference():
+    bt = _ref_module()
+    for name in ("tiny", "small", "medium", "large"):
+        assert count_params(SIZES[name]) == bt.count_params(bt.SIZES[name])
+        assert model_flops_per_token(SIZES[name], 1024) == bt.model_flops_per_token(bt.SIZES[name], 1024)
+
+
+def test_reference_state_dict_round_trip_bit_exact():
+    bt = _ref_module()
+    cfg = get_config("tiny256")
+    torch.manual_seed(0)
+    ref = bt.LlamaModel(bt.ModelConfig(d=cfg.d, L=cfg.L, H=cfg.H, ffn=cfg.ffn), 128)
+    ours = LlamaModel(cfg, 128)
+    ours.load_state_dict(ref.state_dict())
+    for (k1, v1), (k2, v2) in zip(ref.state_dict().items(), ours.state_dict().items()):
+        assert k1 == k2 and torch.equal(v1, v2)
+    ref.load_state_dict(ours.state_dict())
+
+
+def test_same_seed_same_init_as_reference():
+    bt = _ref_module()
+    cfg = get_config("tiny256")
+    torch.manual_seed(0)
+    ref = bt.LlamaModel(bt.ModelConfig(d=cfg.d, L=cfg.L, H=cfg.H, ffn=cfg.ffn), 128)
+    ours = build_model(cfg, 128, seed=0)
+    for v1, v2 in zip(ref.state_dict().values(), ours.state_dict().values()):
+        assert torch.equal(v1, v2)
+
+
+def test_tiny256_step_matches_reference_fp32():
+    """BASELINE tiny config: b2 s128, fp32 on CPU, one fwd+bwd+AdamW step; loss and grads equal."""
+    bt = _ref_module()
+    cfg = get_config("tiny256")
+    idx, tgt = make_batch(2, 128, cfg.vocab, "cpu", seed=0)
+    torch.manual_seed(0)
+    ref = bt.LlamaModel(bt.ModelConfig(d=cfg.d, L=cfg.L, H=cfg.H, ffn=cfg.ffn), 128, attn_impl="naive")
+    ours = build_model(cfg, 128, seed=0, attn_impl="naive")
+    lr = ref(idx, tgt)
+    lo = ours(idx, tgt)
+    assert abs(lr.item() - lo.item()) < 1e-5
+    lr.backward()
+    lo.backward()
+    for (n, p1), p2 in zip(ref.named_parameters(), ours.parameters()):
+        assert torch.allclose(p1.grad, p2.grad, rtol=1e-4, atol=1e-6), n
+    o1 = torch.optim.AdamW(ref.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    o2 = torch.optim.AdamW(ours.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    o1.step()
+    o2.step()
+    for p1, p2 in zip(ref.parameters(), ours.parameters()):
+        assert torch.allclose(p1, p2, rtol=1e-5, atol=1e-7)
+
+
+def test_gqa_model_runs_on_cpu():
+    cfg = get_config("tiny256", kv_heads=2, rope_base=500000.0)
+    m = build_model(cfg, 64)
+    idx, tgt = make_batch(1, 64, cfg.vocab, "cpu")
+    loss = m(idx, tgt)
+    loss.backward()
+    assert m.blocks[0].attn.qkv.weight.shape == ((4 + 2 * 2) * 64, 256)
+    assert torch.isfinite(loss)
