@@ -129,82 +129,53 @@ inline int ew_grid(int64_t work) {
 
 }  // namespace
 
-void swiglu_fwd(at::Tensor g, at::Tensor u, at::Tensor h) {
-  LLMT_CHECK_DTYPE(g, at::kBFloat16);
-  LLMT_CHECK_DTYPE(u, at::kBFloat16);
-  LLMT_CHECK_DTYPE(h, at::kBFloat16);
-  LLMT_CHECK(g.dim() == 2 && u.dim() == 2 && h.dim() == 2, "SwiGLU operands must be 2D");
-  const int F = g.size(1);
-  const int64_t rows = g.size(0);
-  LLMT_CHECK(F % 8 == 0, "SwiGLU width must be a multiple of 8");
-  LLMT_CHECK(g.stride(1) == 1 && u.stride(1) == 1 && h.stride(1) == 1, "SwiGLU inner dim must be contiguous");
-  LLMT_CHECK(g.stride(0) == u.stride(0), "g and u must share a row stride");
-  if (rows == 0) return;
-  swiglu_fwd_kernel<<<ew_grid(rows * F / 8), 256, 0, cur_stream()>>>(
-      reinterpret_cast<const bf16*>(g.data_ptr()), reinterpret_cast<const bf16*>(u.data_ptr()), g.stride(0),
-      reinterpret_cast<bf16*>(h.data_ptr()), h.stride(0), rows, F);
-  LLMT_LAUNCH_CHECK();
+cudaError_t swiglu_fwd(const void* g, const void* u, int64_t ldgu, void* h, int64_t ldh, int64_t rows, int F,
+                       cudaStream_t st) {
+  LLMT_REQUIRE(F % 8 == 0 && ldgu % 8 == 0 && ldh % 8 == 0, "swiglu: widths and pitches must be multiples of 8");
+  if (rows == 0) return cudaSuccess;
+  swiglu_fwd_kernel<<<ew_grid(rows * F / 8), 256, 0, st>>>(static_cast<const bf16*>(g), static_cast<const bf16*>(u),
+                                                           ldgu, static_cast<bf16*>(h), ldh, rows, F);
+  return cudaGetLastError();
 }
 
-void swiglu_bwd(at::Tensor dh, at::Tensor g, at::Tensor u, at::Tensor dg, at::Tensor du) {
-  LLMT_CHECK(g.dim() == 2 && u.dim() == 2 && dh.dim() == 2 && dg.dim() == 2 && du.dim() == 2,
-             "SwiGLU operands must be 2D");
-  const int F = g.size(1);
-  const int64_t rows = g.size(0);
-  LLMT_CHECK(F % 8 == 0, "SwiGLU width must be a multiple of 8");
-  LLMT_CHECK(g.stride(0) == u.stride(0) && dg.stride(0) == du.stride(0), "paired row strides differ");
-  if (rows == 0) return;
-  swiglu_bwd_kernel<<<ew_grid(rows * F / 8), 256, 0, cur_stream()>>>(
-      reinterpret_cast<const bf16*>(dh.data_ptr()), dh.stride(0), reinterpret_cast<const bf16*>(g.data_ptr()),
-      reinterpret_cast<const bf16*>(u.data_ptr()), g.stride(0), reinterpret_cast<bf16*>(dg.data_ptr()),
-      reinterpret_cast<bf16*>(du.data_ptr()), dg.stride(0), rows, F);
-  LLMT_LAUNCH_CHECK();
+cudaError_t swiglu_bwd(const void* dh, int64_t lddh, const void* g, const void* u, int64_t ldgu, void* dg, void* du,
+                       int64_t lddgu, int64_t rows, int F, cudaStream_t st) {
+  LLMT_REQUIRE(F % 8 == 0 && ldgu % 8 == 0 && lddh % 8 == 0 && lddgu % 8 == 0,
+               "swiglu: widths and pitches must be multiples of 8");
+  if (rows == 0) return cudaSuccess;
+  swiglu_bwd_kernel<<<ew_grid(rows * F / 8), 256, 0, st>>>(static_cast<const bf16*>(dh), lddh,
+                                                           static_cast<const bf16*>(g), static_cast<const bf16*>(u),
+                                                           ldgu, static_cast<bf16*>(dg), static_cast<bf16*>(du), lddgu,
+                                                           rows, F);
+  return cudaGetLastError();
 }
 
-// qkv: (B*T, (H + 2*KV) * hd) bf16, rotated in place. n_rot_heads = H + KV (q and k heads).
-void rope_inplace(at::Tensor qkv, at::Tensor cos_t, at::Tensor sin_t, int64_t T, int64_t n_rot_heads, int64_t hd,
-                  bool backward) {
-  LLMT_CHECK_DTYPE(qkv, at::kBFloat16);
-  LLMT_CHECK_DTYPE(cos_t, at::kFloat);
-  LLMT_CHECK(hd % 16 == 0, "head dim must be a multiple of 16");
-  LLMT_CHECK(cos_t.is_contiguous() && sin_t.is_contiguous(), "rope tables must be contiguous");
-  LLMT_CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd, "rope table too small");
-  LLMT_CHECK(qkv.is_contiguous(), "qkv must be contiguous");
-  const int64_t ld = qkv.size(-1);
-  const int64_t N = qkv.numel() / ld;
+// qkv: (N, ld) bf16 rows; the first n_rot_heads heads (q and k) are rotated in place.
+cudaError_t rope_inplace(void* qkv, const float* cos_t, const float* sin_t, int64_t N, int T, int n_rot_heads, int hd,
+                         int64_t ld, bool backward, cudaStream_t st) {
+  LLMT_REQUIRE(hd % 16 == 0 && ld % 8 == 0, "rope: head dim must be a multiple of 16");
   const int64_t work = N * n_rot_heads * (hd / 16);
-  if (work == 0) return;
+  if (work == 0) return cudaSuccess;
   auto kern = backward ? rope_kernel<true> : rope_kernel<false>;
-  kern<<<ew_grid(work), 256, 0, cur_stream()>>>(reinterpret_cast<bf16*>(qkv.data_ptr()), cos_t.data_ptr<float>(),
-                                                 sin_t.data_ptr<float>(), N, (int)T, (int)n_rot_heads, (int)hd, ld);
-  LLMT_LAUNCH_CHECK();
+  kern<<<ew_grid(work), 256, 0, st>>>(static_cast<bf16*>(qkv), cos_t, sin_t, N, T, n_rot_heads, hd, ld);
+  return cudaGetLastError();
 }
 
-void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at::Tensor> err) {
-  LLMT_CHECK_DTYPE(idx, at::kLong);
-  LLMT_CHECK_DTYPE(W, at::kFloat);
-  LLMT_CHECK(W.size(1) % 4 == 0, "embedding width must be a multiple of 4");
-  LLMT_CHECK(idx.is_contiguous() && W.is_contiguous() && x.is_contiguous(), "embedding operands must be contiguous");
-  const int64_t N = idx.numel();
-  const int d = W.size(1);
-  if (N == 0) return;
-  embedding_fwd_kernel<<<ew_grid(N * d / 4), 256, 0, cur_stream()>>>(
-      idx.data_ptr<int64_t>(), W.data_ptr<float>(), x.data_ptr<float>(), N, d, W.size(0),
-      (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr);
-  LLMT_LAUNCH_CHECK();
+cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int* err,
+                          cudaStream_t st) {
+  LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
+  if (N == 0) return cudaSuccess;
+  embedding_fwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, W, x, N, d, V, err);
+  return cudaGetLastError();
 }
 
 // dW += scatter(dx by idx). The caller zeroes dW for the first micro-batch.
-void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW) {
-  LLMT_CHECK_DTYPE(dx, at::kFloat);
-  LLMT_CHECK_DTYPE(dW, at::kFloat);
-  LLMT_CHECK(dx.is_contiguous() && dW.is_contiguous(), "embedding grads must be contiguous");
-  const int64_t N = idx.numel();
-  const int d = dW.size(1);
-  if (N == 0) return;
-  embedding_bwd_kernel<<<ew_grid(N * d / 4), 256, 0, cur_stream()>>>(idx.data_ptr<int64_t>(), dx.data_ptr<float>(),
-                                                                      dW.data_ptr<float>(), N, d, dW.size(0));
-  LLMT_LAUNCH_CHECK();
+cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V,
+                          cudaStream_t st) {
+  LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
+  if (N == 0) return cudaSuccess;
+  embedding_bwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, dx, dW, N, d, V);
+  return cudaGetLastError();
 }
 
 }  // namespace llmt

@@ -13,14 +13,10 @@
 namespace llmt {
 namespace {
 
-struct AdamArgs {
-  float b1, b2, eps, wd, grad_scale;
-};
-
 template <bool WRITE_BF16>
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, bf16* __restrict__ p16, int64_t n, const float* __restrict__ lr_ptr,
-                             const int* __restrict__ step_ptr, AdamArgs a) {
+                             const int* __restrict__ step_ptr, AdamHyper a) {
   const float lr = *lr_ptr;
   const int t = *step_ptr;
   const float bc1 = 1.f - powf(a.b1, (float)t);
@@ -74,40 +70,23 @@ __global__ void cast_bf16_kernel(const float* __restrict__ x, bf16* __restrict__
 
 }  // namespace
 
-void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16,
-                at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale) {
-  for (auto* t : {&p, &g, &m, &v}) {
-    LLMT_CHECK_DTYPE((*t), at::kFloat);
-    LLMT_CHECK_CONTIG((*t));
-  }
-  LLMT_CHECK(g.numel() == p.numel() && m.numel() == p.numel() && v.numel() == p.numel(), "adamw: size mismatch");
-  LLMT_CHECK_DTYPE(lr, at::kFloat);
-  LLMT_CHECK_DTYPE(step, at::kInt);
-  const bool w16 = p16.has_value() && p16->defined();
-  if (w16) {
-    LLMT_CHECK_DTYPE((*p16), at::kBFloat16);
-    LLMT_CHECK(p16->numel() == p.numel(), "adamw: bf16 copy size mismatch");
-  }
-  const int64_t n = p.numel();
-  if (n == 0) return;
+cudaError_t adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
+                       const int* step, AdamHyper h, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  LLMT_REQUIRE(((uintptr_t)p | (uintptr_t)g | (uintptr_t)m | (uintptr_t)v) % 16 == 0,
+               "adamw: fp32 buffers must be 16-byte aligned");
+  LLMT_REQUIRE(p16 == nullptr || (uintptr_t)p16 % 8 == 0, "adamw: bf16 copy must be 8-byte aligned");
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4 + 1, 256), sm_count() * 8));
-  AdamArgs a{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
-  auto kern = w16 ? adamw_kernel<true> : adamw_kernel<false>;
-  kern<<<grid, 256, 0, cur_stream()>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
-                                       v.data_ptr<float>(), w16 ? reinterpret_cast<bf16*>(p16->data_ptr()) : nullptr, n,
-                                       lr.data_ptr<float>(), step.data_ptr<int>(), a);
-  LLMT_LAUNCH_CHECK();
+  if (p16) adamw_kernel<true><<<grid, 256, 0, st>>>(p, g, m, v, static_cast<bf16*>(p16), n, lr, step, h);
+  else adamw_kernel<false><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
+  return cudaGetLastError();
 }
 
-void cast_bf16(at::Tensor x, at::Tensor y) {
-  LLMT_CHECK_DTYPE(x, at::kFloat);
-  LLMT_CHECK_DTYPE(y, at::kBFloat16);
-  LLMT_CHECK(x.numel() == y.numel() && x.is_contiguous() && y.is_contiguous(), "cast_bf16: bad args");
-  const int64_t n = x.numel();
-  if (n == 0) return;
+cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), sm_count() * 8));
-  cast_bf16_kernel<<<grid, 256, 0, cur_stream()>>>(x.data_ptr<float>(), reinterpret_cast<bf16*>(y.data_ptr()), n);
-  LLMT_LAUNCH_CHECK();
+  cast_bf16_kernel<<<grid, 256, 0, st>>>(x, static_cast<bf16*>(y), n);
+  return cudaGetLastError();
 }
 
 }  // namespace llmt

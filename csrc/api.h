@@ -1,0 +1,97 @@
+// Plain C++ launch API of the llmt sm_100a kernels (no torch types).
+//
+// Every .cu translation unit implements its launchers against raw device pointers and a
+// cudaStream_t; the PyTorch glue (bindings.cpp) validates tensors and calls these. Keeping
+// torch headers out of the CUDA units keeps device compiles to seconds, and gives callers
+// outside PyTorch the same entry points. Launchers return cudaSuccess or an error; for
+// argument errors they return cudaErrorInvalidValue and leave a message in last_error().
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace llmt {
+
+const char* last_error();
+void set_last_error(const char* msg);
+int sm_count();
+
+// ---------------------------------------------------------------- RMSNorm
+cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, void* y_bf16, float* s, float* rstd,
+                            int64_t N, int D, float eps, cudaStream_t st);
+int rmsnorm_bwd_partials(int64_t N, int D);  // rows of the dw partial buffer the backward needs
+cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, const float* rstd, const float* ds_in,
+                        float* ds, void* ds16, float* dw_part, float* dw, unsigned* ticket, int64_t N, int D,
+                        int accumulate, cudaStream_t st);
+
+// ---------------------------------------------------------------- elementwise
+cudaError_t swiglu_fwd(const void* g, const void* u, int64_t ldgu, void* h, int64_t ldh, int64_t rows, int F,
+                       cudaStream_t st);
+cudaError_t swiglu_bwd(const void* dh, int64_t lddh, const void* g, const void* u, int64_t ldgu, void* dg, void* du,
+                       int64_t lddgu, int64_t rows, int F, cudaStream_t st);
+cudaError_t rope_inplace(void* qkv, const float* cos_t, const float* sin_t, int64_t N, int T, int n_rot_heads, int hd,
+                         int64_t ld, bool backward, cudaStream_t st);
+cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int* err,
+                          cudaStream_t st);
+cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V,
+                          cudaStream_t st);
+
+// ---------------------------------------------------------------- optimizer
+struct AdamHyper {
+  float b1, b2, eps, wd, grad_scale;
+};
+cudaError_t adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
+                       const int* step, AdamHyper h, cudaStream_t st);
+cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st);
+
+// ---------------------------------------------------------------- cross entropy rows
+cudaError_t ce_fwd_rows(const void* logits, int64_t ld, const int64_t* tgt, float* lse, float* loss, int64_t R, int V,
+                        cudaStream_t st);
+cudaError_t ce_bwd_rows(void* logits, int64_t ld, const int64_t* tgt, const float* lse, const float* grad_out,
+                        float scale, int64_t R, int V, cudaStream_t st);
+cudaError_t ce_combine(const float* part, const float* tlogit, const int64_t* tgt, float* lse, float* loss, int M,
+                       int nblk, int V, cudaStream_t st);
+
+// ---------------------------------------------------------------- GEMM
+enum EpiKind : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_ROPE = 4, EPI_CE_FWD = 5, EPI_CE_BWD = 6 };
+
+struct GemmArgs {
+  int M, N, K;
+  int m_blocks, n_blocks, k_blocks;
+  void* out;
+  int64_t ldo;
+  int accumulate;
+  int split;  // SWIGLU: row offset of W3 inside W13 (= ffn); SWIGLU_BWD: column offset of u in gu (= ffn)
+  const void* aux;
+  int64_t ld_aux;
+  void* out2;
+  int64_t ldo2;
+  const float* cos_t;
+  const float* sin_t;
+  int T, hd, rot_cols;
+  const int64_t* tgt;
+  const float* lse;
+  const float* grad_out;
+  float* part;    // CE_FWD partials (M, n_blocks, 2)
+  float* tlogit;  // CE_FWD target logits (M)
+  float alpha;
+  int* err;
+};
+
+// out = op(a) @ op(b); a: (ta ? K x M : M x K) row pitch lda, b: (tb ? N x K : K x N) row pitch ldb.
+// The epilogue fields of `g` (out, ldo, accumulate, split, aux, ...) are set by the caller;
+// M/N/K, block counts and err are filled in here. bn = 0 picks the tile width.
+cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
+                 int epi, int bn, GemmArgs g, cudaStream_t st);
+int gemm_pick_bn(int M, int N, int epi);
+int gemm_error_code(bool reset);
+
+// ---------------------------------------------------------------- attention
+cudaError_t flash_attn_fwd(const void* qkv, int64_t ld_qkv, void* o, float* lse, int B, int T, int H, int KV, int hd,
+                           bool causal, float scale, cudaStream_t st);
+// dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
+cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
+                           const float* cos_t, const float* sin_t, void* dqkv, float* dsum, float* dq_acc, int B,
+                           int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st);
+int attn_error_code(bool reset);
+
+}  // namespace llmt

@@ -373,81 +373,71 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, bf16* __r
 }
 
 template <int HD>
-void launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args) {
+cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args, cudaStream_t st) {
   auto kern = flash_bwd_kernel<HD>;
   constexpr size_t smem = BwdSmem<HD>::TOTAL;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((int)cdiv(args.T, kBM), args.B * args.KV);
-  kern<<<grid, kBwdThreads, smem, cur_stream()>>>(tq, tdo, args);
-  LLMT_LAUNCH_CHECK();
+  dim3 grid((unsigned)cdiv(args.T, kBM), args.B * args.KV);
+  kern<<<grid, kBwdThreads, smem, st>>>(tq, tdo, args);
+  return cudaGetLastError();
 }
 
 }  // namespace
 
-// Returns dqkv (B*T, (H + 2*KV) * hd) bf16 with the RoPE backward applied to the q and k parts.
-at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor cos_t,
-                          at::Tensor sin_t, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, bool causal,
-                          double scale) {
-  LLMT_CHECK_DTYPE(dO, at::kBFloat16);
-  LLMT_CHECK_DTYPE(qkv, at::kBFloat16);
-  LLMT_CHECK_DTYPE(o, at::kBFloat16);
-  LLMT_CHECK_DTYPE(lse, at::kFloat);
-  LLMT_CHECK(hd == 64 || hd == 128, "flash_attn_bwd: head dim must be 64 or 128");
-  LLMT_CHECK(dO.is_contiguous() && o.is_contiguous() && qkv.is_contiguous() && lse.is_contiguous(),
-             "flash_attn_bwd: operands must be contiguous");
-  LLMT_CHECK(dO.numel() == B * T * H * hd && o.numel() == dO.numel(), "flash_attn_bwd: dO/o shape");
-  LLMT_CHECK(qkv.size(0) == B * T && qkv.size(1) == (H + 2 * KV) * hd, "flash_attn_bwd: qkv shape");
-  LLMT_CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd && cos_t.is_contiguous() && sin_t.is_contiguous(),
-             "flash_attn_bwd: rope tables");
-  LLMT_CHECK(tma_ok(qkv.data_ptr(), qkv.stride(0), 2) && tma_ok(dO.data_ptr(), H * hd, 2),
-             "flash_attn_bwd: TMA alignment");
-  auto dqkv = at::empty_like(qkv);
-  auto dsum = at::empty({B, H, T}, lse.options());
-  auto dq_acc = at::empty({B * T, H * hd}, lse.options());
-  const int64_t rows = B * T;
+// dqkv (B*T, ld_qkv) bf16 receives the gradient w.r.t. the packed *pre-RoPE* qkv rows.
+// dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
+cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
+                           const float* cos_t, const float* sin_t, void* dqkv, float* dsum, float* dq_acc, int B,
+                           int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st) {
+  LLMT_REQUIRE(hd == 64 || hd == 128, "flash_attn_bwd: head dim must be 64 or 128");
+  LLMT_REQUIRE(KV > 0 && H % KV == 0, "flash_attn_bwd: H must be a multiple of KV");
+  LLMT_REQUIRE(tma_ok(qkv, ld_qkv, 2) && tma_ok(dO, (int64_t)H * hd, 2), "flash_attn_bwd: TMA alignment");
+  if (B == 0 || T == 0) return cudaSuccess;
+  const int64_t rows = (int64_t)B * T;
   {
     const int64_t n = rows * H;
     auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
-    k<<<cdiv(n, 256), 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
-                                              reinterpret_cast<const bf16*>(dO.data_ptr()), dsum.data_ptr<float>(),
-                                              dq_acc.data_ptr<float>(), (int)rows, (int)T, (int)H);
-    LLMT_LAUNCH_CHECK();
+    k<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum, dq_acc,
+                                              (int)rows, T, H);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
   }
   AttnBwdArgs args{};
-  args.lse = lse.data_ptr<float>();
-  args.dsum = dsum.data_ptr<float>();
-  args.dq_acc = dq_acc.data_ptr<float>();
-  args.dqkv = reinterpret_cast<bf16*>(dqkv.data_ptr());
-  args.cos_t = cos_t.data_ptr<float>();
-  args.sin_t = sin_t.data_ptr<float>();
-  args.B = (int)B;
-  args.T = (int)T;
-  args.H = (int)H;
-  args.KV = (int)KV;
-  args.ld_qkv = (int)qkv.size(1);
-  args.ld_dq = (int)(H * hd);
-  args.scale = (float)scale;
-  args.scale_log2 = (float)(scale * 1.4426950408889634);
+  args.lse = lse;
+  args.dsum = dsum;
+  args.dq_acc = dq_acc;
+  args.dqkv = static_cast<bf16*>(dqkv);
+  args.cos_t = cos_t;
+  args.sin_t = sin_t;
+  args.B = B;
+  args.T = T;
+  args.H = H;
+  args.KV = KV;
+  args.ld_qkv = (int)ld_qkv;
+  args.ld_dq = H * hd;
+  args.scale = scale;
+  args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
   args.err = attn_err_word();
   alignas(64) CUtensorMap tq, tdo;
-  make_tmap_2d(&tq, qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.size(1), rows, qkv.stride(0), 64, 128);
-  make_tmap_2d(&tdo, dO.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H * hd, rows, H * hd, 64, 128);
-  if (hd == 64) launch_bwd<64>(tq, tdo, args);
-  else launch_bwd<128>(tq, tdo, args);
+  const bool ok =
+      make_tmap_2d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows, ld_qkv, 64, 128) &&
+      make_tmap_2d(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * hd, rows, (uint64_t)H * hd, 64, 128);
+  LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
+  cudaError_t e = hd == 64 ? launch_bwd<64>(tq, tdo, args, st) : launch_bwd<128>(tq, tdo, args, st);
+  if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);
     auto k = hd == 64 ? attn_bwd_post_kernel<64> : attn_bwd_post_kernel<128>;
-    k<<<cdiv(n, 256), 256, 0, cur_stream()>>>(dq_acc.data_ptr<float>(), reinterpret_cast<bf16*>(dqkv.data_ptr()),
-                                              cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)rows, (int)T,
-                                              (int)H, (int)qkv.size(1));
-    LLMT_LAUNCH_CHECK();
+    k<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(dq_acc, static_cast<bf16*>(dqkv), cos_t, sin_t, (int)rows, T, H,
+                                              (int)ld_qkv);
   }
-  return dqkv;
+  return cudaGetLastError();
 }
 
 }  // namespace llmt

@@ -22,6 +22,7 @@
 #include "../common/tma.h"
 
 namespace llmt {
+int* attn_err_word();
 namespace {
 
 using namespace sm100;
@@ -285,65 +286,65 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
 }
 
 template <int HD>
-void launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb) {
+cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb, cudaStream_t st) {
   auto kern = flash_fwd_kernel<HD>;
   constexpr size_t smem = FwdSmem<HD>::TOTAL;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   dim3 grid(args.B * args.H, nqb);
-  kern<<<grid, kAttnThreads, smem, cur_stream()>>>(tm, args);
-  LLMT_LAUNCH_CHECK();
+  kern<<<grid, kAttnThreads, smem, st>>>(tm, args);
+  return cudaGetLastError();
 }
 
 }  // namespace
 
 int* attn_err_word() {
-  static int* p = nullptr;
-  if (!p) C10_CUDA_CHECK(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_attn_err));
-  return p;
+  static int* p[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!p[dev]) cudaGetSymbolAddress(reinterpret_cast<void**>(&p[dev]), g_attn_err);
+  return p[dev];
 }
 
 int attn_error_code(bool reset) {
   int v = 0;
-  C10_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(int)));
+  cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(int));
   if (reset) {
     int z = 0;
-    C10_CUDA_CHECK(cudaMemcpyToSymbol(g_attn_err, &z, sizeof(int)));
+    cudaMemcpyToSymbol(g_attn_err, &z, sizeof(int));
   }
   return v;
 }
 
-// qkv: (B*T, (H + 2*KV) * hd) bf16 (post-RoPE). Returns (o (B*T, H*hd) bf16, lse (B, H, T) fp32).
-std::vector<at::Tensor> flash_attn_fwd(at::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
-                                       bool causal, double scale) {
-  LLMT_CHECK_DTYPE(qkv, at::kBFloat16);
-  LLMT_CHECK(qkv.is_cuda() && qkv.dim() == 2 && qkv.stride(1) == 1, "flash_attn_fwd: qkv must be a 2D CUDA tensor");
-  LLMT_CHECK(qkv.size(0) == B * T && qkv.size(1) == (H + 2 * KV) * hd, "flash_attn_fwd: qkv shape mismatch");
-  LLMT_CHECK(hd == 64 || hd == 128, "flash_attn_fwd: head dim must be 64 or 128");
-  LLMT_CHECK(H % KV == 0, "flash_attn_fwd: H must be a multiple of KV");
-  LLMT_CHECK(tma_ok(qkv.data_ptr(), qkv.stride(0), 2), "flash_attn_fwd: qkv pitch/alignment not TMA-legal");
-  auto o = at::empty({B * T, H * hd}, qkv.options());
-  auto lse = at::empty({B, H, T}, qkv.options().dtype(at::kFloat));
+// qkv: (B*T, ld_qkv) bf16 packed post-RoPE rows ((H + 2*KV) * hd columns used);
+// o: (B*T, H*hd) bf16; lse: (B, H, T) fp32.
+cudaError_t flash_attn_fwd(const void* qkv, int64_t ld_qkv, void* o, float* lse, int B, int T, int H, int KV, int hd,
+                           bool causal, float scale, cudaStream_t st) {
+  LLMT_REQUIRE(hd == 64 || hd == 128, "flash_attn_fwd: head dim must be 64 or 128");
+  LLMT_REQUIRE(KV > 0 && H % KV == 0, "flash_attn_fwd: H must be a multiple of KV");
+  LLMT_REQUIRE(tma_ok(qkv, ld_qkv, 2), "flash_attn_fwd: qkv pitch/alignment not TMA-legal");
+  if (B == 0 || T == 0) return cudaSuccess;
   AttnFwdArgs args{};
-  args.o = reinterpret_cast<bf16*>(o.data_ptr());
-  args.lse = lse.data_ptr<float>();
-  args.B = (int)B;
-  args.T = (int)T;
-  args.H = (int)H;
-  args.KV = (int)KV;
-  args.ld_o = (int)(H * hd);
-  args.scale_log2 = (float)(scale * 1.4426950408889634);
+  args.o = static_cast<bf16*>(o);
+  args.lse = lse;
+  args.B = B;
+  args.T = T;
+  args.H = H;
+  args.KV = KV;
+  args.ld_o = H * hd;
+  args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
   args.err = attn_err_word();
   alignas(64) CUtensorMap tm;
-  make_tmap_2d(&tm, qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.size(1), B * T, qkv.stride(0), 64, 128);
+  LLMT_REQUIRE(make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd,
+                            (uint64_t)B * T, ld_qkv, 64, 128),
+               "flash_attn_fwd: tensor map rejected");
   const int nqb = (int)cdiv(T, kBlockM);
-  if (hd == 64) launch_fwd<64>(tm, args, nqb);
-  else launch_fwd<128>(tm, args, nqb);
-  return {o, lse};
+  return hd == 64 ? launch_fwd<64>(tm, args, nqb, st) : launch_fwd<128>(tm, args, nqb, st);
 }
 
 }  // namespace llmt

@@ -1,63 +1,331 @@
-// Python bindings of the llmt native extension (one module, llmt._C).
+// PyTorch glue of the llmt native extension (module llmt._C).
+//
+// The only translation unit that includes torch: it validates tensors (device, dtype,
+// layout), allocates outputs through the caching allocator, and calls the plain launch API
+// of api.h on the current CUDA stream. Launch errors become Python exceptions.
 #include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
 
-namespace llmt {
+#include "api.h"
+
+#define CHECK(cond, ...) TORCH_CHECK(cond, "llmt: ", __VA_ARGS__)
+#define CHECK_DT(t, dt) CHECK((t).scalar_type() == (dt), #t " has dtype ", (t).scalar_type(), ", expected ", (dt))
+
+namespace {
+
+cudaStream_t stream() { return c10::cuda::getCurrentCUDAStream().stream(); }
+
+void ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return;
+  if (e == cudaErrorInvalidValue && llmt::last_error()[0]) {
+    TORCH_CHECK(false, "llmt: ", what, ": ", llmt::last_error());
+  }
+  TORCH_CHECK(false, "llmt: ", what, ": ", cudaGetErrorString(e));
+}
+
+void cuda2d(const at::Tensor& t, const char* name) {
+  CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2D with unit inner stride");
+}
+
+const void* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+
+// ---------------------------------------------------------------- norms
 std::vector<at::Tensor> add_rmsnorm_fwd(c10::optional<at::Tensor> a, at::Tensor r, at::Tensor w, double eps,
-                                        bool write_s);
+                                        bool write_s) {
+  CHECK(r.is_cuda() && r.is_contiguous(), "r must be a contiguous CUDA tensor");
+  CHECK_DT(r, at::kFloat);
+  CHECK_DT(w, at::kFloat);
+  const int D = r.size(-1);
+  const int64_t N = r.numel() / D;
+  CHECK(w.numel() == D && w.is_contiguous(), "w must be contiguous with ", D, " elements");
+  const bool has_a = a.has_value() && a->defined();
+  if (has_a) {
+    CHECK_DT((*a), at::kBFloat16);
+    CHECK(a->is_contiguous() && a->numel() == r.numel(), "a must be contiguous and match r");
+  }
+  auto y = at::empty(r.sizes(), r.options().dtype(at::kBFloat16));
+  auto rstd = at::empty({N}, r.options());
+  at::Tensor s;
+  if (write_s) s = at::empty_like(r);
+  ok(llmt::add_rmsnorm_fwd(has_a ? a->data_ptr() : nullptr, r.data_ptr<float>(), w.data_ptr<float>(), y.data_ptr(),
+                           write_s ? s.data_ptr<float>() : nullptr, rstd.data_ptr<float>(), N, D, (float)eps, stream()),
+     "add_rmsnorm_fwd");
+  return {y, s, rstd};
+}
+
 std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor s, at::Tensor w, at::Tensor rstd,
                                     c10::optional<at::Tensor> ds_in, at::Tensor dw, at::Tensor ticket,
-                                    bool write_ds16, bool accumulate);
-void swiglu_fwd(at::Tensor g, at::Tensor u, at::Tensor h);
-void swiglu_bwd(at::Tensor dh, at::Tensor g, at::Tensor u, at::Tensor dg, at::Tensor du);
+                                    bool write_ds16, bool accumulate) {
+  CHECK_DT(dy, at::kBFloat16);
+  CHECK_DT(s, at::kFloat);
+  CHECK_DT(dw, at::kFloat);
+  CHECK_DT(ticket, at::kInt);
+  CHECK(dy.is_contiguous() && s.is_contiguous() && dy.numel() == s.numel(), "dy/s must be contiguous and match");
+  const int D = s.size(-1);
+  const int64_t N = s.numel() / D;
+  CHECK(dw.numel() == D && dw.is_contiguous(), "dw must be contiguous with ", D, " elements");
+  const bool has_dsin = ds_in.has_value() && ds_in->defined();
+  if (has_dsin) {
+    CHECK_DT((*ds_in), at::kFloat);
+    CHECK(ds_in->is_contiguous() && ds_in->numel() == s.numel(), "ds_in must be contiguous and match s");
+  }
+  auto ds = at::empty_like(s);
+  at::Tensor ds16;
+  if (write_ds16) ds16 = at::empty(s.sizes(), s.options().dtype(at::kBFloat16));
+  auto part = at::empty({llmt::rmsnorm_bwd_partials(N, D), D}, s.options());
+  ok(llmt::rmsnorm_bwd(dy.data_ptr(), s.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(),
+                       has_dsin ? ds_in->data_ptr<float>() : nullptr, ds.data_ptr<float>(),
+                       write_ds16 ? ds16.data_ptr() : nullptr, part.data_ptr<float>(), dw.data_ptr<float>(),
+                       reinterpret_cast<unsigned*>(ticket.data_ptr<int>()), N, D, accumulate ? 1 : 0, stream()),
+     "rmsnorm_bwd");
+  return {ds, ds16};
+}
+
+// ---------------------------------------------------------------- elementwise
+void swiglu_fwd(at::Tensor g, at::Tensor u, at::Tensor h) {
+  cuda2d(g, "g");
+  cuda2d(u, "u");
+  cuda2d(h, "h");
+  CHECK(g.stride(0) == u.stride(0), "g and u must share a row stride");
+  CHECK_DT(g, at::kBFloat16);
+  ok(llmt::swiglu_fwd(g.data_ptr(), u.data_ptr(), g.stride(0), h.data_ptr(), h.stride(0), g.size(0), g.size(1),
+                      stream()),
+     "swiglu_fwd");
+}
+
+void swiglu_bwd(at::Tensor dh, at::Tensor g, at::Tensor u, at::Tensor dg, at::Tensor du) {
+  for (auto* t : {&dh, &g, &u, &dg, &du}) cuda2d(*t, "swiglu operand");
+  CHECK(g.stride(0) == u.stride(0) && dg.stride(0) == du.stride(0), "paired row strides differ");
+  ok(llmt::swiglu_bwd(dh.data_ptr(), dh.stride(0), g.data_ptr(), u.data_ptr(), g.stride(0), dg.data_ptr(),
+                      du.data_ptr(), dg.stride(0), g.size(0), g.size(1), stream()),
+     "swiglu_bwd");
+}
+
 void rope_inplace(at::Tensor qkv, at::Tensor cos_t, at::Tensor sin_t, int64_t T, int64_t n_rot_heads, int64_t hd,
-                  bool backward);
-void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at::Tensor> err);
-void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW);
-void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16,
-                at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale);
-void cast_bf16(at::Tensor x, at::Tensor y);
-void ce_fwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor loss);
+                  bool backward) {
+  CHECK_DT(qkv, at::kBFloat16);
+  CHECK_DT(cos_t, at::kFloat);
+  CHECK(qkv.is_contiguous() && cos_t.is_contiguous() && sin_t.is_contiguous(), "rope operands must be contiguous");
+  CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd, "rope table too small");
+  const int64_t ld = qkv.size(-1);
+  ok(llmt::rope_inplace(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), qkv.numel() / ld, (int)T,
+                        (int)n_rot_heads, (int)hd, ld, backward, stream()),
+     "rope_inplace");
+}
+
+void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at::Tensor> err) {
+  CHECK_DT(idx, at::kLong);
+  CHECK_DT(W, at::kFloat);
+  CHECK(idx.is_contiguous() && W.is_contiguous() && x.is_contiguous(), "embedding operands must be contiguous");
+  ok(llmt::embedding_fwd(idx.data_ptr<int64_t>(), W.data_ptr<float>(), x.data_ptr<float>(), idx.numel(), W.size(1),
+                         W.size(0), err.has_value() && err->defined() ? err->data_ptr<int>() : nullptr, stream()),
+     "embedding_fwd");
+}
+
+void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW) {
+  CHECK_DT(dx, at::kFloat);
+  CHECK_DT(dW, at::kFloat);
+  CHECK(idx.is_contiguous() && dx.is_contiguous() && dW.is_contiguous(), "embedding grads must be contiguous");
+  ok(llmt::embedding_bwd(idx.data_ptr<int64_t>(), dx.data_ptr<float>(), dW.data_ptr<float>(), idx.numel(), dW.size(1),
+                         dW.size(0), stream()),
+     "embedding_bwd");
+}
+
+// ---------------------------------------------------------------- optimizer
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16, at::Tensor lr,
+                at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale) {
+  for (auto* t : {&p, &g, &m, &v}) {
+    CHECK_DT((*t), at::kFloat);
+    CHECK(t->is_contiguous() && t->numel() == p.numel(), "adamw buffers must be contiguous and equal-sized");
+  }
+  CHECK_DT(lr, at::kFloat);
+  CHECK_DT(step, at::kInt);
+  void* p16p = nullptr;
+  if (p16.has_value() && p16->defined()) {
+    CHECK_DT((*p16), at::kBFloat16);
+    CHECK(p16->numel() == p.numel() && p16->is_contiguous(), "adamw: bf16 copy size mismatch");
+    p16p = p16->data_ptr();
+  }
+  llmt::AdamHyper h{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
+  ok(llmt::adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p16p,
+                      p.numel(), lr.data_ptr<float>(), step.data_ptr<int>(), h, stream()),
+     "adamw_step");
+}
+
+void cast_bf16(at::Tensor x, at::Tensor y) {
+  CHECK_DT(x, at::kFloat);
+  CHECK_DT(y, at::kBFloat16);
+  CHECK(x.numel() == y.numel() && x.is_contiguous() && y.is_contiguous(), "cast_bf16: bad args");
+  ok(llmt::cast_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream()), "cast_bf16");
+}
+
+// ---------------------------------------------------------------- cross entropy
+void ce_fwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor loss) {
+  cuda2d(logits, "logits");
+  CHECK_DT(logits, at::kBFloat16);
+  CHECK_DT(targets, at::kLong);
+  ok(llmt::ce_fwd_rows(logits.data_ptr(), logits.stride(0), targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+                       loss.data_ptr<float>(), logits.size(0), logits.size(1), stream()),
+     "ce_fwd_rows");
+}
+
 void ce_bwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, c10::optional<at::Tensor> grad_out,
-                 double scale);
-void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor out, bool accumulate,
-          c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split,
-          c10::optional<at::Tensor> cos_t, c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols,
-          c10::optional<at::Tensor> tgt, c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out,
-          c10::optional<at::Tensor> part, c10::optional<at::Tensor> tlogit, double alpha, int64_t bn);
-int gemm_error_code(bool reset);
+                 double scale) {
+  cuda2d(logits, "logits");
+  CHECK_DT(logits, at::kBFloat16);
+  ok(llmt::ce_bwd_rows(logits.data_ptr(), logits.stride(0), targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+                       static_cast<const float*>(opt_ptr(grad_out)), (float)scale, logits.size(0), logits.size(1),
+                       stream()),
+     "ce_bwd_rows");
+}
+
 void ce_combine(at::Tensor part, at::Tensor tlogit, at::Tensor tgt, at::Tensor lse, at::Tensor loss, int64_t nblk,
-                int64_t V);
+                int64_t V) {
+  ok(llmt::ce_combine(part.data_ptr<float>(), tlogit.data_ptr<float>(), tgt.data_ptr<int64_t>(), lse.data_ptr<float>(),
+                      loss.data_ptr<float>(), (int)lse.numel(), (int)nblk, (int)V, stream()),
+     "ce_combine");
+}
+
+// ---------------------------------------------------------------- GEMM
+void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor out, bool accumulate,
+          c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split, c10::optional<at::Tensor> cos_t,
+          c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols, c10::optional<at::Tensor> tgt,
+          c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
+          c10::optional<at::Tensor> tlogit, double alpha, int64_t bn) {
+  cuda2d(a, "a");
+  cuda2d(b, "b");
+  CHECK_DT(a, at::kBFloat16);
+  CHECK_DT(b, at::kBFloat16);
+  CHECK(out.is_cuda(), "out must be a CUDA tensor");
+  const int M = ta ? a.size(1) : a.size(0);
+  const int K = ta ? a.size(0) : a.size(1);
+  int N = tb ? b.size(0) : b.size(1);
+  const int Kb = tb ? b.size(1) : b.size(0);
+  CHECK(K == Kb, "gemm inner dims differ: ", K, " vs ", Kb);
+  if (epi == llmt::EPI_SWIGLU) {
+    CHECK(tb && b.size(0) == 2 * split, "SWIGLU gemm: b must be W13 (2*ffn, K)");
+    N = (int)split;
+  }
+  switch (epi) {
+    case llmt::EPI_BF16: case llmt::EPI_ROPE: case llmt::EPI_CE_BWD: case llmt::EPI_SWIGLU:
+      CHECK_DT(out, at::kBFloat16);
+      CHECK(out.dim() == 2 && out.size(0) >= M && out.size(1) >= N && out.stride(1) == 1 && out.stride(0) % 8 == 0,
+            "gemm: bf16 output must be (M, N) row-major with a 16-byte-multiple pitch");
+      break;
+    case llmt::EPI_F32:
+      CHECK_DT(out, at::kFloat);
+      CHECK(out.dim() == 2 && out.size(0) >= M && out.size(1) >= N && out.stride(1) == 1 && out.stride(0) % 4 == 0,
+            "gemm: fp32 output must be (M, N) row-major with a 16-byte-multiple pitch");
+      break;
+    case llmt::EPI_SWIGLU_BWD: case llmt::EPI_CE_FWD: break;
+    default: CHECK(false, "gemm: unknown epilogue ", epi);
+  }
+  llmt::GemmArgs g{};
+  g.out = out.data_ptr();
+  g.ldo = out.dim() == 2 ? out.stride(0) : N;
+  g.accumulate = accumulate ? 1 : 0;
+  g.split = (int)split;
+  g.alpha = (float)alpha;
+  if (aux.has_value() && aux->defined()) {
+    CHECK_DT((*aux), at::kBFloat16);
+    g.aux = aux->data_ptr();
+    g.ld_aux = aux->stride(0);
+  }
+  if (out2.has_value() && out2->defined()) {
+    CHECK_DT((*out2), at::kBFloat16);
+    g.out2 = out2->data_ptr();
+    g.ldo2 = out2->stride(0);
+  }
+  g.cos_t = static_cast<const float*>(opt_ptr(cos_t));
+  g.sin_t = static_cast<const float*>(opt_ptr(sin_t));
+  g.T = (int)T;
+  g.hd = (int)hd;
+  g.rot_cols = (int)rot_cols;
+  g.tgt = static_cast<const int64_t*>(opt_ptr(tgt));
+  g.lse = static_cast<const float*>(opt_ptr(lse));
+  g.grad_out = static_cast<const float*>(opt_ptr(grad_out));
+  g.part = static_cast<float*>(const_cast<void*>(opt_ptr(part)));
+  g.tlogit = static_cast<float*>(const_cast<void*>(opt_ptr(tlogit)));
+  if (epi == llmt::EPI_ROPE) CHECK(g.cos_t && g.sin_t && T > 0, "ROPE gemm needs rope tables and T");
+  if (epi == llmt::EPI_SWIGLU) CHECK(g.aux && aux->stride(0) % 8 == 0, "SWIGLU gemm needs the gu save buffer");
+  if (epi == llmt::EPI_SWIGLU_BWD) CHECK(g.aux && g.out2 && split == N, "SWIGLU_BWD gemm args");
+  if (epi == llmt::EPI_CE_FWD) {
+    CHECK(g.tgt && g.part && g.tlogit, "CE_FWD gemm args");
+    const int BN = bn ? (int)bn : llmt::gemm_pick_bn(M, N, (int)epi);
+    CHECK(part->numel() >= (int64_t)M * ((N + BN - 1) / BN) * 2, "CE_FWD partial buffer too small");
+  }
+  if (epi == llmt::EPI_CE_BWD) CHECK(g.tgt && g.lse, "CE_BWD gemm args");
+  ok(llmt::gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), ta, tb, M, N, K, (int)epi, (int)bn, g, stream()),
+     "gemm");
+}
+
+// ---------------------------------------------------------------- attention
 std::vector<at::Tensor> flash_attn_fwd(at::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd,
-                                       bool causal, double scale);
+                                       bool causal, double scale) {
+  cuda2d(qkv, "qkv");
+  CHECK_DT(qkv, at::kBFloat16);
+  CHECK(qkv.size(0) == B * T && qkv.size(1) >= (H + 2 * KV) * hd, "flash_attn_fwd: qkv shape mismatch");
+  auto o = at::empty({B * T, H * hd}, qkv.options());
+  auto lse = at::empty({B, H, T}, qkv.options().dtype(at::kFloat));
+  ok(llmt::flash_attn_fwd(qkv.data_ptr(), qkv.stride(0), o.data_ptr(), lse.data_ptr<float>(), (int)B, (int)T, (int)H,
+                          (int)KV, (int)hd, causal, (float)scale, stream()),
+     "flash_attn_fwd");
+  return {o, lse};
+}
+
 at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse, at::Tensor cos_t,
                           at::Tensor sin_t, int64_t B, int64_t T, int64_t H, int64_t KV, int64_t hd, bool causal,
-                          double scale);
-int attn_error_code(bool reset);
-}  // namespace llmt
+                          double scale) {
+  CHECK_DT(dO, at::kBFloat16);
+  CHECK_DT(qkv, at::kBFloat16);
+  CHECK_DT(o, at::kBFloat16);
+  CHECK_DT(lse, at::kFloat);
+  CHECK(dO.is_contiguous() && o.is_contiguous() && qkv.is_contiguous() && lse.is_contiguous(),
+        "flash_attn_bwd: operands must be contiguous");
+  CHECK(dO.numel() == B * T * H * hd && o.numel() == dO.numel(), "flash_attn_bwd: dO/o shape");
+  CHECK(qkv.size(0) == B * T && qkv.size(1) == (H + 2 * KV) * hd, "flash_attn_bwd: qkv shape");
+  CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd && cos_t.is_contiguous() && sin_t.is_contiguous(),
+        "flash_attn_bwd: rope tables");
+  auto dqkv = at::empty_like(qkv);
+  auto dsum = at::empty({B, H, T}, lse.options());
+  auto dq_acc = at::empty({B * T, H * hd}, lse.options());
+  ok(llmt::flash_attn_bwd(dO.data_ptr(), qkv.data_ptr(), qkv.stride(0), o.data_ptr(), lse.data_ptr<float>(),
+                          cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), dqkv.data_ptr(), dsum.data_ptr<float>(),
+                          dq_acc.data_ptr<float>(), (int)B, (int)T, (int)H, (int)KV, (int)hd, causal, (float)scale,
+                          stream()),
+     "flash_attn_bwd");
+  return dqkv;
+}
+
+}  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   namespace py = pybind11;
   using namespace pybind11::literals;
   m.doc() = "llmt native sm_100a kernels";
-  m.def("add_rmsnorm_fwd", &llmt::add_rmsnorm_fwd, "a"_a, "r"_a, "w"_a, "eps"_a, "write_s"_a);
-  m.def("rmsnorm_bwd", &llmt::rmsnorm_bwd, "dy"_a, "s"_a, "w"_a, "rstd"_a, "ds_in"_a, "dw"_a, "ticket"_a,
-        "write_ds16"_a, "accumulate"_a);
-  m.def("swiglu_fwd", &llmt::swiglu_fwd);
-  m.def("swiglu_bwd", &llmt::swiglu_bwd);
-  m.def("rope_inplace", &llmt::rope_inplace);
-  m.def("embedding_fwd", &llmt::embedding_fwd);
-  m.def("embedding_bwd", &llmt::embedding_bwd);
-  m.def("adamw_step", &llmt::adamw_step);
-  m.def("cast_bf16", &llmt::cast_bf16);
-  m.def("ce_fwd_rows", &llmt::ce_fwd_rows);
-  m.def("ce_bwd_rows", &llmt::ce_bwd_rows);
-  m.def("gemm", &llmt::gemm, "a"_a, "b"_a, "ta"_a, "tb"_a, "epi"_a, "out"_a, "accumulate"_a = false,
-        "aux"_a = py::none(), "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(),
-        "T"_a = 0, "hd"_a = 0, "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(),
-        "grad_out"_a = py::none(), "part"_a = py::none(), "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd, "a"_a, "r"_a, "w"_a, "eps"_a, "write_s"_a);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, "dy"_a, "s"_a, "w"_a, "rstd"_a, "ds_in"_a, "dw"_a, "ticket"_a, "write_ds16"_a,
+        "accumulate"_a);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("rope_inplace", &rope_inplace);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("cast_bf16", &cast_bf16);
+  m.def("ce_fwd_rows", &ce_fwd_rows);
+  m.def("ce_bwd_rows", &ce_bwd_rows);
+  m.def("ce_combine", &ce_combine);
+  m.def("gemm", &gemm, "a"_a, "b"_a, "ta"_a, "tb"_a, "epi"_a, "out"_a, "accumulate"_a = false, "aux"_a = py::none(),
+        "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
+        "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
+        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
-  m.def("ce_combine", &llmt::ce_combine);
-  m.def("flash_attn_fwd", &llmt::flash_attn_fwd);
-  m.def("flash_attn_bwd", &llmt::flash_attn_bwd);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
+  m.def("sm_count", &llmt::sm_count);
 }

@@ -82,31 +82,20 @@ ce_bwd_rows_kernel(bf16* __restrict__ logits, int64_t ld, const int64_t* __restr
 
 }  // namespace
 
-void ce_fwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor loss) {
-  LLMT_CHECK_DTYPE(logits, at::kBFloat16);
-  LLMT_CHECK_DTYPE(targets, at::kLong);
-  const int64_t R = logits.size(0);
-  const int V = logits.size(1);
-  LLMT_CHECK(V % 8 == 0 && logits.stride(1) == 1 && logits.stride(0) % 8 == 0, "ce: logits layout");
-  if (R == 0) return;
-  ce_fwd_rows_kernel<<<R, kCeThreads, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(logits.data_ptr()),
-                                                         logits.stride(0), targets.data_ptr<int64_t>(),
-                                                         lse.data_ptr<float>(), loss.data_ptr<float>(), V);
-  LLMT_LAUNCH_CHECK();
+cudaError_t ce_fwd_rows(const void* logits, int64_t ld, const int64_t* tgt, float* lse, float* loss, int64_t R, int V,
+                        cudaStream_t st) {
+  LLMT_REQUIRE(V % 8 == 0 && ld % 8 == 0, "ce: vocab and pitch must be multiples of 8");
+  if (R == 0) return cudaSuccess;
+  ce_fwd_rows_kernel<<<(unsigned)R, kCeThreads, 0, st>>>(static_cast<const bf16*>(logits), ld, tgt, lse, loss, V);
+  return cudaGetLastError();
 }
 
-void ce_bwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, c10::optional<at::Tensor> grad_out,
-                 double scale) {
-  LLMT_CHECK_DTYPE(logits, at::kBFloat16);
-  const int64_t R = logits.size(0);
-  const int V = logits.size(1);
-  LLMT_CHECK(V % 8 == 0 && logits.stride(1) == 1 && logits.stride(0) % 8 == 0, "ce: logits layout");
-  if (R == 0) return;
-  const float* go = (grad_out.has_value() && grad_out->defined()) ? grad_out->data_ptr<float>() : nullptr;
-  ce_bwd_rows_kernel<<<R, kCeThreads, 0, cur_stream()>>>(reinterpret_cast<bf16*>(logits.data_ptr()), logits.stride(0),
-                                                         targets.data_ptr<int64_t>(), lse.data_ptr<float>(), go,
-                                                         (float)scale, V);
-  LLMT_LAUNCH_CHECK();
+cudaError_t ce_bwd_rows(void* logits, int64_t ld, const int64_t* tgt, const float* lse, const float* grad_out,
+                        float scale, int64_t R, int V, cudaStream_t st) {
+  LLMT_REQUIRE(V % 8 == 0 && ld % 8 == 0, "ce: vocab and pitch must be multiples of 8");
+  if (R == 0) return cudaSuccess;
+  ce_bwd_rows_kernel<<<(unsigned)R, kCeThreads, 0, st>>>(static_cast<bf16*>(logits), ld, tgt, lse, grad_out, scale, V);
+  return cudaGetLastError();
 }
 
 }  // namespace llmt

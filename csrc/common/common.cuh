@@ -1,7 +1,5 @@
-// Shared helpers for every llmt CUDA kernel (sm_100a only).
-//
-// Vector load/store wrappers, bf16 conversion, warp reductions and the launch-check
-// macro used by all translation units of the extension.
+// Shared device helpers for every llmt CUDA kernel (sm_100a only): vector load/store
+// wrappers, bf16 conversion, warp reductions. No torch headers (see api.h).
 #pragma once
 
 #include <cuda.h>
@@ -9,32 +7,23 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include <ATen/cuda/CUDAContext.h>
-#include <c10/cuda/CUDAException.h>
-#include <torch/extension.h>
+#include <algorithm>
 
-#define LLMT_CHECK(cond, ...) TORCH_CHECK(cond, "llmt: ", __VA_ARGS__)
-#define LLMT_CHECK_CUDA(t) LLMT_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
-#define LLMT_CHECK_CONTIG(t) LLMT_CHECK((t).is_contiguous(), #t " must be contiguous")
-#define LLMT_CHECK_DTYPE(t, dt) LLMT_CHECK((t).scalar_type() == (dt), #t " has dtype ", (t).scalar_type(), ", expected ", (dt))
-#define LLMT_LAUNCH_CHECK() C10_CUDA_KERNEL_LAUNCH_CHECK()
+#include "../api.h"
+
+// Argument check inside a launcher: records the message and returns cudaErrorInvalidValue.
+#define LLMT_REQUIRE(cond, msg)          \
+  do {                                   \
+    if (!(cond)) {                       \
+      ::llmt::set_last_error(msg);       \
+      return cudaErrorInvalidValue;      \
+    }                                    \
+  } while (0)
 
 namespace llmt {
 
 using bf16 = __nv_bfloat16;
 using bf162 = __nv_bfloat162;
-
-inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
-
-inline int sm_count() {
-  static int n = -1;
-  if (n < 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -1,0 +1,24 @@
+// Host-side runtime helpers shared by all launchers: last-error message, SM count.
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "../api.h"
+
+namespace llmt {
+namespace {
+thread_local std::string g_last_error;
+}
+
+const char* last_error() { return g_last_error.c_str(); }
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
+}
+}  // namespace llmt

@@ -6,8 +6,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include <torch/extension.h>
-
 namespace llmt {
 
 inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
@@ -16,8 +14,7 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p, "llmt: cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
 }
@@ -29,18 +26,19 @@ inline bool tma_ok(const void* ptr, uint64_t ld, int elem_bytes) {
 
 // Row-major 2D matrix of `outer` rows x `inner` elements (row pitch `ld` elements),
 // tiled in boxes of box_outer rows x box_inner elements with 128-byte swizzling.
-inline void make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+// Returns false if the driver rejects the description.
+inline bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
                          uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
                          CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * (uint64_t)elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = tmap_encode_fn()(m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "llmt: cuTensorMapEncodeTiled failed (", (int)r, ") inner=", inner, " outer=", outer,
-              " ld=", ld, " box=", box_inner, "x", box_outer);
+  auto fn = tmap_encode_fn();
+  if (!fn || !tma_ok(ptr, ld, elem_bytes)) return false;
+  CUresult r = fn(m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 }  // namespace llmt

@@ -33,40 +33,17 @@
 
 namespace llmt {
 
-enum EpiKind : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_ROPE = 4, EPI_CE_FWD = 5, EPI_CE_BWD = 6 };
-
-struct GemmArgs {
-  int M, N, K;
-  int m_blocks, n_blocks, k_blocks;
-  void* out;
-  int64_t ldo;
-  int accumulate;
-  int split;  // SWIGLU: row offset of W3 inside W13 (= ffn); SWIGLU_BWD: column offset of u in gu (= ffn)
-  const void* aux;
-  int64_t ld_aux;
-  void* out2;
-  int64_t ldo2;
-  const float* cos_t;
-  const float* sin_t;
-  int T, hd, rot_cols;
-  const int64_t* tgt;
-  const float* lse;
-  const float* grad_out;
-  float* part;    // CE_FWD partials (M, n_blocks, 2)
-  float* tlogit;  // CE_FWD target logits (M)
-  float alpha;
-  int* err;
-};
-
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
 
-// Host launchers, one translation unit per operand layout (keeps build parallel).
-void gemm_launch_kk(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // fwd
-void gemm_launch_km(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // dgrad
-void gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g);  // wgrad
-int* gemm_err_word();
+// Host launchers, one translation unit per operand layout (keeps the build parallel).
+cudaError_t gemm_launch_kk(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                           cudaStream_t st);  // fwd
+cudaError_t gemm_launch_km(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                           cudaStream_t st);  // dgrad
+cudaError_t gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                           cudaStream_t st);  // wgrad
 
 namespace gemm_detail {
 
@@ -406,18 +383,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args) {
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t st) {
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024 + 256;
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   const int tiles = args.m_blocks * args.n_blocks;
   const int grid = std::min(tiles, sm_count());
-  kern<<<grid, kGemmThreads, smem, cur_stream()>>>(ta, tb, args);
-  LLMT_LAUNCH_CHECK();
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, args);
+  return cudaGetLastError();
 }
 
 template <int BN>

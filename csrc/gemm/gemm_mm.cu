@@ -6,17 +6,17 @@ namespace llmt {
 using namespace gemm_detail;
 
 template <int BN>
-static void run_mm(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g) {
+static cudaError_t run_mm(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
   constexpr int S = stages_for<BN>();
   switch (epi) {
-    case EPI_BF16: launch<BN, S, true, true, EPI_BF16>(ta, tb, g); break;
-    case EPI_F32: launch<BN, S, true, true, EPI_F32>(ta, tb, g); break;
-    default: TORCH_CHECK(false, "llmt: epilogue ", epi, " not built for the dy^T x layout");
+    case EPI_BF16: return launch<BN, S, true, true, EPI_BF16>(ta, tb, g, st);
+    case EPI_F32: return launch<BN, S, true, true, EPI_F32>(ta, tb, g, st);
+    default: set_last_error("gemm: epilogue not built for the dy^T x layout"); return cudaErrorInvalidValue;
   }
 }
 
-void gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g) {
-  if (bn == 256) run_mm<256>(epi, ta, tb, g);
-  else run_mm<128>(epi, ta, tb, g);
+cudaError_t gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
+                           cudaStream_t st) {
+  return bn == 256 ? run_mm<256>(epi, ta, tb, g, st) : run_mm<128>(epi, ta, tb, g, st);
 }
 }  // namespace llmt

@@ -205,99 +205,67 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
 }
 
 template <typename F>
-void dispatch_tpr(int D, F&& f) {
-  LLMT_CHECK(D % 8 == 0, "RMSNorm width must be a multiple of 8, got ", D);
+bool dispatch_tpr(int D, F&& f) {
+  if (D % 8 != 0) return false;
   if (D <= 32 * 8 * kMaxChunks) f(std::integral_constant<int, 32>{});
   else if (D <= 64 * 8 * kMaxChunks) f(std::integral_constant<int, 64>{});
   else if (D <= 128 * 8 * kMaxChunks) f(std::integral_constant<int, 128>{});
   else if (D <= 256 * 8 * kMaxChunks) f(std::integral_constant<int, 256>{});
-  else LLMT_CHECK(false, "RMSNorm width ", D, " exceeds 8192");
+  else return false;
+  return true;
 }
 
 }  // namespace
 
-// y = rmsnorm(r + a) * w.  Returns (y bf16, s fp32 or undefined, rstd fp32).
-std::vector<at::Tensor> add_rmsnorm_fwd(c10::optional<at::Tensor> a, at::Tensor r, at::Tensor w, double eps,
-                                        bool write_s) {
-  LLMT_CHECK_CUDA(r);
-  LLMT_CHECK_CONTIG(r);
-  LLMT_CHECK_DTYPE(r, at::kFloat);
-  LLMT_CHECK_DTYPE(w, at::kFloat);
-  const int D = r.size(-1);
-  const int64_t N = r.numel() / D;
-  auto y = at::empty(r.sizes(), r.options().dtype(at::kBFloat16));
-  auto rstd = at::empty({N}, r.options());
-  at::Tensor s;
-  const bool has_a = a.has_value() && a->defined();
-  if (has_a) {
-    LLMT_CHECK_DTYPE((*a), at::kBFloat16);
-    LLMT_CHECK_CONTIG((*a));
-    LLMT_CHECK(a->numel() == r.numel(), "a and r differ in size");
-  }
-  if (write_s) s = at::empty_like(r);
-  if (N == 0) return {y, s, rstd};
+// y = rmsnorm(r + a) * w; a (bf16) and s (fp32 out) optional.
+cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, void* y_bf16, float* s, float* rstd,
+                            int64_t N, int D, float eps, cudaStream_t st) {
+  LLMT_REQUIRE(D % 8 == 0 && D <= 8192, "rmsnorm: width must be a multiple of 8 and at most 8192");
+  if (N == 0) return cudaSuccess;
+  const bf16* ap = static_cast<const bf16*>(a_bf16);
+  bf16* y = static_cast<bf16*>(y_bf16);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
     constexpr int RPC = kThreads / TPR;
-    dim3 grid(cdiv(N, RPC));
-    const bf16* ap = has_a ? reinterpret_cast<const bf16*>(a->data_ptr()) : nullptr;
-    auto launch = [&](auto kern) {
-      kern<<<grid, kThreads, 0, cur_stream()>>>(ap, r.data_ptr<float>(), w.data_ptr<float>(),
-                                                 reinterpret_cast<bf16*>(y.data_ptr()),
-                                                 write_s ? s.data_ptr<float>() : nullptr, rstd.data_ptr<float>(),
-                                                 N, D, (float)eps);
-    };
-    if (has_a && write_s) launch(add_rmsnorm_fwd_kernel<TPR, true, true>);
-    else if (has_a) launch(add_rmsnorm_fwd_kernel<TPR, true, false>);
-    else if (write_s) launch(add_rmsnorm_fwd_kernel<TPR, false, true>);
+    dim3 grid((unsigned)cdiv(N, RPC));
+    auto launch = [&](auto kern) { kern<<<grid, kThreads, 0, st>>>(ap, r, w, y, s, rstd, N, D, eps); };
+    if (ap && s) launch(add_rmsnorm_fwd_kernel<TPR, true, true>);
+    else if (ap) launch(add_rmsnorm_fwd_kernel<TPR, true, false>);
+    else if (s) launch(add_rmsnorm_fwd_kernel<TPR, false, true>);
     else launch(add_rmsnorm_fwd_kernel<TPR, false, false>);
-    LLMT_LAUNCH_CHECK();
   });
-  return {y, s, rstd};
+  return cudaGetLastError();
 }
 
-// Returns (ds fp32, ds16 bf16 or undefined). dw (fp32, D) is written or accumulated in place.
-std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor s, at::Tensor w, at::Tensor rstd,
-                                    c10::optional<at::Tensor> ds_in, at::Tensor dw, at::Tensor ticket,
-                                    bool write_ds16, bool accumulate) {
-  LLMT_CHECK_DTYPE(dy, at::kBFloat16);
-  LLMT_CHECK_DTYPE(s, at::kFloat);
-  LLMT_CHECK_DTYPE(dw, at::kFloat);
-  LLMT_CHECK_DTYPE(ticket, at::kInt);
-  LLMT_CHECK_CONTIG(dy);
-  LLMT_CHECK_CONTIG(s);
-  const int D = s.size(-1);
-  const int64_t N = s.numel() / D;
-  LLMT_CHECK(dy.numel() == s.numel(), "dy and s differ in size");
-  auto ds = at::empty_like(s);
-  at::Tensor ds16;
-  if (write_ds16) ds16 = at::empty(s.sizes(), s.options().dtype(at::kBFloat16));
-  const bool has_dsin = ds_in.has_value() && ds_in->defined();
-  if (has_dsin) {
-    LLMT_CHECK_DTYPE((*ds_in), at::kFloat);
-    LLMT_CHECK_CONTIG((*ds_in));
-  }
-  if (N == 0) return {ds, ds16};
+int rmsnorm_bwd_partials(int64_t N, int D) {
+  int tpr = D <= 1024 ? 32 : D <= 2048 ? 64 : D <= 4096 ? 128 : 256;
+  const int rpc = kThreads / tpr;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc), 2 * sm_count()));
+}
+
+// ds = rmsnorm backward + ds_in (optional); ds16 (bf16 copy) optional; dw written or accumulated.
+// dw_part must hold rmsnorm_bwd_partials(N, D) x D floats; ticket is a zero-initialised word
+// the kernel re-arms itself.
+cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, const float* rstd, const float* ds_in,
+                        float* ds, void* ds16, float* dw_part, float* dw, unsigned* ticket, int64_t N, int D,
+                        int accumulate, cudaStream_t st) {
+  LLMT_REQUIRE(D % 8 == 0 && D <= 8192, "rmsnorm: width must be a multiple of 8 and at most 8192");
+  if (N == 0) return cudaSuccess;
+  const bf16* dy = static_cast<const bf16*>(dy_bf16);
+  bf16* d16 = static_cast<bf16*>(ds16);
+  const int grid = rmsnorm_bwd_partials(N, D);
+  const size_t smem = D * sizeof(float);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
-    constexpr int RPC = kThreads / TPR;
-    int grid = (int)std::min<int64_t>(cdiv(N, RPC), 2 * sm_count());
-    auto part = at::empty({grid, D}, s.options());
-    const size_t smem = D * sizeof(float);
     auto launch = [&](auto kern) {
-      kern<<<grid, kThreads, smem, cur_stream()>>>(
-          reinterpret_cast<const bf16*>(dy.data_ptr()), s.data_ptr<float>(), w.data_ptr<float>(),
-          rstd.data_ptr<float>(), has_dsin ? ds_in->data_ptr<float>() : nullptr, ds.data_ptr<float>(),
-          write_ds16 ? reinterpret_cast<bf16*>(ds16.data_ptr()) : nullptr, part.data_ptr<float>(),
-          dw.data_ptr<float>(), reinterpret_cast<unsigned int*>(ticket.data_ptr<int>()), N, D, accumulate ? 1 : 0);
+      kern<<<grid, kThreads, smem, st>>>(dy, s, w, rstd, ds_in, ds, d16, dw_part, dw, ticket, N, D, accumulate);
     };
-    if (has_dsin && write_ds16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
-    else if (has_dsin) launch(rmsnorm_bwd_kernel<TPR, true, false>);
-    else if (write_ds16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
+    if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
+    else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
+    else if (d16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
     else launch(rmsnorm_bwd_kernel<TPR, false, false>);
-    LLMT_LAUNCH_CHECK();
   });
-  return {ds, ds16};
+  return cudaGetLastError();
 }
 
 }  // namespace llmt
