@@ -65,10 +65,10 @@ class FlatParams:
                 p.data = self.master[o:o + n].view(p.shape)
                 p.main_grad = self.grad[o:o + n].view(p.shape)
                 p.w16 = self.shadow[o:o + n].view(p.shape)
+        pos = {id(p): o for p, o in zip(self.params, self.offsets)}
         for blk in model.blocks:
             w1, w3 = blk.mlp.w1.weight, blk.mlp.w3.weight
-            o1 = self.offsets[self.params.index(w1)]
-            o3 = self.offsets[self.params.index(w3)]
+            o1, o3 = pos[id(w1)], pos[id(w3)]
             if o3 != o1 + w1.numel():
                 raise RuntimeError("w1 and w3 must be adjacent in the flat buffer (ffn*d must be a multiple of 64)")
             ffn, d = w1.shape

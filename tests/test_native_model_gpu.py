@@ -1,0 +1,72 @@
+"""Native training path (every op on llmt._C) vs the plain PyTorch fp32 model on the same weights."""
+import pytest
+import torch
+
+from tests.helpers import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(cfg, T, seed=0):
+    from llmt.models.llama import build_model
+    from llmt.models.native import NativeLlama
+    ref = build_model(cfg, T, seed=seed, device="cuda")
+    ours = build_model(cfg, T, seed=seed, device="cuda")
+    return ref, ours, NativeLlama(ours)
+
+
+@pytest.mark.parametrize("overrides", [{}, {"kv_heads": 2}, {"H": 2}])
+def test_native_loss_and_grads_match_fp32(overrides):
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.ops import functions as Fn
+    from llmt.ops import native
+    cfg = get_config("tiny256", **overrides)
+    B, T = 2, 128
+    ref, ours, net = _pair(cfg, T)
+    idx, tgt = make_batch(B, T, cfg.vocab, "cuda")
+    loss_ref = ref(idx, tgt)
+    loss_ref.backward()
+    Fn.FLAGS.reset()
+    loss = net(idx, tgt)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert native.gemm_error_code() == 0 and native.attn_error_code() == 0
+    assert abs(loss.item() - loss_ref.item()) / loss_ref.item() < 1e-2
+    for (name, p_ref), p in zip(ref.named_parameters(), ours.parameters()):
+        assert p.grad is None
+        assert rel_err(p.main_grad, p_ref.grad) < 5e-2, name
+
+
+def test_native_training_decreases_loss_and_graph_matches_eager():
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.train import Trainer
+    cfg = get_config("tiny256")
+    idx, tgt = make_batch(2, 128, cfg.vocab, "cpu")
+    eager = Trainer(cfg, 2, 128, cuda_graph=False)
+    graph = Trainer(cfg, 2, 128, cuda_graph=True)
+    le = [eager.train_step(idx, tgt) for _ in range(8)]
+    lg = [graph.train_step(idx, tgt) for _ in range(8)]
+    assert le[-1] < le[0] - 0.5
+    # graph capture runs two eager warm-up steps inside the first call, so compare shifted curves
+    assert abs(lg[0] - le[2]) / le[2] < 2e-2
+    graph.release()
+
+
+def test_native_step_matches_reference_adamw():
+    """One full step (fwd + bwd + fused AdamW) vs torch.optim.AdamW on the fp32 model."""
+    from llmt.config import get_config
+    from llmt.models.llama import build_model, make_batch
+    from llmt.train import Trainer
+    cfg = get_config("tiny256")
+    idx, tgt = make_batch(2, 128, cfg.vocab, "cpu")
+    ref = build_model(cfg, 128, seed=0, device="cuda")
+    opt = torch.optim.AdamW(ref.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    ref(idx.cuda(), tgt.cuda()).backward()
+    opt.step()
+    tr = Trainer(cfg, 2, 128, cuda_graph=False)
+    tr.train_step(idx, tgt)
+    for (name, p_ref), p in zip(ref.named_parameters(), tr.model.parameters()):
+        # one Adam step moves each weight by ~lr; compare the update directions
+        assert rel_err(p.detach(), p_ref.detach()) < 1e-3, name
