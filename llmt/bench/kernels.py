@@ -1,0 +1,185 @@
+"""Kernel microbenchmarks at the model's shapes (the reference's kernels/bench_kernels.py).
+
+Each op is timed with CUDA events, median of repeats, with a 256 MB buffer written between
+repeats to flush the 126 MB L2 (reference bench_kernels.py:155-157 flushes the same way).
+GEMMs and attention report TFLOP/s and the fraction of the measured bf16 peak; memory-bound
+ops report GB/s of algorithmic traffic and the fraction of the measured HBM copy bandwidth
+(MEASURED_PEAKS.json). The PyTorch/cuBLAS/SDPA equivalent of each op runs alongside.
+
+    python -m llmt.bench.kernels --size medium --batch 4 --seq 1024 [--ops gemm,attn,norm,adamw]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"])
+    except Exception:  # noqa: BLE001
+        return 1590.0, 6650.0
+
+
+_flush = None
+
+
+def flush_l2():
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    _flush.fill_(1.0)
+
+
+def time_ms(fn, reps=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(reps):
+        flush_l2()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def gemm_shapes(cfg, tokens):
+    d, f, qo, V = cfg.d, cfg.ffn, cfg.qkv_out, cfg.vocab
+    hd_out = cfg.H * cfg.hd
+    return [
+        # name, M, N, K, ta, tb  (out = op(a) @ op(b))
+        ("qkv fwd", tokens, qo, d, False, True), ("qkv dgrad", tokens, d, qo, False, False),
+        ("qkv wgrad", qo, d, tokens, True, False),
+        ("wo fwd", tokens, d, hd_out, False, True), ("wo dgrad", tokens, hd_out, d, False, False),
+        ("wo wgrad", d, hd_out, tokens, True, False),
+        ("w13 fwd", tokens, 2 * f, d, False, True), ("w13 dgrad", tokens, d, 2 * f, False, False),
+        ("w13 wgrad", 2 * f, d, tokens, True, False),
+        ("w2 fwd", tokens, d, f, False, True), ("w2 dgrad", tokens, f, d, False, False),
+        ("w2 wgrad", d, f, tokens, True, False),
+        ("head fwd", tokens, V, d, False, True), ("head dgrad", tokens, d, V, False, False),
+        ("head wgrad", V, d, tokens, True, False),
+    ]
+
+
+def bench_gemm(cfg, tokens, rows):
+    from llmt.ops import native as N
+    peak, _ = peaks()
+    for name, M, Nn, K, ta, tb in gemm_shapes(cfg, tokens):
+        a = torch.randn((K, M) if ta else (M, K), device="cuda").bfloat16()
+        b = torch.randn((Nn, K) if tb else (K, Nn), device="cuda").bfloat16()
+        wgrad = ta
+        out = torch.empty(M, Nn, device="cuda", dtype=torch.float32 if wgrad else torch.bfloat16)
+        ours = time_ms(lambda: N.gemm(a, b, ta=ta, tb=tb, out=out))
+        aa = a.t() if ta else a
+        bb = b.t() if tb else b
+        ref = time_ms(lambda: torch.matmul(aa, bb, out_dtype=torch.float32) if wgrad else torch.matmul(aa, bb))
+        fl = 2.0 * M * Nn * K
+        rows.append(dict(op=f"gemm {name}", shape=f"{M}x{Nn}x{K}", ms=round(ours, 4), ref_ms=round(ref, 4),
+                         tflops=round(fl / ours / 1e9, 1), ref_tflops=round(fl / ref / 1e9, 1),
+                         frac_peak=round(fl / ours / 1e9 / peak, 3)))
+
+
+def bench_attn(cfg, B, T, rows):
+    from llmt.models.llama import rope_tables
+    from llmt.ops import native as N
+    peak, _ = peaks()
+    H, KV, hd = cfg.H, cfg.kvh, cfg.hd
+    qkv = torch.randn(B * T, (H + 2 * KV) * hd, device="cuda").bfloat16()
+    cos, sin = rope_tables(T, hd, cfg.rope_base, "cuda")
+    o, lse = N.flash_attn_fwd(qkv, B, T, H, KV, hd)
+    do = torch.randn_like(o)
+    fwd = time_ms(lambda: N.flash_attn_fwd(qkv, B, T, H, KV, hd))
+    bwd = time_ms(lambda: N.flash_attn_bwd(do, qkv, o, lse, cos, sin, B, T, H, KV, hd))
+    q = qkv.view(B, T, -1, hd)[:, :, :H].transpose(1, 2).contiguous().requires_grad_(True)
+    k = qkv.view(B, T, -1, hd)[:, :, H:H + KV].transpose(1, 2).repeat_interleave(H // KV, 1).contiguous().requires_grad_(True)
+    v = qkv.view(B, T, -1, hd)[:, :, H + KV:].transpose(1, 2).repeat_interleave(H // KV, 1).contiguous().requires_grad_(True)
+    y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    dy = torch.randn_like(y)
+    rf = time_ms(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True))
+    rb = time_ms(lambda: torch.autograd.grad(y, (q, k, v), dy, retain_graph=True))
+    fl = 4.0 * B * H * T * T * hd / 2  # causal
+    rows.append(dict(op="attn fwd", shape=f"B{B} H{H}/{KV} T{T} hd{hd}", ms=round(fwd, 4), ref_ms=round(rf, 4),
+                     tflops=round(fl / fwd / 1e9, 1), ref_tflops=round(fl / rf / 1e9, 1),
+                     frac_peak=round(fl / fwd / 1e9 / peak, 3)))
+    rows.append(dict(op="attn bwd", shape=f"B{B} H{H}/{KV} T{T} hd{hd}", ms=round(bwd, 4), ref_ms=round(rb, 4),
+                     tflops=round(2.5 * fl / bwd / 1e9, 1), ref_tflops=round(2.5 * fl / rb / 1e9, 1),
+                     frac_peak=round(2.5 * fl / bwd / 1e9 / peak, 3)))
+
+
+def _bw_row(rows, op, shape, ms, ref_ms, nbytes):
+    _, hbm = peaks()
+    rows.append(dict(op=op, shape=shape, ms=round(ms, 4), ref_ms=round(ref_ms, 4) if ref_ms else None,
+                     gbs=round(nbytes / ms / 1e6, 1), frac_hbm=round(nbytes / ms / 1e6 / hbm, 3)))
+
+
+def bench_memory_ops(cfg, tokens, rows):
+    from llmt.ops import native as N
+    d = cfg.d
+    r = torch.randn(tokens, d, device="cuda")
+    a = torch.randn(tokens, d, device="cuda").bfloat16()
+    w = torch.ones(d, device="cuda")
+    ms = time_ms(lambda: N.add_rmsnorm_fwd(a, r, w, 1e-5))
+
+    def ref_fwd():
+        s = r + a.float()
+        return (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5) * w).bfloat16(), s
+    _bw_row(rows, "add_rmsnorm fwd", f"{tokens}x{d}", ms, time_ms(ref_fwd), tokens * d * (2 + 4 + 4 + 2))
+    y, s, rstd = N.add_rmsnorm_fwd(a, r, w, 1e-5)
+    dy = torch.randn(tokens, d, device="cuda").bfloat16()
+    dw = torch.zeros(d, device="cuda")
+    ms = time_ms(lambda: N.rmsnorm_bwd(dy, s, w, rstd, r, dw, False))
+    _bw_row(rows, "add_rmsnorm bwd", f"{tokens}x{d}", ms, None, tokens * d * (2 + 4 + 4 + 4 + 2))
+    n = sum(p.numel() for p in [torch.empty(0)]) or 100_000_000
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    lr = torch.full((1,), 3e-4, device="cuda")
+    st = torch.ones(1, device="cuda", dtype=torch.int32)
+    ms = time_ms(lambda: N.adamw_step(p, g, m, v, p16, lr, st, 0.9, 0.95, 1e-8, 0.1))
+    pp = torch.nn.Parameter(p.clone())
+    pp.grad = g.clone()
+    opt = torch.optim.AdamW([pp], lr=3e-4, fused=True)
+    _bw_row(rows, "adamw (+bf16 copy)", f"{n}", ms, time_ms(opt.step), n * (16 + 12 + 2))
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--size", default="medium")
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--seq", type=int, default=1024)
+    p.add_argument("--ops", default="gemm,attn,mem")
+    p.add_argument("--json", default=None)
+    args = p.parse_args()
+    from llmt.config import get_config
+    cfg = get_config(args.size)
+    rows = []
+    ops = args.ops.split(",")
+    if "gemm" in ops:
+        bench_gemm(cfg, args.batch * args.seq, rows)
+    if "attn" in ops:
+        bench_attn(cfg, args.batch, args.seq, rows)
+    if "mem" in ops:
+        bench_memory_ops(cfg, args.batch * args.seq, rows)
+    for r in rows:
+        extra = (f"{r['tflops']:7.1f} TF/s (ref {r['ref_tflops']:7.1f}) {100 * r['frac_peak']:5.1f}% of peak"
+                 if "tflops" in r else f"{r['gbs']:7.1f} GB/s {100 * r['frac_hbm']:5.1f}% of HBM")
+        print(f"{r['op']:22s} {r['shape']:22s} {r['ms']:8.4f} ms (ref {r['ref_ms']}) {extra}")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"config": vars(args), "rows": rows}, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()
