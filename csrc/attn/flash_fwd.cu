@@ -5,16 +5,16 @@
 // packed post-RoPE qkv rows (B*T, (H + 2*KV) * hd) and o is written as (B*T, H*hd), the layout
 // the wo GEMM consumes. Online softmax (Milakov & Gimelshein 2018; FlashAttention, Dao et al.).
 //
-// One CTA per (batch*head, 128-query block); heaviest causal blocks are scheduled first.
-//   warp 0     TMA producer: Q once, K/V blocks of 128 keys through a 2-stage ring
+// One CTA per (batch*head, 128-query block), heaviest causal blocks first, two CTAs per SM
+// (head dim 64) so one CTA's softmax overlaps the other's MMAs:
+//   warp 0     TMA producer: Q once, K/V blocks of 128 keys through a STAGES-deep ring
 //   warp 1     TMEM allocator + single-thread MMA issuer:
-//                S_j  = Q K_j^T        (M=128, N=128, K=hd)  -> TMEM S[j%2]
-//                O'_j = P_j V_j        (M=128, N=hd,  K=128) -> TMEM O[j%2]
-//              S_{j+1} is issued before O'_j so the tensor core works while softmax runs
-//   warps 2-5  one thread per query row: two passes over S_j in TMEM (row max, then
-//              exp2 and the row sum), P_j written as bf16 into 128B-swizzled shared memory
-//              (the K-major A operand of the PV MMA), and O accumulated in registers:
-//              O = O * exp2(m_old - m_new) + O'_j.
+//                S_j  = Q K_j^T   (SS form, M=128, N=128, K=hd)    -> TMEM cols [0, 128)
+//                O'_j = P_j V_j   (TS form: P_j read from TMEM)    -> TMEM cols [128, 128+hd)
+//   warps 2-5  one thread per query row: row max of S_j (tree reduction, diagonal block
+//              masked branch-free), P = 2^(S*scale*log2e - m) on the SFU, row sum, P packed to
+//              bf16 and stored back over the consumed S columns with tcgen05.st; O is kept in
+//              registers, O = O * 2^(m_old - m_new) + O'_j.
 // GQA: query head h reads key/value head h / (H / KV). Keys past T or past the query
 // (causal) are masked. Saves lse (B, H, T) in natural-log units for the backward.
 #include "../common/common.cuh"
@@ -29,7 +29,6 @@ using namespace sm100;
 
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kStages = 2;
 constexpr int kAttnThreads = 192;
 
 struct AttnFwdArgs {
@@ -51,36 +50,34 @@ __device__ __forceinline__ uint32_t sw128_row_unit(int r, int u) {
 
 template <int HD>
 struct FwdSmem {
+  static constexpr int STAGES = HD == 64 ? 2 : 1;
   static constexpr uint32_t Q_BYTES = kBlockM * HD * 2;
   static constexpr uint32_t KV_BYTES = kBlockN * HD * 2;
-  static constexpr uint32_t P_BYTES = kBlockM * kBlockN * 2;
   static constexpr uint32_t Q_OFF = 0;
   static constexpr uint32_t K_OFF = Q_OFF + Q_BYTES;
-  static constexpr uint32_t V_OFF = K_OFF + kStages * KV_BYTES;
-  static constexpr uint32_t P_OFF = V_OFF + kStages * KV_BYTES;
-  static constexpr uint32_t BAR_OFF = P_OFF + 2 * P_BYTES;
-  static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
+  static constexpr uint32_t V_OFF = K_OFF + STAGES * KV_BYTES;
+  static constexpr uint32_t BAR_OFF = V_OFF + STAGES * KV_BYTES;
+  static constexpr uint32_t TOTAL = BAR_OFF + 128 + 1024;
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kAttnThreads, HD == 64 ? 2 : 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
   using L = FwdSmem<HD>;
-  constexpr int TMEM_COLS = 512;  // S[2] at 0/128, O[2] at 256/256+HD
+  constexpr int ST = L::STAGES;
+  constexpr int TMEM_COLS = 256;        // S/P at [0, 128), O' at [128, 128 + HD)
+  constexpr uint32_t C_O = 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;       // [kStages]
-  uint64_t* v_full = bars + 3;       // [kStages]
-  uint64_t* kv_empty = bars + 5;     // [kStages]
-  uint64_t* s_full = bars + 7;       // [2]
-  uint64_t* s_empty = bars + 9;      // [2]
-  uint64_t* p_full = bars + 11;      // [2]
-  uint64_t* p_empty = bars + 13;     // [2]
-  uint64_t* o_full = bars + 15;      // [2]
-  uint64_t* o_empty = bars + 17;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* k_full = bars + 1;       // [ST]
+  uint64_t* v_full = bars + 3;       // [ST]
+  uint64_t* kv_empty = bars + 5;     // [ST]
+  uint64_t* s_full = bars + 7;
+  uint64_t* p_full = bars + 8;       // 128 arrivals
+  uint64_t* o_full = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int bh = blockIdx.x;
@@ -95,19 +92,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
 
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < ST; ++s) {
       bar_init(&k_full[s], 1);
       bar_init(&v_full[s], 1);
       bar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      bar_init(&s_full[i], 1);
-      bar_init(&s_empty[i], 128);
-      bar_init(&p_full[i], 128);
-      bar_init(&p_empty[i], 1);
-      bar_init(&o_full[i], 1);
-      bar_init(&o_empty[i], 128);
-    }
+    bar_init(s_full, 1);
+    bar_init(p_full, 128);
+    bar_init(o_full, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
@@ -124,8 +116,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) tma_load_2d(smem + L::Q_OFF + c * 16384, &tm_qkv, q_full, qcol + c * 64, row0 + q0);
       for (int j = 0; j < nkv; ++j) {
-        const int s = j % kStages;
-        if (!wait_bar(&kv_empty[s], ((j / kStages) & 1) ^ 1, err, 11)) break;
+        const int s = j % ST;
+        if (!wait_bar(&kv_empty[s], ((j / ST) & 1) ^ 1, err, 11)) break;
         bar_arrive_expect_tx(&k_full[s], L::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
@@ -142,127 +134,133 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       constexpr uint32_t idesc_o = make_idesc_bf16(kBlockM, HD, false, true);
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       bool ok = wait_bar(q_full, 0, err, 12);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % kStages, pb = i & 1;
-        if (!wait_bar(&v_full[s], (i / kStages) & 1, err, 13)) return false;
-        if (!wait_bar(&p_full[pb], (i >> 1) & 1, err, 14)) return false;
-        if (!wait_bar(&o_empty[pb], ((i >> 1) & 1) ^ 1, err, 15)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + L::P_OFF + pb * L::P_BYTES);
-        const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
-#pragma unroll
-        for (int k = 0; k < kBlockN / 16; ++k) {
-          const uint64_t ad = make_sw128_desc(p_addr + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
-          const uint64_t bd = make_sw128_desc(v_addr + k * 2048, 16384, 1024);
-          mma_f16(tmem + 256 + pb * HD, ad, bd, idesc_o, k > 0 ? 1u : 0u);
-        }
-        mma_commit(&o_full[pb]);
-        mma_commit(&p_empty[pb]);
-        mma_commit(&kv_empty[s]);
-        return true;
-      };
       for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % kStages, sb = j & 1;
-        if (!wait_bar(&k_full[s], (j / kStages) & 1, err, 16)) { ok = false; break; }
-        if (!wait_bar(&s_empty[sb], ((j >> 1) & 1) ^ 1, err, 17)) { ok = false; break; }
+        const int s = j % ST;
+        if (!wait_bar(&k_full[s], (j / ST) & 1, err, 16)) break;
+        // P_{j-1} (aliasing S) must have been read by PV_{j-1} before S_j overwrites it.
+        if (j > 0 && !wait_bar(o_full, (j - 1) & 1, err, 17)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + L::K_OFF + s * L::KV_BYTES);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          mma_f16(tmem + sb * 128, make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024),
-                  idesc_s, k > 0 ? 1u : 0u);
+          mma_f16(tmem, make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024), idesc_s,
+                  k > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[sb]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        mma_commit(s_full);
+        if (!wait_bar(&v_full[s], (j / ST) & 1, err, 13)) break;
+        if (!wait_bar(p_full, j & 1, err, 14)) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < kBlockN / 16; ++k)
+          mma_f16_ts(tmem + C_O, tmem + k * 8, make_sw128_desc(v_addr + k * 2048, 16384, 1024), idesc_o, k > 0 ? 1u : 0u);
+        mma_commit(o_full);
+        mma_commit(&kv_empty[s]);
       }
-      if (ok && nkv >= 1) issue_pv(nkv - 1);
     }
   } else {
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row within the block
     const int q = q0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t t_s = tmem + lane_off;
+    const float sl2 = a.scale_log2;
     float o_acc[HD];
 #pragma unroll
     for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    uint8_t* p_base = smem + L::P_OFF;
     bool ok = true;
-
-    auto consume_o = [&](int i, float alpha) -> bool {
-      const int pb = i & 1;
-      if (!wait_bar(&o_full[pb], (i >> 1) & 1, err, 18)) return false;
+    for (int j = 0; j < nkv && ok; ++j) {
+      if (!wait_bar(s_full, j & 1, err, 19)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = j * kBlockN;
+      // keys allowed for this row: key < lim (causal: key <= q; always key < T)
+      const int lim = a.causal ? min(q + 1, a.T) : a.T;
+      const bool need_mask = k0 + kBlockN > (a.causal ? q0 + 1 : a.T) || k0 + kBlockN > a.T;
+      // pass 1: row max, 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_s + c * 32, v);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = (k0 + c * 32 + e < lim) ? __uint_as_float(v[e]) : -INFINITY;
+            mx8[e & 7] = fmaxf(mx8[e & 7], x);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[e]));
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m, mx * sl2);
+      const float msub = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2_approx(m - msub);  // m = -inf on the first block -> 0
+      // O'_{j-1} finished before S_j started (same MMA issue order), fold it in now.
+      if (j > 0) {
+        if (!wait_bar(o_full, (j - 1) & 1, err, 18)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_s + C_O + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
+        }
+      }
+      // pass 2: P = 2^(s * scale_log2 - m_new) as bf16 over the consumed S columns, row sum
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_s + c * 32, v);
+        tmem_wait_ld();
+        float p[32];
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            p[e] = (k0 + c * 32 + e < lim) ? ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -msub)) : 0.f;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) p[e] = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -msub));
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          sum8[e & 7] += p[2 * e] + p[2 * e + 1];
+          pk[e] = pack_bf16x2(p[2 * e], p[2 * e + 1]);
+        }
+        tmem_st16(t_s + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      bar_arrive(p_full);
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l = l * alpha + sum;
+      m = m_new;
+      alpha_prev = alpha;
+    }
+    if (ok && nkv >= 1 && wait_bar(o_full, (nkv - 1) & 1, err, 18)) {
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + 256 + pb * HD + c * 32, v);
+        tmem_ld32(t_s + C_O + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = o_acc[c * 32 + e] * alpha + __uint_as_float(v[e]);
+        for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
       }
-      tc_fence_before();
-      bar_arrive(&o_empty[pb]);
-      return true;
-    };
-
-    for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      if (!wait_bar(&s_full[sb], (j >> 1) & 1, err, 19)) { ok = false; break; }
-      tc_fence_after();
-      const int k0 = j * kBlockN;
-      const bool need_mask = (a.causal && k0 + kBlockN - 1 > q0) || (k0 + kBlockN > a.T);
-      // pass 1: row max
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + sb * 128 + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + c * 32 + e;
-          const bool valid = !need_mask || (key < a.T && (!a.causal || key <= q));
-          if (valid) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
-      }
-      const float m_new = fmaxf(m, mx * a.scale_log2);
-      const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m - m_new);
-      const float msub = (m_new == -INFINITY) ? 0.f : m_new;
-      // pass 2: probabilities -> bf16 P tile (swizzled), row sum
-      if (!wait_bar(&p_empty[sb], ((j >> 1) & 1) ^ 1, err, 20)) { ok = false; break; }
-      uint8_t* prow = p_base + sb * L::P_BYTES;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + sb * 128 + c * 32, v);
-        tmem_wait_ld();
-        float p[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + c * 32 + e;
-          const bool valid = !need_mask || (key < a.T && (!a.causal || key <= q));
-          p[e] = valid ? exp2f(__uint_as_float(v[e]) * a.scale_log2 - msub) : 0.f;
-          sum += p[e];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          BF16x8 pk = float_to_bf16x8(p + u * 8);
-          *reinterpret_cast<BF16x8*>(prow + sw128_row_unit(r, c * 4 + u)) = pk;
-        }
-      }
-      tc_fence_before();
-      bar_arrive(&s_empty[sb]);
-      fence_proxy_async_smem();
-      bar_arrive(&p_full[sb]);
-      l = l * alpha + sum;
-      m = m_new;
-      if (j >= 1 && !consume_o(j - 1, alpha_prev)) { ok = false; break; }
-      alpha_prev = alpha;
     }
-    if (ok && nkv >= 1) ok = consume_o(nkv - 1, alpha_prev);
     if (q < a.T) {
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       bf16* orow = a.o + (int64_t)(row0 + q) * a.ld_o + h * HD;

@@ -10,10 +10,9 @@
 //
 // Layout: TPR threads per row (a power of two, 32..256), each owning up to 4 chunks of 8
 // consecutive elements, 256 threads per CTA (256/TPR rows per CTA). The backward is
-// persistent; every CTA keeps its dw partial in registers, writes one (D) partial row and
-// the last CTA to finish (atomic ticket) sums the partials in a fixed order, so dw is
-// deterministic and needs no extra launch (the reference sums its (P, D) partials with a
-// separate host-side dwp.sum(0), add_rmsnorm_ext.py:70).
+// persistent; every CTA keeps its dw partial in registers and writes one (D) partial row,
+// and a column-parallel reduce kernel sums the partials in a fixed order (deterministic dw;
+// the reference reduces its (P, D) partials with a separate dwp.sum(0), add_rmsnorm_ext.py:70).
 #include "../common/common.cuh"
 
 namespace llmt {
@@ -95,26 +94,23 @@ add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, 
 }
 
 // dy bf16, s fp32, ds_in fp32 (optional); ds fp32 and ds16 bf16 (optional) out.
+// Two passes over each row's registers-free chunks (the second re-reads dy and s from L1),
+// so the kernel keeps only the dw partial in registers and runs several CTAs per SM.
+// Each CTA writes one (D) dw partial row; dw_reduce_kernel sums them in a fixed order.
 template <int TPR, bool HAS_DSIN, bool WRITE_DS16>
 __global__ void __launch_bounds__(kThreads)
 rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, const float* __restrict__ w,
                    const float* __restrict__ rstd_in, const float* __restrict__ ds_in,
-                   float* __restrict__ ds, bf16* __restrict__ ds16, float* __restrict__ dw_part,
-                   float* __restrict__ dw, unsigned int* __restrict__ ticket, int64_t N, int D,
-                   int accumulate) {
+                   float* __restrict__ ds, bf16* __restrict__ ds16, float* __restrict__ dw_part, int64_t N, int D) {
   __shared__ float red[kThreads / 32];
-  __shared__ bool is_last;
   constexpr int RPC = kThreads / TPR;
   const int t = threadIdx.x % TPR;
   const int rgroup = threadIdx.x / TPR;
-  float wv[kMaxChunks][8];
   float dwacc[kMaxChunks][8];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int e = (c * TPR + t) * 8;
+  for (int c = 0; c < kMaxChunks; ++c)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) { dwacc[c][j] = 0.f; wv[c][j] = (e < D) ? w[e + j] : 0.f; }
-  }
+    for (int j = 0; j < 8; ++j) dwacc[c][j] = 0.f;
   const int64_t stride = (int64_t)gridDim.x * RPC;
   // Every row group runs the same number of iterations so the block-wide barriers in
   // row_sum line up; rows past N are masked.
@@ -122,26 +118,23 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
   for (int64_t it = 0; it < iters; ++it) {
     const int64_t row = it * stride + (int64_t)blockIdx.x * RPC + rgroup;
     const bool valid = row < N;
-    float g[kMaxChunks][8], sv[kMaxChunks][8];
     float dot = 0.f;
     const float rs = valid ? rstd_in[row] : 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int e = (c * TPR + t) * 8;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { g[c][j] = 0.f; sv[c][j] = 0.f; }
       if (valid && e < D) {
         const int64_t off = row * D + e;
         float dyf[8];
         bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dy + off), dyf);
-        float4 s0 = ld_f4(s + off), s1 = ld_f4(s + off + 4);
-        sv[c][0] = s0.x; sv[c][1] = s0.y; sv[c][2] = s0.z; sv[c][3] = s0.w;
-        sv[c][4] = s1.x; sv[c][5] = s1.y; sv[c][6] = s1.z; sv[c][7] = s1.w;
+        const float4 s0 = ld_f4(s + off), s1 = ld_f4(s + off + 4);
+        const float4 w0 = ld_f4(w + e), w1 = ld_f4(w + e + 4);
+        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          g[c][j] = dyf[j] * wv[c][j];
-          dot += g[c][j] * sv[c][j];
-          dwacc[c][j] += dyf[j] * sv[c][j] * rs;
+          dot += dyf[j] * wv[j] * sv[j];
+          dwacc[c][j] += dyf[j] * sv[j] * rs;
         }
       }
     }
@@ -154,11 +147,17 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
         const int e = (c * TPR + t) * 8;
         if (e < D) {
           const int64_t off = row * D + e;
+          float dyf[8];
+          bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dy + off), dyf);
+          const float4 s0 = ld_f4(s + off), s1 = ld_f4(s + off + 4);
+          const float4 w0 = ld_f4(w + e), w1 = ld_f4(w + e + 4);
+          const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
           float o[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = rs * g[c][j] - sv[c][j] * rs3 * cc;
+          for (int j = 0; j < 8; ++j) o[j] = rs * dyf[j] * wv[j] - sv[j] * rs3 * cc;
           if constexpr (HAS_DSIN) {
-            float4 d0 = ld_f4(ds_in + off), d1 = ld_f4(ds_in + off + 4);
+            const float4 d0 = ld_f4(ds_in + off), d1 = ld_f4(ds_in + off + 4);
             o[0] += d0.x; o[1] += d0.y; o[2] += d0.z; o[3] += d0.w;
             o[4] += d1.x; o[5] += d1.y; o[6] += d1.z; o[7] += d1.w;
           }
@@ -187,21 +186,23 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
     __syncthreads();
   }
   for (int i = threadIdx.x; i < D; i += kThreads) dw_part[(int64_t)blockIdx.x * D + i] = sdw[i];
-  __threadfence();
+}
+
+// dw[j] (+)= sum_p part[p, j], fixed order over p: 32 columns x 8 row groups per CTA.
+__global__ void dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, int D, int accumulate) {
+  __shared__ float acc[8][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  float a = 0.f;
+  if (col < D)
+    for (int p = threadIdx.y; p < P; p += 8) a += part[(int64_t)p * D + col];
+  acc[threadIdx.y][threadIdx.x] = a;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned int prev = atomicAdd(ticket, 1u);
-    is_last = (prev == gridDim.x - 1);
+  if (threadIdx.y == 0 && col < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += acc[i][threadIdx.x];
+    dw[col] = accumulate ? dw[col] + t : t;
   }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int i = threadIdx.x; i < D; i += kThreads) {
-    float acc = 0.f;
-    for (int p = 0; p < (int)gridDim.x; ++p) acc += __ldcg(dw_part + (int64_t)p * D + i);
-    dw[i] = accumulate ? dw[i] + acc : acc;
-  }
-  if (threadIdx.x == 0) *ticket = 0u;  // re-arm for the next call
 }
 
 template <typename F>
@@ -240,15 +241,15 @@ cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, 
 int rmsnorm_bwd_partials(int64_t N, int D) {
   int tpr = D <= 1024 ? 32 : D <= 2048 ? 64 : D <= 4096 ? 128 : 256;
   const int rpc = kThreads / tpr;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc), 2 * sm_count()));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc * 4), 2 * sm_count()));
 }
 
 // ds = rmsnorm backward + ds_in (optional); ds16 (bf16 copy) optional; dw written or accumulated.
-// dw_part must hold rmsnorm_bwd_partials(N, D) x D floats; ticket is a zero-initialised word
-// the kernel re-arms itself.
+// dw_part must hold rmsnorm_bwd_partials(N, D) x D floats. `ticket` is unused (kept for ABI).
 cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, const float* rstd, const float* ds_in,
                         float* ds, void* ds16, float* dw_part, float* dw, unsigned* ticket, int64_t N, int D,
                         int accumulate, cudaStream_t st) {
+  (void)ticket;
   LLMT_REQUIRE(D % 8 == 0 && D <= 8192, "rmsnorm: width must be a multiple of 8 and at most 8192");
   if (N == 0) return cudaSuccess;
   const bf16* dy = static_cast<const bf16*>(dy_bf16);
@@ -257,14 +258,15 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
   const size_t smem = D * sizeof(float);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
-    auto launch = [&](auto kern) {
-      kern<<<grid, kThreads, smem, st>>>(dy, s, w, rstd, ds_in, ds, d16, dw_part, dw, ticket, N, D, accumulate);
-    };
+    auto launch = [&](auto kern) { kern<<<grid, kThreads, smem, st>>>(dy, s, w, rstd, ds_in, ds, d16, dw_part, N, D); };
     if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
     else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
     else if (d16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
     else launch(rmsnorm_bwd_kernel<TPR, false, false>);
   });
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dw_reduce_kernel<<<(unsigned)cdiv(D, 32), dim3(32, 8), 0, st>>>(dw_part, dw, grid, D, accumulate);
   return cudaGetLastError();
 }
 
