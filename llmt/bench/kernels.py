@@ -74,15 +74,17 @@ def gemm_shapes(cfg, tokens):
     ]
 
 
-def bench_gemm(cfg, tokens, rows):
+def bench_gemm(cfg, tokens, rows, only=None, reps=10):
     from llmt.ops import native as N
     peak, _ = peaks()
     for name, M, Nn, K, ta, tb in gemm_shapes(cfg, tokens):
+        if only and name not in only:
+            continue
         a = torch.randn((K, M) if ta else (M, K), device="cuda").bfloat16()
         b = torch.randn((Nn, K) if tb else (K, Nn), device="cuda").bfloat16()
         wgrad = ta
         out = torch.empty(M, Nn, device="cuda", dtype=torch.float32 if wgrad else torch.bfloat16)
-        ours = time_ms(lambda: N.gemm(a, b, ta=ta, tb=tb, out=out))
+        ours = time_ms(lambda: N.gemm(a, b, ta=ta, tb=tb, out=out), reps=reps)
         aa = a.t() if ta else a
         bb = b.t() if tb else b
         ref = time_ms(lambda: torch.matmul(aa, bb))  # cuBLAS, bf16 out
@@ -161,13 +163,15 @@ def main():
     p.add_argument("--seq", type=int, default=1024)
     p.add_argument("--ops", default="gemm,attn,mem")
     p.add_argument("--json", default=None)
+    p.add_argument("--only", default=None, help="comma list of GEMM names, e.g. 'head fwd,wo fwd'")
+    p.add_argument("--reps", type=int, default=10)
     args = p.parse_args()
     from llmt.config import get_config
     cfg = get_config(args.size)
     rows = []
     ops = args.ops.split(",")
     if "gemm" in ops:
-        bench_gemm(cfg, args.batch * args.seq, rows)
+        bench_gemm(cfg, args.batch * args.seq, rows, args.only.split(",") if args.only else None, args.reps)
     if "attn" in ops:
         bench_attn(cfg, args.batch, args.seq, rows)
     if "mem" in ops:
