@@ -41,4 +41,19 @@ inline bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt
   return r == CUDA_SUCCESS;
 }
 
+// 3D map: dims (inner, mid, outer) with pitches (ld_mid, ld_outer) in elements.
+inline bool make_tmap_3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                         uint64_t mid, uint64_t outer, uint64_t ld_mid, uint64_t ld_outer, uint32_t box_inner,
+                         uint32_t box_mid, uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  cuuint64_t dims[3] = {inner, mid, outer};
+  cuuint64_t strides[2] = {ld_mid * (uint64_t)elem_bytes, ld_outer * (uint64_t)elem_bytes};
+  cuuint32_t box[3] = {box_inner, box_mid, box_outer};
+  cuuint32_t estr[3] = {1, 1, 1};
+  auto fn = tmap_encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || strides[0] % 16 || strides[1] % 16) return false;
+  CUresult r = fn(m, dtype, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace llmt

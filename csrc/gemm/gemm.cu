@@ -1,6 +1,8 @@
 // Host entry of the tcgen05 GEMM: operand validation, TMA tensor maps, tile-width choice,
 // dispatch to the per-layout instantiations (gemm_kk.cu, gemm_km.cu, gemm_mm.cu), and the
 // per-row combine of the cross-entropy epilogue's partials.
+#include <string.h>
+
 #include "gemm_kernel.cuh"
 
 namespace llmt {
@@ -54,20 +56,39 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   g.k_blocks = (int)cdiv(K, kGemmBK);
   g.err = gemm_err_word();
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  alignas(64) CUtensorMap tmA;
-  alignas(64) CUtensorMap tmB;
-  bool ok = ta ? make_tmap_2d(&tmA, a, dt, 2, M, K, lda, 64, kGemmBK)
-               : make_tmap_2d(&tmA, a, dt, 2, K, M, lda, kGemmBK, kGemmBM);
+  alignas(64) GemmMaps mp;
+  memset(&mp, 0, sizeof(mp));
+  bool ok = ta ? make_tmap_2d(&mp.a, a, dt, 2, M, K, lda, 64, kGemmBK)
+               : make_tmap_2d(&mp.a, a, dt, 2, K, M, lda, kGemmBK, kGemmBM);
   if (tb) {
     const int rows = epi == EPI_SWIGLU ? 2 * N : N;
-    ok = ok && make_tmap_2d(&tmB, b, dt, 2, K, rows, ldb, kGemmBK, epi == EPI_SWIGLU ? BN / 2 : BN);
+    ok = ok && make_tmap_2d(&mp.b, b, dt, 2, K, rows, ldb, kGemmBK, epi == EPI_SWIGLU ? BN / 2 : BN);
   } else {
-    ok = ok && make_tmap_2d(&tmB, b, dt, 2, N, K, ldb, 64, kGemmBK);
+    ok = ok && make_tmap_2d(&mp.b, b, dt, 2, N, K, ldb, 64, kGemmBK);
   }
   LLMT_REQUIRE(ok, "gemm: cuTensorMapEncodeTiled rejected an operand");
-  if (!ta && tb) return gemm_launch_kk(BN, epi, tmA, tmB, g, st);
-  if (!ta && !tb) return gemm_launch_km(BN, epi, tmA, tmB, g, st);
-  return gemm_launch_mm(BN, epi, tmA, tmB, g, st);
+  // Epilogue output maps: 32x32 boxes, one per epilogue warp and chunk (see Stager).
+  switch (epi) {
+    case EPI_F32:
+      ok = make_tmap_2d(&mp.c, g.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, g.ldo, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+      break;
+    case EPI_BF16: case EPI_CE_BWD: case EPI_ROPE:
+      ok = make_tmap_2d(&mp.c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+      break;
+    case EPI_SWIGLU:
+      ok = make_tmap_2d(&mp.c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+           make_tmap_3d(&mp.c2, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+      break;
+    case EPI_SWIGLU_BWD:
+      ok = make_tmap_3d(&mp.c2, g.out2, dt, 2, N, 2, M, N, g.ldo2, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+      break;
+    default: break;
+  }
+  LLMT_REQUIRE(ok, "gemm: output tensor map rejected (pitch/alignment)");
+  if (!ta && tb) return gemm_launch_kk(BN, epi, mp, g, st);
+  if (!ta && !tb) return gemm_launch_km(BN, epi, mp, g, st);
+  return gemm_launch_mm(BN, epi, mp, g, st);
 }
 
 namespace {

@@ -36,14 +36,15 @@ namespace llmt {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
+constexpr int kEpiStageBytes = 4 * 2 * 4096;
 
 // Host launchers, one translation unit per operand layout (keeps the build parallel).
-cudaError_t gemm_launch_kk(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                           cudaStream_t st);  // fwd
-cudaError_t gemm_launch_km(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                           cudaStream_t st);  // dgrad
-cudaError_t gemm_launch_mm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                           cudaStream_t st);  // wgrad
+struct GemmMaps {
+  CUtensorMap a, b, c, c2;  // operands, main output, auxiliary output
+};
+cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // fwd
+cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // dgrad
+cudaError_t gemm_launch_mm(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // wgrad
 
 namespace gemm_detail {
 
@@ -51,13 +52,6 @@ using namespace sm100;
 
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
-
-__device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v, int col0, int N) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    if (col0 + q * 8 < N) *reinterpret_cast<BF16x8*>(dst + q * 8) = float_to_bf16x8(v + q * 8);
-  }
-}
 
 __device__ __forceinline__ void load_bf16x32(const bf16* src, float* v, int col0, int N) {
 #pragma unroll
@@ -71,8 +65,60 @@ __device__ __forceinline__ void load_bf16x32(const bf16* src, float* v, int col0
   }
 }
 
+// Per-warp output staging: each epilogue warp owns 32 accumulator rows and two 4 KB shared
+// buffers. A 32x32 chunk is written into a buffer in the TMA swizzle layout (64B swizzle for
+// bf16 rows of 64 B, 128B swizzle for fp32 rows of 128 B: conflict-free for the 32 row
+// writers) and leaves with one bulk-tensor store issued by lane 0. Out-of-range rows and
+// columns are clipped by the TMA unit, so the stores need no masks.
+struct Stager {
+  uint8_t* base;
+  int buf;
+  int lane;
+  __device__ __forceinline__ uint8_t* acquire() {
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    uint8_t* b = base + buf * 4096;
+    buf ^= 1;
+    return b;
+  }
+  __device__ __forceinline__ void put_bf16(uint8_t* b, const float* v) const {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      *reinterpret_cast<BF16x8*>(b + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = float_to_bf16x8(v + u * 8);
+  }
+  __device__ __forceinline__ void put_f32(uint8_t* b, const float* v) const {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      *reinterpret_cast<float4*>(b + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+  }
+  __device__ __forceinline__ void store2d(const CUtensorMap* tm, uint8_t* b, int x, int y, bool reduce = false) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (reduce) tma_reduce_add_2d(tm, b, x, y);
+      else tma_store_2d(tm, b, x, y);
+      bulk_commit();
+    }
+  }
+  __device__ __forceinline__ void store3d(const CUtensorMap* tm, uint8_t* b, int x, int y, int z) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tm, b, x, y, z);
+      bulk_commit();
+    }
+  }
+  __device__ __forceinline__ void drain() {
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+};
+
+// row: this thread's accumulator row; wrow: the warp's first row (TMA box origin).
 template <int EPI, int BN>
-__device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, const GemmArgs& a) {
+__device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow, int nb, const GemmArgs& a,
+                                              const CUtensorMap* tmC, const CUtensorMap* tmC2, Stager& st) {
   const bool rv = row < a.M;
   if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_CE_BWD) {
     float l = 0.f, scale = 0.f;
@@ -86,48 +132,37 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
     }
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= a.N) break;  // uniform across the warp
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();
-      const int col0 = nb * BN + c * 32;
-      if (!rv || col0 >= a.N) continue;
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
-      if constexpr (EPI == EPI_BF16) {
-        store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, v, col0, a.N);
-      } else if constexpr (EPI == EPI_CE_BWD) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = (__expf(v[j] - l) - ((int64_t)(col0 + j) == t ? 1.f : 0.f)) * scale;
-        store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, v, col0, a.N);
+      uint8_t* b = st.acquire();
+      if constexpr (EPI == EPI_F32) {
+        st.put_f32(b, v);
+        st.store2d(tmC, b, col0, wrow, a.accumulate != 0);
       } else {
-        float* o = reinterpret_cast<float*>(a.out) + (int64_t)row * a.ldo + col0;
+        if constexpr (EPI == EPI_CE_BWD) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (col0 + q * 4 < a.N) {
-            float4 x = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            if (a.accumulate) {
-              const float4 y = *reinterpret_cast<const float4*>(o + 4 * q);
-              x.x += y.x;
-              x.y += y.y;
-              x.z += y.z;
-              x.w += y.w;
-            }
-            *reinterpret_cast<float4*>(o + 4 * q) = x;
-          }
+          for (int j = 0; j < 32; ++j) v[j] = (__expf(v[j] - l) - ((int64_t)(col0 + j) == t ? 1.f : 0.f)) * scale;
         }
+        st.put_bf16(b, v);
+        st.store2d(tmC, b, col0, wrow);
       }
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     const int F = a.split;
 #pragma unroll 1
     for (int c = 0; c < BN / 64; ++c) {
+      const int col0 = nb * (BN / 2) + c * 32;
+      if (col0 >= F) break;
       uint32_t rg[32], ru[32];
       tmem_ld32(taddr + c * 32, rg);
       tmem_ld32(taddr + BN / 2 + c * 32, ru);
       tmem_wait_ld();
-      const int col0 = nb * (BN / 2) + c * 32;
-      if (!rv || col0 >= F) continue;
       float g[32], u[32], h[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -135,24 +170,34 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
         u[j] = u2f(ru[j]);
         h[j] = g[j] * sigm(g[j]) * u[j];
       }
-      store_bf16x32(reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo + col0, h, col0, F);
-      bf16* gu = reinterpret_cast<bf16*>(const_cast<void*>(a.aux)) + (int64_t)row * a.ld_aux;
-      store_bf16x32(gu + col0, g, col0, F);
-      store_bf16x32(gu + F + col0, u, col0, F);
+      uint8_t* b = st.acquire();
+      st.put_bf16(b, h);
+      st.store2d(tmC, b, col0, wrow);
+      b = st.acquire();
+      st.put_bf16(b, g);
+      st.store3d(tmC2, b, col0, 0, wrow);
+      b = st.acquire();
+      st.put_bf16(b, u);
+      st.store3d(tmC2, b, col0, 1, wrow);
     }
   } else if constexpr (EPI == EPI_SWIGLU_BWD) {
     const int F = a.split;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= a.N) break;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
-      tmem_wait_ld();
-      const int col0 = nb * BN + c * 32;
-      if (!rv || col0 >= a.N) continue;
-      const bf16* gu = reinterpret_cast<const bf16*>(a.aux) + (int64_t)row * a.ld_aux;
       float g[32], u[32], dg[32], du[32];
-      load_bf16x32(gu + col0, g, col0, F);
-      load_bf16x32(gu + F + col0, u, col0, F);
+      if (rv) {
+        const bf16* gu = reinterpret_cast<const bf16*>(a.aux) + (int64_t)row * a.ld_aux;
+        load_bf16x32(gu + col0, g, col0, F);
+        load_bf16x32(gu + F + col0, u, col0, F);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) g[j] = u[j] = 0.f;
+      }
+      tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float d = u2f(r[j]);
@@ -160,9 +205,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
         dg[j] = d * u[j] * sg * (1.f + g[j] * (1.f - sg));
         du[j] = d * g[j] * sg;
       }
-      bf16* o = reinterpret_cast<bf16*>(a.out2) + (int64_t)row * a.ldo2;
-      store_bf16x32(o + col0, dg, col0, F);
-      store_bf16x32(o + F + col0, du, col0, F);
+      uint8_t* b = st.acquire();
+      st.put_bf16(b, dg);
+      st.store3d(tmC2, b, col0, 0, wrow);
+      b = st.acquire();
+      st.put_bf16(b, du);
+      st.store3d(tmC2, b, col0, 1, wrow);
     }
   } else if constexpr (EPI == EPI_ROPE) {
     const int hd = a.hd, half = hd / 2;
@@ -174,12 +222,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
 #pragma unroll 1
       for (int j = 0; j < half / 32; ++j) {
         const int c1 = hl * hd + j * 32;
+        const int col1 = nb * BN + c1;
+        if (col1 >= a.N) break;
         uint32_t r1[32], r2[32];
         tmem_ld32(taddr + c1, r1);
         tmem_ld32(taddr + c1 + half, r2);
         tmem_wait_ld();
-        const int col1 = nb * BN + c1;
-        if (!rv || col1 >= a.N) continue;
         float x1[32], x2[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -197,9 +245,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
             x2[e] = y2;
           }
         }
-        bf16* o = reinterpret_cast<bf16*>(a.out) + (int64_t)row * a.ldo;
-        store_bf16x32(o + col1, x1, col1, a.N);
-        store_bf16x32(o + col1 + half, x2, col1 + half, a.N);
+        uint8_t* b = st.acquire();
+        st.put_bf16(b, x1);
+        st.store2d(tmC, b, col1, wrow);
+        b = st.acquire();
+        st.put_bf16(b, x2);
+        st.store2d(tmC, b, col1 + half, wrow);
       }
     }
   } else if constexpr (EPI == EPI_CE_FWD) {
@@ -208,10 +259,11 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
     bool has_t = false;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= a.N) break;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();
-      const int col0 = nb * BN + c * 32;
       float cm = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -222,7 +274,6 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
           has_t = true;
         }
       }
-      if (cm == -INFINITY) continue;
       float cs = 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
@@ -242,7 +293,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int nb, c
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
   constexpr int BM = kGemmBM, BK = kGemmBK;
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -250,7 +302,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   constexpr int TMEM_COLS = 2 * BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* stage_out = smem + STAGES * STAGE_BYTES;  // 4 warps x 2 x 4 KB epilogue staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -360,6 +413,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    Stager st{stage_out + (warp - 2) * 8192, 0, lane};
     int buf = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -367,12 +421,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<EPI, BN>(taddr, mb * BM + row_in_tile, nb, args);
+      epilogue_tile<EPI, BN>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
       tc_fence_before();
       bar_arrive(&tempty[buf]);
       buf ^= 1;
       if (buf == 0) aphase ^= 1;
     }
+    st.drain();
   }
   tc_fence_before();
   __syncthreads();
@@ -383,9 +438,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
-cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t st) {
+cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
-  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + 1024 + 256;
+  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + kEpiStageBytes + 1024 + 256;
+  static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -394,7 +450,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
   }
   const int tiles = args.m_blocks * args.n_blocks;
   const int grid = std::min(tiles, sm_count());
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, args);
+  kern<<<grid, kGemmThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();
 }
 

@@ -6,21 +6,20 @@ namespace llmt {
 using namespace gemm_detail;
 
 template <int BN>
-static cudaError_t run_kk(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
+static cudaError_t run_kk(int epi, const GemmMaps& mp, const GemmArgs& g, cudaStream_t st) {
   constexpr int S = stages_for<BN>();
   switch (epi) {
-    case EPI_BF16: return launch<BN, S, false, false, EPI_BF16>(ta, tb, g, st);
-    case EPI_F32: return launch<BN, S, false, false, EPI_F32>(ta, tb, g, st);
-    case EPI_SWIGLU: return launch<BN, S, false, false, EPI_SWIGLU>(ta, tb, g, st);
-    case EPI_ROPE: return launch<BN, S, false, false, EPI_ROPE>(ta, tb, g, st);
-    case EPI_CE_FWD: return launch<BN, S, false, false, EPI_CE_FWD>(ta, tb, g, st);
-    case EPI_CE_BWD: return launch<BN, S, false, false, EPI_CE_BWD>(ta, tb, g, st);
+    case EPI_BF16: return launch<BN, S, false, false, EPI_BF16>(mp, g, st);
+    case EPI_F32: return launch<BN, S, false, false, EPI_F32>(mp, g, st);
+    case EPI_SWIGLU: return launch<BN, S, false, false, EPI_SWIGLU>(mp, g, st);
+    case EPI_ROPE: return launch<BN, S, false, false, EPI_ROPE>(mp, g, st);
+    case EPI_CE_FWD: return launch<BN, S, false, false, EPI_CE_FWD>(mp, g, st);
+    case EPI_CE_BWD: return launch<BN, S, false, false, EPI_CE_BWD>(mp, g, st);
     default: set_last_error("gemm: epilogue not built for the x W^T layout"); return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t gemm_launch_kk(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                           cudaStream_t st) {
-  return bn == 256 ? run_kk<256>(epi, ta, tb, g, st) : run_kk<128>(epi, ta, tb, g, st);
+cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& mp, const GemmArgs& g, cudaStream_t st) {
+  return bn == 256 ? run_kk<256>(epi, mp, g, st) : run_kk<128>(epi, mp, g, st);
 }
 }  // namespace llmt

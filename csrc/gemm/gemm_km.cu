@@ -6,18 +6,17 @@ namespace llmt {
 using namespace gemm_detail;
 
 template <int BN>
-static cudaError_t run_km(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
+static cudaError_t run_km(int epi, const GemmMaps& mp, const GemmArgs& g, cudaStream_t st) {
   constexpr int S = stages_for<BN>();
   switch (epi) {
-    case EPI_BF16: return launch<BN, S, false, true, EPI_BF16>(ta, tb, g, st);
-    case EPI_F32: return launch<BN, S, false, true, EPI_F32>(ta, tb, g, st);
-    case EPI_SWIGLU_BWD: return launch<BN, S, false, true, EPI_SWIGLU_BWD>(ta, tb, g, st);
+    case EPI_BF16: return launch<BN, S, false, true, EPI_BF16>(mp, g, st);
+    case EPI_F32: return launch<BN, S, false, true, EPI_F32>(mp, g, st);
+    case EPI_SWIGLU_BWD: return launch<BN, S, false, true, EPI_SWIGLU_BWD>(mp, g, st);
     default: set_last_error("gemm: epilogue not built for the dy W layout"); return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t gemm_launch_km(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
-                           cudaStream_t st) {
-  return bn == 256 ? run_km<256>(epi, ta, tb, g, st) : run_km<128>(epi, ta, tb, g, st);
+cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& mp, const GemmArgs& g, cudaStream_t st) {
+  return bn == 256 ? run_km<256>(epi, mp, g, st) : run_km<128>(epi, mp, g, st);
 }
 }  // namespace llmt
