@@ -7,14 +7,16 @@
 // and in the same pass writes the bf16 shadow copy that the GEMMs read, so no separate
 // weight cast kernel runs per step (the autocast casts of the reference, roofline.py:164).
 // The step count t and lr live on the device so a captured CUDA graph replays correctly.
-// grad_scale multiplies g first (DP averaging / loss scaling folded in).
+// grad_scale multiplies g first (DP averaging / loss scaling folded in). With zero_grad the
+// kernel also clears g after reading it, so every gradient producer of the next step can
+// accumulate (TMA reduce-add, split-K) without a separate zeroing pass.
 #include "../common/common.cuh"
 
 namespace llmt {
 namespace {
 
-template <bool WRITE_BF16>
-__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+template <bool WRITE_BF16, bool ZERO_GRAD>
+__global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, bf16* __restrict__ p16, int64_t n, const float* __restrict__ lr_ptr,
                              const int* __restrict__ step_ptr, AdamHyper a) {
   const float lr = *lr_ptr;
@@ -40,6 +42,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
       pe[j] = pe[j] * decay - step_size * me[j] / denom;
     }
     st_f4(p + 4 * i, pp);
+    if (ZERO_GRAD) st_f4(g + 4 * i, make_float4(0.f, 0.f, 0.f, 0.f));
     st_f4(m + 4 * i, mm);
     st_f4(v + 4 * i, vv);
     if (WRITE_BF16) {
@@ -59,6 +62,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
     m[i] = mj;
     v[i] = vj;
     p[i] = pj;
+    if (ZERO_GRAD) g[i] = 0.f;
     if (WRITE_BF16) p16[i] = __float2bfloat16_rn(pj);
   }
 }
@@ -70,15 +74,19 @@ __global__ void cast_bf16_kernel(const float* __restrict__ x, bf16* __restrict__
 
 }  // namespace
 
-cudaError_t adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
-                       const int* step, AdamHyper h, cudaStream_t st) {
+// zero_grad: also reset g to 0 after reading it (the next step's gradients accumulate into it).
+cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
+                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   LLMT_REQUIRE(((uintptr_t)p | (uintptr_t)g | (uintptr_t)m | (uintptr_t)v) % 16 == 0,
                "adamw: fp32 buffers must be 16-byte aligned");
   LLMT_REQUIRE(p16 == nullptr || (uintptr_t)p16 % 8 == 0, "adamw: bf16 copy must be 8-byte aligned");
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4 + 1, 256), sm_count() * 8));
-  if (p16) adamw_kernel<true><<<grid, 256, 0, st>>>(p, g, m, v, static_cast<bf16*>(p16), n, lr, step, h);
-  else adamw_kernel<false><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
+  bf16* q = static_cast<bf16*>(p16);
+  if (p16 && zero_grad) adamw_kernel<true, true><<<grid, 256, 0, st>>>(p, g, m, v, q, n, lr, step, h);
+  else if (p16) adamw_kernel<true, false><<<grid, 256, 0, st>>>(p, g, m, v, q, n, lr, step, h);
+  else if (zero_grad) adamw_kernel<false, true><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
+  else adamw_kernel<false, false><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
   return cudaGetLastError();
 }
 

@@ -39,8 +39,8 @@ cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_
 struct AdamHyper {
   float b1, b2, eps, wd, grad_scale;
 };
-cudaError_t adamw_step(float* p, const float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
-                       const int* step, AdamHyper h, cudaStream_t st);
+cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
+                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st);
 cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st);
 
 // ---------------------------------------------------------------- cross entropy rows
@@ -57,6 +57,7 @@ enum EpiKind : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD =
 struct GemmArgs {
   int M, N, K;
   int m_blocks, n_blocks, k_blocks;
+  int splits, k_per_split;  // split-K (fp32 reduce-add output only)
   void* out;
   int64_t ldo;
   int accumulate;
@@ -79,10 +80,12 @@ struct GemmArgs {
 
 // out = op(a) @ op(b); a: (ta ? K x M : M x K) row pitch lda, b: (tb ? N x K : K x N) row pitch ldb.
 // The epilogue fields of `g` (out, ldo, accumulate, split, aux, ...) are set by the caller;
-// M/N/K, block counts and err are filled in here. bn = 0 picks the tile width.
+// M/N/K, block counts, split-K and err are filled in here. bn = 0 picks the tile width; an
+// fp32 output with accumulate=1 (TMA reduce-add) may also be split along K to fill the SMs.
 cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
                  int epi, int bn, GemmArgs g, cudaStream_t st);
 int gemm_pick_bn(int M, int N, int epi);
+void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* splits);
 int gemm_error_code(bool reset);
 
 // ---------------------------------------------------------------- attention

@@ -136,7 +136,7 @@ void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW) {
 
 // ---------------------------------------------------------------- optimizer
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16, at::Tensor lr,
-                at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale) {
+                at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale, bool zero_grad) {
   for (auto* t : {&p, &g, &m, &v}) {
     CHECK_DT((*t), at::kFloat);
     CHECK(t->is_contiguous() && t->numel() == p.numel(), "adamw buffers must be contiguous and equal-sized");
@@ -151,7 +151,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
   }
   llmt::AdamHyper h{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
   ok(llmt::adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p16p,
-                      p.numel(), lr.data_ptr<float>(), step.data_ptr<int>(), h, stream()),
+                      p.numel(), lr.data_ptr<float>(), step.data_ptr<int>(), h, zero_grad, stream()),
      "adamw_step");
 }
 
@@ -314,7 +314,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_inplace", &rope_inplace);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
-  m.def("adamw_step", &adamw_step);
+  m.def("adamw_step", &adamw_step, "p"_a, "g"_a, "m"_a, "v"_a, "p16"_a, "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a,
+        "wd"_a, "grad_scale"_a, "zero_grad"_a = false);
   m.def("cast_bf16", &cast_bf16);
   m.def("ce_fwd_rows", &ce_fwd_rows);
   m.def("ce_bwd_rows", &ce_bwd_rows);

@@ -29,6 +29,32 @@ int gemm_pick_bn(int M, int N, int epi) {
   return t256 <= t128 ? 256 : 128;
 }
 
+// Tile width and split-K from a wave model: cost = waves x (k-blocks per unit + fixed
+// per-unit overhead) x tile width; splits only when the output is an fp32 reduce-add.
+void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* splits) {
+  const int sms = sm_count();
+  const int64_t mb = cdiv(M, kGemmBM), kb = cdiv(K, kGemmBK);
+  double best = 1e30;
+  *bn = gemm_pick_bn(M, N, epi);
+  *splits = 1;
+  for (int BN : {128, 256}) {
+    if (epi == EPI_SWIGLU || epi == EPI_ROPE) BN = *bn;
+    const int64_t tiles = mb * cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
+    const int smax = can_split ? (int)std::min<int64_t>(16, std::max<int64_t>(1, kb / 4)) : 1;
+    for (int s = 1; s <= smax; ++s) {
+      const int64_t kps = cdiv(kb, s);
+      const int64_t units = tiles * cdiv(kb, kps);
+      const double cost = (double)cdiv(units, sms) * (double)(kps + 3) * (BN / 128.0);
+      if (cost < best - 1e-9) {
+        best = cost;
+        *bn = BN;
+        *splits = (int)cdiv(kb, kps);
+      }
+    }
+    if (epi == EPI_SWIGLU || epi == EPI_ROPE) break;
+  }
+}
+
 int gemm_error_code(bool reset) {
   int v = 0;
   cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(int));
@@ -45,7 +71,8 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   LLMT_REQUIRE(M > 0 && N > 0 && K > 0, "gemm: empty problem");
   LLMT_REQUIRE(N % 8 == 0, "gemm: N must be a multiple of 8");
   LLMT_REQUIRE(tma_ok(a, lda, 2) && tma_ok(b, ldb, 2), "gemm: operands need 16-byte aligned bases and row pitches");
-  const int BN = bn ? bn : gemm_pick_bn(M, N, epi);
+  int BN = bn, splits = 1;
+  if (!BN) gemm_plan(M, N, K, epi, epi == EPI_F32 && g.accumulate, &BN, &splits);
   LLMT_REQUIRE(BN == 128 || BN == 256, "gemm: BN must be 128 or 256");
   if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm: bad RoPE epilogue shape");
   g.M = M;
@@ -54,6 +81,8 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   g.m_blocks = (int)cdiv(M, kGemmBM);
   g.n_blocks = (int)cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
   g.k_blocks = (int)cdiv(K, kGemmBK);
+  g.k_per_split = (int)cdiv(g.k_blocks, splits);
+  g.splits = (int)cdiv(g.k_blocks, g.k_per_split);
   g.err = gemm_err_word();
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   alignas(64) GemmMaps mp;

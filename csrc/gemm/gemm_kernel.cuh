@@ -331,7 +331,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_tiles = args.m_blocks * args.n_blocks;
+  const int mn_tiles = args.m_blocks * args.n_blocks;
+  const int num_tiles = mn_tiles * args.splits;
+  const int kpb = args.k_per_split;  // k-blocks per split (splits > 1 only with reduce-add output)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -339,8 +341,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % args.m_blocks, nb = tile / args.m_blocks;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        const int rest = tile % mn_tiles, ks = tile / mn_tiles;
+        const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
+        const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
+        for (int kb = k_lo; kb < k_hi; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, err, 1)) {
             ok = false;
             break;
@@ -380,10 +384,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       uint32_t phase = 0, aphase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int ks = tile / mn_tiles;
+        const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
         if (!wait_bar(&tempty[buf], aphase ^ 1, err, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = k_lo; kb < k_hi; ++kb) {
           if (!wait_bar(&full[stage], phase, err, 3)) {
             ok = false;
             break;
@@ -396,7 +402,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 A_MN ? make_sw128_desc(sa + k * 2048, 8192, 1024) : make_sw128_desc(sa + k * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sw128_desc(sb + k * 2048, 8192, 1024) : make_sw128_desc(sb + k * 32, 16, 1024);
-            mma_f16(d, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_f16(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -417,7 +423,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     int buf = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mb = tile % args.m_blocks, nb = tile / args.m_blocks;
+      const int rest = tile % mn_tiles;
+      const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
@@ -448,7 +455,7 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = args.m_blocks * args.n_blocks;
+  const int tiles = args.m_blocks * args.n_blocks * args.splits;
   const int grid = std::min(tiles, sm_count());
   kern<<<grid, kGemmThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();

@@ -1,10 +1,11 @@
 """Autograd Functions of the native training path.
 
 Each Function covers one fused region of the step and calls only sm_100a kernels of
-llmt._C. Weight gradients never go through autograd: every backward writes its fp32 weight
-gradient straight into the parameter's `main_grad` view of the flat gradient buffer
-(overwrite on the first micro-batch, accumulate afterwards; see GradFlags), so the
-optimizer and the data-parallel reduce-scatter read one contiguous buffer.
+llmt._C. Weight gradients never go through autograd: every backward accumulates its fp32
+weight gradient straight into the parameter's `main_grad` view of the flat gradient buffer
+(TMA reduce-add in the GEMM epilogue, so split-K and micro-batch accumulation are free), and
+the fused optimizer zeroes the buffer after consuming it. The optimizer and the
+data-parallel reduce-scatter read one contiguous buffer.
 
 Regions (reference equivalents in bench_train.py / kernels/triton_ops.py):
   Embed          emb(idx)                                        bench_train.py:213
@@ -22,26 +23,6 @@ import torch
 from llmt.ops import native as N
 
 
-class GradFlags:
-    """Tracks which parameters already hold a gradient in this step (write vs accumulate)."""
-
-    def __init__(self):
-        self._written: set[int] = set()
-
-    def reset(self):
-        self._written.clear()
-
-    def accumulate(self, p) -> bool:
-        """True if p's main_grad already holds this step's gradient; marks it as written."""
-        key = id(p)
-        acc = key in self._written
-        self._written.add(key)
-        return acc
-
-
-FLAGS = GradFlags()
-
-
 class Embed(torch.autograd.Function):
     @staticmethod
     def forward(ctx, idx, w):
@@ -52,10 +33,7 @@ class Embed(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dx):
         (idx,) = ctx.saved_tensors
-        w = ctx.w
-        if not FLAGS.accumulate(w):
-            w.main_grad.zero_()
-        N.embedding_bwd(idx, dx.contiguous(), w.main_grad)
+        N.embedding_bwd(idx, dx.contiguous(), ctx.w.main_grad)
         return None, None
 
 
@@ -73,7 +51,7 @@ class RMSNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         x, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, _ = N.rmsnorm_bwd(dy.contiguous(), x, w, rstd, None, w.main_grad, FLAGS.accumulate(w), write_ds16=False)
+        ds, _ = N.rmsnorm_bwd(dy.contiguous(), x, w, rstd, None, w.main_grad, True, write_ds16=False)
         return ds, None, None
 
 
@@ -91,7 +69,7 @@ class AddRMSNormFn(torch.autograd.Function):
     def backward(ctx, dy, ds_in):
         s, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, ds_in, w.main_grad, FLAGS.accumulate(w), write_ds16=True)
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, ds_in, w.main_grad, True, write_ds16=True)
         return ds16, ds, None, None
 
 
@@ -109,13 +87,13 @@ class FinalNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         s, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, None, w.main_grad, FLAGS.accumulate(w), write_ds16=True)
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, None, w.main_grad, True, write_ds16=True)
         return ds16, ds, None, None
 
 
 def _wgrad(dy, x, p):
     """p.main_grad (out, in) (+)= dy^T x, fp32, on the tcgen05 GEMM."""
-    N.gemm(dy, x, ta=True, tb=False, out=p.main_grad, accumulate=FLAGS.accumulate(p))
+    N.gemm(dy, x, ta=True, tb=False, out=p.main_grad, accumulate=True)
 
 
 class QKVAttention(torch.autograd.Function):
@@ -179,9 +157,7 @@ class SwiGLUMLP(torch.autograd.Function):
         dgu = N.gemm_swiglu_bwd(dm, w2.w16, gu, ffn)
         _wgrad(dm, h, w2)
         dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
-        acc = FLAGS.accumulate(w1)
-        FLAGS.accumulate(w1.w3_param)
-        N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=acc)
+        N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=True)
         return dx, None, None, None
 
 
@@ -203,11 +179,10 @@ class HeadCE(torch.autograd.Function):
         n = h.shape[0]
         g = g.reshape(1).float().contiguous()
         dh = torch.empty_like(h)
-        acc = FLAGS.accumulate(w)
-        for i, c0 in enumerate(range(0, n, chunk)):
+        for c0 in range(0, n, chunk):
             c1 = min(n, c0 + chunk)
             hc = h[c0:c1]
             dl = N.gemm_ce_bwd(hc, w.w16, targets[c0:c1], lse[c0:c1], g, 1.0 / n)
             N.gemm(dl, w.w16, ta=False, tb=False, out=dh[c0:c1])
-            N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=acc or i > 0)
+            N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=True)
         return dh, None, None, None

@@ -215,8 +215,9 @@ def embedding_bwd(idx, dx, dW):
     ext().embedding_bwd(idx.reshape(-1), dx, dW)
 
 
-def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0):
-    ext().adamw_step(p, g, m, v, p16, lr, step, float(b1), float(b2), float(eps), float(wd), float(grad_scale))
+def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0, zero_grad=False):
+    ext().adamw_step(p, g, m, v, p16, lr, step, float(b1), float(b2), float(eps), float(wd), float(grad_scale),
+                     bool(zero_grad))
 
 
 def cast_bf16(x, y):

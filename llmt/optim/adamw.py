@@ -2,8 +2,9 @@
 
 Same hyper-parameters and update as the reference's torch.optim.AdamW (bench_train.py:467-469:
 lr 3e-4, betas (0.9, 0.95), weight decay 0.1 on every parameter, eps 1e-8). The kernel
-also writes the bf16 shadow weights that the GEMMs read. lr and the step count live on
-the device, so `step()` can be captured in a CUDA graph and replayed.
+also writes the bf16 shadow weights that the GEMMs read and zeroes the gradient buffer for
+the next step's accumulation. lr and the step count live on the device, so `step()` can be
+captured in a CUDA graph and replayed.
 
 State layout: exp_avg / exp_avg_sq flat fp32 buffers; `state_dict()` returns them per
 parameter under torch.optim.AdamW's keys (exp_avg, exp_avg_sq, step) so checkpoints keep the
@@ -37,7 +38,7 @@ class FusedAdamW:
     def step(self):
         self.step_t.add_(1)
         N.adamw_step(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.shadow, self.lr_t, self.step_t,
-                     self.betas[0], self.betas[1], self.eps, self.weight_decay, self.grad_scale)
+                     self.betas[0], self.betas[1], self.eps, self.weight_decay, self.grad_scale, zero_grad=True)
 
     def state_dict(self, flat=None):
         """torch.optim.AdamW-style state: {'state': {i: {step, exp_avg, exp_avg_sq}}, 'param_groups': [...]}."""

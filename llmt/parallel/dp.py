@@ -80,6 +80,7 @@ class DataParallel:
             self.fused.step()
             return
         dist.reduce_scatter_tensor(opt.grad_shard, f.grad, op=dist.ReduceOp.SUM, group=self.group)
+        f.grad.zero_()  # gradients accumulate into the flat buffer
         opt.step_local()
         dist.all_gather_into_tensor(f.shadow, f.shadow[opt.lo:opt.hi].clone(), group=self.group)
 

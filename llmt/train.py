@@ -19,7 +19,6 @@ import torch
 from llmt.config import ModelConfig
 from llmt.models.llama import build_model
 from llmt.models.native import NativeLlama
-from llmt.ops import functions as Fn
 from llmt.optim.adamw import FusedAdamW
 
 
@@ -51,7 +50,6 @@ class Trainer:
     # ------------------------------------------------------------------ step body
     def _body(self):
         self.body_calls += 1
-        Fn.FLAGS.reset()
         total = None
         for i in range(self.microbatches):
             loss = self.net(self.idx[i], self.tgt[i])

@@ -19,7 +19,6 @@ def _pair(cfg, T, seed=0):
 def test_native_loss_and_grads_match_fp32(overrides):
     from llmt.config import get_config
     from llmt.models.llama import make_batch
-    from llmt.ops import functions as Fn
     from llmt.ops import native
     cfg = get_config("tiny256", **overrides)
     B, T = 2, 128
@@ -27,7 +26,6 @@ def test_native_loss_and_grads_match_fp32(overrides):
     idx, tgt = make_batch(B, T, cfg.vocab, "cuda")
     loss_ref = ref(idx, tgt)
     loss_ref.backward()
-    Fn.FLAGS.reset()
     loss = net(idx, tgt)
     loss.backward()
     torch.cuda.synchronize()
