@@ -83,7 +83,7 @@ struct GemmArgs {
 // M/N/K, block counts, split-K and err are filled in here. bn = 0 picks the tile width; an
 // fp32 output with accumulate=1 (TMA reduce-add) may also be split along K to fill the SMs.
 cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
-                 int epi, int bn, GemmArgs g, cudaStream_t st);
+                 int epi, int bn, GemmArgs g, cudaStream_t st, int splits = 0);
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* splits);
 int gemm_error_code(bool reset);

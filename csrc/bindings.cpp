@@ -194,7 +194,7 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
           c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split, c10::optional<at::Tensor> cos_t,
           c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols, c10::optional<at::Tensor> tgt,
           c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
-          c10::optional<at::Tensor> tlogit, double alpha, int64_t bn) {
+          c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits) {
   cuda2d(a, "a");
   cuda2d(b, "b");
   CHECK_DT(a, at::kBFloat16);
@@ -258,7 +258,8 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
     CHECK(part->numel() >= (int64_t)M * ((N + BN - 1) / BN) * 2, "CE_FWD partial buffer too small");
   }
   if (epi == llmt::EPI_CE_BWD) CHECK(g.tgt && g.lse, "CE_BWD gemm args");
-  ok(llmt::gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), ta, tb, M, N, K, (int)epi, (int)bn, g, stream()),
+  ok(llmt::gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), ta, tb, M, N, K, (int)epi, (int)bn, g, stream(),
+                (int)splits),
      "gemm");
 }
 
@@ -323,7 +324,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "a"_a, "b"_a, "ta"_a, "tb"_a, "epi"_a, "out"_a, "accumulate"_a = false, "aux"_a = py::none(),
         "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
         "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
-        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0);
+        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);

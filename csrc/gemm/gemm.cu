@@ -44,7 +44,8 @@ void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* split
     for (int s = 1; s <= smax; ++s) {
       const int64_t kps = cdiv(kb, s);
       const int64_t units = tiles * cdiv(kb, kps);
-      const double cost = (double)cdiv(units, sms) * (double)(kps + 3) * (BN / 128.0);
+      // BN=128 tiles reach ~70% of the BN=256 per-FLOP rate (operand smem bandwidth)
+      const double cost = (double)cdiv(units, sms) * (double)(kps + 3) * (BN == 256 ? 2.0 : 1.45) * (s > 1 ? 1.15 : 1.0);
       if (cost < best - 1e-9) {
         best = cost;
         *bn = BN;
@@ -66,13 +67,18 @@ int gemm_error_code(bool reset) {
 }
 
 cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
-                 int epi, int bn, GemmArgs g, cudaStream_t st) {
+                 int epi, int bn, GemmArgs g, cudaStream_t st, int force_splits) {
   LLMT_REQUIRE(!(ta && tb), "gemm: a^T b^T is not a supported layout");
   LLMT_REQUIRE(M > 0 && N > 0 && K > 0, "gemm: empty problem");
   LLMT_REQUIRE(N % 8 == 0, "gemm: N must be a multiple of 8");
   LLMT_REQUIRE(tma_ok(a, lda, 2) && tma_ok(b, ldb, 2), "gemm: operands need 16-byte aligned bases and row pitches");
   int BN = bn, splits = 1;
-  if (!BN) gemm_plan(M, N, K, epi, epi == EPI_F32 && g.accumulate, &BN, &splits);
+  const bool can_split = epi == EPI_F32 && g.accumulate;
+  if (!BN) gemm_plan(M, N, K, epi, can_split, &BN, &splits);
+  if (force_splits > 0) {
+    LLMT_REQUIRE(force_splits == 1 || can_split, "gemm: split-K needs an fp32 reduce-add output");
+    splits = force_splits;
+  }
   LLMT_REQUIRE(BN == 128 || BN == 256, "gemm: BN must be 128 or 256");
   if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm: bad RoPE epilogue shape");
   g.M = M;

@@ -156,6 +156,25 @@ def bench_memory_ops(cfg, tokens, rows):
     _bw_row(rows, "adamw (+bf16 copy)", f"{n}", ms, time_ms(opt.step), n * (16 + 12 + 2))
 
 
+def sweep_gemm(cfg, tokens, names):
+    """Tile width x split-K sweep for the named GEMM shapes (wgrad shapes accumulate in fp32)."""
+    from llmt.ops import native as N
+    for name, M, Nn, K, ta, tb in gemm_shapes(cfg, tokens):
+        if name not in names:
+            continue
+        a = torch.randn((K, M) if ta else (M, K), device="cuda").bfloat16()
+        b = torch.randn((Nn, K) if tb else (K, Nn), device="cuda").bfloat16()
+        out = torch.zeros(M, Nn, device="cuda", dtype=torch.float32 if ta else torch.bfloat16)
+        fl = 2.0 * M * Nn * K
+        res = []
+        for bn in (128, 256):
+            for sp in ((1, 2, 3, 4, 6, 8) if ta else (1,)):
+                ms = time_ms(lambda: N.gemm(a, b, ta=ta, tb=tb, out=out, accumulate=ta, bn=bn, splits=sp), reps=5)
+                res.append(f"bn{bn}/s{sp}:{fl / ms / 1e9:.0f}")
+        auto = time_ms(lambda: N.gemm(a, b, ta=ta, tb=tb, out=out, accumulate=ta), reps=5)
+        print(f"{name:12s} {M}x{Nn}x{K} auto {fl / auto / 1e9:.0f} TF/s | " + " ".join(res), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--size", default="medium")
@@ -170,6 +189,8 @@ def main():
     cfg = get_config(args.size)
     rows = []
     ops = args.ops.split(",")
+    if "sweep" in ops:
+        sweep_gemm(cfg, args.batch * args.seq, args.only.split(",") if args.only else [n for n, *_ in gemm_shapes(cfg, 1)])
     if "gemm" in ops:
         bench_gemm(cfg, args.batch * args.seq, rows, args.only.split(",") if args.only else None, args.reps)
     if "attn" in ops:

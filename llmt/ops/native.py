@@ -106,7 +106,7 @@ def rmsnorm_bwd(dy, s, w, rstd, ds_in, dw, accumulate, write_ds16=True):
 
 
 # ---------------------------------------------------------------- GEMM
-def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate=False, bn=0):
+def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate=False, bn=0, splits=0):
     """out = op(a) @ op(b) on the tcgen05 GEMM (bf16 operands, fp32 accumulation).
 
     ta=False, tb=True  : forward   y  = x  @ W^T
@@ -121,7 +121,7 @@ def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
-    ext().gemm(a, b, ta, tb, epi, out, accumulate=accumulate, bn=bn)
+    ext().gemm(a, b, ta, tb, epi, out, accumulate=accumulate, bn=bn, splits=splits)
     return out
 
 
