@@ -12,7 +12,8 @@
 //   S^T  = K Q^T,  dP^T = V dO^T                 (M = 128 keys)
 //   P^T  = exp(scale S^T - lse),  dS^T = P^T (dP^T - D)   (one thread per key row)
 //   dV  += P^T dO,  dK += dS^T Q                  (P^T, dS^T staged in swizzled smem)
-//   dQ   = dS K  (dS^T read as an MN-major A operand) -> fp32 atomics into dq_acc
+//   dQ   = dS K  (dS^T read as an MN-major A operand) -> TMA reduce-add into fp32 dq_acc
+// Eight compute warps: two per TMEM lane quadrant, each taking half of the columns.
 // D = rowsum(dO * O) comes from a small pre-pass; a post-pass turns dq_acc into bf16 with
 // the RoPE backward applied. dK gets its RoPE backward in this kernel's epilogue.
 #include "../common/common.cuh"
@@ -28,7 +29,8 @@ using namespace sm100;
 
 constexpr int kBM = 128;  // keys per CTA
 constexpr int kBN = 128;  // queries per step
-constexpr int kBwdThreads = 192;
+constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 compute warps (2 per TMEM lane quadrant)
+constexpr int kComputeThreads = 256;
 
 struct AttnBwdArgs {
   const float* lse;   // (B, H, T) natural log
@@ -47,7 +49,7 @@ __device__ __forceinline__ uint32_t sw_unit(int r, int u) {
   return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
 }
 
-__device__ __forceinline__ void named_bar_compute() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_bar_compute() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 template <int HD>
 struct BwdSmem {
@@ -60,14 +62,16 @@ struct BwdSmem {
   static constexpr uint32_t P_OFF = DO_OFF + STAGES * T_BYTES;
   static constexpr uint32_t DS_OFF = P_OFF + 128 * 128 * 2;
   static constexpr uint32_t VEC_OFF = DS_OFF + 128 * 128 * 2;  // lse (128) + D (128) floats
-  static constexpr uint32_t BAR_OFF = VEC_OFF + 1024;
+  static constexpr int EPI_BUFS = HD == 64 ? 2 : 1;              // dQ staging buffers per compute warp
+  static constexpr uint32_t STG_OFF = VEC_OFF + 1024;            // 8 warps x EPI_BUFS x 4 KB (32x32 fp32)
+  static constexpr uint32_t BAR_OFF = STG_OFF + 8 * EPI_BUFS * 4096;
   static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
 };
 
 template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                 const AttnBwdArgs a) {
+                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
   using L = BwdSmem<HD>;
   constexpr int ST = L::STAGES;
   constexpr int TMEM_COLS = 512;
@@ -109,10 +113,10 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       bar_init(&q_empty[s], 1);
     }
     bar_init(s_full, 1);
-    bar_init(pds_full, 128);
+    bar_init(pds_full, kComputeThreads);
     bar_init(pds_empty, 1);
     bar_init(dq_full, 1);
-    bar_init(tm_free, 128);
+    bar_init(tm_free, kComputeThreads);
     bar_init(dkv_full, 1);
     fence_barrier_init();
   }
@@ -197,21 +201,25 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       }
       if (ok) mma_commit(dkv_full);
     }
-  } else {
+  } else if (warp >= 2) {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // column half handled by this warp (2 warps per lane quadrant)
     const int r = quad * 32 + lane;
+    const int ct = (warp - 2) * 32 + lane;  // 0..255
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
+    uint8_t* stg = smem + L::STG_OFF + (warp - 2) * (L::EPI_BUFS * 4096);
+    int sbuf = 0;
     bool ok = true;
     for (int n = 0; n < n_items; ++n) {
       const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
       const int qbase = i * kBN;
       named_bar_compute();
-      {
-        const int qq = qbase + r;
+      if (ct < 128) {
+        const int qq = qbase + ct;
         const int64_t vi = ((int64_t)b * a.H + hq) * a.T + qq;
-        lse_s[r] = qq < a.T ? a.lse[vi] * 1.4426950408889634f : INFINITY;
-        d_s[r] = qq < a.T ? a.dsum[vi] : 0.f;
+        lse_s[ct] = qq < a.T ? a.lse[vi] * 1.4426950408889634f : INFINITY;
+        d_s[ct] = qq < a.T ? a.dsum[vi] : 0.f;
       }
       named_bar_compute();
       if (!wait_bar(s_full, n & 1, err, 36)) { ok = false; break; }
@@ -220,21 +228,32 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       uint8_t* pt = smem + L::P_OFF;
       uint8_t* dst = smem + L::DS_OFF;
       const bool diag = a.causal && (qbase < k0 + kBM);
+      const bool key_ok = kk < a.T;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
         uint32_t sv[32], dv[32];
         tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
         tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
         tmem_wait_ld();
         float p[32], ds[32];
+        if (diag || !key_ok) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qi = c * 32 + e;
-          const int qq = qbase + qi;
-          const bool valid = (kk < a.T) && (!diag || qq >= kk);
-          const float pe = valid ? exp2f(__uint_as_float(sv[e]) * a.scale_log2 - lse_s[qi]) : 0.f;
-          p[e] = pe;
-          ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          for (int e = 0; e < 32; ++e) {
+            const int qi = c * 32 + e;
+            const bool valid = key_ok && (!diag || qbase + qi >= kk);
+            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi])) : 0.f;
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qi = c * 32 + e;
+            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi]));
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -245,63 +264,61 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       tc_fence_before();
       fence_proxy_async_smem();
       bar_arrive(pds_full);
-      // dQ rows (thread = query row of this block)
+      // dQ rows (thread = query row of this block): scale, stage as 32x32 fp32 boxes, TMA reduce-add
       if (!wait_bar(dq_full, n & 1, err, 38)) { ok = false; break; }
       tc_fence_after();
-      const int qq = qbase + r;
-      float* dqrow = a.dq_acc + (int64_t)(row0 + qq) * a.ld_dq + hq * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = half * (HD / 2) + c * 32;
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + C_DQ + c * 32, v);
+        tmem_ld32(tmem + lane_off + C_DQ + col, v);
+        if (lane == 0) bulk_wait_read<L::EPI_BUFS - 1>();
+        __syncwarp();
+        uint8_t* buf = stg + sbuf * 4096;
+        sbuf = (sbuf + 1) % L::EPI_BUFS;
         tmem_wait_ld();
-        if (qq < a.T) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 t = make_float4(__uint_as_float(v[e]) * a.scale, __uint_as_float(v[e + 1]) * a.scale,
-                                   __uint_as_float(v[e + 2]) * a.scale, __uint_as_float(v[e + 3]) * a.scale);
-            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + e), t);
-          }
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
+                          __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_dq, buf, hq * HD + col, row0 + qbase + quad * 32);
+          bulk_commit();
         }
       }
       tc_fence_before();
       bar_arrive(tm_free);
     }
-    // dK (scaled, RoPE backward) and dV rows -> packed dqkv
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second
     if (ok && wait_bar(dkv_full, 0, err, 39)) {
       tc_fence_after();
       float x[HD];
+      const uint32_t col = half == 0 ? C_DK : C_DV;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + C_DK + c * 32, v);
+        tmem_ld32(tmem + lane_off + col + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * a.scale;
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * (half == 0 ? a.scale : 1.f);
       }
       if (kk < a.T) {
-        const float* cr = a.cos_t + (int64_t)kk * HD;
-        const float* sr = a.sin_t + (int64_t)kk * HD;
-        float y[HD];
+        if (half == 0) {
+          const float* cr = a.cos_t + (int64_t)kk * HD;
+          const float* sr = a.sin_t + (int64_t)kk * HD;
 #pragma unroll
-        for (int e = 0; e < HD / 2; ++e) {
-          y[e] = x[e] * cr[e] + x[e + HD / 2] * sr[e + HD / 2];
-          y[e + HD / 2] = x[e + HD / 2] * cr[e + HD / 2] - x[e] * sr[e];
+          for (int e = 0; e < HD / 2; ++e) {
+            const float x1 = x[e], x2 = x[e + HD / 2];
+            x[e] = x1 * cr[e] + x2 * sr[e + HD / 2];
+            x[e + HD / 2] = x2 * cr[e + HD / 2] - x1 * sr[e];
+          }
         }
-        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (a.H + kvh) * HD;
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(y + c * 8);
-      }
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + C_DV + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]);
-      }
-      if (kk < a.T) {
-        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (a.H + a.KV + kvh) * HD;
+        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(x + c * 8);
       }
@@ -316,29 +333,35 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
 }
 
 // D = rowsum(dO * O) per (b, h, t); also zeroes the fp32 dQ accumulator row slice.
+// One thread per 8-wide chunk; the HD/8 threads of a (row, head) reduce with shuffles.
 template <int HD>
 __global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dO, float* __restrict__ dsum,
                                     float* __restrict__ dq_acc, int BT, int T, int H) {
-  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // (row, head)
-  if (idx >= (int64_t)BT * H) return;
-  const int64_t row = idx / H;
-  const int h = (int)(idx % H);
-  const bf16* op = o + row * (int64_t)H * HD + h * HD;
-  const bf16* dp = dO + row * (int64_t)H * HD + h * HD;
-  float* dq = dq_acc + row * (int64_t)H * HD + h * HD;
+  constexpr int G = HD / 8;  // threads per (row, head): 8 or 16, divides the warp
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)BT * H * G;
+  const bool valid = idx < total;
+  const int64_t rh = valid ? idx / G : 0;
+  const int c = (int)(idx % G) * 8;
   float acc = 0.f;
-#pragma unroll
-  for (int c = 0; c < HD / 8; ++c) {
+  if (valid) {
+    const int64_t off = rh * HD + c;  // (row, head) pairs are contiguous HD-element slices
     float x[8], y[8];
-    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(op + c * 8), x);
-    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dp + c * 8), y);
+    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(o + off), x);
+    bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dO + off), y);
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc += x[e] * y[e];
-    st_f4(dq + c * 8, make_float4(0.f, 0.f, 0.f, 0.f));
-    st_f4(dq + c * 8 + 4, make_float4(0.f, 0.f, 0.f, 0.f));
+    st_f4(dq_acc + off, make_float4(0.f, 0.f, 0.f, 0.f));
+    st_f4(dq_acc + off + 4, make_float4(0.f, 0.f, 0.f, 0.f));
   }
-  const int b = (int)(row / T), t = (int)(row % T);
-  dsum[((int64_t)b * H + h) * T + t] = acc;
+#pragma unroll
+  for (int w = G / 2; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
+  if (valid && c == 0) {
+    const int64_t row = rh / H;
+    const int h = (int)(rh % H);
+    const int b = (int)(row / T), t = (int)(row % T);
+    dsum[((int64_t)b * H + h) * T + t] = acc;
+  }
 }
 
 // dq (bf16, RoPE backward) <- dq_acc (fp32), into the q columns of the packed dqkv rows.
@@ -373,7 +396,8 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, bf16* __r
 }
 
 template <int HD>
-cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args, cudaStream_t st) {
+cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq, const AttnBwdArgs& args,
+                       cudaStream_t st) {
   auto kern = flash_bwd_kernel<HD>;
   constexpr size_t smem = BwdSmem<HD>::TOTAL;
   static bool attr = false;
@@ -383,7 +407,7 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const Attn
     attr = true;
   }
   dim3 grid((unsigned)cdiv(args.T, kBM), args.B * args.KV);
-  kern<<<grid, kBwdThreads, smem, st>>>(tq, tdo, args);
+  kern<<<grid, kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
   return cudaGetLastError();
 }
 
@@ -400,7 +424,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   if (B == 0 || T == 0) return cudaSuccess;
   const int64_t rows = (int64_t)B * T;
   {
-    const int64_t n = rows * H;
+    const int64_t n = rows * H * (hd / 8);
     auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
     k<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum, dq_acc,
                                               (int)rows, T, H);
@@ -424,12 +448,14 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
   args.err = attn_err_word();
-  alignas(64) CUtensorMap tq, tdo;
+  alignas(64) CUtensorMap tq, tdo, tdq;
   const bool ok =
       make_tmap_2d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows, ld_qkv, 64, 128) &&
-      make_tmap_2d(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * hd, rows, (uint64_t)H * hd, 64, 128);
+      make_tmap_2d(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)H * hd, rows, (uint64_t)H * hd, 64, 128) &&
+      make_tmap_2d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * hd, rows, (uint64_t)H * hd, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
   LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
-  cudaError_t e = hd == 64 ? launch_bwd<64>(tq, tdo, args, st) : launch_bwd<128>(tq, tdo, args, st);
+  cudaError_t e = hd == 64 ? launch_bwd<64>(tq, tdo, tdq, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
   if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);
