@@ -22,7 +22,6 @@ int* gemm_err_word() {
 // Estimated time ~ waves x tile width; ties go to the wider (more efficient) tile.
 int gemm_pick_bn(int M, int N, int epi) {
   if (epi == EPI_SWIGLU) return N >= 512 ? 256 : 128;
-  if (epi == EPI_ROPE) return 128;
   const int64_t mb = cdiv(M, kGemmBM);
   const int64_t t128 = cdiv(mb * cdiv(N, 128), sm_count()) * 1;
   const int64_t t256 = cdiv(mb * cdiv(N, 256), sm_count()) * 2;
@@ -38,7 +37,8 @@ void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* split
   *bn = gemm_pick_bn(M, N, epi);
   *splits = 1;
   for (int BN : {128, 256}) {
-    if (epi == EPI_SWIGLU || epi == EPI_ROPE) BN = *bn;
+    if (epi == EPI_SWIGLU) BN = *bn;
+    if (epi == EPI_ROPE && BN % 128) continue;
     const int64_t tiles = mb * cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
     const int smax = can_split ? (int)std::min<int64_t>(16, std::max<int64_t>(1, kb / 4)) : 1;
     for (int s = 1; s <= smax; ++s) {
@@ -52,7 +52,7 @@ void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* split
         *splits = (int)cdiv(kb, kps);
       }
     }
-    if (epi == EPI_SWIGLU || epi == EPI_ROPE) break;
+    if (epi == EPI_SWIGLU) break;
   }
 }
 
@@ -115,8 +115,9 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
       ok = make_tmap_2d(&mp.c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
            make_tmap_3d(&mp.c2, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
       break;
-    case EPI_SWIGLU_BWD:
-      ok = make_tmap_3d(&mp.c2, g.out2, dt, 2, N, 2, M, N, g.ldo2, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    case EPI_SWIGLU_BWD:  // c: the saved [g | u] rows (loaded), c2: [dg | du] (stored)
+      ok = make_tmap_3d(&mp.c, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+           make_tmap_3d(&mp.c2, g.out2, dt, 2, N, 2, M, N, g.ldo2, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
       break;
     default: break;
   }

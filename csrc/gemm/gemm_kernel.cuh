@@ -74,6 +74,29 @@ struct Stager {
   uint8_t* base;
   int buf;
   int lane;
+  uint64_t* bar;      // per-warp mbarrier for epilogue-side TMA loads
+  uint32_t bar_phase;
+  // TMA-load two 32x32 bf16 boxes (halves 0 and 1 of a 3D map) into base[0:2K] and base[2K:4K];
+  // the caller's previous stores from that buffer must have been read (acquire_all first).
+  __device__ __forceinline__ bool load_pair3d(const CUtensorMap* tm, int x, int y, int* err) {
+    if (lane == 0) {
+      bar_arrive_expect_tx(bar, 4096);
+      tma_load_3d(base, tm, bar, x, 0, y);
+      tma_load_3d(base + 2048, tm, bar, x, 1, y);
+    }
+    const bool ok = wait_bar(bar, bar_phase, err, 5);
+    bar_phase ^= 1;
+    return ok;
+  }
+  __device__ __forceinline__ void wait_all_reads() {
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+  }
+  __device__ __forceinline__ void get_bf16(const uint8_t* b, float* v) const {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      bf16x8_to_float(*reinterpret_cast<const BF16x8*>(b + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)), v + u * 8);
+  }
   __device__ __forceinline__ uint8_t* acquire() {
     if (lane == 0) bulk_wait_read<1>();
     __syncwarp();
@@ -114,6 +137,8 @@ struct Stager {
     __syncwarp();
   }
 };
+
+__device__ __forceinline__ bool lane_is_zero(const Stager& st) { return st.lane == 0; }
 
 // row: this thread's accumulator row; wrow: the warp's first row (TMA box origin).
 template <int EPI, int BN>
@@ -181,22 +206,19 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       st.store3d(tmC2, b, col0, 1, wrow);
     }
   } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-    const int F = a.split;
+    // g and u arrive by TMA (3D map over the saved [g | u] rows) into staging buffer 0; dg and
+    // du leave by TMA from buffer 1.
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col0 = nb * BN + c * 32;
       if (col0 >= a.N) break;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
+      st.wait_all_reads();
+      if (!st.load_pair3d(tmC, col0, wrow, a.err)) break;
       float g[32], u[32], dg[32], du[32];
-      if (rv) {
-        const bf16* gu = reinterpret_cast<const bf16*>(a.aux) + (int64_t)row * a.ld_aux;
-        load_bf16x32(gu + col0, g, col0, F);
-        load_bf16x32(gu + F + col0, u, col0, F);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) g[j] = u[j] = 0.f;
-      }
+      st.get_bf16(st.base, g);
+      st.get_bf16(st.base + 2048, u);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -205,12 +227,16 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
         dg[j] = d * u[j] * sg * (1.f + g[j] * (1.f - sg));
         du[j] = d * g[j] * sg;
       }
-      uint8_t* b = st.acquire();
-      st.put_bf16(b, dg);
-      st.store3d(tmC2, b, col0, 0, wrow);
-      b = st.acquire();
-      st.put_bf16(b, du);
-      st.store3d(tmC2, b, col0, 1, wrow);
+      uint8_t* ob = st.base + 4096;
+      st.put_bf16(ob, dg);
+      st.put_bf16(ob + 2048, du);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane_is_zero(st)) {
+        tma_store_3d(tmC2, ob, col0, 0, wrow);
+        tma_store_3d(tmC2, ob + 2048, col0, 1, wrow);
+        bulk_commit();
+      }
     }
   } else if constexpr (EPI == EPI_ROPE) {
     const int hd = a.hd, half = hd / 2;
@@ -237,12 +263,19 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
         if (col1 < a.rot_cols) {
           const int f1 = j * 32, f2 = half + j * 32;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float c1v = cr[f1 + e], s1v = sr[f1 + e], c2v = cr[f2 + e], s2v = sr[f2 + e];
-            const float y1 = x1[e] * c1v - x2[e] * s1v;
-            const float y2 = x2[e] * c2v + x1[e] * s2v;
-            x1[e] = y1;
-            x2[e] = y2;
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 c1v = ld_f4(cr + f1 + 4 * e4), s1v = ld_f4(sr + f1 + 4 * e4);
+            const float4 c2v = ld_f4(cr + f2 + 4 * e4), s2v = ld_f4(sr + f2 + 4 * e4);
+            const float c1a[4] = {c1v.x, c1v.y, c1v.z, c1v.w}, s1a[4] = {s1v.x, s1v.y, s1v.z, s1v.w};
+            const float c2a[4] = {c2v.x, c2v.y, c2v.z, c2v.w}, s2a[4] = {s2v.x, s2v.y, s2v.z, s2v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int e = 4 * e4 + q;
+              const float y1 = x1[e] * c1a[q] - x2[e] * s1a[q];
+              const float y2 = x2[e] * c2a[q] + x1[e] * s2a[q];
+              x1[e] = y1;
+              x2[e] = y2;
+            }
           }
         }
         uint8_t* b = st.acquire();
@@ -307,7 +340,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* ebar = tempty + 2;  // [4] epilogue-warp TMA load barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 4);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   int* err = args.err;
@@ -320,6 +354,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       bar_init(&tfull[b], 1);
       bar_init(&tempty[b], 128);
     }
+    for (int b = 0; b < 4; ++b) bar_init(&ebar[b], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -419,7 +454,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
-    Stager st{stage_out + (warp - 2) * 8192, 0, lane};
+    Stager st{stage_out + (warp - 2) * 8192, 0, lane, &ebar[warp - 2], 0u};
     int buf = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {

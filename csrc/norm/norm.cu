@@ -241,7 +241,7 @@ cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, 
 int rmsnorm_bwd_partials(int64_t N, int D) {
   int tpr = D <= 1024 ? 32 : D <= 2048 ? 64 : D <= 4096 ? 128 : 256;
   const int rpc = kThreads / tpr;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc * 4), 2 * sm_count()));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc), 4 * sm_count()));
 }
 
 // ds = rmsnorm backward + ds_in (optional); ds16 (bf16 copy) optional; dw written or accumulated.

@@ -94,6 +94,33 @@ def bench_gemm(cfg, tokens, rows, only=None, reps=10):
                          frac_peak=round(fl / ours / 1e9 / peak, 3)))
 
 
+def bench_fused_gemm(cfg, B, T, rows):
+    """The fused-epilogue GEMMs of the native path at the model's shapes (vs the plain GEMM)."""
+    from llmt.models.llama import rope_tables
+    from llmt.ops import native as N
+    peak, _ = peaks()
+    tok, d, f = B * T, cfg.d, cfg.ffn
+    x = torch.randn(tok, d, device="cuda").bfloat16()
+    wqkv = torch.randn(cfg.qkv_out, d, device="cuda").bfloat16()
+    cos, sin = rope_tables(T, cfg.hd, cfg.rope_base, "cuda")
+    ms = time_ms(lambda: N.gemm_rope(x, wqkv, cos, sin, T, cfg.hd, (cfg.H + cfg.kvh) * cfg.hd))
+    fl = 2.0 * tok * cfg.qkv_out * d
+    rows.append(dict(op="gemm qkv+rope", shape=f"{tok}x{cfg.qkv_out}x{d}", ms=round(ms, 4), ref_ms=None,
+                     tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
+    w13 = torch.randn(2 * f, d, device="cuda").bfloat16()
+    ms = time_ms(lambda: N.gemm_swiglu(x, w13, f))
+    fl = 2.0 * tok * 2 * f * d
+    rows.append(dict(op="gemm w13+swiglu", shape=f"{tok}x{2 * f}x{d}", ms=round(ms, 4), ref_ms=None,
+                     tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
+    dm = torch.randn(tok, d, device="cuda").bfloat16()
+    w2 = torch.randn(d, f, device="cuda").bfloat16()
+    gu = torch.randn(tok, 2 * f, device="cuda").bfloat16()
+    ms = time_ms(lambda: N.gemm_swiglu_bwd(dm, w2, gu, f))
+    fl = 2.0 * tok * f * d
+    rows.append(dict(op="gemm w2dgrad+swiglu_bwd", shape=f"{tok}x{f}x{d}", ms=round(ms, 4), ref_ms=None,
+                     tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
+
+
 def bench_attn(cfg, B, T, rows):
     from llmt.models.llama import rope_tables
     from llmt.ops import native as N
@@ -180,7 +207,7 @@ def main():
     p.add_argument("--size", default="medium")
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--seq", type=int, default=1024)
-    p.add_argument("--ops", default="gemm,attn,mem")
+    p.add_argument("--ops", default="gemm,fused,attn,mem")
     p.add_argument("--json", default=None)
     p.add_argument("--only", default=None, help="comma list of GEMM names, e.g. 'head fwd,wo fwd'")
     p.add_argument("--reps", type=int, default=10)
@@ -193,6 +220,8 @@ def main():
         sweep_gemm(cfg, args.batch * args.seq, args.only.split(",") if args.only else [n for n, *_ in gemm_shapes(cfg, 1)])
     if "gemm" in ops:
         bench_gemm(cfg, args.batch * args.seq, rows, args.only.split(",") if args.only else None, args.reps)
+    if "fused" in ops:
+        bench_fused_gemm(cfg, args.batch, args.seq, rows)
     if "attn" in ops:
         bench_attn(cfg, args.batch, args.seq, rows)
     if "mem" in ops:
