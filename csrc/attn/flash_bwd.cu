@@ -31,6 +31,7 @@ constexpr int kBM = 128;  // keys per CTA
 constexpr int kBN = 128;  // queries per step
 constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 compute warps (2 per TMEM lane quadrant)
 constexpr int kComputeThreads = 256;
+constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnBwdArgs {
   const float* lse;   // (B, H, T) natural log
@@ -61,9 +62,9 @@ struct BwdSmem {
   static constexpr uint32_t DO_OFF = Q_OFF + STAGES * T_BYTES;
   static constexpr uint32_t P_OFF = DO_OFF + STAGES * T_BYTES;
   static constexpr uint32_t DS_OFF = P_OFF + 128 * 128 * 2;
-  static constexpr uint32_t VEC_OFF = DS_OFF + 128 * 128 * 2;  // lse (128) + D (128) floats
-  static constexpr int EPI_BUFS = HD == 64 ? 2 : 1;              // dQ staging buffers per compute warp
-  static constexpr uint32_t STG_OFF = VEC_OFF + 1024;            // 8 warps x EPI_BUFS x 4 KB (32x32 fp32)
+  static constexpr uint32_t VEC_OFF = DS_OFF + 128 * 128 * 2;  // per stage: lse (128) + D (128) floats
+  static constexpr int EPI_BUFS = 1;                             // dQ staging buffers per compute warp
+  static constexpr uint32_t STG_OFF = VEC_OFF + STAGES * 1024;   // 8 warps x EPI_BUFS x 4 KB (32x32 fp32)
   static constexpr uint32_t BAR_OFF = STG_OFF + 8 * EPI_BUFS * 4096;
   static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
 };
@@ -90,8 +91,6 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
   uint64_t* tm_free = bars + 9;    // 128 arrivals: S/dP/dQ columns free again
   uint64_t* dkv_full = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  float* lse_s = reinterpret_cast<float*>(smem + L::VEC_OFF);
-  float* d_s = lse_s + 128;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kb = blockIdx.x;             // key block
@@ -141,7 +140,13 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
         const int s = n % ST;
         const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
         if (!wait_bar(&q_empty[s], ((n / ST) & 1) ^ 1, err, 31)) break;
-        bar_arrive_expect_tx(&q_full[s], 2 * L::T_BYTES);
+        // lse and D of this query block ride along (row-vectors of the (B, H, T) layouts)
+        const int nq = min(kBN, a.T - i * kBN);
+        const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
+        bar_arrive_expect_tx(&q_full[s], 2 * L::T_BYTES + 2 * vbytes);
+        const int64_t vbase = ((int64_t)b * a.H + hq) * a.T + (int64_t)i * kBN;
+        bulk_load(smem + L::VEC_OFF + s * 1024, a.lse + vbase, vbytes, &q_full[s]);
+        bulk_load(smem + L::VEC_OFF + s * 1024 + 512, a.dsum + vbase, vbytes, &q_full[s]);
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c) {
           tma_load_2d(smem + L::Q_OFF + s * L::T_BYTES + c * 16384, &tm_qkv, &q_full[s], hq * HD + c * 64,
@@ -205,7 +210,6 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // column half handled by this warp (2 warps per lane quadrant)
     const int r = quad * 32 + lane;
-    const int ct = (warp - 2) * 32 + lane;  // 0..255
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
     uint8_t* stg = smem + L::STG_OFF + (warp - 2) * (L::EPI_BUFS * 4096);
@@ -214,14 +218,9 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
     for (int n = 0; n < n_items; ++n) {
       const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
       const int qbase = i * kBN;
-      named_bar_compute();
-      if (ct < 128) {
-        const int qq = qbase + ct;
-        const int64_t vi = ((int64_t)b * a.H + hq) * a.T + qq;
-        lse_s[ct] = qq < a.T ? a.lse[vi] * 1.4426950408889634f : INFINITY;
-        d_s[ct] = qq < a.T ? a.dsum[vi] : 0.f;
-      }
-      named_bar_compute();
+      // s_full implies this item's Q/dO stage (and its lse / D vectors) has landed
+      const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n % ST) * 1024);
+      const float* d_s = lse_s + 128;
       if (!wait_bar(s_full, n & 1, err, 36)) { ok = false; break; }
       if (!wait_bar(pds_empty, (n & 1) ^ 1, err, 37)) { ok = false; break; }
       tc_fence_after();
@@ -229,6 +228,7 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       uint8_t* dst = smem + L::DS_OFF;
       const bool diag = a.causal && (qbase < k0 + kBM);
       const bool key_ok = kk < a.T;
+      const bool q_tail = qbase + kBN > a.T;  // columns past T hold stale lse / D: mask them
 #pragma unroll 1
       for (int cc = 0; cc < 2; ++cc) {
         const int c = half * 2 + cc;
@@ -237,12 +237,12 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
         tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
         tmem_wait_ld();
         float p[32], ds[32];
-        if (diag || !key_ok) {
+        if (diag || !key_ok || q_tail) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int qi = c * 32 + e;
-            const bool valid = key_ok && (!diag || qbase + qi >= kk);
-            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi])) : 0.f;
+            const bool valid = key_ok && (!diag || qbase + qi >= kk) && qbase + qi < a.T;
+            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e)) : 0.f;
             p[e] = pe;
             ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
           }
@@ -250,7 +250,7 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int qi = c * 32 + e;
-            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi]));
+            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e));
             p[e] = pe;
             ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
           }
@@ -421,6 +421,8 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   LLMT_REQUIRE(hd == 64 || hd == 128, "flash_attn_bwd: head dim must be 64 or 128");
   LLMT_REQUIRE(KV > 0 && H % KV == 0, "flash_attn_bwd: H must be a multiple of KV");
   LLMT_REQUIRE(tma_ok(qkv, ld_qkv, 2) && tma_ok(dO, (int64_t)H * hd, 2), "flash_attn_bwd: TMA alignment");
+  LLMT_REQUIRE(T % 4 == 0 && (reinterpret_cast<uintptr_t>(lse) & 15) == 0,
+               "flash_attn_bwd: T must be a multiple of 4 (16-byte lse rows)");
   if (B == 0 || T == 0) return cudaSuccess;
   const int64_t rows = (int64_t)B * T;
   {

@@ -206,20 +206,33 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       st.store3d(tmC2, b, col0, 1, wrow);
     }
   } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-    // g and u arrive by TMA (3D map over the saved [g | u] rows) into staging buffer 0; dg and
-    // du leave by TMA from buffer 1.
+    // g and u arrive by TMA (3D map over the saved [g | u] rows) one chunk ahead, into the
+    // warp's two 4 KB buffers; dg and du are written back in place and leave by TMA.
+    const int nchunks = min(BN / 32, (int)cdiv(a.N - nb * BN, 32));
+    auto issue = [&](int c) {
+      uint8_t* b = st.base + (c & 1) * 4096;
+      if (st.lane == 0) {
+        bulk_wait_read<0>();  // the store that last used this buffer has read it
+        bar_arrive_expect_tx(&st.bar[c & 1], 4096);
+        tma_load_3d(b, tmC, &st.bar[c & 1], nb * BN + c * 32, 0, wrow);
+        tma_load_3d(b + 2048, tmC, &st.bar[c & 1], nb * BN + c * 32, 1, wrow);
+      }
+    };
+    if (nchunks > 0) issue(0);
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < nchunks; ++c) {
       const int col0 = nb * BN + c * 32;
-      if (col0 >= a.N) break;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
-      st.wait_all_reads();
-      if (!st.load_pair3d(tmC, col0, wrow, a.err)) break;
+      if (c + 1 < nchunks) issue(c + 1);
+      uint8_t* b = st.base + (c & 1) * 4096;
+      const bool ok = wait_bar(&st.bar[c & 1], (st.bar_phase >> (c & 1)) & 1, a.err, 5);
+      st.bar_phase ^= 1u << (c & 1);
       float g[32], u[32], dg[32], du[32];
-      st.get_bf16(st.base, g);
-      st.get_bf16(st.base + 2048, u);
+      st.get_bf16(b, g);
+      st.get_bf16(b + 2048, u);
       tmem_wait_ld();
+      if (!ok) break;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float d = u2f(r[j]);
@@ -227,14 +240,14 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
         dg[j] = d * u[j] * sg * (1.f + g[j] * (1.f - sg));
         du[j] = d * g[j] * sg;
       }
-      uint8_t* ob = st.base + 4096;
-      st.put_bf16(ob, dg);
-      st.put_bf16(ob + 2048, du);
+      __syncwarp();  // every lane has read g, u before the buffer is overwritten
+      st.put_bf16(b, dg);
+      st.put_bf16(b + 2048, du);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane_is_zero(st)) {
-        tma_store_3d(tmC2, ob, col0, 0, wrow);
-        tma_store_3d(tmC2, ob + 2048, col0, 1, wrow);
+        tma_store_3d(tmC2, b, col0, 0, wrow);
+        tma_store_3d(tmC2, b + 2048, col0, 1, wrow);
         bulk_commit();
       }
     }
@@ -340,8 +353,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* ebar = tempty + 2;  // [4] epilogue-warp TMA load barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 4);
+  uint64_t* ebar = tempty + 2;  // [4 warps x 2] epilogue-warp TMA load barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 8);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   int* err = args.err;
@@ -354,7 +367,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       bar_init(&tfull[b], 1);
       bar_init(&tempty[b], 128);
     }
-    for (int b = 0; b < 4; ++b) bar_init(&ebar[b], 1);
+    for (int b = 0; b < 8; ++b) bar_init(&ebar[b], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -454,7 +467,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
-    Stager st{stage_out + (warp - 2) * 8192, 0, lane, &ebar[warp - 2], 0u};
+    Stager st{stage_out + (warp - 2) * 8192, 0, lane, &ebar[(warp - 2) * 2], 0u};
     int buf = 0;
     uint32_t aphase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
