@@ -271,3 +271,71 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
 }
 
 }  // namespace llmt
+
+// ---------------------------------------------------------------- allocation-free entry point
+// See norm/noalloc.h. The dw partial sums live in this fixed device array instead of a
+// buffer the caller allocates; every GPU that loads the library holds it until exit.
+#include "noalloc.h"
+
+namespace {
+static __device__ __align__(256) float g_rmsnorm_noalloc_scratch[LLMT_NOALLOC_SCRATCH_FLOATS];
+
+// Device address of the scratch array for the current device, looked up once per device
+// (host code cannot use the array's name as a device pointer).
+float* noalloc_scratch_ptr(cudaError_t* err) {
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_rmsnorm_noalloc_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  return ptrs[dev];
+}
+}  // namespace
+
+extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, const float* w, const float* rstd,
+                                        const float* ds_in, float* ds, void* ds16, float* dw, int64_t N, int D,
+                                        int accumulate, cudaStream_t stream) {
+  using namespace llmt;
+  if (D <= 0 || D % 8 != 0 || D > LLMT_NOALLOC_MAX_WIDTH) {
+    set_last_error("llmt_rmsnorm_bwd_noalloc: width must be a positive multiple of 8 and at most 8192");
+    return (int)cudaErrorInvalidValue;
+  }
+  if (N < 0) {
+    set_last_error("llmt_rmsnorm_bwd_noalloc: negative row count");
+    return (int)cudaErrorInvalidValue;
+  }
+  if (N == 0) return (int)cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  float* part = noalloc_scratch_ptr(&e);
+  if (!part) return (int)e;
+  // One partial row per CTA; the scratch holds LLMT_NOALLOC_SCRATCH_FLOATS / D of them.
+  const int grid = std::max(1, std::min(rmsnorm_bwd_partials(N, D), LLMT_NOALLOC_SCRATCH_FLOATS / D));
+  const bf16* dy = static_cast<const bf16*>(dy_bf16);
+  bf16* d16 = static_cast<bf16*>(ds16);
+  const size_t smem = D * sizeof(float);
+  dispatch_tpr(D, [&](auto tpr) {
+    constexpr int TPR = decltype(tpr)::value;
+    auto launch = [&](auto kern) {
+      kern<<<grid, kThreads, smem, stream>>>(dy, s, w, rstd, ds_in, ds, d16, part, N, D);
+    };
+    if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
+    else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
+    else if (d16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
+    else launch(rmsnorm_bwd_kernel<TPR, false, false>);
+  });
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return (int)e;
+  dw_reduce_kernel<<<(unsigned)cdiv(D, 32), dim3(32, 8), 0, stream>>>(part, dw, grid, D, accumulate);
+  return (int)cudaGetLastError();
+}
+
+extern "C" const char* llmt_noalloc_last_error() { return llmt::last_error(); }
