@@ -169,10 +169,10 @@ def run_native(args, rank, world, local):
     tok_s = tokens / (ms_step / 1e3)
     e2e_tok_s = tokens / (e2e_wall / args.steps / 1e3)
     tflops = model_flops_per_token(cfg, SEQ) * tok_s / world / 1e12
-    err = native.gemm_error_code() | native.attn_error_code()
+    err = native.gemm_error_code() | native.attn_error_code() | native.ext().dp_error_code(False)
+    tr.release()
     if dp is not None:
         dp.close()
-    tr.release()
     return dict(value=tok_s, ms_per_step=ms_step, mfu=tflops / peak_tflops(), tflops_per_gpu=tflops,
                 e2e=dict(value=round(e2e_tok_s, 1), unit="tokens/s", h2d_bytes_per_step=2 * idx.numel() * 8,
                          d2h_bytes_per_step=4, wall_ms_per_step=round(e2e_wall / args.steps, 3)),
@@ -235,7 +235,7 @@ def main():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="6 fused Triton kernels")
-    p.add_argument("--dp-mode", default="nccl", choices=["fused", "nccl"])
+    p.add_argument("--dp-mode", default="fused", choices=["fused", "nccl"])
     p.add_argument("--no-graph", action="store_true")
     args = p.parse_args()
     if args.warmup < 3:

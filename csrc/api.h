@@ -97,4 +97,18 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
                            int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st);
 int attn_error_code(bool reset);
 
+// ---------------------------------------------------------------- data-parallel transport
+// CUDA-IPC buffers (64-byte handles exchanged by the caller), a flag barrier with bounded
+// spins, and the fused reduce-scatter + sharded AdamW + all-gather kernel (comm/dp_fused.cu).
+cudaError_t ipc_alloc(size_t bytes, void** ptr, void* handle64);
+cudaError_t ipc_open(const void* handle64, void** ptr);
+cudaError_t ipc_close(void* ptr);
+cudaError_t ipc_free(void* ptr);
+cudaError_t dp_barrier(uint32_t* const* pads_dev, uint32_t* my_pad, uint32_t* epoch, int rank, int world, int code,
+                       cudaStream_t st);
+cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, float* master, float* m, float* v,
+                           int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
+                           cudaStream_t st);
+int dp_error_code(bool reset);
+
 }  // namespace llmt

@@ -301,6 +301,55 @@ at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tenso
   return dqkv;
 }
 
+// ---------------------------------------------------------------- data-parallel transport
+pybind11::tuple ipc_alloc(int64_t bytes) {
+  void* ptr = nullptr;
+  char h[64];
+  ok(llmt::ipc_alloc((size_t)bytes, &ptr, h), "ipc_alloc");
+  return pybind11::make_tuple((int64_t)reinterpret_cast<uintptr_t>(ptr), pybind11::bytes(h, 64));
+}
+
+int64_t ipc_open(pybind11::bytes handle) {
+  std::string h = handle;
+  CHECK(h.size() == 64, "ipc handle must be 64 bytes");
+  void* ptr = nullptr;
+  ok(llmt::ipc_open(h.data(), &ptr), "ipc_open");
+  return (int64_t)reinterpret_cast<uintptr_t>(ptr);
+}
+
+void ipc_close(int64_t ptr) { ok(llmt::ipc_close(reinterpret_cast<void*>(ptr)), "ipc_close"); }
+void ipc_free(int64_t ptr) { ok(llmt::ipc_free(reinterpret_cast<void*>(ptr)), "ipc_free"); }
+
+// Non-owning tensor over device memory this library allocated (the Python owner frees it).
+at::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device) {
+  return at::from_blob(reinterpret_cast<void*>(ptr), {numel},
+                       at::TensorOptions().dtype(dtype).device(at::Device(at::kCUDA, (int)device)));
+}
+
+void dp_barrier(at::Tensor pads_dev, int64_t my_pad, at::Tensor epoch, int64_t rank, int64_t world, int64_t code) {
+  CHECK_DT(pads_dev, at::kLong);
+  CHECK_DT(epoch, at::kInt);
+  ok(llmt::dp_barrier(reinterpret_cast<uint32_t* const*>(pads_dev.data_ptr<int64_t>()),
+                      reinterpret_cast<uint32_t*>(my_pad), reinterpret_cast<uint32_t*>(epoch.data_ptr<int>()),
+                      (int)rank, (int)world, (int)code, stream()),
+     "dp_barrier");
+}
+
+void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor master, at::Tensor m, at::Tensor v,
+                    int64_t lo, int64_t n, at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd,
+                    double grad_scale, int64_t world) {
+  CHECK_DT(grads_dev, at::kLong);
+  CHECK_DT(shadows_dev, at::kLong);
+  CHECK(grads_dev.numel() == world && shadows_dev.numel() == world, "peer pointer arrays must have world entries");
+  CHECK(m.numel() >= n && v.numel() >= n && master.numel() >= lo + n, "shard bounds exceed the buffers");
+  llmt::AdamHyper h{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
+  ok(llmt::dp_fused_adamw(reinterpret_cast<float* const*>(grads_dev.data_ptr<int64_t>()),
+                          reinterpret_cast<void* const*>(shadows_dev.data_ptr<int64_t>()), master.data_ptr<float>(),
+                          m.data_ptr<float>(), v.data_ptr<float>(), lo, n, lr.data_ptr<float>(), step.data_ptr<int>(),
+                          h, (int)world, stream()),
+     "dp_fused_adamw");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -330,4 +379,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
   m.def("sm_count", &llmt::sm_count);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_free", &ipc_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("dp_barrier", &dp_barrier);
+  m.def("dp_fused_adamw", &dp_fused_adamw);
+  m.def("dp_error_code", &llmt::dp_error_code, "reset"_a = false);
 }

@@ -56,26 +56,33 @@ class FlatParams:
         self.numel = off
         dev = torch.device(device)
         self.master = torch.zeros(off, dtype=torch.float32, device=dev)
-        self.grad = torch.zeros(off, dtype=torch.float32, device=dev)
-        self.shadow = torch.zeros(off, dtype=torch.bfloat16, device=dev)
         with torch.no_grad():
             for p, o in zip(self.params, self.offsets):
                 n = p.numel()
                 self.master[o:o + n].copy_(p.detach().reshape(-1).to(dev, torch.float32))
                 p.data = self.master[o:o + n].view(p.shape)
-                p.main_grad = self.grad[o:o + n].view(p.shape)
-                p.w16 = self.shadow[o:o + n].view(p.shape)
+        self.blocks = list(model.blocks)
+        self.rebind(grad=torch.zeros(off, dtype=torch.float32, device=dev),
+                    shadow=torch.zeros(off, dtype=torch.bfloat16, device=dev))
+        self.refresh_shadow()
+
+    def rebind(self, grad, shadow):
+        """Point every parameter's main_grad / w16 (and the merged w1||w3 views) at new flat buffers."""
+        self.grad, self.shadow = grad, shadow
+        for p, o in zip(self.params, self.offsets):
+            n = p.numel()
+            p.main_grad = grad[o:o + n].view(p.shape)
+            p.w16 = shadow[o:o + n].view(p.shape)
         pos = {id(p): o for p, o in zip(self.params, self.offsets)}
-        for blk in model.blocks:
+        for blk in self.blocks:
             w1, w3 = blk.mlp.w1.weight, blk.mlp.w3.weight
             o1, o3 = pos[id(w1)], pos[id(w3)]
             if o3 != o1 + w1.numel():
                 raise RuntimeError("w1 and w3 must be adjacent in the flat buffer (ffn*d must be a multiple of 64)")
             ffn, d = w1.shape
-            w1.w13_16 = self.shadow[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
-            w1.w13_grad = self.grad[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
+            w1.w13_16 = shadow[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
+            w1.w13_grad = grad[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
             w1.w3_param = w3
-        self.refresh_shadow()
 
     def refresh_shadow(self):
         """bf16 shadow := master (after init or a checkpoint load)."""

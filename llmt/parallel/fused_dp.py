@@ -1,0 +1,90 @@
+"""Fused data-parallel step over NVLink peer memory (host side of csrc/comm/dp_fused.cu).
+
+Replaces NCCL reduce_scatter + sharded AdamW + all_gather (llmt.parallel.dp, mode "nccl") by
+one kernel per step. Set-up: the flat fp32 gradient and bf16 shadow-weight buffers are
+re-allocated as CUDA-IPC exportable memory, their 64-byte handles are exchanged over the
+process group, and every rank opens every peer's buffers, so the kernel can load and store
+peer memory directly through NVSwitch. A small signal pad per rank carries the epoch flags of
+the device-side barrier (bounded spins; a timeout sets an error code readable with
+error_code()). No multicast is used.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from llmt.ops import native as N
+
+
+class FusedDP:
+    def __init__(self, flat, opt, rank: int, world: int, group=None):
+        self.flat, self.opt, self.rank, self.world, self.group = flat, opt, rank, world, group
+        C = N.ext()
+        dev = flat.master.device
+        self.device = dev
+        self._own = []
+        gp, gh = C.ipc_alloc(flat.numel * 4)
+        sp, sh = C.ipc_alloc(flat.numel * 2)
+        pp, ph = C.ipc_alloc(4096)
+        self._own = [gp, sp, pp]
+        grad = C.tensor_from_ptr(gp, flat.numel, torch.float32, dev.index)
+        shadow = C.tensor_from_ptr(sp, flat.numel, torch.bfloat16, dev.index)
+        grad.copy_(flat.grad)
+        shadow.copy_(flat.shadow)
+        flat.rebind(grad=grad, shadow=shadow)
+        mine = torch.tensor(list(gh + sh + ph), dtype=torch.uint8, device=dev)
+        allh = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allh, mine, group=group)
+        self._peers = []
+        gptr, sptr, pptr = [], [], []
+        for p, h in enumerate(allh):
+            b = bytes(h.cpu().tolist())
+            if p == rank:
+                gptr.append(gp)
+                sptr.append(sp)
+                pptr.append(pp)
+                continue
+            g_, s_, p_ = C.ipc_open(b[0:64]), C.ipc_open(b[64:128]), C.ipc_open(b[128:192])
+            self._peers += [g_, s_, p_]
+            gptr.append(g_)
+            sptr.append(s_)
+            pptr.append(p_)
+        self.grads_dev = torch.tensor(gptr, dtype=torch.int64, device=dev)
+        self.shadows_dev = torch.tensor(sptr, dtype=torch.int64, device=dev)
+        self.pads_dev = torch.tensor(pptr, dtype=torch.int64, device=dev)
+        self.my_pad = pp
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    @torch.no_grad()
+    def step(self):
+        C, o, f = N.ext(), self.opt, self.flat
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 100)
+        o.step_t.add_(1)
+        b1, b2 = o.betas
+        C.dp_fused_adamw(self.grads_dev, self.shadows_dev, f.master, o.exp_avg, o.exp_avg_sq, o.lo, o.hi - o.lo,
+                         o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay, o.grad_scale, self.world)
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 200)
+
+    def error_code(self, reset=False) -> int:
+        return N.ext().dp_error_code(reset)
+
+    def close(self):
+        if not self._own:
+            return
+        C = N.ext()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._peers:
+            C.ipc_close(p)
+        self._peers = []
+        dist.barrier(group=self.group)
+        # the flat views must not outlive the memory: hand the model ordinary buffers back
+        grad = self.flat.grad.clone()
+        shadow = self.flat.shadow.clone()
+        self.flat.rebind(grad=grad, shadow=shadow)
+        torch.cuda.synchronize(self.device)
+        for p in self._own:
+            C.ipc_free(p)
+        self._own = []
