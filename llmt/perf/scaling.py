@@ -1,0 +1,213 @@
+"""DP x TP x PP scaling model: step time, MFU and tokens/s for a global batch on n GPUs
+(reference: perf_model/scaling.py, which only predicts; here the intra-node constants are the
+B200 pool's measured NVLink 5 numbers and the prediction is checked against real runs).
+
+Per layout (dp, tp, pp, micro-batch mb; m = G / (dp * mb) micro-batches):
+  compute   roofline/calibrated prediction (llmt.perf.roofline) of one micro-batch with the
+            block GEMMs sharded tp ways, divided over pp stages
+  TP        sequence-parallel Megatron: per layer 2 all-gathers (qkv, gate/up inputs) and 2
+            reduce-scatters (wo, down outputs) of the (mb, T, d) bf16 activation in the forward,
+            the same in the backward; `fused=True` models them inside the GEMMs (overlapped up to
+            the GEMM time), else exposed
+  PP        1F1B: (m + p - 1) slots per stage, one (mb, T, d) bf16 send per micro-batch per
+            direction; sends overlap compute when `overlap_pp`
+  DP        ZeRO-1: reduce-scatter fp32 grads + all-gather bf16 weights per step, overlapped
+            with the last micro-batch's backward when `overlap_dp`
+  optimizer AdamW on params / (tp * pp * dp) (34 B/param incl. bf16 copy and grad zeroing)
+  memory    fp32 master + grads (sharded as the layout shards them), bf16 weights, Adam state /
+            dp, activations in flight; must fit 90% of the GPU
+
+    python -m llmt.perf.scaling --models medium,llama3-8b --gpus 8,64,1024 --system b200_nvl8_ib
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+from dataclasses import dataclass
+
+from llmt.config import SIZES, count_params, model_flops_per_token
+from llmt.perf.roofline import Machine, inventory, load_shape_times, predict
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+WORKLOADS = {"small": ("small", 1024, 512), "medium": ("medium", 1024, 512), "large": ("large", 1024, 512),
+             "llama3-8b": ("llama3-8b", 4096, 1024), "llama3-70b": ("llama3-70b", 4096, 1024)}
+
+
+@dataclass
+class Link:
+    bw_gbs: float
+    p2p_gbs: float
+    latency_us: float
+
+
+def load_links(path=None):
+    with open(path or os.path.join(HERE, "links.json")) as f:
+        return json.load(f)
+
+
+def link(cfg, name) -> Link:
+    d = cfg["links"][name]
+    return Link(d["bw_gbs"], d.get("p2p_gbs", d["bw_gbs"]), d["latency_us"])
+
+
+def ring_allreduce_s(nbytes, n, lk: Link):
+    if n <= 1:
+        return 0.0
+    return 2 * (n - 1) / n * nbytes / (lk.bw_gbs * 1e9) + 2 * (n - 1) * lk.latency_us * 1e-6
+
+
+def reduce_scatter_s(nbytes, n, lk: Link):
+    """Half of a ring all-reduce (also the cost of an all-gather of the same total size)."""
+    if n <= 1:
+        return 0.0
+    return (n - 1) / n * nbytes / (lk.bw_gbs * 1e9) + (n - 1) * lk.latency_us * 1e-6
+
+
+def hier(fn, nbytes, n, g, intra: Link, inter: Link):
+    """Inside a node of g GPUs first, then across nodes on the 1/g share."""
+    if n <= g:
+        return fn(nbytes, n, intra)
+    return fn(nbytes, g, intra) + fn(nbytes / g, n // g, inter)
+
+
+def p2p_s(nbytes, lk: Link):
+    return nbytes / (lk.p2p_gbs * 1e9) + lk.latency_us * 1e-6
+
+
+class StageCompute:
+    """Cached per-micro-batch compute time (s) for a tp degree and micro-batch size."""
+
+    def __init__(self, cfg, seq, machine, shape_times=None, path="native"):
+        self.cfg, self.seq, self.m, self.st, self.path = cfg, seq, machine, shape_times or {}, path
+        self._c = {}
+
+    def get(self, tp, mb, ckpt=False):
+        k = (tp, mb, ckpt)
+        if k not in self._c:
+            ops = inventory(self.cfg, mb, self.seq, self.path, tp=tp)
+            ops = [o for o in ops if o.phase != "opt"]
+            p = predict(ops, self.m, self.st)
+            bwd = sum(o["ms"] for o in p.ops if o["phase"] == "bwd") / 1e3
+            tot = p.total_ms / 1e3
+            fwd = tot - bwd
+            self._c[k] = (tot + (fwd if ckpt else 0.0), bwd + (fwd if ckpt else 0.0))
+        return self._c[k]
+
+
+def evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp: StageCompute, links, system, ckpt=False, fused_tp=True,
+             overlap_dp=True, overlap_pp=True):
+    if dp * tp * pp != n or G % (dp * mb) or cfg.L % pp or cfg.H % tp or cfg.kvh % tp:
+        return None
+    m = G // (dp * mb)
+    if m < pp and pp > 1:
+        return None
+    sysd = links["systems"][system]
+    g = sysd["gpus_per_node"]
+    intra, inter = link(links, sysd["intra"]), link(links, sysd["inter"])
+    if tp > g:
+        return None
+    total, _ = count_params(cfg)
+    p_gpu = total / (tp * pp)
+    in_flight = min(m, pp)
+    act_c = links["activation_bytes_per_token_per_layer_per_d_ckpt" if ckpt else "activation_bytes_per_token_per_layer_per_d"]
+    act = act_c * cfg.d * seq * mb * (cfg.L / pp) * in_flight / tp
+    mem = p_gpu * (4 + 4 + 2) + p_gpu * 8 / dp + act
+    if mem > 0.9 * sysd["gpu_memory_gb"] * 1e9:
+        return None
+    t_mb, t_mb_bwd = comp.get(tp, mb, ckpt)
+    t_stage, t_stage_bwd = t_mb / pp, t_mb_bwd / pp
+    act_bytes = mb * seq * cfg.d * 2
+    tp_link = intra
+    t_tp_raw = 8 * (cfg.L / pp) * reduce_scatter_s(act_bytes, tp, tp_link) if tp > 1 else 0.0
+    t_tp = max(0.0, t_tp_raw - 0.8 * t_stage) if fused_tp else t_tp_raw
+    pp_link = intra if tp * pp <= g else inter
+    t_send = p2p_s(act_bytes, pp_link) if pp > 1 else 0.0
+    slots = m + pp - 1
+    t_pipe = slots * (t_stage + t_tp + (0.0 if overlap_pp else 2 * t_send)) + (2 * t_send * pp if overlap_pp else 0.0)
+    g_dp = max(1, g // (tp * pp)) if tp * pp < g else 1
+    t_dp = hier(reduce_scatter_s, p_gpu * 4, dp, g_dp, intra, inter) + hier(reduce_scatter_s, p_gpu * 2, dp, g_dp, intra, inter)
+    hidden = min(t_dp, t_stage_bwd) if overlap_dp else 0.0
+    t_opt = (p_gpu / dp) * 34 / (comp.m.hbm_gbs * 1e9)
+    step = t_pipe + (t_dp - hidden) + t_opt
+    tokens = G * seq
+    mfu = model_flops_per_token(cfg, seq) * tokens / step / n / (comp.m.bf16_tflops * 1e12)
+    return {"dp": dp, "tp": tp, "pp": pp, "mb": mb, "m": m, "ckpt": ckpt, "step_s": step, "tokens_per_s": tokens / step,
+            "mfu": mfu, "mem_gb": mem / 1e9,
+            "breakdown_s": {"compute": m * t_stage, "pipeline bubble": (pp - 1) * t_stage, "tp comm (exposed)": slots * t_tp,
+                            "pp sends": (2 * t_send * pp if overlap_pp else slots * 2 * t_send),
+                            "dp comm (exposed)": t_dp - hidden, "optimizer": t_opt}}
+
+
+def divisors(x, cap):
+    return [d for d in range(1, min(x, cap) + 1) if x % d == 0]
+
+
+def all_layouts(cfg, seq, G, n, comp, links, system, restrict=None, **kw):
+    out = []
+    for tp in (1, 2, 4, 8):
+        for pp in divisors(cfg.L, 64):
+            if n % (tp * pp):
+                continue
+            dp = n // (tp * pp)
+            for mb in (1, 2, 4, 8, 16):
+                for ck in (False, True):
+                    if restrict and not restrict(dp, tp, pp, mb):
+                        continue
+                    r = evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp, links, system, ck, **kw)
+                    if r:
+                        out.append(r)
+    return sorted(out, key=lambda r: -r["tokens_per_s"])
+
+
+def search(cfg, seq, G, n, comp, links, system, **kw):
+    rows = all_layouts(cfg, seq, G, n, comp, links, system, **kw)
+    return rows[0] if rows else None
+
+
+def layout_str(r):
+    return f"dp{r['dp']} tp{r['tp']} pp{r['pp']} mb{r['mb']}" + (" ckpt" if r["ckpt"] else "")
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--models", default="medium,llama3-8b")
+    ap.add_argument("--gpus", default="8,64,1024")
+    ap.add_argument("--system", default="b200_nvl8_ib")
+    ap.add_argument("--links", default=None)
+    ap.add_argument("--shape-times", default=None)
+    ap.add_argument("--show-top", type=int, default=1)
+    ap.add_argument("--layout", default=None, help="evaluate one layout, e.g. 'dp2,tp2,pp2,mb1' (needs one --gpus)")
+    ap.add_argument("--global-batch", type=int, default=None)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args()
+    links = load_links(args.links)
+    m = Machine.from_peaks()
+    st = load_shape_times(args.shape_times)
+    res = []
+    for name in args.models.split(","):
+        size, seq, G = WORKLOADS[name]
+        G = args.global_batch or G
+        cfg = SIZES[size]
+        comp = StageCompute(cfg, seq, m, st)
+        for n in (int(x) for x in args.gpus.split(",")):
+            if args.layout:
+                kv = dict((p[:2], int(p[2:])) for p in args.layout.split(","))
+                r = evaluate(cfg, seq, G, n, kv["dp"], kv["tp"], kv["pp"], kv["mb"], comp, links, args.system)
+                rows = [r] if r else []
+            else:
+                rows = all_layouts(cfg, seq, G, n, comp, links, args.system)[: args.show_top]
+            for r in rows:
+                print(f"{name:10s} {n:5d} GPUs  {layout_str(r):22s} {r['step_s'] * 1e3:9.2f} ms "
+                      f"{r['tokens_per_s'] / 1e6:8.3f} M tok/s  MFU {100 * r['mfu']:5.1f}%  mem {r['mem_gb']:.1f} GB")
+                res.append({"model": name, "gpus": n, **r})
+            if not rows:
+                print(f"{name:10s} {n:5d} GPUs  no layout fits")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(res, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

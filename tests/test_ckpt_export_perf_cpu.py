@@ -1,0 +1,122 @@
+"""CPU tests: Chakra export checks, perf-model consistency, scaling model, checkpoint layout."""
+import math
+import os
+import sys
+
+import pytest
+import torch
+
+from llmt.config import SIZES, get_config, model_flops_per_token
+from llmt.export import chakra as ck
+from llmt.export import trace
+from llmt.perf import roofline, scaling
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_chakra_node_roundtrip(tmp_path):
+    nodes = [{"id": 0, "name": "gemm", "type": ck.COMP_NODE, "data_deps": [], "ctrl_deps": [], "duration_micros": 7,
+              "inputs": {"shapes": "[[4, 4]]"}, "outputs": {"shapes": "[[4, 4]]"},
+              "attrs": [("num_ops", "int64_val", 123), ("tensor_size", "uint64_val", 2 ** 40), ("is_cpu_op", "bool_val", False)]},
+             {"id": 1, "name": "rs", "type": ck.COMM_COLL_NODE, "data_deps": [0], "ctrl_deps": [],
+              "attrs": [("comm_type", "int64_val", ck.REDUCE_SCATTER), ("comm_size", "int64_val", 4096),
+                        ("pg_name", "string_val", "3"), ("neg", "int64_val", -5)]}]
+    p = tmp_path / "w.et"
+    ck.write_et(p, nodes, [("rank", "int64_val", 0)])
+    meta, got = ck.read_et(p)
+    assert meta["version"] == ck.SCHEMA_VERSION
+    assert [n["id"] for n in got] == [0, 1]
+    assert got[1]["data_deps"] == [0]
+    assert ck.attr(got[0], "tensor_size") == 2 ** 40
+    assert ck.attr(got[1], "neg") == -5
+    assert ck.attr(got[1], "pg_name") == "3"
+
+
+@pytest.mark.parametrize("dp,tp,pp,m", [(2, 2, 2, 4), (1, 1, 4, 8), (4, 2, 1, 2)])
+def test_export_graph_checks(tmp_path, dp, tp, pp, m):
+    cfg = SIZES["tiny"]
+    graphs, table = trace.export(cfg, 2, 256, dp, tp, pp, m, str(tmp_path))
+    g = trace.check_graphs(graphs, table)
+    assert g["pass"], g["errors"]
+    assert trace.cross_check(cfg, 2, 256, dp, tp, pp, m, graphs)["pass"]
+    assert trace.check_roundtrip(graphs, str(tmp_path))["pass"]
+    if pp > 1:
+        assert g["send_recv_pairs"] == 2 * (pp - 1) * m * dp * tp
+    kinds = {ck.attr(n, "comm_type") for n in ck.read_et(tmp_path / "workload.0.et")[1] if n["type"] == ck.COMM_COLL_NODE}
+    if dp > 1:
+        assert ck.REDUCE_SCATTER in kinds and ck.ALL_GATHER in kinds
+
+
+def test_schedule_1f1b_covers_all_microbatches():
+    for p in (1, 2, 4):
+        for s in range(p):
+            order = trace.schedule_1f1b(s, p, 6)
+            assert sorted(i for k, i in order if k == "F") == list(range(6))
+            assert sorted(i for k, i in order if k == "B") == list(range(6))
+            # a backward never precedes its forward
+            pos = {(k, i): j for j, (k, i) in enumerate(order)}
+            assert all(pos[("F", i)] < pos[("B", i)] for i in range(6))
+
+
+def test_native_inventory_matmul_flops_match_model_flops():
+    """GEMM FLOPs of the native inventory = 6 x matmul params x tokens + the recomputed lm head."""
+    cfg = SIZES["medium"]
+    B, T = 4, 1024
+    ops = roofline.inventory(cfg, B, T, "native")
+    gemm = sum(o.total_flops for o in ops if o.cat in ("matmul", "loss"))
+    att = sum(o.total_flops for o in ops if o.cat == "attention")
+    N = B * T
+    head_recompute = 2.0 * N * cfg.vocab * cfg.d
+    norm_params = 2 * cfg.d * cfg.L + cfg.d  # counted by the reference's "matmul params", not GEMMs
+    assert math.isclose(gemm - head_recompute,
+                        model_flops_per_token(cfg, T) * N - 12 * cfg.L * cfg.d * T * N - 6 * norm_params * N,
+                        rel_tol=1e-9)
+    # causal attention: fwd 2 + bwd 5 = 7 B H T^2 hd per layer (the 12 L d T term counts full attention)
+    assert math.isclose(att, 7.0 * B * cfg.H * T * T * cfg.hd * cfg.L, rel_tol=1e-9)
+
+
+def test_predict_paths_ordering():
+    cfg = SIZES["medium"]
+    m = roofline.Machine.from_peaks()
+    t = {p: roofline.predict(roofline.inventory(cfg, 4, 1024, p), m, graph=(p == "native")).total_ms
+         for p in ("native", "triton", "eager")}
+    assert t["native"] < t["triton"] < t["eager"]
+
+
+def test_scaling_model_layouts():
+    cfg = SIZES["medium"]
+    links = scaling.load_links()
+    comp = scaling.StageCompute(cfg, 1024, roofline.Machine.from_peaks())
+    r = scaling.evaluate(cfg, 1024, 16, 8, 2, 2, 2, 1, comp, links, "b200_nvl8_ib")
+    assert r is not None and r["step_s"] > 0 and 0 < r["mfu"] < 1
+    assert scaling.evaluate(cfg, 1024, 16, 8, 3, 1, 1, 1, comp, links, "b200_nvl8_ib") is None  # 3 x 1 x 1 != 8
+    best = scaling.search(cfg, 1024, 512, 64, comp, links, "b200_nvl8_ib")
+    assert best and best["dp"] * best["tp"] * best["pp"] == 64
+    # more GPUs never lower the aggregate throughput of the best layout here
+    b8 = scaling.search(cfg, 1024, 512, 8, comp, links, "b200_nvl8_ib")
+    assert best["tokens_per_s"] > b8["tokens_per_s"]
+
+
+def test_checkpoint_file_loads_into_reference_model(tmp_path):
+    """A gathered checkpoint's model state_dict has exactly the reference keys and loads there."""
+    from llmt.ckpt import checkpoint
+    from llmt.models.llama import build_model
+    cfg = get_config("tiny256")
+    m = build_model(cfg, 128, seed=3)
+    path = str(tmp_path / "ck.pt")
+    checkpoint.save(path, m, meta={"step": 7})
+    ck_ = torch.load(path)
+    assert ck_["meta"]["step"] == 7
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref, "bench_train.py")):
+        pytest.skip("reference not installed under baseline/_ref")
+    sys.path.insert(0, ref)
+    import bench_train as bt
+    r = bt.LlamaModel(bt.ModelConfig(d=cfg.d, L=cfg.L, H=cfg.H, ffn=cfg.ffn), 128)
+    r.load_state_dict(ck_["model"])
+    for k, v in r.state_dict().items():
+        assert torch.equal(v, m.state_dict()[k])
+    m2 = build_model(cfg, 128, seed=9)
+    checkpoint.load(path, m2)
+    for k, v in m2.state_dict().items():
+        assert torch.equal(v, m.state_dict()[k])
