@@ -1,0 +1,156 @@
+"""Machine calibration on this GPU (reference: bench_train.py:346-433, roofline.py:419-467).
+
+Measures, with CUDA events after warm-up: dense matmul throughput per precision at 8192^3
+(torch/cuBLAS for fp32, tf32, fp16, bf16; torch._scaled_mm for fp8 e4m3; this framework's
+tcgen05 GEMM for bf16), a 1 GiB device copy (HBM bandwidth, read + write bytes), an L2-resident
+copy, the CPU launch cost of an eager kernel and the GPU gap between kernels replayed from a
+CUDA graph. Under torchrun with 2+ ranks it adds NVLink probes: a peer copy between rank 0 and
+rank 1 and the NCCL all-reduce bus bandwidth at 1 GiB. Never records the product name.
+
+    python -m llmt.bench.calibrate --label b200 [--out results/calibration_b200.json]
+    torchrun --nproc-per-node 8 -m llmt.bench.calibrate --links --out results/links_b200.json
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import time
+
+import torch
+
+
+def _time(fn, warmup=3, iters=20, repeats=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(repeats):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b) / 1e3 / iters)
+    return best
+
+
+def env_info(label):
+    p = torch.cuda.get_device_properties(0)
+    major, minor = torch.cuda.get_device_capability()
+    return {"arch": f"sm_{major}{minor}", "label": label, "torch": torch.__version__, "cuda": torch.version.cuda,
+            "os": platform.platform(), "gpu_count": torch.cuda.device_count(), "sm_count": p.multi_processor_count,
+            "gpu_mem_gb": round(p.total_memory / 1e9, 1)}
+
+
+def matmul_tflops(precision, n=8192):
+    flops = 2.0 * n ** 3
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        if precision in ("fp32", "tf32"):
+            torch.backends.cuda.matmul.allow_tf32 = precision == "tf32"
+            a, b = torch.randn(n, n, device="cuda"), torch.randn(n, n, device="cuda")
+            fn = lambda: a @ b  # noqa: E731
+        elif precision in ("fp16", "bf16"):
+            dt = torch.float16 if precision == "fp16" else torch.bfloat16
+            a, b = torch.randn(n, n, device="cuda", dtype=dt), torch.randn(n, n, device="cuda", dtype=dt)
+            fn = lambda: a @ b  # noqa: E731
+        elif precision == "fp8":
+            a = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
+            b = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn).t()
+            one = torch.tensor(1.0, device="cuda")
+            fn = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)  # noqa: E731
+        elif precision == "bf16_llmt":
+            from llmt.ops import native as N
+            a = torch.randn(n, n, device="cuda").bfloat16()
+            b = torch.randn(n, n, device="cuda").bfloat16()
+            out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
+            fn = lambda: N.gemm(a, b, out=out)  # noqa: E731
+        else:
+            raise ValueError(precision)
+        sec = _time(fn)
+        return {"status": "ok", "tflops": round(flops / sec / 1e12, 1), "ms": round(sec * 1e3, 3)}
+    except Exception as e:  # noqa: BLE001 - keep calibrating the other precisions
+        return {"status": "error", "error": f"{type(e).__name__}: {e}"[:300]}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+        torch.cuda.empty_cache()
+
+
+def copy_gbs(nbytes=1 << 30):
+    src = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst = torch.empty_like(src)
+    sec = _time(lambda: dst.copy_(src), iters=10)
+    return round(2 * nbytes / sec / 1e9, 1)
+
+
+def graph_gap_us(n=1000):
+    from llmt.perf.validate import measure_gap_us
+    return round(measure_gap_us(n), 3)
+
+
+def launch_us():
+    x = torch.zeros(1, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(2000):
+        x.add_(1.0)
+    t1 = time.perf_counter()
+    torch.cuda.synchronize()
+    return round((t1 - t0) / 2000 * 1e6, 2)
+
+
+def calibrate(label):
+    info = env_info(label)
+    mm = {p: matmul_tflops(p) for p in ("fp32", "tf32", "fp16", "bf16", "fp8", "bf16_llmt")}
+    return {**info, "time": time.strftime("%Y-%m-%d %H:%M:%S"), "matmul": mm, "hbm_gbs": copy_gbs(),
+            "l2_copy_gbs": copy_gbs(16 << 20), "launch_overhead_us": launch_us(), "gpu_gap_us": graph_gap_us()}
+
+
+def link_probes():
+    import datetime
+
+    import torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    out = {"world": world}
+    n = 1 << 30
+    x = torch.ones(n // 2, dtype=torch.bfloat16, device="cuda")
+    sec = _time(lambda: dist.all_reduce(x), warmup=2, iters=5, repeats=2)
+    out["nccl_allreduce_busbw_gbs"] = round(2 * (world - 1) / world * n / sec / 1e9, 1)
+    y = torch.empty(n // world, dtype=torch.uint8, device="cuda")
+    z = torch.empty(n, dtype=torch.uint8, device="cuda")
+    sec = _time(lambda: dist.reduce_scatter_tensor(y, z), warmup=2, iters=5, repeats=2)
+    out["nccl_reduce_scatter_busbw_gbs"] = round((world - 1) / world * n / sec / 1e9, 1)
+    dist.barrier()
+    if rank == 0 and world >= 2 and torch.cuda.device_count() >= 2:
+        a = torch.empty(n, dtype=torch.uint8, device="cuda:0")
+        b = torch.empty(n, dtype=torch.uint8, device="cuda:1")
+        sec = _time(lambda: b.copy_(a, non_blocking=True), warmup=2, iters=5, repeats=2)
+        out["p2p_copy_gbs"] = round(n / sec / 1e9, 1)
+    dist.barrier()
+    dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--label", default="b200")
+    ap.add_argument("--links", action="store_true", help="NVLink / NCCL probes (run under torchrun)")
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+    res = link_probes() if args.links else calibrate(args.label)
+    if res is None:
+        return
+    print(json.dumps(res, indent=1))
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump(res, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -15,6 +15,7 @@ runs every GEMM in bf16 with fp32 accumulation, and never materializes logits.
 from __future__ import annotations
 
 import torch
+import torch.utils.checkpoint
 
 from llmt.models.llama import LlamaModel
 from llmt.ops import functions as Fn
@@ -97,8 +98,9 @@ class NativeLlama:
 
     A plain wrapper (not an nn.Module), so model.state_dict() keeps the reference keys."""
 
-    def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1):
+    def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False):
         self.model = model
+        self.ckpt = ckpt
         self.cfg = model.cfg
         dev = model.emb.weight.device
         if dev.type != "cuda":
@@ -114,16 +116,24 @@ class NativeLlama:
         x = Fn.Embed.apply(idx.reshape(-1), m.emb.weight)
         a, r = None, x
         for blk in m.blocks:
-            if a is None:
-                n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
+            if self.ckpt and torch.is_grad_enabled():
+                # per-block recompute (reference bench_train.py:217-218): keep only the block input
+                a, r = torch.utils.checkpoint.checkpoint(self._block, blk, a, r, cos, sin, B, T, use_reentrant=False,
+                                                      preserve_rng_state=False)
             else:
-                n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
-            o = Fn.QKVAttention.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
-            att = Fn.Linear.apply(o, blk.attn.wo.weight)
-            n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
-            a = Fn.SwiGLUMLP.apply(n2, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn)
-            r = s2
+                a, r = self._block(blk, a, r, cos, sin, B, T)
         h = Fn.FinalNormFn.apply(a, r, m.norm_f.weight, cfg.eps)
         return Fn.HeadCE.apply(h, m.head.weight, targets.reshape(-1), self.ce_chunk)
+
+    def _block(self, blk, a, r, cos, sin, B, T):
+        cfg = self.cfg
+        if a is None:
+            n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
+        else:
+            n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+        o = Fn.QKVAttention.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
+        att = Fn.Linear.apply(o, blk.attn.wo.weight)
+        n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+        return Fn.SwiGLUMLP.apply(n2, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn), s2
 
     __call__ = forward

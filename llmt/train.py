@@ -24,14 +24,14 @@ from llmt.optim.adamw import FusedAdamW
 
 class Trainer:
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
-                 cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192):
+                 cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False):
         self.cfg, self.batch, self.seq = cfg, batch, seq
         self.device = torch.device(device)
         self.microbatches = microbatches
         self.dp = dp
         self.model = build_model(cfg, seq, seed=seed, device=self.device)
         pad_to = dp.world_size if dp is not None else 1
-        self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to)
+        self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
         flat = self.net.flat
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
