@@ -51,7 +51,13 @@ namespace gemm_detail {
 using namespace sm100;
 
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+// sigmoid on the SFU: 2^(-x log2 e) and a reciprocal, both approximate hardware ops
+__device__ __forceinline__ float sigm(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
+  return r;
+}
 
 __device__ __forceinline__ void load_bf16x32(const bf16* src, float* v, int col0, int N) {
 #pragma unroll
