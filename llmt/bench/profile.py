@@ -8,6 +8,7 @@ reference's classifier (profile_step.py:44-68) with attention matched before mat
 framework carry bucket keywords (gemm_*, flash_*, adamw_*, *rmsnorm*, dp_* / nccl).
 
     python -m llmt.bench.profile --size medium --batch 4 --seq 1024 [--graph] [--json out.json]
+    python -m llmt.bench.profile --impl reference --ref-row "5 + torch.compile"   # a reference row
 Profiler numbers are for the breakdown only (shares); the clean step time is the figure.
 """
 from __future__ import annotations
@@ -102,6 +103,20 @@ def profile_step(step, prof_steps=3, top=25):
     }
 
 
+def reference_step(size, batch, seq, row_name):
+    """One training step of a reference ladder row, built by the installed reference's own
+    build() (bench_train.py:436-500) from baseline/_ref."""
+    import os
+    import sys
+    ref = os.path.join(os.path.dirname(__file__), "..", "..", "baseline", "_ref")
+    sys.path.insert(0, os.path.abspath(ref))
+    import bench_train as bt
+    row = dict(bt.LADDER)[row_name]
+    run = dict(name=row_name, size=size, batch=batch, seq=seq, ckpt=False, nvtx=False, lr=3e-4, **row)
+    _, _, step = bt.build(bt.SIZES[size], run, device="cuda")
+    return step
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--size", default="medium")
@@ -111,19 +126,26 @@ def main():
     p.add_argument("--prof-steps", type=int, default=3)
     p.add_argument("--top", type=int, default=25)
     p.add_argument("--json", default=None)
+    p.add_argument("--impl", default="native", choices=["native", "reference"])
+    p.add_argument("--ref-row", default="5 + torch.compile", help="reference ladder row for --impl reference")
     args = p.parse_args()
-    from llmt.config import get_config
-    from llmt.models.llama import make_batch
-    from llmt.train import Trainer
-    cfg = get_config(args.size)
-    tr = Trainer(cfg, args.batch, args.seq, cuda_graph=args.graph)
-    idx, tgt = make_batch(args.batch, args.seq, cfg.vocab, "cuda")
-    tr.set_batch(idx, tgt)
-    ms = clean_ms(tr.run_step)
-    res = profile_step(tr.run_step, args.prof_steps, args.top)
+    if args.impl == "reference":
+        step = reference_step(args.size, args.batch, args.seq, args.ref_row)
+    else:
+        from llmt.config import get_config
+        from llmt.models.llama import make_batch
+        from llmt.train import Trainer
+        cfg = get_config(args.size)
+        tr = Trainer(cfg, args.batch, args.seq, cuda_graph=args.graph)
+        idx, tgt = make_batch(args.batch, args.seq, cfg.vocab, "cuda")
+        tr.set_batch(idx, tgt)
+        step = tr.run_step
+    ms = clean_ms(step)
+    res = profile_step(step, args.prof_steps, args.top)
     res["clean_ms_per_step"] = ms
     res["idle_pct"] = round(100.0 * (1 - res["busy_ms_per_step"] / ms), 2) if ms > 0 else None
-    res["config"] = {"size": args.size, "batch": args.batch, "seq": args.seq, "graph": args.graph}
+    res["config"] = {"size": args.size, "batch": args.batch, "seq": args.seq, "graph": args.graph,
+                     "impl": args.impl, **({"ref_row": args.ref_row} if args.impl == "reference" else {})}
     print(f"clean step {ms:.3f} ms | GPU kernel time {res['gpu_ms_per_step']:.3f} ms | "
           f"launches/step {res['launches_per_step']:.0f} | idle {res['idle_pct']}%")
     for b, v in res["buckets_pct"].items():
