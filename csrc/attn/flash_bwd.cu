@@ -50,8 +50,6 @@ __device__ __forceinline__ uint32_t sw_unit(int r, int u) {
   return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
 }
 
-__device__ __forceinline__ void named_bar_compute() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
 template <int HD>
 struct BwdSmem {
   static constexpr int STAGES = HD == 64 ? 2 : 1;
@@ -332,6 +330,296 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
   }
 }
 
+// ---------------------------------------------------------------- pipelined kernel (hd = 64)
+// Same math as flash_bwd_kernel, software-pipelined over the query blocks of a CTA so the
+// tensor core and the compute warps overlap:
+//   MMA warp, step n:  wait P/dS(n) -> S^T, dP^T of block n+1 -> dV, dK += ... (n)
+//                      -> wait dQ(n-1) drained -> dQ(n)
+//   compute warps:     P, dS of block n (S^T/dP^T(n) already in TMEM) -> drain dQ(n-1)
+// so block n+1's S^T/dP^T and block n's dV/dK/dQ run while the compute warps turn block
+// n+1 into P/dS. P and dS are double-buffered in shared memory; dQ leaves TMEM one block
+// late as vector fp32 reductions straight from registers (red.global.add.v4.f32), with no
+// staging buffer. TMEM: S^T 0-127, dP^T 128-255, dV 256-319, dK 320-383, dQ 384-447.
+struct BwdSmemP {
+  static constexpr uint32_t TILE = 128 * 64 * 2;  // one 128 x 64 bf16 tile (16 KB)
+  static constexpr uint32_t K_OFF = 0;
+  static constexpr uint32_t V_OFF = K_OFF + TILE;
+  static constexpr uint32_t Q_OFF = V_OFF + TILE;         // 2 stages
+  static constexpr uint32_t DO_OFF = Q_OFF + 2 * TILE;    // 2 stages
+  static constexpr uint32_t P_OFF = DO_OFF + 2 * TILE;    // 2 buffers of 128 x 128 bf16
+  static constexpr uint32_t DS_OFF = P_OFF + 2 * 32768;   // 2 buffers
+  static constexpr uint32_t VEC_OFF = DS_OFF + 2 * 32768; // per stage: lse (128) + D (128) floats
+  static constexpr uint32_t BAR_OFF = VEC_OFF + 2 * 1024;
+  static constexpr uint32_t TOTAL = BAR_OFF + 256;        // the base must be 1024-aligned (checked)
+};
+static_assert(BwdSmemP::TOTAL <= 232448, "pipelined attention backward exceeds 227 KB of shared memory");
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                           const AttnBwdArgs a) {
+  using L = BwdSmemP;
+  constexpr int HD = 64;
+  constexpr int TMEM_COLS = 512;
+  constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // the layout has no slack for realignment
+    if (threadIdx.x == 0) atomicCAS(a.err, 0, 40);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;     // [2]
+  uint64_t* q_empty = bars + 3;    // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* pds_full = bars + 6;   // 256 arrivals
+  uint64_t* pds_empty = bars + 7;  // [2]
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_free = bars + 10;   // 256 arrivals
+  uint64_t* dkv_full = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bk = blockIdx.x;  // b * KV + kv head
+  const int kb = blockIdx.y;  // key block: y = 0 (most query blocks under causal) launches first
+  const int b = bk / a.KV, kvh = bk % a.KV;
+  const int group = a.H / a.KV;
+  const int nqb = (int)cdiv(a.T, kBN);
+  const int i_start = a.causal ? kb : 0;
+  const int n_i = nqb - i_start;
+  const int n_items = group * n_i;
+  const int row0 = b * a.T;
+  const int k0 = kb * kBM;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    bar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      bar_init(&q_full[s], 1);
+      bar_init(&q_empty[s], 1);
+      bar_init(&pds_empty[s], 1);
+    }
+    bar_init(s_full, 1);
+    bar_init(pds_full, kComputeThreads);
+    bar_init(dq_full, 1);
+    bar_init(dq_free, kComputeThreads);
+    bar_init(dkv_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_qkv);
+      prefetch_tmap(&tm_do);
+      const int kcol = (a.H + kvh) * HD, vcol = (a.H + a.KV + kvh) * HD;
+      bar_arrive_expect_tx(kv_full, 2 * L::TILE);
+      tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, row0 + k0);
+      tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, row0 + k0);
+      for (int n = 0; n < n_items; ++n) {
+        const int s = n & 1;
+        const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
+        if (!wait_bar(&q_empty[s], ((n >> 1) & 1) ^ 1, err, 41)) break;
+        const int nq = min(kBN, a.T - i * kBN);
+        const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
+        bar_arrive_expect_tx(&q_full[s], 2 * L::TILE + 2 * vbytes);
+        const int64_t vbase = ((int64_t)b * a.H + hq) * a.T + (int64_t)i * kBN;
+        bulk_load(smem + L::VEC_OFF + s * 1024, a.lse + vbase, vbytes, &q_full[s]);
+        bulk_load(smem + L::VEC_OFF + s * 1024 + 512, a.dsum + vbase, vbytes, &q_full[s]);
+        tma_load_2d(smem + L::Q_OFF + s * L::TILE, &tm_qkv, &q_full[s], hq * HD, row0 + i * kBN);
+        tma_load_2d(smem + L::DO_OFF + s * L::TILE, &tm_do, &q_full[s], hq * HD, row0 + i * kBN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = make_idesc_bf16(kBM, kBN, false, false);  // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_bf16(kBM, HD, false, true);  // dV, dK (B MN-major)
+      constexpr uint32_t id_q = make_idesc_bf16(kBN, HD, true, true);    // dQ (A = dS MN-major)
+      const uint32_t k_addr = smem_u32(smem + L::K_OFF), v_addr = smem_u32(smem + L::V_OFF);
+      auto issue_sdp = [&](int s) {
+        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::TILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO_OFF + s * L::TILE);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          mma_f16(tmem + C_S, make_sw128_desc(k_addr + k * 32, 16, 1024), make_sw128_desc(q_addr + k * 32, 16, 1024),
+                  id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          mma_f16(tmem + C_DP, make_sw128_desc(v_addr + k * 32, 16, 1024), make_sw128_desc(do_addr + k * 32, 16, 1024),
+                  id_s, k > 0);
+        mma_commit(s_full);
+      };
+      bool ok = wait_bar(kv_full, 0, err, 42) && wait_bar(&q_full[0], 0, err, 43);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0);
+      }
+      for (int n = 0; n < n_items && ok; ++n) {
+        const int s = n & 1, pb = n & 1;
+        if (!wait_bar(pds_full, n & 1, err, 44)) { ok = false; break; }
+        tc_fence_after();
+        if (n + 1 < n_items) {  // S^T / dP^T columns were read out before pds_full arrived
+          if (!wait_bar(&q_full[(n + 1) & 1], ((n + 1) >> 1) & 1, err, 45)) { ok = false; break; }
+          issue_sdp((n + 1) & 1);
+        }
+        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::TILE);
+        const uint32_t do_addr = smem_u32(smem + L::DO_OFF + s * L::TILE);
+        const uint32_t p_addr = smem_u32(smem + L::P_OFF + pb * 32768);
+        const uint32_t ds_addr = smem_u32(smem + L::DS_OFF + pb * 32768);
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          const uint32_t offk = (k >> 2) * 16384 + (k & 3) * 32;  // K-major step over queries
+          const uint32_t offm = k * 2048;                          // MN-major step over queries
+          mma_f16(tmem + C_DV, make_sw128_desc(p_addr + offk, 16, 1024), make_sw128_desc(do_addr + offm, 16384, 1024),
+                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
+          mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024), make_sw128_desc(q_addr + offm, 16384, 1024),
+                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
+        }
+        if (n > 0 && !wait_bar(dq_free, (n - 1) & 1, err, 46)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBM / 16; ++k)  // contraction over keys
+          mma_f16(tmem + C_DQ, make_sw128_desc(ds_addr + k * 2048, 16384, 1024),
+                  make_sw128_desc(k_addr + k * 2048, 16384, 1024), id_q, k > 0);
+        mma_commit(dq_full);
+        mma_commit(&pds_empty[pb]);
+        mma_commit(&q_empty[s]);
+      }
+      if (ok) mma_commit(dkv_full);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // column half handled by this warp (2 warps per lane quadrant)
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
+    bool ok = true;
+    // dQ of step m: TMEM -> registers -> fp32 reductions into dq_acc (one query row per thread)
+    auto drain_dq = [&](int m) -> bool {
+      if (!wait_bar(dq_full, m & 1, err, 47)) return false;
+      tc_fence_after();
+      const int hq = kvh * group + m / n_i, qrow = (i_start + m % n_i) * kBN + quad * 32 + lane;
+      const int col = half * 32;
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_off + C_DQ + col, v);
+      tmem_wait_ld();
+      tc_fence_before();
+      bar_arrive(dq_free);
+      if (qrow < a.T) {
+        float* dst = a.dq_acc + (int64_t)(row0 + qrow) * a.ld_dq + hq * HD + col;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          red_add_v4(dst + 4 * u, __uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
+                     __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+      }
+      return true;
+    };
+    for (int n = 0; n < n_items && ok; ++n) {
+      const int pb = n & 1;
+      const int i = i_start + n % n_i;
+      const int qbase = i * kBN;
+      const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n & 1) * 1024);
+      const float* d_s = lse_s + 128;
+      if (!wait_bar(s_full, n & 1, err, 48)) { ok = false; break; }
+      if (!wait_bar(&pds_empty[pb], ((n >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
+      tc_fence_after();
+      uint8_t* pt = smem + L::P_OFF + pb * 32768;
+      uint8_t* dst = smem + L::DS_OFF + pb * 32768;
+      const bool diag = a.causal && (qbase < k0 + kBM);
+      const bool key_ok = kk < a.T;
+      const bool q_tail = qbase + kBN > a.T;  // columns past T hold stale lse / D: mask them
+#pragma unroll 1
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
+        tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
+        tmem_wait_ld();
+        float p[32], ds[32];
+        if (diag || !key_ok || q_tail) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qi = c * 32 + e;
+            const bool valid = key_ok && (!diag || qbase + qi >= kk) && qbase + qi < a.T;
+            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e)) : 0.f;
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qi = c * 32 + e;
+            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e));
+            p[e] = pe;
+            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          *reinterpret_cast<BF16x8*>(pt + sw_unit(r, c * 4 + u)) = float_to_bf16x8(p + u * 8);
+          *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      bar_arrive(pds_full);
+      if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
+    }
+    if (ok && n_items > 0) ok = drain_dq(n_items - 1);
+    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second
+    if (ok && wait_bar(dkv_full, 0, err, 50)) {
+      tc_fence_after();
+      float x[HD];
+      const uint32_t col = half == 0 ? C_DK : C_DV;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + col + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * (half == 0 ? a.scale : 1.f);
+      }
+      if (kk < a.T) {
+        if (half == 0) {
+          const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD);
+          const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD);
+#pragma unroll
+          for (int e4 = 0; e4 < HD / 8; ++e4) {
+            const float4 c1 = cr[e4], c2 = cr[e4 + HD / 8], s1 = sr[e4], s2 = sr[e4 + HD / 8];
+            const float cl[4] = {c1.x, c1.y, c1.z, c1.w}, ch[4] = {c2.x, c2.y, c2.z, c2.w};
+            const float sl[4] = {s1.x, s1.y, s1.z, s1.w}, sh[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e = e4 * 4 + j;
+              const float x1 = x[e], x2 = x[e + HD / 2];
+              x[e] = x1 * cl[j] + x2 * sh[j];
+              x[e + HD / 2] = x2 * ch[j] - x1 * sl[j];
+            }
+          }
+        }
+        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(x + c * 8);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<TMEM_COLS>(tmem);
+  }
+}
+
 // D = rowsum(dO * O) per (b, h, t); also zeroes the fp32 dQ accumulator row slice.
 // One thread per 8-wide chunk; the HD/8 threads of a (row, head) reduce with shuffles.
 template <int HD>
@@ -411,6 +699,21 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
   return cudaGetLastError();
 }
 
+cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args,
+                                 cudaStream_t st) {
+  constexpr size_t smem = BwdSmemP::TOTAL;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(flash_bwd_pipelined_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid(args.B * args.KV, (unsigned)cdiv(args.T, kBM));
+  flash_bwd_pipelined_kernel<<<grid, kBwdThreads, smem, st>>>(tq, tdo, args);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 // dqkv (B*T, ld_qkv) bf16 receives the gradient w.r.t. the packed *pre-RoPE* qkv rows.
@@ -457,7 +760,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
       make_tmap_2d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * hd, rows, (uint64_t)H * hd, 32, 32,
                    CU_TENSOR_MAP_SWIZZLE_128B);
   LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
-  cudaError_t e = hd == 64 ? launch_bwd<64>(tq, tdo, tdq, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
+  cudaError_t e = hd == 64 ? launch_bwd_pipelined(tq, tdo, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
   if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);

@@ -51,12 +51,13 @@ __device__ __forceinline__ bool bar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity. On timeout records `code` in *err
 // (first error wins) and returns false.
+// The timer is read once per 64 failed polls (try_wait itself blocks for a while each time).
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (bar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  while (true) {
+  for (uint32_t spin = 1;; ++spin) {
     if (bar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if ((spin & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

@@ -119,6 +119,22 @@ def bench_fused_gemm(cfg, B, T, rows):
     fl = 2.0 * tok * f * d
     rows.append(dict(op="gemm w2dgrad+swiglu_bwd", shape=f"{tok}x{f}x{d}", ms=round(ms, 4), ref_ms=None,
                      tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
+    # the same two steps as a plain GEMM followed by the standalone elementwise kernel
+    gu2 = torch.empty(tok, 2 * f, device="cuda", dtype=torch.bfloat16)
+    h2 = torch.empty(tok, f, device="cuda", dtype=torch.bfloat16)
+    ms = time_ms(lambda: N.swiglu_fwd(*N.gemm(x, w13, ta=False, tb=True, out=gu2).split(f, 1), h=h2))
+    fl = 2.0 * tok * 2 * f * d
+    rows.append(dict(op="gemm w13, then swiglu", shape=f"{tok}x{2 * f}x{d}", ms=round(ms, 4), ref_ms=None,
+                     tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
+
+    def unfused_bwd():
+        dh = N.gemm(dm, w2, ta=False, tb=False, out=h2)
+        g_, u_ = gu.split(f, 1)
+        N.swiglu_bwd(dh, g_, u_, dg=g_, du=u_)
+    ms = time_ms(unfused_bwd)
+    fl = 2.0 * tok * f * d
+    rows.append(dict(op="gemm w2dgrad, then swiglu_bwd", shape=f"{tok}x{f}x{d}", ms=round(ms, 4), ref_ms=None,
+                     tflops=round(fl / ms / 1e9, 1), ref_tflops=0.0, frac_peak=round(fl / ms / 1e9 / peak, 3)))
 
 
 def bench_attn(cfg, B, T, rows):

@@ -18,9 +18,16 @@ Regions (reference equivalents in bench_train.py / kernels/triton_ops.py):
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from llmt.ops import native as N
+
+# SwiGLU inside the GEMM epilogues (True) or as a separate elementwise kernel (False), per direction;
+# LLMT_SWIGLU_EPILOGUE="fwd,bwd" / "fwd" / "bwd" / "none" overrides the default.
+_sw = os.environ.get("LLMT_SWIGLU_EPILOGUE", "fwd,bwd")
+SWIGLU_EPILOGUE = {"fwd": "fwd" in _sw, "bwd": "bwd" in _sw}
 
 
 class Embed(torch.autograd.Function):
@@ -139,11 +146,19 @@ class Linear(torch.autograd.Function):
 
 
 class SwiGLUMLP(torch.autograd.Function):
-    """m = (silu(x W1^T) * (x W3^T)) W2^T with W1, W3 packed adjacently (one merged GEMM)."""
+    """m = (silu(x W1^T) * (x W3^T)) W2^T with W1, W3 packed adjacently (one merged GEMM).
+
+    SwiGLU runs either inside the GEMM epilogues (merged gate/up GEMM writes h and keeps [g | u];
+    the w2 dgrad writes [dg | du]) or as the standalone elementwise kernel after a plain GEMM;
+    SWIGLU_EPILOGUE selects per direction."""
 
     @staticmethod
     def forward(ctx, x, w1, w2, ffn):
-        h, gu = N.gemm_swiglu(x, w1.w13_16, ffn)
+        if SWIGLU_EPILOGUE["fwd"]:
+            h, gu = N.gemm_swiglu(x, w1.w13_16, ffn)
+        else:
+            gu = N.gemm(x, w1.w13_16, ta=False, tb=True)
+            h = N.swiglu_fwd(gu[:, :ffn], gu[:, ffn:])
         m = N.gemm(h, w2.w16, ta=False, tb=True)
         ctx.save_for_backward(x, h, gu)
         ctx.w1, ctx.w2, ctx.ffn = w1, w2, ffn
@@ -154,8 +169,15 @@ class SwiGLUMLP(torch.autograd.Function):
         x, h, gu = ctx.saved_tensors
         w1, w2, ffn = ctx.w1, ctx.w2, ctx.ffn
         dm = dm.contiguous()
-        dgu = N.gemm_swiglu_bwd(dm, w2.w16, gu, ffn)
-        _wgrad(dm, h, w2)
+        if SWIGLU_EPILOGUE["bwd"]:
+            dgu = N.gemm_swiglu_bwd(dm, w2.w16, gu, ffn)
+            _wgrad(dm, h, w2)
+        else:
+            _wgrad(dm, h, w2)
+            dh = N.gemm(dm, w2.w16, ta=False, tb=False, out=h)  # h is dead after the w2 wgrad
+            g, u = gu[:, :ffn], gu[:, ffn:]
+            N.swiglu_bwd(dh, g, u, dg=g, du=u)  # [dg | du] overwrite [g | u] in place
+            dgu = gu
         dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
         N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=True)
         return dx, None, None, None

@@ -68,3 +68,23 @@ def test_native_step_matches_reference_adamw():
     for (name, p_ref), p in zip(ref.named_parameters(), tr.model.parameters()):
         # one Adam step moves each weight by ~lr; compare the update directions
         assert rel_err(p.detach(), p_ref.detach()) < 5e-3, name
+
+
+@pytest.mark.parametrize("mode", [{"fwd": False, "bwd": False}, {"fwd": True, "bwd": False}, {"fwd": False, "bwd": True}])
+def test_swiglu_unfused_paths_match_fp32(mode, monkeypatch):
+    """The standalone-kernel SwiGLU paths give the same loss and gradients as the fp32 model."""
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.ops import functions
+    monkeypatch.setattr(functions, "SWIGLU_EPILOGUE", dict(mode))
+    cfg = get_config("tiny256")
+    ref, ours, net = _pair(cfg, 128)
+    idx, tgt = make_batch(2, 128, cfg.vocab, "cuda")
+    loss_ref = ref(idx, tgt)
+    loss_ref.backward()
+    loss = net(idx, tgt)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert abs(loss.item() - loss_ref.item()) / loss_ref.item() < 1e-2
+    for (name, p_ref), p in zip(ref.named_parameters(), ours.parameters()):
+        assert rel_err(p.main_grad, p_ref.grad) < 5e-2, name
