@@ -44,7 +44,15 @@ struct AttnBwdArgs {
   float scale, scale_log2;
   int causal;
   int* err;
+  long long* trace;  // optional event log of CTA (0, 0): 4 regions of 256 (clock64 << 8 | event id)
 };
+
+// Timestamped event of CTA (0, 0) into slot `region` of the trace (plain stores, no atomics).
+__device__ __forceinline__ void trace_at(long long* tr, int region, int& k, int id) {
+  if (tr == nullptr || blockIdx.x != 0 || blockIdx.y != 0) return;
+  if (k < 255) tr[region * 256 + k] = (clock64() << 8) | id;
+  ++k;
+}
 
 __device__ __forceinline__ uint32_t sw_unit(int r, int u) {
   return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
@@ -396,6 +404,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
   const int row0 = b * a.T;
   const int k0 = kb * kBM;
   int* err = a.err;
+  int tk = 0;  // trace slot of this thread
 
   if (threadIdx.x == 0) {
     bar_init(kv_full, 1);
@@ -419,6 +428,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 
   if (warp == 0) {
     if (lane == 0) {
+      trace_at(a.trace, 3, tk, 0);
       prefetch_tmap(&tm_qkv);
       prefetch_tmap(&tm_do);
       const int kcol = (a.H + kvh) * HD, vcol = (a.H + a.KV + kvh) * HD;
@@ -429,6 +439,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const int s = n & 1;
         const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
         if (!wait_bar(&q_empty[s], ((n >> 1) & 1) ^ 1, err, 41)) break;
+        trace_at(a.trace, 3, tk, 30);
         const int nq = min(kBN, a.T - i * kBN);
         const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
         bar_arrive_expect_tx(&q_full[s], 2 * L::TILE + 2 * vbytes);
@@ -466,9 +477,11 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
       for (int n = 0; n < n_items && ok; ++n) {
         const int s = n & 1, pb = n & 1;
         if (!wait_bar(pds_full, n & 1, err, 44)) { ok = false; break; }
+        trace_at(a.trace, 0, tk, 1);
         tc_fence_after();
         if (n + 1 < n_items) {  // S^T / dP^T columns were read out before pds_full arrived
           if (!wait_bar(&q_full[(n + 1) & 1], ((n + 1) >> 1) & 1, err, 45)) { ok = false; break; }
+          trace_at(a.trace, 0, tk, 2);
           issue_sdp((n + 1) & 1);
         }
         const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::TILE);
@@ -484,7 +497,9 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
           mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024), make_sw128_desc(q_addr + offm, 16384, 1024),
                   id_kv, (n > 0 || k > 0) ? 1u : 0u);
         }
+        trace_at(a.trace, 0, tk, 4);
         if (n > 0 && !wait_bar(dq_free, (n - 1) & 1, err, 46)) { ok = false; break; }
+        trace_at(a.trace, 0, tk, 5);
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kBM / 16; ++k)  // contraction over keys
@@ -493,6 +508,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         mma_commit(dq_full);
         mma_commit(&pds_empty[pb]);
         mma_commit(&q_empty[s]);
+        trace_at(a.trace, 0, tk, 6);
       }
       if (ok) mma_commit(dkv_full);
     }
@@ -502,10 +518,13 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
+    const bool tr_thread = lane == 0 && (warp == 2 || warp == 9);
+    const int tr_region = warp == 2 ? 1 : 2;
     bool ok = true;
     // dQ of step m: TMEM -> registers -> fp32 reductions into dq_acc (one query row per thread)
     auto drain_dq = [&](int m) -> bool {
       if (!wait_bar(dq_full, m & 1, err, 47)) return false;
+      if (tr_thread) trace_at(a.trace, tr_region, tk, 13);
       tc_fence_after();
       const int hq = kvh * group + m / n_i, qrow = (i_start + m % n_i) * kBN + quad * 32 + lane;
       const int col = half * 32;
@@ -530,6 +549,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
       const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n & 1) * 1024);
       const float* d_s = lse_s + 128;
       if (!wait_bar(s_full, n & 1, err, 48)) { ok = false; break; }
+      if (tr_thread) trace_at(a.trace, tr_region, tk, 10);
       if (!wait_bar(&pds_empty[pb], ((n >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
       tc_fence_after();
       uint8_t* pt = smem + L::P_OFF + pb * 32768;
@@ -569,10 +589,12 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
           *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
         }
       }
+      if (tr_thread) trace_at(a.trace, tr_region, tk, 12);
       tc_fence_before();
       fence_proxy_async_smem();
       bar_arrive(pds_full);
       if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
+      if (tr_thread) trace_at(a.trace, tr_region, tk, 14);
     }
     if (ok && n_items > 0) ok = drain_dq(n_items - 1);
     // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second
@@ -716,6 +738,12 @@ cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, 
 
 }  // namespace
 
+// Event tracing of the pipelined backward (for profiling): a zeroed device buffer of 1024
+// int64 (4 regions of 256 events of CTA (0, 0): MMA thread, compute warps 2 and 9, TMA
+// thread), or nullptr to turn it off.
+static long long* g_bwd_trace = nullptr;
+void attn_bwd_set_trace(long long* buf) { g_bwd_trace = buf; }
+
 // dqkv (B*T, ld_qkv) bf16 receives the gradient w.r.t. the packed *pre-RoPE* qkv rows.
 // dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
 cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
@@ -753,6 +781,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
   args.err = attn_err_word();
+  args.trace = hd == 64 ? g_bwd_trace : nullptr;
   alignas(64) CUtensorMap tq, tdo, tdq;
   const bool ok =
       make_tmap_2d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows, ld_qkv, 64, 128) &&

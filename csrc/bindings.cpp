@@ -378,6 +378,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
+  m.def("attn_bwd_set_trace", [](c10::optional<at::Tensor> buf) {
+    if (buf && buf->defined()) {
+      CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 1024,
+            "trace buffer: 1024 int64 on the GPU");
+      llmt::attn_bwd_set_trace(reinterpret_cast<long long*>(buf->data_ptr<int64_t>()));
+    } else {
+      llmt::attn_bwd_set_trace(nullptr);
+    }
+  }, "buf"_a = py::none());
   m.def("sm_count", &llmt::sm_count);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
