@@ -94,16 +94,23 @@ __global__ void rope_kernel(bf16* __restrict__ qkv, const float* __restrict__ co
   }
 }
 
+// W holds vocabulary rows [v0, v0 + V). With `partial` (a vocabulary-parallel shard) ids
+// outside that range give zero rows; otherwise they are an error (recorded, row 0 used).
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ W,
-                                     float* __restrict__ x, int64_t N, int d, int64_t V, int* __restrict__ err) {
+                                     float* __restrict__ x, int64_t N, int d, int64_t V, int64_t v0, bool partial,
+                                     int* __restrict__ err) {
   const int vpr = d / 4;
   const int64_t total = N * vpr;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i / vpr;
     const int c = (int)(i % vpr) * 4;
-    int64_t tok = idx[n];
-    if (tok < 0 || tok >= V) {  // record and clamp instead of reading out of bounds
-      if (err) atomicExch(err, 1);
+    int64_t tok = idx[n] - v0;
+    if (tok < 0 || tok >= V) {
+      if (partial) {
+        st_f4(x + n * d + c, make_float4(0.f, 0.f, 0.f, 0.f));
+        continue;
+      }
+      if (err) atomicExch(err, 1);  // record and clamp instead of reading out of bounds
       tok = 0;
     }
     st_f4(x + n * d + c, ld_f4(W + tok * d + c));
@@ -111,13 +118,13 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const floa
 }
 
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ dx,
-                                     float* __restrict__ dW, int64_t N, int d, int64_t V) {
+                                     float* __restrict__ dW, int64_t N, int d, int64_t V, int64_t v0) {
   const int vpr = d / 4;
   const int64_t total = N * vpr;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i / vpr;
     const int c = (int)(i % vpr) * 4;
-    const int64_t tok = idx[n];
+    const int64_t tok = idx[n] - v0;
     if (tok < 0 || tok >= V) continue;
     atomicAdd(reinterpret_cast<float4*>(dW + tok * d + c), ld_f4(dx + n * d + c));
   }
@@ -161,20 +168,21 @@ cudaError_t rope_inplace(void* qkv, const float* cos_t, const float* sin_t, int6
   return cudaGetLastError();
 }
 
-cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int* err,
-                          cudaStream_t st) {
+cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int64_t v0,
+                          bool partial, int* err, cudaStream_t st) {
   LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
   if (N == 0) return cudaSuccess;
-  embedding_fwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, W, x, N, d, V, err);
+  embedding_fwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, W, x, N, d, V, v0, partial, err);
   return cudaGetLastError();
 }
 
-// dW += scatter(dx by idx). The caller zeroes dW for the first micro-batch.
-cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V,
+// dW += scatter(dx by idx - v0); ids outside [v0, v0 + V) are skipped. The caller zeroes dW
+// for the first micro-batch.
+cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V, int64_t v0,
                           cudaStream_t st) {
   LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
   if (N == 0) return cudaSuccess;
-  embedding_bwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, dx, dW, N, d, V);
+  embedding_bwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, dx, dW, N, d, V, v0);
   return cudaGetLastError();
 }
 

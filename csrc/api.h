@@ -30,9 +30,11 @@ cudaError_t swiglu_bwd(const void* dh, int64_t lddh, const void* g, const void* 
                        int64_t lddgu, int64_t rows, int F, cudaStream_t st);
 cudaError_t rope_inplace(void* qkv, const float* cos_t, const float* sin_t, int64_t N, int T, int n_rot_heads, int hd,
                          int64_t ld, bool backward, cudaStream_t st);
-cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int* err,
-                          cudaStream_t st);
-cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V,
+// W holds vocabulary rows [v0, v0 + V); `partial` (a vocabulary-parallel shard) gives zero rows
+// for ids outside it instead of flagging them.
+cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t N, int d, int64_t V, int64_t v0,
+                          bool partial, int* err, cudaStream_t st);
+cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_t N, int d, int64_t V, int64_t v0,
                           cudaStream_t st);
 
 // ---------------------------------------------------------------- optimizer

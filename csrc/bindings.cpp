@@ -116,21 +116,23 @@ void rope_inplace(at::Tensor qkv, at::Tensor cos_t, at::Tensor sin_t, int64_t T,
      "rope_inplace");
 }
 
-void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at::Tensor> err) {
+void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at::Tensor> err, int64_t v0,
+                   bool partial) {
   CHECK_DT(idx, at::kLong);
   CHECK_DT(W, at::kFloat);
   CHECK(idx.is_contiguous() && W.is_contiguous() && x.is_contiguous(), "embedding operands must be contiguous");
   ok(llmt::embedding_fwd(idx.data_ptr<int64_t>(), W.data_ptr<float>(), x.data_ptr<float>(), idx.numel(), W.size(1),
-                         W.size(0), err.has_value() && err->defined() ? err->data_ptr<int>() : nullptr, stream()),
+                         W.size(0), v0, partial, err.has_value() && err->defined() ? err->data_ptr<int>() : nullptr,
+                         stream()),
      "embedding_fwd");
 }
 
-void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW) {
+void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW, int64_t v0) {
   CHECK_DT(dx, at::kFloat);
   CHECK_DT(dW, at::kFloat);
   CHECK(idx.is_contiguous() && dx.is_contiguous() && dW.is_contiguous(), "embedding grads must be contiguous");
   ok(llmt::embedding_bwd(idx.data_ptr<int64_t>(), dx.data_ptr<float>(), dW.data_ptr<float>(), idx.numel(), dW.size(1),
-                         dW.size(0), stream()),
+                         dW.size(0), v0, stream()),
      "embedding_bwd");
 }
 
@@ -362,8 +364,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("rope_inplace", &rope_inplace);
-  m.def("embedding_fwd", &embedding_fwd);
-  m.def("embedding_bwd", &embedding_bwd);
+  m.def("embedding_fwd", &embedding_fwd, "idx"_a, "W"_a, "x"_a, "err"_a = py::none(), "v0"_a = 0,
+        "partial"_a = false);
+  m.def("embedding_bwd", &embedding_bwd, "idx"_a, "dx"_a, "dW"_a, "v0"_a = 0);
   m.def("adamw_step", &adamw_step, "p"_a, "g"_a, "m"_a, "v"_a, "p16"_a, "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a,
         "wd"_a, "grad_scale"_a, "zero_grad"_a = false);
   m.def("cast_bf16", &cast_bf16);

@@ -21,10 +21,11 @@ class ModelConfig:
     eps: float = 1e-5
     rope_base: float = 10000.0
     kv_heads: int | None = None   # grouped-query attention; None means kv_heads == H
+    head_dim: int | None = None   # None means d // H (set for tensor-parallel shards, where H is local)
 
     @property
     def hd(self) -> int:
-        return self.d // self.H
+        return self.head_dim or self.d // self.H
 
     @property
     def kvh(self) -> int:

@@ -44,6 +44,23 @@ class Embed(torch.autograd.Function):
         return None, None
 
 
+class EmbedVP(torch.autograd.Function):
+    """Vocabulary-parallel embedding: rows for the ids in this shard [v0, v0 + V/tp), zeros
+    elsewhere (the reduce-scatter that follows sums the shards)."""
+
+    @staticmethod
+    def forward(ctx, idx, w, v0):
+        ctx.save_for_backward(idx)
+        ctx.w, ctx.v0 = w, v0
+        return N.embedding_fwd(idx, w, v0=v0, partial=True)
+
+    @staticmethod
+    def backward(ctx, dx):
+        (idx,) = ctx.saved_tensors
+        N.embedding_bwd(idx, dx.contiguous(), ctx.w.main_grad, v0=ctx.v0)
+        return None, None, None
+
+
 class RMSNormFn(torch.autograd.Function):
     """y = rmsnorm(x) * w on the fp32 residual x (no add); y bf16."""
 
@@ -181,6 +198,44 @@ class SwiGLUMLP(torch.autograd.Function):
         dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
         N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=True)
         return dx, None, None, None
+
+
+class HeadCEVP(torch.autograd.Function):
+    """Cross entropy over a vocabulary-parallel head (rows [v0, v0 + V/tp) on this rank).
+
+    Forward: the fused head GEMM reduces this shard's logit tiles to a per-row log-sum-exp and
+    target logit (targets shifted by v0; a target outside the shard contributes nothing); the
+    (N,) log-sum-exps of all shards are all-gathered and combined, the target logits summed.
+    Backward recomputes this shard's logits into bf16 (softmax - onehot) / N chunks and returns
+    the partial dh (the all-gather that produced h sums the shards' partials)."""
+
+    @staticmethod
+    def forward(ctx, h, w, targets, v0, group, chunk):
+        tl_targets = targets - v0
+        lse_l, _, tl = N.gemm_ce_fwd(h, w.w16, tl_targets, return_target_logit=True)
+        world = torch.distributed.get_world_size(group)
+        allse = torch.empty((world,) + tuple(lse_l.shape), dtype=lse_l.dtype, device=lse_l.device)
+        torch.distributed.all_gather_into_tensor(allse, lse_l, group=group)
+        lse = torch.logsumexp(allse, dim=0)
+        torch.distributed.all_reduce(tl, group=group)
+        ctx.save_for_backward(h, tl_targets, lse)
+        ctx.w, ctx.chunk = w, chunk
+        return (lse - tl).mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        h, targets, lse = ctx.saved_tensors
+        w, chunk = ctx.w, ctx.chunk
+        n = h.shape[0]
+        g = g.reshape(1).float().contiguous()
+        dh = torch.empty_like(h)
+        for c0 in range(0, n, chunk):
+            c1 = min(n, c0 + chunk)
+            hc = h[c0:c1]
+            dl = N.gemm_ce_bwd(hc, w.w16, targets[c0:c1], lse[c0:c1], g, 1.0 / n)
+            N.gemm(dl, w.w16, ta=False, tb=False, out=dh[c0:c1])
+            N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=True)
+        return dh, None, None, None, None, None
 
 
 class HeadCE(torch.autograd.Function):

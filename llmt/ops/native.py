@@ -156,8 +156,11 @@ def gemm_rope(x, wqkv, cos, sin, T, hd, rot_cols, out=None, bn=0):
     return out
 
 
-def gemm_ce_fwd(h, w, targets, bn=256):
-    """Logit tiles reduced in the epilogue: returns (lse fp32 (M,), loss fp32 (M,)); no logits written."""
+def gemm_ce_fwd(h, w, targets, bn=256, return_target_logit=False):
+    """Logit tiles reduced in the epilogue: returns (lse fp32 (M,), loss fp32 (M,)); no logits written.
+    Targets outside [0, V) contribute no target logit (their loss is 0): a vocabulary-parallel
+    shard passes targets shifted by its first row and combines lse / target logits across shards.
+    With return_target_logit the (M,) target logits (0 where the target is outside) come third."""
     M, V = h.shape[0], w.shape[0]
     nblk = -(-V // bn)
     part = torch.empty((M, nblk, 2), dtype=torch.float32, device=h.device)
@@ -167,7 +170,7 @@ def gemm_ce_fwd(h, w, targets, bn=256):
     lse = torch.empty((M,), dtype=torch.float32, device=h.device)
     loss = torch.empty((M,), dtype=torch.float32, device=h.device)
     ext().ce_combine(part, tl, targets, lse, loss, nblk, V)
-    return lse, loss
+    return (lse, loss, tl) if return_target_logit else (lse, loss)
 
 
 def gemm_ce_bwd(h, w, targets, lse, grad_out, scale, out=None, bn=0):
@@ -206,15 +209,18 @@ def rope_inplace(qkv2d, cos, sin, T, n_rot_heads, hd, backward=False):
     return qkv2d
 
 
-def embedding_fwd(idx, W, out=None):
+def embedding_fwd(idx, W, out=None, v0=0, partial=False):
+    """x[n] = W[idx[n] - v0]; W holds vocabulary rows [v0, v0 + W.shape[0]). With `partial`
+    (a vocabulary-parallel shard) ids outside that range give zero rows."""
     if out is None:
         out = torch.empty((idx.numel(), W.shape[1]), dtype=torch.float32, device=W.device)
-    ext().embedding_fwd(idx.reshape(-1), W, out, None)
+    ext().embedding_fwd(idx.reshape(-1), W, out, None, int(v0), bool(partial))
     return out
 
 
-def embedding_bwd(idx, dx, dW):
-    ext().embedding_bwd(idx.reshape(-1), dx, dW)
+def embedding_bwd(idx, dx, dW, v0=0):
+    """dW[idx[n] - v0] += dx[n] for ids inside the shard."""
+    ext().embedding_bwd(idx.reshape(-1), dx, dW, int(v0))
 
 
 def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0, zero_grad=False):

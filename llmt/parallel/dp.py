@@ -66,7 +66,8 @@ class DataParallel:
         opt = ShardedAdamW(flat, lo, hi, lr=lr, grad_scale=1.0 / self.world_size, **kw)
         # all ranks start from rank 0's weights (the same seed already makes them equal; this
         # makes it a guarantee)
-        dist.broadcast(flat.master, 0, group=self.group)
+        src = dist.get_global_rank(self.group, 0) if self.group is not None else 0
+        dist.broadcast(flat.master, src, group=self.group)
         flat.refresh_shadow()
         if self.mode == "fused":
             from llmt.parallel.fused_dp import FusedDP

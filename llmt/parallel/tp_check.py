@@ -1,0 +1,68 @@
+"""Multi-GPU numerics check of tensor + sequence parallelism (torchrun, one rank per GPU).
+
+All ranks form one tensor-parallel group and train the tiny256 model (sharded from the same
+seeded full model) on one batch; rank 0 also trains the unsharded model alone on that batch.
+After a few steps the shards' fp32 master weights are gathered, reassembled into the full
+layout and compared. Prints one JSON line; exit code 0 when within the bound.
+
+    torchrun --nproc-per-node 2 -m llmt.parallel.tp_check [--graph] [--kv-heads 2]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--graph", action="store_true")
+    p.add_argument("--kv-heads", type=int, default=None)
+    args = p.parse_args()
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.ops import native
+    from llmt.parallel.tp import unshard_state
+    from llmt.train import Trainer
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    cfg = get_config("tiny256", kv_heads=args.kv_heads)
+    B, T = 2, 128
+    idx, tgt = make_batch(B, T, cfg.vocab, "cpu", seed=0)
+    group = dist.new_group(list(range(world)))
+    tr = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=args.graph, tp_group=group)
+    losses = [tr.train_step(idx, tgt) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    codes = {"gemm": native.gemm_error_code(), "attn": native.attn_error_code()}
+    sd = {k: v.detach().float().contiguous() for k, v in tr.model.state_dict().items()}
+    gathered = [None] * world
+    dist.all_gather_object(gathered, {k: v.cpu() for k, v in sd.items()})
+    ok = True
+    if rank == 0:
+        full = unshard_state(gathered, cfg)
+        ref = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=False)
+        ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps)]
+        rsd = ref.model.state_dict()
+        num = sum(float((full[k].to(rsd[k].device) - rsd[k].float()).norm() ** 2) for k in rsd)
+        den = sum(float(rsd[k].float().norm() ** 2) for k in rsd)
+        rel = (num / den) ** 0.5
+        loss_gap = max(abs(a - b) for a, b in zip(losses, ref_losses))
+        ok = rel < 2e-3 and loss_gap < 2e-2 and all(v == 0 for v in codes.values())
+        print(json.dumps({"tp": world, "graph": args.graph, "kv_heads": cfg.kvh, "rel_err_master": rel,
+                          "losses": losses, "ref_losses": ref_losses, "error_codes": codes, "ok": ok}), flush=True)
+    tr.release()
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -23,15 +23,27 @@ from llmt.optim.adamw import FusedAdamW
 
 
 class Trainer:
+    """tp_group: tensor + sequence parallel group (the model is then this rank's shard, see
+    llmt.parallel.tp); dp: a DataParallel over the data-parallel group (ZeRO-1)."""
+
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
-                 cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False):
+                 cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False,
+                 tp_group=None, init: str = "full"):
         self.cfg, self.batch, self.seq = cfg, batch, seq
         self.device = torch.device(device)
         self.microbatches = microbatches
         self.dp = dp
-        self.model = build_model(cfg, seq, seed=seed, device=self.device)
+        self.tp_group = tp_group
         pad_to = dp.world_size if dp is not None else 1
-        self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
+        if tp_group is not None:
+            import torch.distributed as dist
+            from llmt.parallel.tp import TPNativeLlama, build_local_model
+            tp, r = dist.get_world_size(tp_group), dist.get_rank(tp_group)
+            self.model = build_local_model(cfg, seq, tp, r, seed=seed, device=self.device, init=init)
+            self.net = TPNativeLlama(self.model, tp_group, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
+        else:
+            self.model = build_model(cfg, seq, seed=seed, device=self.device)
+            self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
         flat = self.net.flat
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
@@ -55,6 +67,8 @@ class Trainer:
             loss = self.net(self.idx[i], self.tgt[i])
             (loss / self.microbatches).backward()
             total = loss.detach() if total is None else total + loss.detach()
+        if self.tp_group is not None:
+            self.net.sync_replicated_grads()
         if self.dp is not None:
             self.dp.reduce_and_step(self.opt)
         else:
