@@ -25,15 +25,22 @@ ALIGN = 64  # elements; keeps every view 256-byte (fp32) / 128-byte (bf16) align
 
 
 def param_order(model: LlamaModel):
-    """(name, parameter) in flat-buffer order: per block qkv, wo, w1, w3, w2, norms; then emb, norm_f, head."""
+    """(name, parameter) in flat-buffer order: per block qkv, wo, w1, w3, w2, norms; then emb, norm_f, head.
+
+    A pipeline stage (llmt.parallel.pp.StageModel) has only some blocks (named by their global
+    index, `block_offset`) and lacks emb or norm_f / head."""
     out = []
+    base = getattr(model, "block_offset", 0)
     for i, blk in enumerate(model.blocks):
-        p = f"blocks.{i}."
+        p = f"blocks.{base + i}."
         out += [(p + "attn.qkv.weight", blk.attn.qkv.weight), (p + "attn.wo.weight", blk.attn.wo.weight),
                 (p + "mlp.w1.weight", blk.mlp.w1.weight), (p + "mlp.w3.weight", blk.mlp.w3.weight),
                 (p + "mlp.w2.weight", blk.mlp.w2.weight), (p + "norm1.weight", blk.norm1.weight),
                 (p + "norm2.weight", blk.norm2.weight)]
-    out += [("emb.weight", model.emb.weight), ("norm_f.weight", model.norm_f.weight), ("head.weight", model.head.weight)]
+    for name in ("emb", "norm_f", "head"):
+        mod = getattr(model, name, None)
+        if mod is not None:
+            out.append((f"{name}.weight", mod.weight))
     return out
 
 

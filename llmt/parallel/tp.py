@@ -124,7 +124,9 @@ def replicated_params(model: LlamaModel):
     ps = []
     for blk in model.blocks:
         ps += [blk.norm1.weight, blk.norm2.weight]
-    return ps + [model.norm_f.weight]
+    if getattr(model, "norm_f", None) is not None:
+        ps.append(model.norm_f.weight)
+    return ps
 
 
 def sync_replicated_grads(model: LlamaModel, group, main_grad: bool = False):
