@@ -23,19 +23,33 @@ void ok(cudaError_t e, const char* what) {
   TORCH_CHECK(false, "llmt: ", what, ": ", cudaGetErrorString(e));
 }
 
+void on_device(const at::Tensor& t, const char* name);
+
 void cuda2d(const at::Tensor& t, const char* name) {
-  CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  on_device(t, name);
   CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2D with unit inner stride");
 }
 
-const void* opt_ptr(const c10::optional<at::Tensor>& t) {
-  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+// Every pointer a kernel dereferences must be memory of the launching device.
+void on_device(const at::Tensor& t, const char* name) {
+  CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  CHECK(t.get_device() == c10::cuda::current_device(), name, " is on cuda:", t.get_device(), ", the launch on cuda:",
+        (int)c10::cuda::current_device());
+}
+
+const void* opt_ptr(const c10::optional<at::Tensor>& t, const char* name = "operand") {
+  if (!(t.has_value() && t->defined())) return nullptr;
+  on_device(*t, name);
+  return t->data_ptr();
 }
 
 // ---------------------------------------------------------------- norms
 std::vector<at::Tensor> add_rmsnorm_fwd(c10::optional<at::Tensor> a, at::Tensor r, at::Tensor w, double eps,
                                         bool write_s) {
   CHECK(r.is_cuda() && r.is_contiguous(), "r must be a contiguous CUDA tensor");
+  on_device(r, "r");
+  on_device(w, "w");
+  if (a.has_value() && a->defined()) on_device(*a, "a");
   CHECK_DT(r, at::kFloat);
   CHECK_DT(w, at::kFloat);
   const int D = r.size(-1);
@@ -63,6 +77,8 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor s, at::Tensor w, a
   CHECK_DT(s, at::kFloat);
   CHECK_DT(dw, at::kFloat);
   CHECK_DT(ticket, at::kInt);
+  for (auto* t : {&dy, &s, &w, &rstd, &dw}) on_device(*t, "rmsnorm_bwd operand");
+  if (ds_in.has_value() && ds_in->defined()) on_device(*ds_in, "ds_in");
   CHECK(dy.is_contiguous() && s.is_contiguous() && dy.numel() == s.numel(), "dy/s must be contiguous and match");
   const int D = s.size(-1);
   const int64_t N = s.numel() / D;
@@ -108,6 +124,7 @@ void rope_inplace(at::Tensor qkv, at::Tensor cos_t, at::Tensor sin_t, int64_t T,
                   bool backward) {
   CHECK_DT(qkv, at::kBFloat16);
   CHECK_DT(cos_t, at::kFloat);
+  for (auto* t : {&qkv, &cos_t, &sin_t}) on_device(*t, "rope operand");
   CHECK(qkv.is_contiguous() && cos_t.is_contiguous() && sin_t.is_contiguous(), "rope operands must be contiguous");
   CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd, "rope table too small");
   const int64_t ld = qkv.size(-1);
@@ -120,6 +137,7 @@ void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at:
                    bool partial) {
   CHECK_DT(idx, at::kLong);
   CHECK_DT(W, at::kFloat);
+  for (auto* t : {&idx, &W, &x}) on_device(*t, "embedding operand");
   CHECK(idx.is_contiguous() && W.is_contiguous() && x.is_contiguous(), "embedding operands must be contiguous");
   ok(llmt::embedding_fwd(idx.data_ptr<int64_t>(), W.data_ptr<float>(), x.data_ptr<float>(), idx.numel(), W.size(1),
                          W.size(0), v0, partial, err.has_value() && err->defined() ? err->data_ptr<int>() : nullptr,
@@ -130,6 +148,7 @@ void embedding_fwd(at::Tensor idx, at::Tensor W, at::Tensor x, c10::optional<at:
 void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW, int64_t v0) {
   CHECK_DT(dx, at::kFloat);
   CHECK_DT(dW, at::kFloat);
+  for (auto* t : {&idx, &dx, &dW}) on_device(*t, "embedding operand");
   CHECK(idx.is_contiguous() && dx.is_contiguous() && dW.is_contiguous(), "embedding grads must be contiguous");
   ok(llmt::embedding_bwd(idx.data_ptr<int64_t>(), dx.data_ptr<float>(), dW.data_ptr<float>(), idx.numel(), dW.size(1),
                          dW.size(0), v0, stream()),
@@ -139,6 +158,7 @@ void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW, int64_t v0) {
 // ---------------------------------------------------------------- optimizer
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16, at::Tensor lr,
                 at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale, bool zero_grad) {
+  for (auto* t : {&p, &g, &m, &v, &lr, &step}) on_device(*t, "adamw operand");
   for (auto* t : {&p, &g, &m, &v}) {
     CHECK_DT((*t), at::kFloat);
     CHECK(t->is_contiguous() && t->numel() == p.numel(), "adamw buffers must be contiguous and equal-sized");
@@ -160,6 +180,8 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
 void cast_bf16(at::Tensor x, at::Tensor y) {
   CHECK_DT(x, at::kFloat);
   CHECK_DT(y, at::kBFloat16);
+  on_device(x, "x");
+  on_device(y, "y");
   CHECK(x.numel() == y.numel() && x.is_contiguous() && y.is_contiguous(), "cast_bf16: bad args");
   ok(llmt::cast_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream()), "cast_bf16");
 }
@@ -179,13 +201,14 @@ void ce_bwd_rows(at::Tensor logits, at::Tensor targets, at::Tensor lse, c10::opt
   cuda2d(logits, "logits");
   CHECK_DT(logits, at::kBFloat16);
   ok(llmt::ce_bwd_rows(logits.data_ptr(), logits.stride(0), targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
-                       static_cast<const float*>(opt_ptr(grad_out)), (float)scale, logits.size(0), logits.size(1),
+                       static_cast<const float*>(opt_ptr(grad_out, "grad_out")), (float)scale, logits.size(0), logits.size(1),
                        stream()),
      "ce_bwd_rows");
 }
 
 void ce_combine(at::Tensor part, at::Tensor tlogit, at::Tensor tgt, at::Tensor lse, at::Tensor loss, int64_t nblk,
                 int64_t V) {
+  for (auto* t : {&part, &tlogit, &tgt, &lse, &loss}) on_device(*t, "ce_combine operand");
   ok(llmt::ce_combine(part.data_ptr<float>(), tlogit.data_ptr<float>(), tgt.data_ptr<int64_t>(), lse.data_ptr<float>(),
                       loss.data_ptr<float>(), (int)lse.numel(), (int)nblk, (int)V, stream()),
      "ce_combine");
@@ -201,7 +224,7 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
   cuda2d(b, "b");
   CHECK_DT(a, at::kBFloat16);
   CHECK_DT(b, at::kBFloat16);
-  CHECK(out.is_cuda(), "out must be a CUDA tensor");
+  on_device(out, "out");
   const int M = ta ? a.size(1) : a.size(0);
   const int K = ta ? a.size(0) : a.size(1);
   int N = tb ? b.size(0) : b.size(1);
@@ -232,25 +255,27 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
   g.split = (int)split;
   g.alpha = (float)alpha;
   if (aux.has_value() && aux->defined()) {
+    on_device(*aux, "aux");
     CHECK_DT((*aux), at::kBFloat16);
     g.aux = aux->data_ptr();
     g.ld_aux = aux->stride(0);
   }
   if (out2.has_value() && out2->defined()) {
+    on_device(*out2, "out2");
     CHECK_DT((*out2), at::kBFloat16);
     g.out2 = out2->data_ptr();
     g.ldo2 = out2->stride(0);
   }
-  g.cos_t = static_cast<const float*>(opt_ptr(cos_t));
-  g.sin_t = static_cast<const float*>(opt_ptr(sin_t));
+  g.cos_t = static_cast<const float*>(opt_ptr(cos_t, "cos_t"));
+  g.sin_t = static_cast<const float*>(opt_ptr(sin_t, "sin_t"));
   g.T = (int)T;
   g.hd = (int)hd;
   g.rot_cols = (int)rot_cols;
-  g.tgt = static_cast<const int64_t*>(opt_ptr(tgt));
-  g.lse = static_cast<const float*>(opt_ptr(lse));
-  g.grad_out = static_cast<const float*>(opt_ptr(grad_out));
-  g.part = static_cast<float*>(const_cast<void*>(opt_ptr(part)));
-  g.tlogit = static_cast<float*>(const_cast<void*>(opt_ptr(tlogit)));
+  g.tgt = static_cast<const int64_t*>(opt_ptr(tgt, "tgt"));
+  g.lse = static_cast<const float*>(opt_ptr(lse, "lse"));
+  g.grad_out = static_cast<const float*>(opt_ptr(grad_out, "grad_out"));
+  g.part = static_cast<float*>(const_cast<void*>(opt_ptr(part, "part")));
+  g.tlogit = static_cast<float*>(const_cast<void*>(opt_ptr(tlogit, "tlogit")));
   if (epi == llmt::EPI_ROPE) CHECK(g.cos_t && g.sin_t && T > 0, "ROPE gemm needs rope tables and T");
   if (epi == llmt::EPI_SWIGLU) CHECK(g.aux && aux->stride(0) % 8 == 0, "SWIGLU gemm needs the gu save buffer");
   if (epi == llmt::EPI_SWIGLU_BWD) CHECK(g.aux && g.out2 && split == N, "SWIGLU_BWD gemm args");
@@ -286,6 +311,7 @@ at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tenso
   CHECK_DT(qkv, at::kBFloat16);
   CHECK_DT(o, at::kBFloat16);
   CHECK_DT(lse, at::kFloat);
+  for (auto* t : {&dO, &qkv, &o, &lse, &cos_t, &sin_t}) on_device(*t, "flash_attn_bwd operand");
   CHECK(dO.is_contiguous() && o.is_contiguous() && qkv.is_contiguous() && lse.is_contiguous(),
         "flash_attn_bwd: operands must be contiguous");
   CHECK(dO.numel() == B * T * H * hd && o.numel() == dO.numel(), "flash_attn_bwd: dO/o shape");

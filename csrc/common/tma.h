@@ -19,6 +19,26 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
   return fn;
 }
 
+// cuTensorMapEncodeTiled is a driver call and needs a current context on the calling thread.
+// A thread that has made no runtime call yet (PyTorch's autograd worker, when a backward
+// starts with one of our ops) has none: a no-op runtime call binds the device's primary
+// context, then the encode is retried.
+template <typename F>
+inline CUresult encode_with_context(F&& encode) {
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    cudaFree(nullptr);
+    r = encode();
+  }
+  return r;
+}
+
+// Result of the last cuTensorMapEncodeTiled call on this thread (for error messages).
+inline int& last_tmap_result() {
+  static thread_local int r = 0;
+  return r;
+}
+
 // True when a 2D bf16/fp32 operand can be described by a TMA map (checked before encoding).
 inline bool tma_ok(const void* ptr, uint64_t ld, int elem_bytes) {
   return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * elem_bytes) % 16 == 0;
@@ -35,9 +55,13 @@ inline bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   auto fn = tmap_encode_fn();
+  last_tmap_result() = fn ? -2 : -1;
   if (!fn || !tma_ok(ptr, ld, elem_bytes)) return false;
-  CUresult r = fn(m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_with_context([&] {
+    return fn(m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  });
+  last_tmap_result() = (int)r;
   return r == CUDA_SUCCESS;
 }
 
@@ -51,8 +75,10 @@ inline bool make_tmap_3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt
   cuuint32_t estr[3] = {1, 1, 1};
   auto fn = tmap_encode_fn();
   if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || strides[0] % 16 || strides[1] % 16) return false;
-  CUresult r = fn(m, dtype, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_with_context([&] {
+    return fn(m, dtype, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  });
   return r == CUDA_SUCCESS;
 }
 

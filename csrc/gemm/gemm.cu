@@ -3,6 +3,8 @@
 // per-row combine of the cross-entropy epilogue's partials.
 #include <string.h>
 
+#include <stdio.h>
+
 #include "gemm_kernel.cuh"
 
 namespace llmt {
@@ -93,15 +95,27 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   alignas(64) GemmMaps mp;
   memset(&mp, 0, sizeof(mp));
-  bool ok = ta ? make_tmap_2d(&mp.a, a, dt, 2, M, K, lda, 64, kGemmBK)
-               : make_tmap_2d(&mp.a, a, dt, 2, K, M, lda, kGemmBK, kGemmBM);
+  const bool ok_a = ta ? make_tmap_2d(&mp.a, a, dt, 2, M, K, lda, 64, kGemmBK)
+                       : make_tmap_2d(&mp.a, a, dt, 2, K, M, lda, kGemmBK, kGemmBM);
+  const int code_a = last_tmap_result();
+  bool ok_b;
   if (tb) {
     const int rows = epi == EPI_SWIGLU ? 2 * N : N;
-    ok = ok && make_tmap_2d(&mp.b, b, dt, 2, K, rows, ldb, kGemmBK, epi == EPI_SWIGLU ? BN / 2 : BN);
+    ok_b = make_tmap_2d(&mp.b, b, dt, 2, K, rows, ldb, kGemmBK, epi == EPI_SWIGLU ? BN / 2 : BN);
   } else {
-    ok = ok && make_tmap_2d(&mp.b, b, dt, 2, N, K, ldb, 64, kGemmBK);
+    ok_b = make_tmap_2d(&mp.b, b, dt, 2, N, K, ldb, 64, kGemmBK);
   }
-  LLMT_REQUIRE(ok, "gemm: cuTensorMapEncodeTiled rejected an operand");
+  if (!ok_a || !ok_b) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "gemm: cuTensorMapEncodeTiled rejected operand %s (result %d; M=%d N=%d K=%d ta=%d tb=%d lda=%lld "
+             "ldb=%lld a%%16=%d b%%16=%d epi=%d)",
+             ok_a ? "B" : "A", ok_a ? last_tmap_result() : code_a, M, N, K, (int)ta, (int)tb, (long long)lda, (long long)ldb,
+             (int)(reinterpret_cast<uintptr_t>(a) & 15), (int)(reinterpret_cast<uintptr_t>(b) & 15), epi);
+    set_last_error(msg);
+    return cudaErrorInvalidValue;
+  }
+  bool ok = true;
   // Epilogue output maps: 32x32 boxes, one per epilogue warp and chunk (see Stager).
   switch (epi) {
     case EPI_F32:

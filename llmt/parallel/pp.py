@@ -30,6 +30,8 @@ from llmt.export.trace import schedule_1f1b
 from llmt.models.llama import Block, RMSNorm, build_model, rope_tables
 from llmt.parallel.collectives import gather_rows, scatter_rows
 
+_DEBUG = bool(int(__import__("os").environ.get("LLMT_PP_DEBUG", "0")))
+
 
 def stage_layers(L: int, pp: int, s: int):
     """Blocks [l0, l1) of stage s; the first L % pp stages take one extra block."""
@@ -94,7 +96,8 @@ def build_stage(cfg: ModelConfig, max_seq: int, pp: int, s: int, tp: int = 1, tp
         return st.to(device)
     with torch.device(device):
         torch.manual_seed(seed * 1000 + s * 100 + tp_rank)
-        return StageModel(lcfg, max_seq, l0, l1, s == 0, s == pp - 1)
+        st = StageModel(lcfg, max_seq, l0, l1, s == 0, s == pp - 1)
+    return st.to(device)  # the rope tables are built on the CPU
 
 
 # ---------------------------------------------------------------- stage executors
@@ -240,6 +243,11 @@ class Pipeline1F1B:
             if self.last:
                 outputs[i].backward()
             else:
+                if _DEBUG:
+                    for name, t in (("out", outputs[i]), ("grad", grads)):
+                        print(f"[pp stage {self.s} mb {i}] {name}: " + ", ".join(
+                            f"{tuple(x.shape)}/{x.stride()}/{x.dtype}/{x.device}/ptr%256={x.data_ptr() % 256}"
+                            f"/off={x.storage_offset()}" for x in t), flush=True)
                 torch.autograd.backward(list(outputs[i]), list(grads))
             g_in = None if self.first else [t.grad for t in inputs[i]]
             inputs[i] = outputs[i] = None

@@ -116,7 +116,8 @@ def build_local_model(cfg: ModelConfig, max_seq: int, tp: int, r: int, seed: int
         raise ValueError(f"unknown init {init!r}")
     with torch.device(device):
         torch.manual_seed(seed * 1000 + r)
-        return LlamaModel(lcfg, max_seq)
+        local = LlamaModel(lcfg, max_seq)
+    return local.to(device)  # the rope tables are built on the CPU
 
 
 def replicated_params(model: LlamaModel):
