@@ -54,7 +54,10 @@ cudaError_t ce_combine(const float* part, const float* tlogit, const int64_t* tg
                        int nblk, int V, cudaStream_t st);
 
 // ---------------------------------------------------------------- GEMM
-enum EpiKind : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_ROPE = 4, EPI_CE_FWD = 5, EPI_CE_BWD = 6 };
+enum EpiKind : int {
+  EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_ROPE = 4, EPI_CE_FWD = 5, EPI_CE_BWD = 6,
+  EPI_PEER_RS = 7  // bf16 rows stored straight into their owner rank's reduce-scatter slot (NVLink peer memory)
+};
 
 struct GemmArgs {
   int M, N, K;
@@ -77,6 +80,9 @@ struct GemmArgs {
   float* part;    // CE_FWD partials (M, n_blocks, 2)
   float* tlogit;  // CE_FWD target logits (M)
   float alpha;
+  void* const* peer;   // PEER_RS: device array of every rank's slot buffer (tp, rows_per_rank, ldo) bf16
+  int tp_rank;         // PEER_RS: this rank's slot index in every owner's buffer
+  int rows_per_rank;   // PEER_RS: output row r belongs to rank r / rows_per_rank
   int* err;
 };
 
@@ -100,6 +106,20 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
 int attn_error_code(bool reset);
 // Event trace of the hd-64 attention backward: 1024 int64 on the device, or nullptr (off).
 void attn_bwd_set_trace(long long* buf);
+
+// ---------------------------------------------------------------- tensor-parallel row collectives
+// Over NVLink peer memory (CUDA IPC mappings of every rank's buffers). `dst` / `slots` are
+// device arrays of `tp` peer base pointers (this rank's own buffer included).
+//   allgather_rows: this rank's rows (rows, d) go to rows [row0, row0 + rows) of every peer's
+//                   (N, d) buffer
+//   scatter_rows:   rows of a local (N, d) partial go to slot `rank` of their owner's
+//                   (tp, N/tp, d) slot buffer
+//   sum_slots:      out (n, d) = sum over tp of the local slots (fp32 accumulation)
+cudaError_t tp_allgather_rows(const void* src, void* const* dst, int tp, int64_t row0, int64_t rows, int d,
+                              cudaStream_t st);
+cudaError_t tp_scatter_rows(const void* src, void* const* slots, int tp, int rank, int64_t rows_per_rank, int d,
+                            cudaStream_t st);
+cudaError_t tp_sum_slots(const void* slots, void* out, int tp, int64_t rows, int d, cudaStream_t st);
 
 // ---------------------------------------------------------------- data-parallel transport
 // CUDA-IPC buffers (64-byte handles exchanged by the caller), a flag barrier with bounded

@@ -219,7 +219,8 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
           c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split, c10::optional<at::Tensor> cos_t,
           c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols, c10::optional<at::Tensor> tgt,
           c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
-          c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits) {
+          c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits, c10::optional<at::Tensor> peer,
+          int64_t tp_rank, int64_t rows_per_rank) {
   cuda2d(a, "a");
   cuda2d(b, "b");
   CHECK_DT(a, at::kBFloat16);
@@ -246,6 +247,10 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
             "gemm: fp32 output must be (M, N) row-major with a 16-byte-multiple pitch");
       break;
     case llmt::EPI_SWIGLU_BWD: case llmt::EPI_CE_FWD: break;
+    case llmt::EPI_PEER_RS:
+      CHECK(peer.has_value() && peer->defined() && peer->scalar_type() == at::kLong, "PEER_RS gemm needs peer slots");
+      CHECK(out.dim() == 2 && out.size(1) == N && out.is_contiguous(), "PEER_RS: out is this rank's slot buffer (., N)");
+      break;
     default: CHECK(false, "gemm: unknown epilogue ", epi);
   }
   llmt::GemmArgs g{};
@@ -276,6 +281,9 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
   g.grad_out = static_cast<const float*>(opt_ptr(grad_out, "grad_out"));
   g.part = static_cast<float*>(const_cast<void*>(opt_ptr(part, "part")));
   g.tlogit = static_cast<float*>(const_cast<void*>(opt_ptr(tlogit, "tlogit")));
+  g.peer = reinterpret_cast<void* const*>(const_cast<void*>(opt_ptr(peer, "peer")));
+  g.tp_rank = (int)tp_rank;
+  g.rows_per_rank = (int)rows_per_rank;
   if (epi == llmt::EPI_ROPE) CHECK(g.cos_t && g.sin_t && T > 0, "ROPE gemm needs rope tables and T");
   if (epi == llmt::EPI_SWIGLU) CHECK(g.aux && aux->stride(0) % 8 == 0, "SWIGLU gemm needs the gu save buffer");
   if (epi == llmt::EPI_SWIGLU_BWD) CHECK(g.aux && g.out2 && split == N, "SWIGLU_BWD gemm args");
@@ -402,11 +410,33 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "a"_a, "b"_a, "ta"_a, "tb"_a, "epi"_a, "out"_a, "accumulate"_a = false, "aux"_a = py::none(),
         "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
         "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
-        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0);
+        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0, "peer"_a = py::none(), "tp_rank"_a = 0, "rows_per_rank"_a = 0);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
+  m.def("tp_allgather_rows", [](at::Tensor src, at::Tensor dst, int64_t tp, int64_t row0) {
+    on_device(src, "src");
+    CHECK(src.is_contiguous() && src.scalar_type() == at::kBFloat16 && src.dim() == 2, "tp_allgather_rows: src");
+    ok(llmt::tp_allgather_rows(src.data_ptr(), reinterpret_cast<void* const*>(dst.data_ptr<int64_t>()), (int)tp, row0,
+                               src.size(0), (int)src.size(1), stream()),
+       "tp_allgather_rows");
+  });
+  m.def("tp_scatter_rows", [](at::Tensor src, at::Tensor slots, int64_t tp, int64_t rank) {
+    on_device(src, "src");
+    CHECK(src.is_contiguous() && src.scalar_type() == at::kBFloat16 && src.dim() == 2 && src.size(0) % tp == 0,
+          "tp_scatter_rows: src");
+    ok(llmt::tp_scatter_rows(src.data_ptr(), reinterpret_cast<void* const*>(slots.data_ptr<int64_t>()), (int)tp,
+                             (int)rank, src.size(0) / tp, (int)src.size(1), stream()),
+       "tp_scatter_rows");
+  });
+  m.def("tp_sum_slots", [](at::Tensor slots, at::Tensor out, int64_t tp) {
+    on_device(slots, "slots");
+    on_device(out, "out");
+    CHECK(out.is_contiguous() && slots.is_contiguous() && slots.numel() == tp * out.numel(), "tp_sum_slots: shapes");
+    ok(llmt::tp_sum_slots(slots.data_ptr(), out.data_ptr(), (int)tp, out.size(0), (int)out.size(1), stream()),
+       "tp_sum_slots");
+  });
   m.def("attn_bwd_set_trace", [](c10::optional<at::Tensor> buf) {
     if (buf && buf->defined()) {
       CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 1024,

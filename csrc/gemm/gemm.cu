@@ -82,6 +82,10 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
     splits = force_splits;
   }
   LLMT_REQUIRE(BN == 128 || BN == 256, "gemm: BN must be 128 or 256");
+  if (epi == EPI_PEER_RS)
+    LLMT_REQUIRE(g.peer && g.rows_per_rank > 0 && M % g.rows_per_rank == 0 && N % 32 == 0 && g.ldo % 8 == 0 &&
+                     !ta,
+                 "gemm: PEER_RS needs peer slots, M a multiple of the rows per rank, N a multiple of 32");
   if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm: bad RoPE epilogue shape");
   g.M = M;
   g.N = N;

@@ -211,6 +211,34 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       st.put_bf16(b, u);
       st.store3d(tmC2, b, col0, 1, wrow);
     }
+  } else if constexpr (EPI == EPI_PEER_RS) {
+    // bf16 rows straight into the owner rank's reduce-scatter slot through NVLink
+    bf16* dst = nullptr;
+    if (rv) {
+      const int q = row / a.rows_per_rank;
+      dst = static_cast<bf16*>(a.peer[q]) +
+            ((int64_t)a.tp_rank * a.rows_per_rank + (row - q * a.rows_per_rank)) * a.ldo;
+    }
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= a.N) break;  // uniform across the warp
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      if (rv) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const BF16x8 o = float_to_bf16x8(v + 8 * u);
+          __stcg(d4 + u, *reinterpret_cast<const uint4*>(&o));
+        }
+      }
+    }
+    __threadfence_system();  // this tile's rows are visible to their owners before the barrier
   } else if constexpr (EPI == EPI_SWIGLU_BWD) {
     // g and u arrive by TMA (3D map over the saved [g | u] rows) one chunk ahead, into the
     // warp's two 4 KB buffers; dg and du are written back in place and leave by TMA.

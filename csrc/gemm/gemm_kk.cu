@@ -15,6 +15,7 @@ static cudaError_t run_kk(int epi, const GemmMaps& mp, const GemmArgs& g, cudaSt
     case EPI_ROPE: return launch<BN, S, false, false, EPI_ROPE>(mp, g, st);
     case EPI_CE_FWD: return launch<BN, S, false, false, EPI_CE_FWD>(mp, g, st);
     case EPI_CE_BWD: return launch<BN, S, false, false, EPI_CE_BWD>(mp, g, st);
+    case EPI_PEER_RS: return launch<BN, S, false, false, EPI_PEER_RS>(mp, g, st);
     default: set_last_error("gemm: epilogue not built for the x W^T layout"); return cudaErrorInvalidValue;
   }
 }

@@ -1,5 +1,6 @@
 // tcgen05 GEMM instantiations with K-major A and MN-major B: dgrad (dx = dy W), including
-// the SwiGLU-backward epilogue of the w2 dgrad.
+// the SwiGLU-backward epilogue of the w2 dgrad and the tensor-parallel dgrads whose rows go
+// straight to their owner rank (PEER_RS).
 #include "gemm_kernel.cuh"
 
 namespace llmt {
@@ -12,6 +13,7 @@ static cudaError_t run_km(int epi, const GemmMaps& mp, const GemmArgs& g, cudaSt
     case EPI_BF16: return launch<BN, S, false, true, EPI_BF16>(mp, g, st);
     case EPI_F32: return launch<BN, S, false, true, EPI_F32>(mp, g, st);
     case EPI_SWIGLU_BWD: return launch<BN, S, false, true, EPI_SWIGLU_BWD>(mp, g, st);
+    case EPI_PEER_RS: return launch<BN, S, false, true, EPI_PEER_RS>(mp, g, st);
     default: set_last_error("gemm: epilogue not built for the dy W layout"); return cudaErrorInvalidValue;
   }
 }

@@ -33,6 +33,9 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--dp-mode", default="nccl", choices=["nccl", "fused"])
     p.add_argument("--json", default=None)
+    p.add_argument("--graph", action="store_true", help="capture the step in a CUDA graph (pp = 1 only)")
+    p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"],
+                   help="tensor-parallel row collectives: NCCL, or NVLink peer memory fused with the GEMMs")
     args = p.parse_args()
     from llmt.config import get_config, model_flops_per_token
     from llmt.parallel.engine import ParallelTrainer
@@ -45,7 +48,7 @@ def main():
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     B = args.global_batch // args.dp
     tr = ParallelTrainer(cfg, B, args.seq, lay, microbatches=args.microbatches, device=f"cuda:{local}",
-                         init="local", dp_mode=args.dp_mode)
+                         init="local", dp_mode=args.dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
     g = torch.Generator().manual_seed(1 + tr.groups.dp_rank)
     idx = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
     tgt = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
@@ -68,6 +71,7 @@ def main():
     tokens = args.global_batch * args.seq
     res = {"model": args.model, "seq": args.seq, "global_batch": args.global_batch,
            "layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches, "n_gpus": world,
+           "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm,
            "ms_per_step": round(ms.item(), 3), "tokens_per_s": round(tokens / step_s, 1),
            "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2), "dtype": "bf16",
            "data": "synthetic uniform-random tokens, random-init weights", "timing": "CUDA events, max over ranks"}

@@ -170,15 +170,16 @@ class SwiGLUMLP(torch.autograd.Function):
     SWIGLU_EPILOGUE selects per direction."""
 
     @staticmethod
-    def forward(ctx, x, w1, w2, ffn):
+    def forward(ctx, x, w1, w2, ffn, comm=None):
         if SWIGLU_EPILOGUE["fwd"]:
             h, gu = N.gemm_swiglu(x, w1.w13_16, ffn)
         else:
             gu = N.gemm(x, w1.w13_16, ta=False, tb=True)
             h = N.swiglu_fwd(gu[:, :ffn], gu[:, ffn:])
-        m = N.gemm(h, w2.w16, ta=False, tb=True)
+        # tensor parallel over peer memory: the w2 GEMM stores its rows to their owner ranks
+        m = comm.gemm_rs(h, w2.w16) if comm is not None else N.gemm(h, w2.w16, ta=False, tb=True)
         ctx.save_for_backward(x, h, gu)
-        ctx.w1, ctx.w2, ctx.ffn = w1, w2, ffn
+        ctx.w1, ctx.w2, ctx.ffn, ctx.comm = w1, w2, ffn, comm
         return m
 
     @staticmethod
@@ -186,6 +187,8 @@ class SwiGLUMLP(torch.autograd.Function):
         x, h, gu = ctx.saved_tensors
         w1, w2, ffn = ctx.w1, ctx.w2, ctx.ffn
         dm = dm.contiguous()
+        if ctx.comm is not None:
+            dm = ctx.comm.all_gather_bwd(dm)
         if SWIGLU_EPILOGUE["bwd"]:
             dgu = N.gemm_swiglu_bwd(dm, w2.w16, gu, ffn)
             _wgrad(dm, h, w2)
@@ -197,7 +200,7 @@ class SwiGLUMLP(torch.autograd.Function):
             dgu = gu
         dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
         N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=True)
-        return dx, None, None, None
+        return dx, None, None, None, None
 
 
 class HeadCEVP(torch.autograd.Function):

@@ -27,7 +27,7 @@ from llmt.parallel.tp import sync_replicated_grads
 class ParallelTrainer:
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, layout: Layout, microbatches: int = 1,
                  device="cuda", seed: int = 0, lr: float = 3e-4, impl: str = "native", dp_mode: str = "nccl",
-                 init: str = "full", ce_chunk: int = 8192):
+                 init: str = "full", ce_chunk: int = 8192, cuda_graph: bool = False, tp_comm: str = "nccl"):
         self.cfg, self.batch, self.seq, self.layout, self.m = cfg, batch, seq, layout, microbatches
         if batch % microbatches:
             raise ValueError("batch must be a multiple of microbatches")
@@ -37,7 +37,7 @@ class ParallelTrainer:
         self.stage = build_stage(cfg, seq, layout.pp, g.pp_rank, layout.tp, g.tp_rank, seed=seed, device=self.device,
                                  init=init)
         if impl == "native":
-            self.x = NativeStage(self.stage, g.tp_group, pad_to=layout.dp, ce_chunk=ce_chunk)
+            self.x = NativeStage(self.stage, g.tp_group, pad_to=layout.dp, ce_chunk=ce_chunk, comm=tp_comm)
             flat = self.x.flat
             if layout.dp > 1:
                 from llmt.parallel.dp import DataParallel
@@ -60,6 +60,13 @@ class ParallelTrainer:
             nxt = rank_of(g.dp_rank, s + 1, g.tp_rank, layout.pp, layout.tp) if s < layout.pp - 1 else None
             self.pipe = Pipeline1F1B(self.x, s, layout.pp, prev, nxt, g.pp_group, self.device)
         self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
+        # whole-step CUDA graph (forward, backward, collectives, optimizer) for layouts without a
+        # pipeline: static token buffers, captured after two eager warm-up steps
+        self.use_graph = cuda_graph and impl == "native" and layout.pp == 1
+        self.graph = None
+        if self.use_graph:
+            self.idx_buf = torch.zeros((batch, seq), dtype=torch.long, device=self.device)
+            self.tgt_buf = torch.zeros((batch, seq), dtype=torch.long, device=self.device)
 
     @property
     def is_last_stage(self):
@@ -97,15 +104,40 @@ class ParallelTrainer:
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
 
-    def train_step(self, idx, tgt) -> float:
-        """Public API: one step on this data-parallel rank's tokens; returns the loss (last stage;
-        0.0 on earlier stages)."""
+    def _body(self, idx, tgt):
         loss = self.forward_backward(idx, tgt)
         self.optimizer_step()
         if loss is not None:
             self.loss.copy_(loss)
+
+    def run_step(self, idx, tgt):
+        """One step without a host sync (graph replay when enabled)."""
+        if not self.use_graph:
+            self._body(idx, tgt)
+            return
+        self.idx_buf.copy_(idx, non_blocking=True)
+        self.tgt_buf.copy_(tgt, non_blocking=True)
+        if self.graph is None:
+            s = torch.cuda.Stream(device=self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    self._body(self.idx_buf, self.tgt_buf)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._body(self.idx_buf, self.tgt_buf)
+        self.graph.replay()
+
+    def train_step(self, idx, tgt) -> float:
+        """Public API: one step on this data-parallel rank's tokens; returns the loss (last stage;
+        0.0 on earlier stages)."""
+        self.run_step(idx, tgt)
         return float(self.loss.item())
 
     def close(self):
+        self.graph = None  # a graph holding NCCL calls must go before the process group
+        if hasattr(self.x, "close"):
+            self.x.close()
         if self.dp is not None:
             self.dp.close()

@@ -29,6 +29,8 @@ def main():
     p.add_argument("--microbatches", type=int, default=4)
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--dp-mode", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"])
+    p.add_argument("--graph", action="store_true")
     args = p.parse_args()
     from llmt.config import get_config
     from llmt.models.llama import make_batch
@@ -46,7 +48,7 @@ def main():
     batches = [make_batch(B, T, cfg.vocab, "cpu", seed=d) for d in range(args.dp)]
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     tr = ParallelTrainer(cfg, B, T, lay, microbatches=args.microbatches, device=f"cuda:{local}",
-                         dp_mode=args.dp_mode)
+                         dp_mode=args.dp_mode, tp_comm=args.tp_comm, cuda_graph=args.graph)
     g = tr.groups
     losses = [tr.train_step(*batches[g.dp_rank]) for _ in range(args.steps)]
     torch.cuda.synchronize()
@@ -74,13 +76,15 @@ def main():
                       microbatches=args.microbatches * args.dp)
         idx = torch.cat([b[0] for b in batches])
         tgt = torch.cat([b[1] for b in batches])
-        ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps)]
+        extra = 2 if (args.graph and args.pp == 1) else 0  # a graph trainer warms up with two eager steps
+        ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps + extra)][extra:]
         rsd = ref.model.state_dict()
         num = sum(float((merged[k].to(rsd[k].device) - rsd[k].float()).norm() ** 2) for k in rsd)
         den = sum(float(rsd[k].float().norm() ** 2) for k in rsd)
         rel = (num / den) ** 0.5
         ok = rel < 2e-3 and all(v == 0 for v in codes.values())
         print(json.dumps({"layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches,
+                          "tp_comm": args.tp_comm, "graph": args.graph,
                           "rel_err_master": rel, "losses_last_stage_dp0": last_losses, "ref_losses": ref_losses,
                           "error_codes": codes, "ok": ok}), flush=True)
     tr.close()

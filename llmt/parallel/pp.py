@@ -144,9 +144,10 @@ class NativeStage:
     """Stage on the native kernels (flat fp32 master / grad, bf16 shadow; every weight gradient
     into main_grad). Boundary activation: (pending branch output bf16, fp32 residual)."""
 
-    def __init__(self, stage: StageModel, tp_group=None, pad_to: int = 1, ce_chunk: int = 8192):
+    def __init__(self, stage: StageModel, tp_group=None, pad_to: int = 1, ce_chunk: int = 8192, comm: str = "nccl"):
         from llmt.models.native import FlatParams
         self.m, self.g, self.ce_chunk = stage, tp_group, ce_chunk
+        self.comm_kind, self.comm = comm, None
         self.flat = FlatParams(stage, stage.rope_cos.device if stage.emb is None else stage.emb.weight.device,
                                pad_to=pad_to)
         self.tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
@@ -160,23 +161,30 @@ class NativeStage:
         return scatter_rows(Fn.EmbedVP.apply(idx.reshape(-1), m.emb.weight, v0), g)
 
     def forward_blocks(self, acts, B, T):
-        from llmt.ops import functions as Fn
+        from llmt.parallel.tp import native_tp_block
         m, g, cfg = self.m, self.g, self.m.cfg
         a, r = acts if isinstance(acts, tuple) else (None, acts)
         cos = m.rope_cos[:T].contiguous()
         sin = m.rope_sin[:T].contiguous()
-        for blk in m.blocks:
-            if a is None:
-                n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
-            else:
-                n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
-            o = Fn.QKVAttention.apply(gather_rows(n1, g), blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh,
-                                      cfg.hd)
-            att = scatter_rows(Fn.Linear.apply(o, blk.attn.wo.weight), g)
-            n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
-            mo = Fn.SwiGLUMLP.apply(gather_rows(n2, g), blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn)
-            a, r = scatter_rows(mo, g), s2
+        comm = self._peer_comm(B * T)
+        for i, blk in enumerate(m.blocks):
+            a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i)
         return (a, r)
+
+    def _peer_comm(self, rows):
+        if self.comm_kind != "p2p" or self.g is None:
+            return None
+        if self.comm is None or self.comm.rows != rows:
+            from llmt.parallel.tp_p2p import TPPeerComm
+            if self.comm is not None:
+                self.comm.close()
+            self.comm = TPPeerComm(self.g, rows, self.m.cfg.d, 2 * len(self.m.blocks), self.flat.master.device)
+        return self.comm
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def forward_last(self, acts, targets):
         from llmt.ops import functions as Fn

@@ -211,13 +211,39 @@ class TPTorchLlama(torch.nn.Module):
 
 
 # ---------------------------------------------------------------- native path (sm_100a kernels)
+def native_tp_block(blk, a, r, cos, sin, B, T, cfg, group, comm=None, i=0):
+    """One block on the native kernels over a tensor-parallel group: NCCL row collectives
+    (comm None), or peer-memory ones with the row-parallel GEMMs storing to their owners
+    (comm = TPPeerComm; all-gather sites 2i and 2i+1). group None: no tensor parallelism."""
+    from llmt.ops import functions as Fn
+    from llmt.parallel.tp_p2p import AllGatherP2P, RowLinearRS
+    if a is None:
+        n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
+    else:
+        n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+    n1g = AllGatherP2P.apply(n1, comm, 2 * i) if comm is not None else gather_rows(n1, group)
+    o = Fn.QKVAttention.apply(n1g, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
+    if comm is not None:
+        att = RowLinearRS.apply(o, blk.attn.wo.weight, comm)
+    else:
+        att = scatter_rows(Fn.Linear.apply(o, blk.attn.wo.weight), group)
+    n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+    n2g = AllGatherP2P.apply(n2, comm, 2 * i + 1) if comm is not None else gather_rows(n2, group)
+    if comm is not None:
+        return Fn.SwiGLUMLP.apply(n2g, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn, comm), s2
+    mo = Fn.SwiGLUMLP.apply(n2g, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn)
+    return scatter_rows(mo, group), s2
+
 class TPNativeLlama:
     """The sequence + tensor parallel step on the native kernels (bf16 GEMMs, flash attention,
-    fused norms, vocabulary-parallel fused head + CE), NCCL row all-gathers / reduce-scatters
-    between the regions. Same interface as NativeLlama: forward(idx, targets) -> mean loss,
-    with every weight gradient accumulated into its parameter's main_grad."""
+    fused norms, vocabulary-parallel fused head + CE). Row collectives between the regions run
+    over NCCL (comm="nccl") or over NVLink peer memory fused with their producers
+    (comm="p2p": the wo / w2 GEMMs store their rows straight to the owner ranks). Same
+    interface as NativeLlama: forward(idx, targets) -> mean loss, every weight gradient
+    accumulated into its parameter's main_grad."""
 
-    def __init__(self, local: LlamaModel, group, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False):
+    def __init__(self, local: LlamaModel, group, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
+                 comm: str = "nccl"):
         from llmt.models.native import FlatParams
         self.model = local
         self.cfg = local.cfg
@@ -230,6 +256,19 @@ class TPNativeLlama:
         self.flat = FlatParams(local, dev, pad_to=pad_to)
         self.tp = dist.get_world_size(group) if group is not None else 1
         self.r = dist.get_rank(group) if group is not None else 0
+        self.comm_kind = comm
+        self.comm = None  # TPPeerComm, built on the first forward (needs the token count)
+
+    def _peer_comm(self, rows):
+        if self.comm_kind != "p2p" or self.group is None:
+            return None
+        if self.comm is None or self.comm.rows != rows:
+            from llmt.parallel.tp_p2p import TPPeerComm
+            if self.comm is not None:
+                self.comm.close()
+            self.comm = TPPeerComm(self.group, rows, self.cfg.d, 2 * len(self.model.blocks),
+                                   self.model.emb.weight.device)
+        return self.comm
 
     def forward(self, idx, targets):
         from llmt.ops import functions as Fn
@@ -237,34 +276,27 @@ class TPNativeLlama:
         B, T = idx.shape
         if (B * T) % self.tp:
             raise ValueError(f"{B * T} tokens do not split over tensor parallel {self.tp}")
+        comm = self._peer_comm(B * T)
         cos = m.rope_cos[:T].contiguous()
         sin = m.rope_sin[:T].contiguous()
         v0 = self.r * m.emb.weight.shape[0]
         x = scatter_rows(Fn.EmbedVP.apply(idx.reshape(-1), m.emb.weight, v0), g)
         a, r = None, x
-        for blk in m.blocks:
+        for i, blk in enumerate(m.blocks):
             if self.ckpt and torch.is_grad_enabled():
-                a, r = torch.utils.checkpoint.checkpoint(self._block, blk, a, r, cos, sin, B, T, use_reentrant=False,
-                                                      preserve_rng_state=False)
+                a, r = torch.utils.checkpoint.checkpoint(native_tp_block, blk, a, r, cos, sin, B, T, cfg, g, comm, i,
+                                                      use_reentrant=False, preserve_rng_state=False)
             else:
-                a, r = self._block(blk, a, r, cos, sin, B, T)
+                a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i)
         h = Fn.FinalNormFn.apply(a, r, m.norm_f.weight, cfg.eps)
         return Fn.HeadCEVP.apply(gather_rows(h, g), m.head.weight, targets.reshape(-1), v0, g, self.ce_chunk)
 
-    def _block(self, blk, a, r, cos, sin, B, T):
-        from llmt.ops import functions as Fn
-        cfg, g = self.cfg, self.group
-        if a is None:
-            n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
-        else:
-            n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
-        o = Fn.QKVAttention.apply(gather_rows(n1, g), blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
-        att = scatter_rows(Fn.Linear.apply(o, blk.attn.wo.weight), g)
-        n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
-        mo = Fn.SwiGLUMLP.apply(gather_rows(n2, g), blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn)
-        return scatter_rows(mo, g), s2
-
     def sync_replicated_grads(self):
         sync_replicated_grads(self.model, self.group, main_grad=True)
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     __call__ = forward
