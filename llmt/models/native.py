@@ -105,9 +105,11 @@ class NativeLlama:
 
     A plain wrapper (not an nn.Module), so model.state_dict() keeps the reference keys."""
 
-    def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False):
+    def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
+                 nvtx: bool = False):
         self.model = model
         self.ckpt = ckpt
+        self.nvtx = nvtx  # NVTX range per block (reference bench_train.py:215-222)
         self.cfg = model.cfg
         dev = model.emb.weight.device
         if dev.type != "cuda":
@@ -122,13 +124,17 @@ class NativeLlama:
         sin = m.rope_sin[:T].contiguous()
         x = Fn.Embed.apply(idx.reshape(-1), m.emb.weight)
         a, r = None, x
-        for blk in m.blocks:
+        for i, blk in enumerate(m.blocks):
+            if self.nvtx:
+                torch.cuda.nvtx.range_push(f"block{i}")
             if self.ckpt and torch.is_grad_enabled():
                 # per-block recompute (reference bench_train.py:217-218): keep only the block input
                 a, r = torch.utils.checkpoint.checkpoint(self._block, blk, a, r, cos, sin, B, T, use_reentrant=False,
                                                       preserve_rng_state=False)
             else:
                 a, r = self._block(blk, a, r, cos, sin, B, T)
+            if self.nvtx:
+                torch.cuda.nvtx.range_pop()
         h = Fn.FinalNormFn.apply(a, r, m.norm_f.weight, cfg.eps)
         return Fn.HeadCE.apply(h, m.head.weight, targets.reshape(-1), self.ce_chunk)
 

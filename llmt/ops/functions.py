@@ -28,6 +28,13 @@ from llmt.ops import native as N
 # LLMT_SWIGLU_EPILOGUE="fwd,bwd" / "fwd" / "bwd" / "none" overrides the default.
 _sw = os.environ.get("LLMT_SWIGLU_EPILOGUE", "fwd,bwd")
 SWIGLU_EPILOGUE = {"fwd": "fwd" in _sw, "bwd": "bwd" in _sw}
+# Other fusions that can be switched off (the ablation of llmt.bench.ablate; reference
+# kernels/ablate_kernels.py): "rope" = RoPE in the qkv GEMM epilogue (else the standalone
+# in-place RoPE kernel after a plain GEMM), "head_ce" = cross entropy reduced inside the head
+# GEMM's epilogue with logits never written (else bf16 logits + the row CE kernels).
+# LLMT_UNFUSE="rope,head_ce" switches them off.
+_unf = os.environ.get("LLMT_UNFUSE", "")
+FUSION = {"rope": "rope" not in _unf, "head_ce": "head_ce" not in _unf}
 
 
 class Embed(torch.autograd.Function):
@@ -125,7 +132,11 @@ class QKVAttention(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, w, cos, sin, B, T, H, KV, hd):
-        qkv = N.gemm_rope(x, w.w16, cos, sin, T, hd, (H + KV) * hd)
+        if FUSION["rope"]:
+            qkv = N.gemm_rope(x, w.w16, cos, sin, T, hd, (H + KV) * hd)
+        else:
+            qkv = N.gemm(x, w.w16, ta=False, tb=True)
+            N.rope_inplace(qkv, cos, sin, T, H + KV, hd)
         o, lse = N.flash_attn_fwd(qkv, B, T, H, KV, hd, causal=True)
         ctx.save_for_backward(x, qkv, o, lse, cos, sin)
         ctx.w = w
@@ -243,21 +254,35 @@ class HeadCEVP(torch.autograd.Function):
 
 class HeadCE(torch.autograd.Function):
     """Mean cross entropy of the lm head; logits are never written (forward), and are
-    recomputed tile by tile into bf16 dlogits chunks of at most `chunk` rows (backward)."""
+    recomputed tile by tile into bf16 dlogits chunks of at most `chunk` rows (backward).
+    With FUSION["head_ce"] off: bf16 logits are written and the row CE kernels run on them."""
 
     @staticmethod
     def forward(ctx, h, w, targets, chunk):
+        ctx.w, ctx.chunk = w, chunk
+        if not FUSION["head_ce"]:
+            logits = N.gemm(h, w.w16, ta=False, tb=True)
+            lse = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
+            loss_rows = torch.empty_like(lse)
+            N.ce_fwd_rows(logits, targets, lse, loss_rows)
+            ctx.save_for_backward(h, targets, lse, logits)
+            return loss_rows.mean()
         lse, loss_rows = N.gemm_ce_fwd(h, w.w16, targets)
         ctx.save_for_backward(h, targets, lse)
-        ctx.w, ctx.chunk = w, chunk
         return loss_rows.mean()
 
     @staticmethod
     def backward(ctx, g):
-        h, targets, lse = ctx.saved_tensors
+        h, targets, lse = ctx.saved_tensors[:3]
         w, chunk = ctx.w, ctx.chunk
         n = h.shape[0]
         g = g.reshape(1).float().contiguous()
+        if len(ctx.saved_tensors) == 4:  # unfused: dlogits in place over the saved logits
+            dl = ctx.saved_tensors[3]
+            N.ce_bwd_rows(dl, targets, lse, g, 1.0 / n)
+            dh = N.gemm(dl, w.w16, ta=False, tb=False)
+            N.gemm(dl, h, ta=True, tb=False, out=w.main_grad, accumulate=True)
+            return dh, None, None, None
         dh = torch.empty_like(h)
         for c0 in range(0, n, chunk):
             c1 = min(n, c0 + chunk)

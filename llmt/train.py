@@ -28,8 +28,9 @@ class Trainer:
 
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
                  cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False,
-                 tp_group=None, init: str = "full"):
+                 tp_group=None, init: str = "full", nvtx: bool = False):
         self.cfg, self.batch, self.seq = cfg, batch, seq
+        self.nvtx = nvtx  # NVTX ranges forward / backward / optimizer per step (eager steps; reference --nvtx)
         self.device = torch.device(device)
         self.microbatches = microbatches
         self.dp = dp
@@ -43,7 +44,7 @@ class Trainer:
             self.net = TPNativeLlama(self.model, tp_group, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
         else:
             self.model = build_model(cfg, seq, seed=seed, device=self.device)
-            self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
+            self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt, nvtx=nvtx)
         flat = self.net.flat
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
@@ -60,19 +61,33 @@ class Trainer:
         self.body_calls = 0
 
     # ------------------------------------------------------------------ step body
+    def _range(self, name):
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(name)
+
+    def _end(self):
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
+
     def _body(self):
         self.body_calls += 1
         total = None
         for i in range(self.microbatches):
+            self._range("forward")
             loss = self.net(self.idx[i], self.tgt[i])
+            self._end()
+            self._range("backward")
             (loss / self.microbatches).backward()
+            self._end()
             total = loss.detach() if total is None else total + loss.detach()
+        self._range("optimizer")
         if self.tp_group is not None:
             self.net.sync_replicated_grads()
         if self.dp is not None:
             self.dp.reduce_and_step(self.opt)
         else:
             self.opt.step()
+        self._end()
         self.loss.copy_(total / self.microbatches)
 
     def _capture(self, warmup=2):
