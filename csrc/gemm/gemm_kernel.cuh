@@ -286,14 +286,24 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       }
     }
   } else if constexpr (EPI == EPI_ROPE) {
+    // The tables duplicate their halves (cos[f] == cos[f + hd/2]), and every head of the tile
+    // uses the same row of them: each 32-wide slice of the first half is loaded once per tile
+    // and applied to all heads.
     const int hd = a.hd, half = hd / 2;
     const int tpos = rv ? row % a.T : 0;
     const float* cr = a.cos_t + (int64_t)tpos * hd;
     const float* sr = a.sin_t + (int64_t)tpos * hd;
 #pragma unroll 1
-    for (int hl = 0; hl < BN / hd; ++hl) {
+    for (int j = 0; j < half / 32; ++j) {
+      float cv[32], sv[32];
+#pragma unroll
+      for (int e4 = 0; e4 < 8; ++e4) {
+        const float4 c4 = ld_f4(cr + j * 32 + 4 * e4), s4 = ld_f4(sr + j * 32 + 4 * e4);
+        cv[4 * e4] = c4.x; cv[4 * e4 + 1] = c4.y; cv[4 * e4 + 2] = c4.z; cv[4 * e4 + 3] = c4.w;
+        sv[4 * e4] = s4.x; sv[4 * e4 + 1] = s4.y; sv[4 * e4 + 2] = s4.z; sv[4 * e4 + 3] = s4.w;
+      }
 #pragma unroll 1
-      for (int j = 0; j < half / 32; ++j) {
+      for (int hl = 0; hl < BN / hd; ++hl) {
         const int c1 = hl * hd + j * 32;
         const int col1 = nb * BN + c1;
         if (col1 >= a.N) break;
@@ -308,21 +318,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
           x2[e] = u2f(r2[e]);
         }
         if (col1 < a.rot_cols) {
-          const int f1 = j * 32, f2 = half + j * 32;
 #pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 c1v = ld_f4(cr + f1 + 4 * e4), s1v = ld_f4(sr + f1 + 4 * e4);
-            const float4 c2v = ld_f4(cr + f2 + 4 * e4), s2v = ld_f4(sr + f2 + 4 * e4);
-            const float c1a[4] = {c1v.x, c1v.y, c1v.z, c1v.w}, s1a[4] = {s1v.x, s1v.y, s1v.z, s1v.w};
-            const float c2a[4] = {c2v.x, c2v.y, c2v.z, c2v.w}, s2a[4] = {s2v.x, s2v.y, s2v.z, s2v.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int e = 4 * e4 + q;
-              const float y1 = x1[e] * c1a[q] - x2[e] * s1a[q];
-              const float y2 = x2[e] * c2a[q] + x1[e] * s2a[q];
-              x1[e] = y1;
-              x2[e] = y2;
-            }
+          for (int e = 0; e < 32; ++e) {
+            const float y1 = x1[e] * cv[e] - x2[e] * sv[e];
+            const float y2 = x2[e] * cv[e] + x1[e] * sv[e];
+            x1[e] = y1;
+            x2[e] = y2;
           }
         }
         uint8_t* b = st.acquire();

@@ -24,7 +24,7 @@ def _set(on: dict):
     Fn.SWIGLU_EPILOGUE["fwd"] = on["swiglu_fwd"]
     Fn.SWIGLU_EPILOGUE["bwd"] = on["swiglu_bwd"]
     Fn.FUSION["rope"] = on["rope"]
-    Fn.FUSION["head_ce"] = on["head_ce"]
+    Fn.FUSION["head_ce"] = on["head_ce"]  # True: always the fused head (the "all fused" row)
 
 
 def step_ms(cfg, batch, seq, steps, warmup):
@@ -70,6 +70,8 @@ def main():
         rows.append({"config": name, "ms_per_step": round(ms, 3), "loss": round(loss, 4)})
         print(f"{name:22s} {ms:8.3f} ms  loss {loss:.4f}", flush=True)
     _set({f: True for f in FUSIONS})
+    from llmt.ops import functions as Fn
+    Fn.FUSION["head_ce"] = "auto"
     base = rows[0]["ms_per_step"]
     savings = {r["config"][len("without "):]: round(r["ms_per_step"] - base, 3) for r in rows if r["config"].startswith("without")}
     savings["all"] = round(rows[-1]["ms_per_step"] - base, 3)

@@ -32,9 +32,13 @@ SWIGLU_EPILOGUE = {"fwd": "fwd" in _sw, "bwd": "bwd" in _sw}
 # kernels/ablate_kernels.py): "rope" = RoPE in the qkv GEMM epilogue (else the standalone
 # in-place RoPE kernel after a plain GEMM), "head_ce" = cross entropy reduced inside the head
 # GEMM's epilogue with logits never written (else bf16 logits + the row CE kernels).
-# LLMT_UNFUSE="rope,head_ce" switches them off.
+# LLMT_UNFUSE="rope,head_ce" switches them off. head_ce defaults to "auto": the fused head
+# recomputes the logit GEMM in its backward, which costs more than writing and re-reading bf16
+# logits while they are small, so logits are materialised up to HEAD_LOGITS_BUDGET bytes and
+# never beyond.
 _unf = os.environ.get("LLMT_UNFUSE", "")
-FUSION = {"rope": "rope" not in _unf, "head_ce": "head_ce" not in _unf}
+FUSION = {"rope": "rope" not in _unf, "head_ce": False if "head_ce" in _unf else "auto"}
+HEAD_LOGITS_BUDGET = 2 << 30
 
 
 class Embed(torch.autograd.Function):
@@ -260,7 +264,10 @@ class HeadCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, w, targets, chunk):
         ctx.w, ctx.chunk = w, chunk
-        if not FUSION["head_ce"]:
+        fused = FUSION["head_ce"]
+        if fused == "auto":
+            fused = h.shape[0] * w.shape[0] * 2 > HEAD_LOGITS_BUDGET
+        if not fused:
             logits = N.gemm(h, w.w16, ta=False, tb=True)
             lse = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
             loss_rows = torch.empty_like(lse)

@@ -88,3 +88,24 @@ def test_swiglu_unfused_paths_match_fp32(mode, monkeypatch):
     assert abs(loss.item() - loss_ref.item()) / loss_ref.item() < 1e-2
     for (name, p_ref), p in zip(ref.named_parameters(), ours.parameters()):
         assert rel_err(p.main_grad, p_ref.grad) < 5e-2, name
+
+
+@pytest.mark.parametrize("fusion", [{"head_ce": True}, {"head_ce": False}, {"rope": False}])
+def test_fusion_switches_match_fp32(fusion, monkeypatch):
+    """Fused head CE (logits never written) and materialised-logit CE, and RoPE as a separate
+    kernel, all give the fp32 model's loss and gradients."""
+    from llmt.config import get_config
+    from llmt.models.llama import make_batch
+    from llmt.ops import functions
+    monkeypatch.setattr(functions, "FUSION", {**functions.FUSION, **fusion})
+    cfg = get_config("tiny256")
+    ref, ours, net = _pair(cfg, 128)
+    idx, tgt = make_batch(2, 128, cfg.vocab, "cuda")
+    loss_ref = ref(idx, tgt)
+    loss_ref.backward()
+    loss = net(idx, tgt)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert abs(loss.item() - loss_ref.item()) / loss_ref.item() < 1e-2
+    for (name, p_ref), p in zip(ref.named_parameters(), ours.parameters()):
+        assert rel_err(p.main_grad, p_ref.grad) < 5e-2, name
