@@ -300,33 +300,49 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
-    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second
+    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second; column
+    // pairs (e, e + HD/2) 16 at a time, so no HD-wide row is held in registers
     if (ok && wait_bar(dkv_full, 0, err, 39)) {
       tc_fence_after();
-      float x[HD];
       const uint32_t col = half == 0 ? C_DK : C_DV;
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + col + c * 32, v);
+      const float sc = half == 0 ? a.scale : 1.f;
+      bf16* drow = a.dqkv + (int64_t)(row0 + min(kk, a.T - 1)) * a.ld_qkv +
+                   (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+#pragma unroll 1
+      for (int j = 0; j < HD / 32; ++j) {
+        uint32_t v1[16], v2[16];
+        tmem_ld16(tmem + lane_off + col + j * 16, v1);
+        tmem_ld16(tmem + lane_off + col + HD / 2 + j * 16, v2);
         tmem_wait_ld();
+        float x1[16], x2[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * (half == 0 ? a.scale : 1.f);
-      }
-      if (kk < a.T) {
-        if (half == 0) {
-          const float* cr = a.cos_t + (int64_t)kk * HD;
-          const float* sr = a.sin_t + (int64_t)kk * HD;
-#pragma unroll
-          for (int e = 0; e < HD / 2; ++e) {
-            const float x1 = x[e], x2 = x[e + HD / 2];
-            x[e] = x1 * cr[e] + x2 * sr[e + HD / 2];
-            x[e + HD / 2] = x2 * cr[e + HD / 2] - x1 * sr[e];
-          }
+        for (int e = 0; e < 16; ++e) {
+          x1[e] = __uint_as_float(v1[e]) * sc;
+          x2[e] = __uint_as_float(v2[e]) * sc;
         }
-        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+        if (kk < a.T) {
+          if (half == 0) {
+            const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD + j * 16);
+            const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD + j * 16);
 #pragma unroll
-        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(x + c * 8);
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 c1 = cr[e4], c2 = cr[e4 + HD / 8], s1 = sr[e4], s2 = sr[e4 + HD / 8];
+              const float cl[4] = {c1.x, c1.y, c1.z, c1.w}, ch[4] = {c2.x, c2.y, c2.z, c2.w};
+              const float sl[4] = {s1.x, s1.y, s1.z, s1.w}, sh[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int e = e4 * 4 + q;
+                const float a1 = x1[e], a2 = x2[e];
+                x1[e] = a1 * cl[q] + a2 * sh[q];
+                x2[e] = a2 * ch[q] - a1 * sl[q];
+              }
+            }
+          }
+          *reinterpret_cast<BF16x8*>(drow + j * 16) = float_to_bf16x8(x1);
+          *reinterpret_cast<BF16x8*>(drow + j * 16 + 8) = float_to_bf16x8(x1 + 8);
+          *reinterpret_cast<BF16x8*>(drow + HD / 2 + j * 16) = float_to_bf16x8(x2);
+          *reinterpret_cast<BF16x8*>(drow + HD / 2 + j * 16 + 8) = float_to_bf16x8(x2 + 8);
+        }
       }
     }
   }
@@ -362,14 +378,18 @@ struct BwdSmemP {
 };
 static_assert(BwdSmemP::TOTAL <= 232448, "pipelined attention backward exceeds 227 KB of shared memory");
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
+
+// Tiles are (kv head, 128-key block) pairs; a persistent CTA per SM walks its share in a
+// snake order over rounds (round r: tile r G + i, or r G + G - 1 - i on odd rounds), which
+// puts the long causal tiles (low key blocks) first and balances the CTAs' sums. Every
+// barrier phase runs on counters that continue across tiles, so one CTA keeps its TMEM,
+// barriers and warm caches for all of its tiles, and the MMAs of a tile's first query block
+// run while the compute warps finish the previous tile's dK / dV epilogue.
+__device__ __forceinline__ int snake_tile(int r, int i, int G) { return r * G + ((r & 1) ? (G - 1 - i) : i); }
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                           const AttnBwdArgs a) {
+                           const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
   using L = BwdSmemP;
   constexpr int HD = 64;
   constexpr int TMEM_COLS = 512;
@@ -382,27 +402,25 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
   uint8_t* smem = smem_raw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;     // [2]
-  uint64_t* q_empty = bars + 3;    // [2]
+  uint64_t* q_full = bars + 1;       // [2]
+  uint64_t* q_empty = bars + 3;      // [2]
   uint64_t* s_full = bars + 5;
-  uint64_t* pds_full = bars + 6;   // 256 arrivals
-  uint64_t* pds_empty = bars + 7;  // [2]
+  uint64_t* pds_full = bars + 6;     // 256 arrivals
+  uint64_t* pds_empty = bars + 7;    // [2]
   uint64_t* dq_full = bars + 9;
-  uint64_t* dq_free = bars + 10;   // 256 arrivals
+  uint64_t* dq_free = bars + 10;     // 256 arrivals
   uint64_t* dkv_full = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* stage_free = bars + 12;  // 8 arrivals: every compute warp's dQ reduce has read its staging
+  uint64_t* kv_empty = bars + 13;    // the tile's MMAs have finished reading K / V
+  uint64_t* dkv_free = bars + 14;    // 256 arrivals: the tile's dK / dV are out of TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bk = blockIdx.x;  // b * KV + kv head
-  const int kb = blockIdx.y;  // key block: y = 0 (most query blocks under causal) launches first
-  const int b = bk / a.KV, kvh = bk % a.KV;
   const int group = a.H / a.KV;
   const int nqb = (int)cdiv(a.T, kBN);
-  const int i_start = a.causal ? kb : 0;
-  const int n_i = nqb - i_start;
-  const int n_items = group * n_i;
-  const int row0 = b * a.T;
-  const int k0 = kb * kBM;
+  const int n_bk = a.B * a.KV;
+  const int n_tiles = n_bk * nqb;
+  const int G = gridDim.x;
   int* err = a.err;
   int tk = 0;  // trace slot of this thread
 
@@ -418,6 +436,9 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     bar_init(dq_full, 1);
     bar_init(dq_free, kComputeThreads);
     bar_init(dkv_full, 1);
+    bar_init(stage_free, 8);
+    bar_init(kv_empty, 1);
+    bar_init(dkv_free, kComputeThreads);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
@@ -426,28 +447,61 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // tile t -> (b, kv head, key block); key blocks vary slowest so low (long) ones come first
+  struct Tile {
+    int b, kvh, kb, i_start, n_i, n_items, row0, k0;
+  };
+  auto tile_of = [&](int t) {
+    Tile x;
+    x.kb = t / n_bk;
+    const int bk = t % n_bk;
+    x.b = bk / a.KV;
+    x.kvh = bk % a.KV;
+    x.i_start = a.causal ? x.kb : 0;
+    x.n_i = nqb - x.i_start;
+    x.n_items = group * x.n_i;
+    x.row0 = x.b * a.T;
+    x.k0 = x.kb * kBM;
+    return x;
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       trace_at(a.trace, 3, tk, 0);
       prefetch_tmap(&tm_qkv);
       prefetch_tmap(&tm_do);
-      const int kcol = (a.H + kvh) * HD, vcol = (a.H + a.KV + kvh) * HD;
-      bar_arrive_expect_tx(kv_full, 2 * L::TILE);
-      tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, row0 + k0);
-      tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, row0 + k0);
-      for (int n = 0; n < n_items; ++n) {
-        const int s = n & 1;
-        const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
-        if (!wait_bar(&q_empty[s], ((n >> 1) & 1) ^ 1, err, 41)) break;
-        trace_at(a.trace, 3, tk, 30);
-        const int nq = min(kBN, a.T - i * kBN);
-        const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
-        bar_arrive_expect_tx(&q_full[s], 2 * L::TILE + 2 * vbytes);
-        const int64_t vbase = ((int64_t)b * a.H + hq) * a.T + (int64_t)i * kBN;
-        bulk_load(smem + L::VEC_OFF + s * 1024, a.lse + vbase, vbytes, &q_full[s]);
-        bulk_load(smem + L::VEC_OFF + s * 1024 + 512, a.dsum + vbase, vbytes, &q_full[s]);
-        tma_load_2d(smem + L::Q_OFF + s * L::TILE, &tm_qkv, &q_full[s], hq * HD, row0 + i * kBN);
-        tma_load_2d(smem + L::DO_OFF + s * L::TILE, &tm_do, &q_full[s], hq * HD, row0 + i * kBN);
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r, ++tl) {
+        const int t = snake_tile(r, blockIdx.x, G);
+        if (t >= n_tiles) break;
+        const Tile x = tile_of(t);
+        if (a.trace != nullptr && t < 1024) {
+          uint32_t smid;
+          asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+          a.trace[1024 + 3 * t] = (long long)globaltimer();
+          a.trace[1024 + 3 * t + 1] = smid;
+        }
+        if (tl > 0 && !wait_bar(kv_empty, (tl - 1) & 1, err, 53)) break;
+        trace_at(a.trace, 3, tk, 31);
+        const int kcol = (a.H + x.kvh) * HD, vcol = (a.H + a.KV + x.kvh) * HD;
+        bar_arrive_expect_tx(kv_full, 2 * L::TILE);
+        tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, x.row0 + x.k0);
+        tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, x.row0 + x.k0);
+        for (int n = 0; n < x.n_items; ++n, ++it) {
+          const int s = it & 1;
+          const int hq = x.kvh * group + n / x.n_i, i = x.i_start + n % x.n_i;
+          if (!wait_bar(&q_empty[s], ((it >> 1) & 1) ^ 1, err, 41)) { ok = false; break; }
+          trace_at(a.trace, 3, tk, 30);
+          const int nq = min(kBN, a.T - i * kBN);
+          const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
+          bar_arrive_expect_tx(&q_full[s], 2 * L::TILE + 2 * vbytes);
+          const int64_t vbase = ((int64_t)x.b * a.H + hq) * a.T + (int64_t)i * kBN;
+          bulk_load(smem + L::VEC_OFF + s * 1024, a.lse + vbase, vbytes, &q_full[s]);
+          bulk_load(smem + L::VEC_OFF + s * 1024 + 512, a.dsum + vbase, vbytes, &q_full[s]);
+          tma_load_2d(smem + L::Q_OFF + s * L::TILE, &tm_qkv, &q_full[s], hq * HD, x.row0 + i * kBN);
+          tma_load_2d(smem + L::DO_OFF + s * L::TILE, &tm_do, &q_full[s], hq * HD, x.row0 + i * kBN);
+        }
       }
     }
   } else if (warp == 1) {
@@ -469,170 +523,230 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
                   id_s, k > 0);
         mma_commit(s_full);
       };
-      bool ok = wait_bar(kv_full, 0, err, 42) && wait_bar(&q_full[0], 0, err, 43);
-      if (ok) {
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r, ++tl) {
+        const int t = snake_tile(r, blockIdx.x, G);
+        if (t >= n_tiles) break;
+        const Tile x = tile_of(t);
+        if (!wait_bar(kv_full, tl & 1, err, 42)) break;
+        trace_at(a.trace, 0, tk, 7);
+        if (!wait_bar(&q_full[it & 1], (it >> 1) & 1, err, 43)) break;
+        trace_at(a.trace, 0, tk, 8);
         tc_fence_after();
-        issue_sdp(0);
-      }
-      for (int n = 0; n < n_items && ok; ++n) {
-        const int s = n & 1, pb = n & 1;
-        if (!wait_bar(pds_full, n & 1, err, 44)) { ok = false; break; }
-        trace_at(a.trace, 0, tk, 1);
-        tc_fence_after();
-        if (n + 1 < n_items) {  // S^T / dP^T columns were read out before pds_full arrived
-          if (!wait_bar(&q_full[(n + 1) & 1], ((n + 1) >> 1) & 1, err, 45)) { ok = false; break; }
-          trace_at(a.trace, 0, tk, 2);
-          issue_sdp((n + 1) & 1);
-        }
-        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::TILE);
-        const uint32_t do_addr = smem_u32(smem + L::DO_OFF + s * L::TILE);
-        const uint32_t p_addr = smem_u32(smem + L::P_OFF + pb * 32768);
-        const uint32_t ds_addr = smem_u32(smem + L::DS_OFF + pb * 32768);
+        issue_sdp(it & 1);
+        for (int n = 0; n < x.n_items; ++n) {
+          const int g = it + n;
+          const int s = g & 1, pb = g & 1;
+          if (!wait_bar(pds_full, g & 1, err, 44)) { ok = false; break; }
+          trace_at(a.trace, 0, tk, 1);
+          tc_fence_after();
+          if (n + 1 < x.n_items) {  // S^T / dP^T columns were read out before pds_full arrived
+            if (!wait_bar(&q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, err, 45)) { ok = false; break; }
+            trace_at(a.trace, 0, tk, 2);
+            issue_sdp((g + 1) & 1);
+          }
+          // the previous tile's dK / dV must be out of TMEM before they are overwritten
+          if (n == 0 && tl > 0 && !wait_bar(dkv_free, (tl - 1) & 1, err, 54)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(smem + L::Q_OFF + s * L::TILE);
+          const uint32_t do_addr = smem_u32(smem + L::DO_OFF + s * L::TILE);
+          const uint32_t p_addr = smem_u32(smem + L::P_OFF + pb * 32768);
+          const uint32_t ds_addr = smem_u32(smem + L::DS_OFF + pb * 32768);
 #pragma unroll
-        for (int k = 0; k < kBN / 16; ++k) {
-          const uint32_t offk = (k >> 2) * 16384 + (k & 3) * 32;  // K-major step over queries
-          const uint32_t offm = k * 2048;                          // MN-major step over queries
-          mma_f16(tmem + C_DV, make_sw128_desc(p_addr + offk, 16, 1024), make_sw128_desc(do_addr + offm, 16384, 1024),
-                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
-          mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024), make_sw128_desc(q_addr + offm, 16384, 1024),
-                  id_kv, (n > 0 || k > 0) ? 1u : 0u);
-        }
-        trace_at(a.trace, 0, tk, 4);
-        if (n > 0 && !wait_bar(dq_free, (n - 1) & 1, err, 46)) { ok = false; break; }
-        trace_at(a.trace, 0, tk, 5);
-        tc_fence_after();
+          for (int k = 0; k < kBN / 16; ++k) {
+            const uint32_t offk = (k >> 2) * 16384 + (k & 3) * 32;  // K-major step over queries
+            const uint32_t offm = k * 2048;                          // MN-major step over queries
+            mma_f16(tmem + C_DV, make_sw128_desc(p_addr + offk, 16, 1024),
+                    make_sw128_desc(do_addr + offm, 16384, 1024), id_kv, (n > 0 || k > 0) ? 1u : 0u);
+            mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024),
+                    make_sw128_desc(q_addr + offm, 16384, 1024), id_kv, (n > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&q_empty[s]);  // dQ reads no Q / dO: the stage can refill as soon as dV / dK are done
+          trace_at(a.trace, 0, tk, 4);
+          if (g > 0 && !wait_bar(dq_free, (g - 1) & 1, err, 46)) { ok = false; break; }
+          trace_at(a.trace, 0, tk, 5);
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < kBM / 16; ++k)  // contraction over keys
-          mma_f16(tmem + C_DQ, make_sw128_desc(ds_addr + k * 2048, 16384, 1024),
-                  make_sw128_desc(k_addr + k * 2048, 16384, 1024), id_q, k > 0);
-        mma_commit(dq_full);
-        mma_commit(&pds_empty[pb]);
-        mma_commit(&q_empty[s]);
-        trace_at(a.trace, 0, tk, 6);
+          for (int k = 0; k < kBM / 16; ++k)  // contraction over keys
+            mma_f16(tmem + C_DQ, make_sw128_desc(ds_addr + k * 2048, 16384, 1024),
+                    make_sw128_desc(k_addr + k * 2048, 16384, 1024), id_q, k > 0);
+          mma_commit(dq_full);
+          mma_commit(&pds_empty[pb]);
+          trace_at(a.trace, 0, tk, 6);
+        }
+        if (!ok) break;
+        mma_commit(dkv_full);  // this tile's dK / dV are final
+        mma_commit(kv_empty);  // and its K / V are no longer read
+        it += x.n_items;
       }
-      if (ok) mma_commit(dkv_full);
     }
   } else {
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // column half handled by this warp (2 warps per lane quadrant)
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const int kk = k0 + r;  // this thread's key (S^T / dP^T phase)
     const bool tr_thread = lane == 0 && (warp == 2 || warp == 9);
     const int tr_region = warp == 2 ? 1 : 2;
     bool ok = true;
-    // dQ of step m: TMEM -> registers -> fp32 reductions into dq_acc (one query row per thread)
-    auto drain_dq = [&](int m) -> bool {
-      if (!wait_bar(dq_full, m & 1, err, 47)) return false;
-      if (tr_thread) trace_at(a.trace, tr_region, tk, 13);
-      tc_fence_after();
-      const int hq = kvh * group + m / n_i, qrow = (i_start + m % n_i) * kBN + quad * 32 + lane;
-      const int col = half * 32;
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_off + C_DQ + col, v);
-      tmem_wait_ld();
-      tc_fence_before();
-      bar_arrive(dq_free);
-      if (qrow < a.T) {
-        float* dst = a.dq_acc + (int64_t)(row0 + qrow) * a.ld_dq + hq * HD + col;
+    int it = 0, tl = 0;
+    for (int rr = 0; ok; ++rr, ++tl) {
+      const int t = snake_tile(rr, blockIdx.x, G);
+      if (t >= n_tiles) break;
+      const Tile x = tile_of(t);
+      const int kk = x.k0 + r;  // this thread's key (S^T / dP^T phase)
+      // dQ of item n of this tile: TMEM -> registers -> scaled, staged as one 32 x 32 fp32 box per
+      // warp (SW128) in the item's P buffer (its MMAs are done) -> TMA reduce-add into dq_acc
+      auto drain_dq = [&](int n) -> bool {
+        const int g = it + n;
+        if (!wait_bar(dq_full, g & 1, err, 47)) return false;
+        if (tr_thread) trace_at(a.trace, tr_region, tk, 13);
+        tc_fence_after();
+        const int hq = x.kvh * group + n / x.n_i, qb = (x.i_start + n % x.n_i) * kBN;
+        const int col = half * 32;
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + C_DQ + col, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        bar_arrive(dq_free);
+        uint8_t* buf = smem + L::P_OFF + (g & 1) * 32768 + (warp - 2) * 4096;
 #pragma unroll
         for (int u = 0; u < 8; ++u)
-          red_add_v4(dst + 4 * u, __uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
-                     __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
-      }
-      return true;
-    };
-    for (int n = 0; n < n_items && ok; ++n) {
-      const int pb = n & 1;
-      const int i = i_start + n % n_i;
-      const int qbase = i * kBN;
-      const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n & 1) * 1024);
-      const float* d_s = lse_s + 128;
-      if (!wait_bar(s_full, n & 1, err, 48)) { ok = false; break; }
-      if (tr_thread) trace_at(a.trace, tr_region, tk, 10);
-      if (!wait_bar(&pds_empty[pb], ((n >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
-      tc_fence_after();
-      uint8_t* pt = smem + L::P_OFF + pb * 32768;
-      uint8_t* dst = smem + L::DS_OFF + pb * 32768;
-      const bool diag = a.causal && (qbase < k0 + kBM);
-      const bool key_ok = kk < a.T;
-      const bool q_tail = qbase + kBN > a.T;  // columns past T hold stale lse / D: mask them
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
+                          __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // rows past T (a ragged last block) carry zeros: their dS was masked
+          tma_reduce_add_2d(&tm_dq, buf, hq * HD + col, x.row0 + qb + quad * 32);
+          bulk_commit();
+        }
+        return true;
+      };
+      for (int n = 0; n < x.n_items && ok; ++n) {
+        const int g = it + n;
+        const int pb = g & 1;
+        const int i = x.i_start + n % x.n_i;
+        const int qbase = i * kBN;
+        const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (g & 1) * 1024);
+        const float* d_s = lse_s + 128;
+        if (!wait_bar(s_full, g & 1, err, 48)) { ok = false; break; }
+        if (tr_thread) trace_at(a.trace, tr_region, tk, 10);
+        if (!wait_bar(&pds_empty[pb], ((g >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
+        if (g >= 2) {
+          // buffer pb staged dQ(g - 2) for every warp's TMA reduce: all of them must have read it
+          if (lane == 0) {
+            bulk_wait_read<0>();
+            bar_arrive(stage_free);
+          }
+          __syncwarp();
+          if (!wait_bar(stage_free, (g - 2) & 1, err, 52)) { ok = false; break; }
+        }
+        tc_fence_after();
+        uint8_t* pt = smem + L::P_OFF + pb * 32768;
+        uint8_t* dst = smem + L::DS_OFF + pb * 32768;
+        // valid queries of this key row: [q_lo, q_hi) of the block (causal: query >= key; query < T;
+        // none for keys past T). One predicated loop serves the masked and the full blocks, which
+        // keeps the code small: the first block of every tile is masked.
+        const bool key_ok = kk < a.T;
+        const int q_lo = (a.causal && qbase < x.k0 + kBM) ? kk - qbase : 0;
+        const int q_hi = key_ok ? min(kBN, a.T - qbase) : 0;
 #pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
-        tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
-        tmem_wait_ld();
-        float p[32], ds[32];
-        if (diag || !key_ok || q_tail) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          uint32_t sv[32], dv[32];
+          tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
+          tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
+          tmem_wait_ld();
+          const int lo = q_lo - c * 32, hi = q_hi - c * 32;
+          const float4* l4 = reinterpret_cast<const float4*>(lse_s + c * 32);
+          const float4* d4 = reinterpret_cast<const float4*>(d_s + c * 32);
+          float p[32], ds[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qi = c * 32 + e;
-            const bool valid = key_ok && (!diag || qbase + qi >= kk) && qbase + qi < a.T;
-            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e)) : 0.f;
-            p[e] = pe;
-            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
-          }
-        } else {
+          for (int g4 = 0; g4 < 8; ++g4) {
+            const float4 lv = l4[g4], dd = d4[g4];
+            const float la[4] = {lv.x, lv.y, lv.z, lv.w}, da[4] = {dd.x, dd.y, dd.z, dd.w};
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qi = c * 32 + e;
-            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e));
-            p[e] = pe;
-            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          *reinterpret_cast<BF16x8*>(pt + sw_unit(r, c * 4 + u)) = float_to_bf16x8(p + u * 8);
-          *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
-        }
-      }
-      if (tr_thread) trace_at(a.trace, tr_region, tk, 12);
-      tc_fence_before();
-      fence_proxy_async_smem();
-      bar_arrive(pds_full);
-      if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
-      if (tr_thread) trace_at(a.trace, tr_region, tk, 14);
-    }
-    if (ok && n_items > 0) ok = drain_dq(n_items - 1);
-    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second
-    if (ok && wait_bar(dkv_full, 0, err, 50)) {
-      tc_fence_after();
-      float x[HD];
-      const uint32_t col = half == 0 ? C_DK : C_DV;
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + col + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * (half == 0 ? a.scale : 1.f);
-      }
-      if (kk < a.T) {
-        if (half == 0) {
-          const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD);
-          const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD);
-#pragma unroll
-          for (int e4 = 0; e4 < HD / 8; ++e4) {
-            const float4 c1 = cr[e4], c2 = cr[e4 + HD / 8], s1 = sr[e4], s2 = sr[e4 + HD / 8];
-            const float cl[4] = {c1.x, c1.y, c1.z, c1.w}, ch[4] = {c2.x, c2.y, c2.z, c2.w};
-            const float sl[4] = {s1.x, s1.y, s1.z, s1.w}, sh[4] = {s2.x, s2.y, s2.z, s2.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int e = e4 * 4 + j;
-              const float x1 = x[e], x2 = x[e + HD / 2];
-              x[e] = x1 * cl[j] + x2 * sh[j];
-              x[e + HD / 2] = x2 * ch[j] - x1 * sl[j];
+            for (int q = 0; q < 4; ++q) {
+              const int e = 4 * g4 + q;
+              float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -la[q] * kLog2e));
+              pe = (e >= lo && e < hi) ? pe : 0.f;
+              p[e] = pe;
+              ds[e] = pe * (__uint_as_float(dv[e]) - da[q]);
             }
           }
-        }
-        bf16* drow = a.dqkv + (int64_t)(row0 + kk) * a.ld_qkv + (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
 #pragma unroll
-        for (int c = 0; c < HD / 8; ++c) *reinterpret_cast<BF16x8*>(drow + c * 8) = float_to_bf16x8(x + c * 8);
+          for (int u = 0; u < 4; ++u) {
+            *reinterpret_cast<BF16x8*>(pt + sw_unit(r, c * 4 + u)) = float_to_bf16x8(p + u * 8);
+            *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
+          }
+        }
+        if (tr_thread) trace_at(a.trace, tr_region, tk, 12);
+        tc_fence_before();
+        fence_proxy_async_smem();
+        bar_arrive(pds_full);
+        if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
+        if (tr_thread) trace_at(a.trace, tr_region, tk, 14);
       }
+      if (ok && x.n_items > 0) ok = drain_dq(x.n_items - 1);
+      // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second; column
+      // pairs (e, e + 32) are handled 16 at a time to keep registers low
+      if (ok && wait_bar(dkv_full, tl & 1, err, 50)) {
+        if (tr_thread) trace_at(a.trace, tr_region, tk, 15);
+        tc_fence_after();
+        const uint32_t col = half == 0 ? C_DK : C_DV;
+        const float sc = half == 0 ? a.scale : 1.f;
+        bf16* drow = a.dqkv + (int64_t)(x.row0 + min(kk, a.T - 1)) * a.ld_qkv +
+                     (half == 0 ? (a.H + x.kvh) : (a.H + a.KV + x.kvh)) * HD;
+#pragma unroll 1
+        for (int j = 0; j < 2; ++j) {
+          uint32_t v1[16], v2[16];
+          tmem_ld16(tmem + lane_off + col + j * 16, v1);
+          tmem_ld16(tmem + lane_off + col + 32 + j * 16, v2);
+          tmem_wait_ld();
+          if (j == 1) {
+            tc_fence_before();
+            bar_arrive(dkv_free);  // the next tile's dV / dK may overwrite these columns now
+          }
+          float x1[16], x2[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            x1[e] = __uint_as_float(v1[e]) * sc;
+            x2[e] = __uint_as_float(v2[e]) * sc;
+          }
+          if (kk < a.T) {
+            if (half == 0) {
+              const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD + j * 16);
+              const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD + j * 16);
+#pragma unroll
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const float4 c1 = cr[e4], c2 = cr[e4 + 8], s1 = sr[e4], s2 = sr[e4 + 8];
+                const float cl[4] = {c1.x, c1.y, c1.z, c1.w}, ch[4] = {c2.x, c2.y, c2.z, c2.w};
+                const float sl[4] = {s1.x, s1.y, s1.z, s1.w}, sh[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int e = e4 * 4 + q;
+                  const float a1 = x1[e], a2 = x2[e];
+                  x1[e] = a1 * cl[q] + a2 * sh[q];
+                  x2[e] = a2 * ch[q] - a1 * sl[q];
+                }
+              }
+            }
+            *reinterpret_cast<BF16x8*>(drow + j * 16) = float_to_bf16x8(x1);
+            *reinterpret_cast<BF16x8*>(drow + j * 16 + 8) = float_to_bf16x8(x1 + 8);
+            *reinterpret_cast<BF16x8*>(drow + 32 + j * 16) = float_to_bf16x8(x2);
+            *reinterpret_cast<BF16x8*>(drow + 32 + j * 16 + 8) = float_to_bf16x8(x2 + 8);
+          }
+        }
+      } else {
+        ok = false;
+      }
+      if (tr_thread && warp == 2 && a.trace != nullptr && t < 1024) a.trace[1024 + 3 * t + 2] = (long long)globaltimer();
+      it += x.n_items;
     }
+    if (lane == 0) bulk_wait<0>();  // this warp's dQ reductions are complete before exit
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -721,8 +835,8 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const AttnBwdArgs& args,
-                                 cudaStream_t st) {
+cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
+                                 const AttnBwdArgs& args, cudaStream_t st) {
   constexpr size_t smem = BwdSmemP::TOTAL;
   static bool attr = false;
   if (!attr) {
@@ -731,16 +845,16 @@ cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, 
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid(args.B * args.KV, (unsigned)cdiv(args.T, kBM));
-  flash_bwd_pipelined_kernel<<<grid, kBwdThreads, smem, st>>>(tq, tdo, args);
+  const int tiles = args.B * args.KV * (int)cdiv(args.T, kBM);
+  flash_bwd_pipelined_kernel<<<std::min(tiles, sm_count()), kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-// Event tracing of the pipelined backward (for profiling): a zeroed device buffer of 1024
+// Event tracing of the pipelined backward (for profiling): a zeroed device buffer of 4096
 // int64 (4 regions of 256 events of CTA (0, 0): MMA thread, compute warps 2 and 9, TMA
-// thread), or nullptr to turn it off.
+// thread; then per CTA (up to 1024) its start time, SM and end time in ns), or nullptr.
 static long long* g_bwd_trace = nullptr;
 void attn_bwd_set_trace(long long* buf) { g_bwd_trace = buf; }
 
@@ -789,7 +903,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
       make_tmap_2d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * hd, rows, (uint64_t)H * hd, 32, 32,
                    CU_TENSOR_MAP_SWIZZLE_128B);
   LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
-  cudaError_t e = hd == 64 ? launch_bwd_pipelined(tq, tdo, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
+  cudaError_t e = hd == 64 ? launch_bwd_pipelined(tq, tdo, tdq, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
   if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);

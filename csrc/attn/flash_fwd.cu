@@ -61,7 +61,7 @@ struct FwdSmem {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads, HD == 64 ? 2 : 1)
+__global__ void __launch_bounds__(kAttnThreads, 2)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
   using L = FwdSmem<HD>;
   constexpr int ST = L::STAGES;

@@ -439,8 +439,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("attn_bwd_set_trace", [](c10::optional<at::Tensor> buf) {
     if (buf && buf->defined()) {
-      CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 1024,
-            "trace buffer: 1024 int64 on the GPU");
+      CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 4096,
+            "trace buffer: 4096 int64 on the GPU");
       llmt::attn_bwd_set_trace(reinterpret_cast<long long*>(buf->data_ptr<int64_t>()));
     } else {
       llmt::attn_bwd_set_trace(nullptr);

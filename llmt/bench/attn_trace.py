@@ -19,7 +19,8 @@ import torch
 
 NAMES = {0: "start", 30: "tma:stage free", 1: "mma:P/dS ready", 2: "mma:S/dP out, next Q landed",
          4: "mma:dV/dK issued", 5: "mma:dQ tmem free", 6: "mma:dQ issued", 10: "S/dP ready", 12: "P/dS written",
-         13: "dQ ready", 14: "dQ drained", 15: "dK/dV ready"}
+         13: "dQ ready", 14: "dQ drained", 15: "dK/dV ready", 7: "mma:tile K/V landed", 8: "mma:tile first Q landed",
+         31: "tma:K/V stage free"}
 REGIONS = ["mma", "w2", "w9", "tma"]
 
 
@@ -41,14 +42,34 @@ def main():
     do = torch.randn_like(o)
     for _ in range(3):
         N.flash_attn_bwd(do, qkv, o, lse, cos, sin, B, T, H, KV, hd)
-    buf = torch.zeros(1024, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(4096, dtype=torch.int64, device="cuda")
     ext = N.ext()._mod
     ext.attn_bwd_set_trace(buf)
     N.flash_attn_bwd(do, qkv, o, lse, cos, sin, B, T, H, KV, hd)
     torch.cuda.synchronize()
     ext.attn_bwd_set_trace(None)
+    spans = buf[1024:1024 + 3 * 1024].view(1024, 3).tolist()
+    spans = [(s0, sm, e0) for s0, sm, e0 in spans if s0 > 0]
+    if spans:
+        t_begin = min(s0 for s0, _, _ in spans)
+        t_end = max(e0 for _, _, e0 in spans)
+        durs = sorted(e0 - s0 for s0, _, e0 in spans)
+        per_sm = {}
+        for s0, sm, e0 in spans:
+            per_sm.setdefault(sm, []).append((s0, e0))
+        busy = [sum(e - b for b, e in v) for v in per_sm.values()]
+        print(f"CTAs {len(spans)} on {len(per_sm)} SMs; kernel span {(t_end - t_begin) / 1e3:.1f} us; "
+              f"CTA duration us min/median/max {durs[0] / 1e3:.1f}/{durs[len(durs) // 2] / 1e3:.1f}/{durs[-1] / 1e3:.1f}; "
+              f"SM busy us min/mean/max {min(busy) / 1e3:.1f}/{sum(busy) / len(busy) / 1e3:.1f}/{max(busy) / 1e3:.1f}")
+        by_kb = {}
+        nx = B * KV
+        for c, (s0, sm, e0) in enumerate(buf[1024:1024 + 3 * 1024].view(1024, 3).tolist()):
+            if s0 > 0:
+                by_kb.setdefault(c // nx, []).append((e0 - s0) / 1e3)
+        print("CTA duration by key block (us, mean):",
+              {k: round(sum(v) / len(v), 1) for k, v in sorted(by_kb.items())})
     ev = []
-    for reg, vals in enumerate(buf.view(4, 256).tolist()):
+    for reg, vals in enumerate(buf[:1024].view(4, 256).tolist()):
         ev += [(int(x) >> 8, int(x) & 0xFF, REGIONS[reg]) for x in vals if x != 0]
     ev.sort()
     t0 = ev[0][0] if ev else 0
