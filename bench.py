@@ -236,7 +236,7 @@ def main():
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile",
                    help="reference ladder row (default: its fastest bf16 row on B200)")
-    p.add_argument("--dp-mode", default="fused", choices=["fused", "nccl"])
+    p.add_argument("--dp-mode", default="fused", choices=["fused", "nccl", "fused-overlap"])
     p.add_argument("--no-graph", action="store_true")
     args = p.parse_args()
     if args.warmup < 3:

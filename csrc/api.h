@@ -132,7 +132,7 @@ cudaError_t dp_barrier(uint32_t* const* pads_dev, uint32_t* my_pad, uint32_t* ep
                        cudaStream_t st);
 cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, float* master, float* m, float* v,
                            int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
-                           cudaStream_t st);
+                           cudaStream_t st, int max_blocks = 0);
 int dp_error_code(bool reset);
 
 }  // namespace llmt

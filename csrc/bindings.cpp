@@ -373,7 +373,7 @@ void dp_barrier(at::Tensor pads_dev, int64_t my_pad, at::Tensor epoch, int64_t r
 
 void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor master, at::Tensor m, at::Tensor v,
                     int64_t lo, int64_t n, at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd,
-                    double grad_scale, int64_t world) {
+                    double grad_scale, int64_t world, int64_t max_blocks) {
   CHECK_DT(grads_dev, at::kLong);
   CHECK_DT(shadows_dev, at::kLong);
   CHECK(grads_dev.numel() == world && shadows_dev.numel() == world, "peer pointer arrays must have world entries");
@@ -382,7 +382,7 @@ void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor mas
   ok(llmt::dp_fused_adamw(reinterpret_cast<float* const*>(grads_dev.data_ptr<int64_t>()),
                           reinterpret_cast<void* const*>(shadows_dev.data_ptr<int64_t>()), master.data_ptr<float>(),
                           m.data_ptr<float>(), v.data_ptr<float>(), lo, n, lr.data_ptr<float>(), step.data_ptr<int>(),
-                          h, (int)world, stream()),
+                          h, (int)world, stream(), (int)max_blocks),
      "dp_fused_adamw");
 }
 
@@ -453,6 +453,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_free", &ipc_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("dp_barrier", &dp_barrier);
-  m.def("dp_fused_adamw", &dp_fused_adamw);
+  m.def("dp_fused_adamw", &dp_fused_adamw, "grads_dev"_a, "shadows_dev"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a,
+        "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "world"_a, "max_blocks"_a = 0);
   m.def("dp_error_code", &llmt::dp_error_code, "reset"_a = false);
 }

@@ -160,11 +160,13 @@ cudaError_t dp_barrier(uint32_t* const* pads_dev, uint32_t* my_pad, uint32_t* ep
 
 cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, float* master, float* m, float* v,
                            int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
-                           cudaStream_t st) {
+                           cudaStream_t st, int max_blocks) {
   LLMT_REQUIRE(n % 4 == 0 && lo % 4 == 0, "dp_fused_adamw: shard bounds must be multiples of 4");
   if (n == 0) return cudaSuccess;
   DpArgs a{grads_dev, reinterpret_cast<bf16* const*>(shadows_dev), master, m, v, lo, n, lr, step, h, world};
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4, 256), sm_count() * 4));
+  // max_blocks > 0 keeps the kernel to a few SMs when it runs beside the backward
+  const int64_t cap = max_blocks > 0 ? max_blocks : sm_count() * 4;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4, 256), cap));
   switch (world) {
     case 2: dp_fused_adamw_kernel<2><<<grid, 256, 0, st>>>(a); break;
     case 4: dp_fused_adamw_kernel<4><<<grid, 256, 0, st>>>(a); break;

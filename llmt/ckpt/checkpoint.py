@@ -37,6 +37,15 @@ def _flat_opt_state(opt, flat):
     """(exp_avg, exp_avg_sq, step) as full-length flat fp32 buffers (gathering ZeRO-1 shards)."""
     world, _ = _world()
     step = int(opt.step_t.item())
+    if hasattr(opt, "ranges"):  # BucketShardedAdamW: chunk r of every bucket
+        m = torch.zeros(flat.numel, dtype=torch.float32, device=flat.master.device)
+        v = torch.zeros_like(m)
+        for (lo, hi), moff in zip(flat.buckets, opt.moffs):
+            c = (hi - lo) // world
+            dist.all_gather_into_tensor(m[lo:hi], opt.exp_avg[moff:moff + c].contiguous())
+            dist.all_gather_into_tensor(v[lo:hi], opt.exp_avg_sq[moff:moff + c].contiguous())
+        opt.gather_master()
+        return m, v, step, flat.master
     if hasattr(opt, "lo"):  # ShardedAdamW
         m = _full_flat(opt.exp_avg, flat.numel, world)
         v = _full_flat(opt.exp_avg_sq, flat.numel, world)

@@ -47,20 +47,35 @@ def param_order(model: LlamaModel):
 class FlatParams:
     """Flat fp32 master / fp32 grad / bf16 shadow storage behind a model's parameters."""
 
-    def __init__(self, model: LlamaModel, device, pad_to: int = 1):
+    def __init__(self, model: LlamaModel, device, pad_to: int = 1, bucket_pad: bool = False):
+        """pad_to: the buffer length is a multiple of ALIGN * pad_to (data-parallel sharding).
+        bucket_pad: every block's parameters, and the trailing emb / norm_f / head group, start and
+        end on such a boundary too, so each of these buckets splits into pad_to equal chunks
+        (the overlapped data-parallel step shards every bucket); `buckets` lists them in order."""
         self.names = []
         self.params = []
         self.offsets = []
+        self.buckets = []
         off = 0
+        unit = ALIGN * pad_to
+        cur, b_lo = None, 0
         for name, p in param_order(model):
+            group = name.split(".")[1] if name.startswith("blocks.") else "tail"
+            if bucket_pad and group != cur:
+                if cur is not None:
+                    off += (-off) % unit
+                    self.buckets.append((b_lo, off))
+                cur, b_lo = group, off
             if off % ALIGN:
                 off += ALIGN - off % ALIGN
             self.names.append(name)
             self.params.append(p)
             self.offsets.append(off)
             off += p.numel()
-        if off % (ALIGN * pad_to):
-            off += ALIGN * pad_to - off % (ALIGN * pad_to)
+        if off % unit:
+            off += unit - off % unit
+        if bucket_pad and cur is not None:
+            self.buckets.append((b_lo, off))
         self.numel = off
         dev = torch.device(device)
         self.master = torch.zeros(off, dtype=torch.float32, device=dev)
@@ -106,15 +121,18 @@ class NativeLlama:
     A plain wrapper (not an nn.Module), so model.state_dict() keeps the reference keys."""
 
     def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
-                 nvtx: bool = False):
+                 nvtx: bool = False, bucket_pad: bool = False):
         self.model = model
+        # grad_ready(i) is called from the backward once block i's gradients have all been issued
+        # (a hook on the gradient of the block's input): the overlapped data-parallel step uses it
+        self.grad_ready = None
         self.ckpt = ckpt
         self.nvtx = nvtx  # NVTX range per block (reference bench_train.py:215-222)
         self.cfg = model.cfg
         dev = model.emb.weight.device
         if dev.type != "cuda":
             raise RuntimeError("the native path runs on CUDA (sm_100a) only")
-        self.flat = FlatParams(model, dev, pad_to=pad_to)
+        self.flat = FlatParams(model, dev, pad_to=pad_to, bucket_pad=bucket_pad)
         self.ce_chunk = ce_chunk
 
     def forward(self, idx, targets):
@@ -125,6 +143,8 @@ class NativeLlama:
         x = Fn.Embed.apply(idx.reshape(-1), m.emb.weight)
         a, r = None, x
         for i, blk in enumerate(m.blocks):
+            if self.grad_ready is not None and r.requires_grad and torch.is_grad_enabled():
+                r.register_hook(lambda g, i=i: self.grad_ready(i))
             if self.nvtx:
                 torch.cuda.nvtx.range_push(f"block{i}")
             if self.ckpt and torch.is_grad_enabled():

@@ -53,13 +53,30 @@ class ShardedAdamW:
 
 class DataParallel:
     def __init__(self, world_size: int, rank: int, mode: str = "nccl", group=None):
+        """mode: "nccl" (reduce-scatter / all-gather), "fused" (one peer-memory kernel after the
+        backward) or "fused-overlap" (that kernel per bucket, overlapped with the backward)."""
         self.world_size, self.rank, self.mode, self.group = world_size, rank, mode, group
         self.flat = None
         self.fused = None
 
+    @property
+    def overlap(self):
+        return self.mode == "fused-overlap"
+
     def make_optimizer(self, flat, lr=3e-4, **kw):
         if flat.numel % self.world_size:
             raise ValueError("flat buffer must be padded to a multiple of the world size")
+        if self.overlap:
+            if not flat.buckets:
+                raise ValueError("fused-overlap needs a bucket-padded flat buffer (FlatParams(bucket_pad=True))")
+            self.flat = flat
+            opt = BucketShardedAdamW(flat, self.rank, self.world_size, lr=lr, **kw)
+            src = dist.get_global_rank(self.group, 0) if self.group is not None else 0
+            dist.broadcast(flat.master, src, group=self.group)
+            flat.refresh_shadow()
+            from llmt.parallel.fused_dp import OverlappedFusedDP
+            self.fused = OverlappedFusedDP(flat, opt, self.rank, self.world_size, self.group)
+            return opt
         shard = flat.numel // self.world_size
         self.flat = flat
         lo, hi = self.rank * shard, (self.rank + 1) * shard
@@ -74,9 +91,32 @@ class DataParallel:
             self.fused = FusedDP(flat, opt, self.rank, self.world_size, self.group)
         return opt
 
+    def begin_step(self):
+        if self.overlap:
+            self.fused.begin_step()
+
+    def bucket_ready(self, b):
+        if self.overlap:
+            self.fused.bucket_ready(b)
+
+    def gather_master(self, opt):
+        """Full fp32 masters on every rank (ZeRO-1 leaves other ranks' shards stale)."""
+        f = self.flat
+        if isinstance(opt, BucketShardedAdamW):
+            opt.gather_master(self.group)
+            return
+        shard = f.numel // self.world_size
+        full = torch.empty_like(f.master)
+        dist.all_gather_into_tensor(full, f.master[self.rank * shard:(self.rank + 1) * shard].contiguous(),
+                                    group=self.group)
+        f.master.copy_(full)
+
     @torch.no_grad()
     def reduce_and_step(self, opt: ShardedAdamW):
         f = self.flat
+        if self.overlap:
+            self.fused.finish_step()
+            return
         if self.fused is not None:
             self.fused.step()
             return
@@ -89,3 +129,37 @@ class DataParallel:
         if self.fused is not None:
             self.fused.close()
             self.fused = None
+
+
+class BucketShardedAdamW:
+    """AdamW state for this rank's chunk of every bucket of a bucket-padded flat buffer
+    (FlatParams(bucket_pad=True)): bucket (lo, hi) splits into `world` equal chunks and rank r
+    owns chunk r of each; m / v hold the owned chunks back to back. The overlapped fused
+    data-parallel step updates one bucket as soon as its gradients are final."""
+
+    def __init__(self, flat, rank, world, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1):
+        self.flat, self.rank, self.world = flat, rank, world
+        self.ranges, self.moffs = [], []
+        moff = 0
+        for lo, hi in flat.buckets:
+            c = (hi - lo) // world
+            self.ranges.append((lo + rank * c, lo + (rank + 1) * c))
+            self.moffs.append(moff)
+            moff += c
+        dev = flat.master.device
+        self.exp_avg = torch.zeros(moff, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(moff, dtype=torch.float32, device=dev)
+        self.lr_t = torch.full((1,), float(lr), dtype=torch.float32, device=dev)
+        self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.betas, self.eps, self.weight_decay, self.grad_scale = betas, eps, weight_decay, 1.0 / world
+
+    def set_lr(self, lr):
+        self.lr_t.fill_(float(lr))
+
+    def gather_master(self, group=None):
+        """Every rank's master chunks -> the full fp32 master on every rank (checkpoints, checks)."""
+        f = self.flat
+        for (lo, hi) in f.buckets:
+            c = (hi - lo) // self.world
+            mine = f.master[lo + self.rank * c:lo + (self.rank + 1) * c].clone()
+            dist.all_gather_into_tensor(f.master[lo:hi], mine, group=group)

@@ -21,7 +21,7 @@ import torch.distributed as dist
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--mode", default="fused", choices=["fused", "nccl"])
+    p.add_argument("--mode", default="fused", choices=["fused", "nccl", "fused-overlap"])
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--graph", action="store_true")
     args = p.parse_args()
@@ -43,18 +43,18 @@ def main():
         tr.train_step(*batches[rank])
     torch.cuda.synchronize()
     err_code = native.ext().dp_error_code(False)
-    # gather the sharded fp32 masters into rank 0's view
+    # gather the sharded fp32 masters into every rank's view
     f = tr.net.flat
-    shard = f.numel // world
-    full = torch.empty_like(f.master)
-    dist.all_gather_into_tensor(full, f.master[rank * shard:(rank + 1) * shard].contiguous())
+    dp.gather_master(tr.opt)
+    full = f.master
     ok = True
     res = {"mode": args.mode, "world": world, "dp_error_code": err_code}
     if rank == 0:
         ref = Trainer(cfg, B * world, T, device=f"cuda:{local}", cuda_graph=False, microbatches=world)
         idx = torch.cat([b[0] for b in batches])
         tgt = torch.cat([b[1] for b in batches])
-        for _ in range(args.steps):
+        # a graph trainer runs two eager warm-up steps before its first replay
+        for _ in range(args.steps + (2 if args.graph else 0)):
             ref.train_step(idx, tgt)
         rf = ref.net.flat.master
         rel = ((full - rf).norm() / rf.norm()).item()

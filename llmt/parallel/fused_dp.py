@@ -88,3 +88,61 @@ class FusedDP:
         for p in self._own:
             C.ipc_free(p)
         self._own = []
+
+
+class OverlappedFusedDP(FusedDP):
+    """The fused data-parallel step, one bucket (a block's parameters, or the trailing emb /
+    norm_f / head group) at a time, overlapped with the rest of the backward.
+
+    When a block's backward has been issued (a hook on the gradient of the block's input), a
+    side stream waits for that point, passes a flag barrier (every rank's gradients of the bucket
+    are final) and runs the fused reduce + AdamW + bf16 all-gather on this rank's chunk of the
+    bucket, on at most `max_blocks` CTAs so the backward keeps the rest of the GPU. After the
+    backward the trailing bucket follows, then a final barrier (every rank's new weights are in
+    every peer's buffer) that the main stream joins before the next forward."""
+
+    def __init__(self, flat, opt, rank: int, world: int, group=None, max_blocks: int = 32):
+        super().__init__(flat, opt, rank, world, group)
+        self.max_blocks = max_blocks
+        self.side = torch.cuda.Stream(device=self.device)
+        self.armed = False
+        self.started = False
+        self.done = set()
+
+    def begin_step(self):
+        """Arm the bucket hooks for the backward that follows (the last micro-batch's)."""
+        self.armed, self.started, self.done = True, False, set()
+
+    def _bucket(self, b):
+        C, o, f = N.ext(), self.opt, self.flat
+        lo, hi = o.ranges[b]
+        moff = o.moffs[b]
+        n = hi - lo
+        if not self.started:
+            o.step_t.add_(1)
+            self.started = True
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 700)
+        b1, b2 = o.betas
+        C.dp_fused_adamw(self.grads_dev, self.shadows_dev, f.master, o.exp_avg[moff:moff + n],
+                         o.exp_avg_sq[moff:moff + n], lo, n, o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay,
+                         o.grad_scale, self.world, self.max_blocks)
+
+    def bucket_ready(self, b):
+        """Called (from the backward's hooks) when bucket b's gradients have all been issued."""
+        if not self.armed or b in self.done:
+            return
+        self.done.add(b)
+        cur = torch.cuda.current_stream(self.device)
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            self._bucket(b)
+
+    @torch.no_grad()
+    def finish_step(self):
+        for b in range(len(self.opt.ranges)):  # the trailing bucket, and any a hook did not reach
+            self.bucket_ready(b)
+        cur = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.side):
+            N.ext().dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 800)
+        cur.wait_stream(self.side)
+        self.armed = False

@@ -61,7 +61,8 @@ def _phase(kind, code):
         base = (code // 100) * 100
         names = {100: "data-parallel barrier before the update", 200: "data-parallel barrier after the update",
                  300: "tensor-parallel all-gather barrier", 400: "tensor-parallel reduce-scatter barrier",
-                 500: "tensor-parallel GEMM reduce-scatter barrier", 600: "tensor-parallel backward all-gather barrier"}
+                 500: "tensor-parallel GEMM reduce-scatter barrier", 600: "tensor-parallel backward all-gather barrier",
+                 700: "overlapped data-parallel bucket barrier", 800: "overlapped data-parallel final barrier"}
         return f"{names.get(base, f'barrier {base}')}, waiting for peer {code - base}"
     return f"code {code}"
 

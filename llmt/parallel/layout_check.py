@@ -55,13 +55,8 @@ def main():
     codes = {"gemm": native.gemm_error_code(), "attn": native.attn_error_code(), "dp": native.ext().dp_error_code(False)}
     # ZeRO-1 keeps other ranks' master shards stale on this rank: gather the data-parallel
     # shards first so every rank holds its stage's current masters
-    f = tr.x.flat
     if tr.dp is not None:
-        shard = f.numel // args.dp
-        full = torch.empty_like(f.master)
-        dist.all_gather_into_tensor(full, f.master[g.dp_rank * shard:(g.dp_rank + 1) * shard].contiguous(),
-                                    group=g.dp_group)
-        f.master.copy_(full)
+        tr.dp.gather_master(tr.opt)
     mine = {k: v.detach().float().cpu() for k, v in tr.stage.global_state_dict().items()}
     allsd = [None] * world
     dist.all_gather_object(allsd, {"coords": (g.dp_rank, g.pp_rank, g.tp_rank), "sd": mine, "losses": losses})

@@ -44,7 +44,13 @@ class Trainer:
             self.net = TPNativeLlama(self.model, tp_group, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
         else:
             self.model = build_model(cfg, seq, seed=seed, device=self.device)
-            self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt, nvtx=nvtx)
+            overlap = dp is not None and getattr(dp, "overlap", False)
+            self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt, nvtx=nvtx,
+                                   bucket_pad=overlap)
+            if overlap:
+                if ckpt:
+                    raise ValueError("the overlapped data-parallel step needs ckpt=False")
+                self.net.grad_ready = dp.bucket_ready
         flat = self.net.flat
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
@@ -77,6 +83,8 @@ class Trainer:
             loss = self.net(self.idx[i], self.tgt[i])
             self._end()
             self._range("backward")
+            if self.dp is not None and i == self.microbatches - 1:
+                self.dp.begin_step()  # the last micro-batch's backward releases the buckets
             (loss / self.microbatches).backward()
             self._end()
             total = loss.detach() if total is None else total + loss.detach()
