@@ -1,0 +1,113 @@
+"""ASTRA-sim driver for the exported Chakra workloads (the reference's
+workload_export/run_astra_sim.py).
+
+Writes, next to the per-rank `workload.<r>.et` files of llmt.export.trace, the inputs an
+ASTRA-sim analytical run needs -- a network description (one switch level per node of
+`gpus_per_node` GPUs at the NVLink 5 constants of llmt/perf/links.json, then the
+inter-node link), a system description, an (empty) remote-memory description and the
+communicator groups -- and runs the simulator when a binary is given (--bin or the
+ASTRA_SIM_BIN environment variable). Acceptance follows the reference's crash-tolerant rule:
+a run counts if every rank reported a finish tick and they agree (the simulator's exit code is
+not trusted on its own). The predicted step time is then set against llmt.perf.scaling's
+prediction for the same layout.
+
+ASTRA-sim is not installed in this image; without a binary the inputs are written and the
+result says so.
+
+    python -m llmt.export.astra --size medium --dp 2 --tp 2 --pp 2 --microbatches 4 --out traces
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import shutil
+import subprocess
+
+from llmt.config import SIZES
+from llmt.perf.scaling import load_links
+
+
+def network_yml(world, gpus_per_node, intra, inter):
+    """Two-dimensional switch topology: GPUs of a node behind NVSwitch, nodes behind the IB fabric."""
+    nodes = max(1, (world + gpus_per_node - 1) // gpus_per_node)
+    per = min(world, gpus_per_node)
+    dims = [(per, intra)] + ([(nodes, inter)] if nodes > 1 else [])
+    return ("topology: [ " + ", ".join("Switch" for _ in dims) + " ]\n"
+            f"npus_count: [ {', '.join(str(n) for n, _ in dims)} ]\n"
+            f"bandwidth: [ {', '.join(str(lk['bw_gbs']) for _, lk in dims)} ]  # GB/s\n"
+            f"latency: [ {', '.join(str(lk['latency_us'] * 1000.0) for _, lk in dims)} ]  # ns\n")
+
+
+def system_json(collective="ring"):
+    return {"scheduling-policy": "LIFO", "endpoint-delay": 10, "active-chunks-per-dimension": 1,
+            "preferred-dataset-splits": 4, "all-reduce-implementation": [collective],
+            "all-gather-implementation": [collective], "reduce-scatter-implementation": [collective],
+            "all-to-all-implementation": ["direct"], "collective-optimization": "localBWAware",
+            "local-mem-bw": 6417, "boost-mode": 0}
+
+
+def write_inputs(outdir, world, system="b200_nvl8_ib", links=None):
+    links = links or load_links()
+    sysd = links["systems"][system]
+    intra, inter = links["links"][sysd["intra"]], links["links"][sysd["inter"]]
+    os.makedirs(outdir, exist_ok=True)
+    paths = {"network": os.path.join(outdir, "network.yml"), "system": os.path.join(outdir, "system.json"),
+             "memory": os.path.join(outdir, "remote_memory.json")}
+    with open(paths["network"], "w") as f:
+        f.write(network_yml(world, sysd["gpus_per_node"], intra, inter))
+    with open(paths["system"], "w") as f:
+        json.dump(system_json(), f, indent=1)
+    with open(paths["memory"], "w") as f:
+        json.dump({"memory-type": "NO_MEMORY_EXPANSION"}, f)
+    return paths
+
+
+def accept(stdout: str, world: int):
+    """Finish ticks per rank from the simulator log; accepted if every rank reported and all agree."""
+    ticks = {}
+    for m in re.finditer(r"sys\[(\d+)\][^\n]*?finished,\s*(\d+)\s*cycles", stdout):
+        ticks[int(m.group(1))] = int(m.group(2))
+    ok = len(ticks) == world and len(set(ticks.values())) == 1
+    return ok, ticks
+
+
+def run(outdir, world, binary, timeout_s=3600):
+    paths = write_inputs(outdir, world)
+    if not binary or not shutil.which(binary) and not os.path.exists(binary):
+        return {"status": "unavailable", "reason": "no ASTRA-sim binary (pass --bin or set ASTRA_SIM_BIN)",
+                "inputs": paths}
+    cmd = [binary, f"--workload-configuration={os.path.join(outdir, 'workload')}",
+           f"--comm-group-configuration={os.path.join(outdir, 'comm_group.json')}",
+           f"--system-configuration={paths['system']}", f"--network-configuration={paths['network']}",
+           f"--remote-memory-configuration={paths['memory']}"]
+    try:
+        p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"status": "timeout", "cmd": cmd}
+    ok, ticks = accept(p.stdout + p.stderr, world)
+    return {"status": "ok" if ok else "rejected", "exit_code": p.returncode, "finish_ticks": ticks, "cmd": cmd}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--size", default="medium", choices=list(SIZES))
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--dp", type=int, default=2)
+    ap.add_argument("--tp", type=int, default=2)
+    ap.add_argument("--pp", type=int, default=2)
+    ap.add_argument("--microbatches", type=int, default=4)
+    ap.add_argument("--out", default="traces")
+    ap.add_argument("--bin", default=os.environ.get("ASTRA_SIM_BIN"))
+    args = ap.parse_args()
+    from llmt.export.trace import export
+    cfg = SIZES[args.size]
+    export(cfg, args.batch, args.seq, args.dp, args.tp, args.pp, args.microbatches, outdir=args.out)
+    res = run(args.out, args.dp * args.tp * args.pp, args.bin)
+    print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

@@ -120,3 +120,15 @@ def test_checkpoint_file_loads_into_reference_model(tmp_path):
     checkpoint.load(path, m2)
     for k, v in m2.state_dict().items():
         assert torch.equal(v, m.state_dict()[k])
+
+
+def test_astra_inputs_and_acceptance(tmp_path):
+    from llmt.export.astra import accept, run
+    res = run(str(tmp_path), 8, None)
+    assert res["status"] == "unavailable"
+    net = open(res["inputs"]["network"]).read()
+    assert "npus_count: [ 8 ]" in net and "725.0" in net
+    ok, ticks = accept("sys[0] finished, 100 cycles\nsys[1] finished, 100 cycles", 2)
+    assert ok and ticks == {0: 100, 1: 100}
+    ok, _ = accept("sys[0] finished, 100 cycles\nsys[1] finished, 90 cycles", 2)
+    assert not ok
