@@ -14,6 +14,10 @@ namespace llmt {
 const char* last_error();
 void set_last_error(const char* msg);
 int sm_count();
+// SMs reserved for kernels running beside the persistent ones; persistent grids use the rest.
+void set_reserved_sms(int n);
+int reserved_sms();
+int persistent_sms();
 
 // ---------------------------------------------------------------- RMSNorm
 cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, void* y_bf16, float* s, float* rstd,

@@ -846,7 +846,7 @@ cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, 
     attr = true;
   }
   const int tiles = args.B * args.KV * (int)cdiv(args.T, kBM);
-  flash_bwd_pipelined_kernel<<<std::min(tiles, sm_count()), kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
+  flash_bwd_pipelined_kernel<<<std::min(tiles, persistent_sms()), kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
   return cudaGetLastError();
 }
 

@@ -415,6 +415,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
+  m.def("set_reserved_sms", &llmt::set_reserved_sms, "n"_a);
+  m.def("reserved_sms", &llmt::reserved_sms);
   m.def("tp_allgather_rows", [](at::Tensor src, at::Tensor dst, int64_t tp, int64_t row0) {
     on_device(src, "src");
     CHECK(src.is_contiguous() && src.scalar_type() == at::kBFloat16 && src.dim() == 2, "tp_allgather_rows: src");

@@ -1,3 +1,4 @@
+#include <algorithm>
 // Host-side runtime helpers shared by all launchers: last-error message, SM count.
 #include <cuda_runtime.h>
 
@@ -21,4 +22,12 @@ int sm_count() {
   if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
   return n[dev];
 }
+
+// SMs left to the persistent kernels (GEMM, attention backward): all of them unless some are
+// reserved for kernels that run beside them (the overlapped data-parallel step). A persistent
+// kernel sized to every SM waits, whole, for any SM another stream holds.
+static int g_reserved_sms = 0;
+void set_reserved_sms(int n) { g_reserved_sms = n < 0 ? 0 : n; }
+int reserved_sms() { return g_reserved_sms; }
+int persistent_sms() { return std::max(1, sm_count() - g_reserved_sms); }
 }  // namespace llmt

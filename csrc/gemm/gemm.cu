@@ -25,15 +25,15 @@ int* gemm_err_word() {
 int gemm_pick_bn(int M, int N, int epi) {
   if (epi == EPI_SWIGLU) return N >= 512 ? 256 : 128;
   const int64_t mb = cdiv(M, kGemmBM);
-  const int64_t t128 = cdiv(mb * cdiv(N, 128), sm_count()) * 1;
-  const int64_t t256 = cdiv(mb * cdiv(N, 256), sm_count()) * 2;
+  const int64_t t128 = cdiv(mb * cdiv(N, 128), persistent_sms()) * 1;
+  const int64_t t256 = cdiv(mb * cdiv(N, 256), persistent_sms()) * 2;
   return t256 <= t128 ? 256 : 128;
 }
 
 // Tile width and split-K from a wave model: cost = waves x (k-blocks per unit + fixed
 // per-unit overhead) x tile width; splits only when the output is an fp32 reduce-add.
 void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* splits) {
-  const int sms = sm_count();
+  const int sms = persistent_sms();
   const int64_t mb = cdiv(M, kGemmBM), kb = cdiv(K, kGemmBK);
   double best = 1e30;
   *bn = gemm_pick_bn(M, N, epi);

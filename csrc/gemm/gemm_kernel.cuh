@@ -539,7 +539,7 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     attr = true;
   }
   const int tiles = args.m_blocks * args.n_blocks * args.splits;
-  const int grid = std::min(tiles, sm_count());
+  const int grid = std::min(tiles, persistent_sms());
   kern<<<grid, kGemmThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();
 }

@@ -125,6 +125,11 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
       const int e = (c * TPR + t) * 8;
       if (valid && e < D) {
         const int64_t off = row * D + e;
+        if constexpr (HAS_DSIN) {
+          // the second pass adds ds_in after the row reduction: start its DRAM fetch now so that
+          // pass finds it in L2 instead of paying a second dependent DRAM round trip
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(ds_in + off));
+        }
         float dyf[8];
         bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dy + off), dyf);
         const float4 s0 = ld_f4(s + off), s1 = ld_f4(s + off + 4);

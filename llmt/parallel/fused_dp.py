@@ -104,6 +104,9 @@ class OverlappedFusedDP(FusedDP):
     def __init__(self, flat, opt, rank: int, world: int, group=None, max_blocks: int = 32):
         super().__init__(flat, opt, rank, world, group)
         self.max_blocks = max_blocks
+        # persistent GEMM / attention grids leave these SMs to the bucket kernels (one more for
+        # the flag barrier), so the two streams do not wait on each other for SMs
+        N.ext().set_reserved_sms(max_blocks + 1)
         self.side = torch.cuda.Stream(device=self.device)
         self.armed = False
         self.started = False
@@ -136,6 +139,10 @@ class OverlappedFusedDP(FusedDP):
         self.side.wait_stream(cur)
         with torch.cuda.stream(self.side):
             self._bucket(b)
+
+    def close(self):
+        N.ext().set_reserved_sms(0)
+        super().close()
 
     @torch.no_grad()
     def finish_step(self):
