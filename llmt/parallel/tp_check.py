@@ -24,6 +24,8 @@ def main():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--graph", action="store_true")
     p.add_argument("--kv-heads", type=int, default=None)
+    p.add_argument("--size", default=None, help="model size (default: tiny256 up to tp 2, tiny beyond: its"
+                   " ffn splits into GEMM-aligned shards)")
     args = p.parse_args()
     from llmt.config import get_config
     from llmt.models.llama import make_batch
@@ -34,7 +36,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    cfg = get_config("tiny256", kv_heads=args.kv_heads)
+    size = args.size or ("tiny256" if world <= 2 else "tiny")
+    cfg = get_config(size, kv_heads=args.kv_heads)
     B, T = 2, 128
     idx, tgt = make_batch(B, T, cfg.vocab, "cpu", seed=0)
     group = dist.new_group(list(range(world)))
