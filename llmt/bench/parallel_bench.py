@@ -33,6 +33,8 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--dp-mode", default="nccl", choices=["nccl", "fused"])
     p.add_argument("--json", default=None)
+    p.add_argument("--calibrate", action="store_true",
+                   help="also predict from this rank's GEMM / attention shapes timed on the GPU")
     p.add_argument("--graph", action="store_true", help="capture the step in a CUDA graph (pp = 1 only)")
     p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"],
                    help="tensor-parallel row collectives: NCCL, or NVLink peer memory fused with the GEMMs")
@@ -91,6 +93,17 @@ def main():
                 res["predicted_ms_per_step"] = round(pred["step_s"] * 1e3, 3)
                 res["prediction_error"] = round(pred["step_s"] / step_s - 1, 4)
                 res["predicted_breakdown_ms"] = {k: round(v * 1e3, 3) for k, v in pred["breakdown_s"].items()}
+            if args.calibrate:
+                # the same prediction with this rank's GEMM / attention shapes timed on the GPU
+                from llmt.perf.roofline import inventory, measure_shape_times
+                ops = inventory(cfg, B // args.microbatches, args.seq, "native", tp=args.tp)
+                st = measure_shape_times(ops, "/tmp/llmt_shape_times.json")
+                comp_c = StageCompute(cfg, args.seq, machine, shape_times=st)
+                pc = evaluate(cfg, args.seq, args.global_batch, world, args.dp, args.tp, args.pp,
+                              B // args.microbatches, comp_c, load_links(), "b200_nvl8_ib")
+                if pc:
+                    res["predicted_calibrated_ms_per_step"] = round(pc["step_s"] * 1e3, 3)
+                    res["calibrated_prediction_error"] = round(pc["step_s"] / step_s - 1, 4)
         except Exception as e:  # noqa: BLE001
             res["prediction_unavailable"] = str(e)[:200]
         print(json.dumps(res), flush=True)
