@@ -22,6 +22,7 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf
 
 __global__ void swiglu_fwd_kernel(const bf16* __restrict__ g, const bf16* __restrict__ u, int64_t ldgu,
                                   bf16* __restrict__ h, int64_t ldh, int64_t rows, int F) {
+  pdl_wait();
   const int vec_per_row = F / 8;
   const int64_t total = rows * vec_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -39,6 +40,7 @@ __global__ void swiglu_fwd_kernel(const bf16* __restrict__ g, const bf16* __rest
 __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dh, int64_t lddh, const bf16* __restrict__ g,
                                   const bf16* __restrict__ u, int64_t ldgu, bf16* __restrict__ dg,
                                   bf16* __restrict__ du, int64_t lddgu, int64_t rows, int F) {
+  pdl_wait();
   const int vec_per_row = F / 8;
   const int64_t total = rows * vec_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -63,6 +65,7 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dh, int64_t lddh, con
 template <bool BWD>
 __global__ void rope_kernel(bf16* __restrict__ qkv, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                             int64_t N, int T, int n_rot_heads, int hd, int64_t ld) {
+  pdl_wait();
   const int half = hd / 2;
   const int chunks = half / 8;
   const int64_t total = N * n_rot_heads * chunks;
@@ -99,6 +102,7 @@ __global__ void rope_kernel(bf16* __restrict__ qkv, const float* __restrict__ co
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ W,
                                      float* __restrict__ x, int64_t N, int d, int64_t V, int64_t v0, bool partial,
                                      int* __restrict__ err) {
+  pdl_wait();
   const int vpr = d / 4;
   const int64_t total = N * vpr;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -119,6 +123,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const floa
 
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ dx,
                                      float* __restrict__ dW, int64_t N, int d, int64_t V, int64_t v0) {
+  pdl_wait();
   const int vpr = d / 4;
   const int64_t total = N * vpr;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -140,7 +145,7 @@ cudaError_t swiglu_fwd(const void* g, const void* u, int64_t ldgu, void* h, int6
                        cudaStream_t st) {
   LLMT_REQUIRE(F % 8 == 0 && ldgu % 8 == 0 && ldh % 8 == 0, "swiglu: widths and pitches must be multiples of 8");
   if (rows == 0) return cudaSuccess;
-  swiglu_fwd_kernel<<<ew_grid(rows * F / 8), 256, 0, st>>>(static_cast<const bf16*>(g), static_cast<const bf16*>(u),
+  launch_pdl(swiglu_fwd_kernel, ew_grid(rows * F / 8), 256, 0, st, static_cast<const bf16*>(g), static_cast<const bf16*>(u),
                                                            ldgu, static_cast<bf16*>(h), ldh, rows, F);
   return cudaGetLastError();
 }
@@ -150,7 +155,7 @@ cudaError_t swiglu_bwd(const void* dh, int64_t lddh, const void* g, const void* 
   LLMT_REQUIRE(F % 8 == 0 && ldgu % 8 == 0 && lddh % 8 == 0 && lddgu % 8 == 0,
                "swiglu: widths and pitches must be multiples of 8");
   if (rows == 0) return cudaSuccess;
-  swiglu_bwd_kernel<<<ew_grid(rows * F / 8), 256, 0, st>>>(static_cast<const bf16*>(dh), lddh,
+  launch_pdl(swiglu_bwd_kernel, ew_grid(rows * F / 8), 256, 0, st, static_cast<const bf16*>(dh), lddh,
                                                            static_cast<const bf16*>(g), static_cast<const bf16*>(u),
                                                            ldgu, static_cast<bf16*>(dg), static_cast<bf16*>(du), lddgu,
                                                            rows, F);
@@ -164,7 +169,7 @@ cudaError_t rope_inplace(void* qkv, const float* cos_t, const float* sin_t, int6
   const int64_t work = N * n_rot_heads * (hd / 16);
   if (work == 0) return cudaSuccess;
   auto kern = backward ? rope_kernel<true> : rope_kernel<false>;
-  kern<<<ew_grid(work), 256, 0, st>>>(static_cast<bf16*>(qkv), cos_t, sin_t, N, T, n_rot_heads, hd, ld);
+  launch_pdl(kern, ew_grid(work), 256, 0, st, static_cast<bf16*>(qkv), cos_t, sin_t, N, T, n_rot_heads, hd, ld);
   return cudaGetLastError();
 }
 
@@ -172,7 +177,7 @@ cudaError_t embedding_fwd(const int64_t* idx, const float* W, float* x, int64_t 
                           bool partial, int* err, cudaStream_t st) {
   LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
   if (N == 0) return cudaSuccess;
-  embedding_fwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, W, x, N, d, V, v0, partial, err);
+  launch_pdl(embedding_fwd_kernel, ew_grid(N * d / 4), 256, 0, st, idx, W, x, N, d, V, v0, partial, err);
   return cudaGetLastError();
 }
 
@@ -182,7 +187,7 @@ cudaError_t embedding_bwd(const int64_t* idx, const float* dx, float* dW, int64_
                           cudaStream_t st) {
   LLMT_REQUIRE(d % 4 == 0, "embedding: width must be a multiple of 4");
   if (N == 0) return cudaSuccess;
-  embedding_bwd_kernel<<<ew_grid(N * d / 4), 256, 0, st>>>(idx, dx, dW, N, d, V, v0);
+  launch_pdl(embedding_bwd_kernel, ew_grid(N * d / 4), 256, 0, st, idx, dx, dW, N, d, V, v0);
   return cudaGetLastError();
 }
 

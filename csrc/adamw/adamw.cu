@@ -19,6 +19,7 @@ template <bool WRITE_BF16, bool ZERO_GRAD>
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, bf16* __restrict__ p16, int64_t n, const float* __restrict__ lr_ptr,
                              const int* __restrict__ step_ptr, AdamHyper a) {
+  pdl_wait();
   const float lr = *lr_ptr;
   const int t = *step_ptr;
   const float bc1 = 1.f - powf(a.b1, (float)t);
@@ -68,6 +69,7 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float
 }
 
 __global__ void cast_bf16_kernel(const float* __restrict__ x, bf16* __restrict__ y, int64_t n) {
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16_rn(x[i]);
 }
@@ -83,17 +85,17 @@ cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_
   LLMT_REQUIRE(p16 == nullptr || (uintptr_t)p16 % 8 == 0, "adamw: bf16 copy must be 8-byte aligned");
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4 + 1, 256), sm_count() * 8));
   bf16* q = static_cast<bf16*>(p16);
-  if (p16 && zero_grad) adamw_kernel<true, true><<<grid, 256, 0, st>>>(p, g, m, v, q, n, lr, step, h);
-  else if (p16) adamw_kernel<true, false><<<grid, 256, 0, st>>>(p, g, m, v, q, n, lr, step, h);
-  else if (zero_grad) adamw_kernel<false, true><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
-  else adamw_kernel<false, false><<<grid, 256, 0, st>>>(p, g, m, v, nullptr, n, lr, step, h);
+  if (p16 && zero_grad) launch_pdl(adamw_kernel<true, true>, grid, 256, 0, st, p, g, m, v, q, n, lr, step, h);
+  else if (p16) launch_pdl(adamw_kernel<true, false>, grid, 256, 0, st, p, g, m, v, q, n, lr, step, h);
+  else if (zero_grad) launch_pdl(adamw_kernel<false, true>, grid, 256, 0, st, p, g, m, v, nullptr, n, lr, step, h);
+  else launch_pdl(adamw_kernel<false, false>, grid, 256, 0, st, p, g, m, v, nullptr, n, lr, step, h);
   return cudaGetLastError();
 }
 
 cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), sm_count() * 8));
-  cast_bf16_kernel<<<grid, 256, 0, st>>>(x, static_cast<bf16*>(y), n);
+  launch_pdl(cast_bf16_kernel, grid, 256, 0, st, x, static_cast<bf16*>(y), n);
   return cudaGetLastError();
 }
 

@@ -79,6 +79,7 @@ template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                  const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
+  pdl_wait();
   using L = BwdSmem<HD>;
   constexpr int ST = L::STAGES;
   constexpr int TMEM_COLS = 512;
@@ -346,6 +347,7 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       }
     }
   }
+  pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -390,6 +392,7 @@ __device__ __forceinline__ int snake_tile(int r, int i, int G) { return r * G + 
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                            const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
+  pdl_wait();
   using L = BwdSmemP;
   constexpr int HD = 64;
   constexpr int TMEM_COLS = 512;
@@ -748,6 +751,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     if (lane == 0) bulk_wait<0>();  // this warp's dQ reductions are complete before exit
     __syncwarp();
   }
+  pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -761,6 +765,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 template <int HD>
 __global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dO, float* __restrict__ dsum,
                                     float* __restrict__ dq_acc, int BT, int T, int H) {
+  pdl_wait();
   constexpr int G = HD / 8;  // threads per (row, head): 8 or 16, divides the warp
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)BT * H * G;
@@ -793,6 +798,7 @@ template <int HD>
 __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, bf16* __restrict__ dqkv,
                                      const float* __restrict__ cos_t, const float* __restrict__ sin_t, int BT, int T,
                                      int H, int ld_qkv) {
+  pdl_wait();
   constexpr int HALF = HD / 2;
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // (row, head, 8-chunk of half)
   constexpr int CH = HALF / 8;
@@ -831,7 +837,7 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
     attr = true;
   }
   dim3 grid((unsigned)cdiv(args.T, kBM), args.B * args.KV);
-  kern<<<grid, kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
+  launch_pdl(kern, grid, kBwdThreads, smem, st, tq, tdo, tdq, args);
   return cudaGetLastError();
 }
 
@@ -846,7 +852,7 @@ cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, 
     attr = true;
   }
   const int tiles = args.B * args.KV * (int)cdiv(args.T, kBM);
-  flash_bwd_pipelined_kernel<<<std::min(tiles, persistent_sms()), kBwdThreads, smem, st>>>(tq, tdo, tdq, args);
+  launch_pdl(flash_bwd_pipelined_kernel, std::min(tiles, persistent_sms()), kBwdThreads, smem, st, tq, tdo, tdq, args);
   return cudaGetLastError();
 }
 
@@ -873,7 +879,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   {
     const int64_t n = rows * H * (hd / 8);
     auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
-    k<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum, dq_acc,
+    launch_pdl(k, (unsigned)cdiv(n, 256), 256, 0, st, static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum, dq_acc,
                                               (int)rows, T, H);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -908,7 +914,7 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   {
     const int64_t n = rows * H * (hd / 16);
     auto k = hd == 64 ? attn_bwd_post_kernel<64> : attn_bwd_post_kernel<128>;
-    k<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(dq_acc, static_cast<bf16*>(dqkv), cos_t, sin_t, (int)rows, T, H,
+    launch_pdl(k, (unsigned)cdiv(n, 256), 256, 0, st, dq_acc, static_cast<bf16*>(dqkv), cos_t, sin_t, (int)rows, T, H,
                                               (int)ld_qkv);
   }
   return cudaGetLastError();

@@ -63,6 +63,7 @@ struct FwdSmem {
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads, 2)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
+  pdl_wait();
   using L = FwdSmem<HD>;
   constexpr int ST = L::STAGES;
   constexpr int TMEM_COLS = 256;        // S/P at [0, 128), O' at [128, 128 + HD)
@@ -275,6 +276,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       a.lse[((int64_t)b * a.H + h) * a.T + q] = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
   }
+  pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -294,7 +296,7 @@ cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb, 
     attr = true;
   }
   dim3 grid(args.B * args.H, nqb);
-  kern<<<grid, kAttnThreads, smem, st>>>(tm, args);
+  launch_pdl(kern, grid, kAttnThreads, smem, st, tm, args);
   return cudaGetLastError();
 }
 

@@ -40,6 +40,7 @@ __device__ __forceinline__ void block_lse(float& m, float& s) {
 __global__ void __launch_bounds__(kCeThreads)
 ce_fwd_rows_kernel(const bf16* __restrict__ logits, int64_t ld, const int64_t* __restrict__ tgt, float* __restrict__ lse,
                    float* __restrict__ loss, int V) {
+  pdl_wait();
   const int64_t r = blockIdx.x;
   const bf16* row = logits + r * ld;
   float m = -INFINITY, s = 0.f;
@@ -66,6 +67,7 @@ ce_fwd_rows_kernel(const bf16* __restrict__ logits, int64_t ld, const int64_t* _
 __global__ void __launch_bounds__(kCeThreads)
 ce_bwd_rows_kernel(bf16* __restrict__ logits, int64_t ld, const int64_t* __restrict__ tgt, const float* __restrict__ lse,
                    const float* __restrict__ grad_out, float scale, int V) {
+  pdl_wait();
   const int64_t r = blockIdx.x;
   bf16* row = logits + r * ld;
   const float l = lse[r];
@@ -86,7 +88,7 @@ cudaError_t ce_fwd_rows(const void* logits, int64_t ld, const int64_t* tgt, floa
                         cudaStream_t st) {
   LLMT_REQUIRE(V % 8 == 0 && ld % 8 == 0, "ce: vocab and pitch must be multiples of 8");
   if (R == 0) return cudaSuccess;
-  ce_fwd_rows_kernel<<<(unsigned)R, kCeThreads, 0, st>>>(static_cast<const bf16*>(logits), ld, tgt, lse, loss, V);
+  launch_pdl(ce_fwd_rows_kernel, (unsigned)R, kCeThreads, 0, st, static_cast<const bf16*>(logits), ld, tgt, lse, loss, V);
   return cudaGetLastError();
 }
 
@@ -94,7 +96,7 @@ cudaError_t ce_bwd_rows(void* logits, int64_t ld, const int64_t* tgt, const floa
                         float scale, int64_t R, int V, cudaStream_t st) {
   LLMT_REQUIRE(V % 8 == 0 && ld % 8 == 0, "ce: vocab and pitch must be multiples of 8");
   if (R == 0) return cudaSuccess;
-  ce_bwd_rows_kernel<<<(unsigned)R, kCeThreads, 0, st>>>(static_cast<bf16*>(logits), ld, tgt, lse, grad_out, scale, V);
+  launch_pdl(ce_bwd_rows_kernel, (unsigned)R, kCeThreads, 0, st, static_cast<bf16*>(logits), ld, tgt, lse, grad_out, scale, V);
   return cudaGetLastError();
 }
 

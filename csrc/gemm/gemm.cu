@@ -150,6 +150,7 @@ namespace {
 __global__ void ce_combine_kernel(const float* __restrict__ part, const float* __restrict__ tlogit,
                                   const int64_t* __restrict__ tgt, float* __restrict__ lse, float* __restrict__ loss,
                                   int M, int nblk, int V) {
+  pdl_wait();
   const int row = blockIdx.x * blockDim.y + threadIdx.y;
   if (row >= M) return;
   float m = -INFINITY, s = 0.f;
@@ -181,7 +182,7 @@ cudaError_t ce_combine(const float* part, const float* tlogit, const int64_t* tg
                        int nblk, int V, cudaStream_t st) {
   if (M == 0) return cudaSuccess;
   dim3 block(32, 8);
-  ce_combine_kernel<<<(unsigned)cdiv(M, 8), block, 0, st>>>(part, tlogit, tgt, lse, loss, M, nblk, V);
+  launch_pdl(ce_combine_kernel, (unsigned)cdiv(M, 8), block, 0, st, part, tlogit, tgt, lse, loss, M, nblk, V);
   return cudaGetLastError();
 }
 

@@ -376,6 +376,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
+  pdl_wait();
   constexpr int BM = kGemmBM, BK = kGemmBK;
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -519,6 +520,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     st.drain();
   }
+  pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -540,7 +542,7 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
   }
   const int tiles = args.m_blocks * args.n_blocks * args.splits;
   const int grid = std::min(tiles, persistent_sms());
-  kern<<<grid, kGemmThreads, smem, st>>>(mp.a, mp.b, mp.c, mp.c2, args);
+  launch_pdl(kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();
 }
 

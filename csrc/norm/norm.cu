@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(kThreads)
 add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, const float* __restrict__ w,
                        bf16* __restrict__ y, float* __restrict__ s_out, float* __restrict__ rstd_out,
                        int64_t N, int D, float eps) {
+  pdl_wait();
   __shared__ float red[kThreads / 32];
   constexpr int RPC = kThreads / TPR;
   const int t = threadIdx.x % TPR;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(kThreads)
 rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, const float* __restrict__ w,
                    const float* __restrict__ rstd_in, const float* __restrict__ ds_in,
                    float* __restrict__ ds, bf16* __restrict__ ds16, float* __restrict__ dw_part, int64_t N, int D) {
+  pdl_wait();
   __shared__ float red[kThreads / 32];
   constexpr int RPC = kThreads / TPR;
   const int t = threadIdx.x % TPR;
@@ -196,6 +198,7 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
 
 // dw[j] (+)= sum_p part[p, j], fixed order over p: 32 columns x 8 row groups per CTA.
 __global__ void dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, int D, int accumulate) {
+  pdl_wait();
   __shared__ float acc[8][33];
   const int col = blockIdx.x * 32 + threadIdx.x;
   float a = 0.f;
@@ -235,7 +238,7 @@ cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, 
     constexpr int TPR = decltype(tpr)::value;
     constexpr int RPC = kThreads / TPR;
     dim3 grid((unsigned)cdiv(N, RPC));
-    auto launch = [&](auto kern) { kern<<<grid, kThreads, 0, st>>>(ap, r, w, y, s, rstd, N, D, eps); };
+    auto launch = [&](auto kern) { launch_pdl(kern, grid, kThreads, 0, st, ap, r, w, y, s, rstd, N, D, eps); };
     if (ap && s) launch(add_rmsnorm_fwd_kernel<TPR, true, true>);
     else if (ap) launch(add_rmsnorm_fwd_kernel<TPR, true, false>);
     else if (s) launch(add_rmsnorm_fwd_kernel<TPR, false, true>);
@@ -270,7 +273,7 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
   const size_t smem = D * sizeof(float);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
-    auto launch = [&](auto kern) { kern<<<grid, kThreads, smem, st>>>(dy, s, w, rstd, ds_in, ds, d16, dw_part, N, D); };
+    auto launch = [&](auto kern) { launch_pdl(kern, grid, kThreads, smem, st, dy, s, w, rstd, ds_in, ds, d16, dw_part, N, D); };
     if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
     else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
     else if (d16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
@@ -278,7 +281,7 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
   });
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  dw_reduce_kernel<<<(unsigned)cdiv(D, 32), dim3(32, 8), 0, st>>>(dw_part, dw, grid, D, accumulate);
+  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, 32), dim3(32, 8), 0, st, dw_part, dw, grid, D, accumulate);
   return cudaGetLastError();
 }
 
@@ -337,7 +340,7 @@ extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, con
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
     auto launch = [&](auto kern) {
-      kern<<<grid, kThreads, smem, stream>>>(dy, s, w, rstd, ds_in, ds, d16, part, N, D);
+      launch_pdl(kern, grid, kThreads, smem, stream, dy, s, w, rstd, ds_in, ds, d16, part, N, D);
     };
     if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
     else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
@@ -346,7 +349,7 @@ extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, con
   });
   e = cudaGetLastError();
   if (e != cudaSuccess) return (int)e;
-  dw_reduce_kernel<<<(unsigned)cdiv(D, 32), dim3(32, 8), 0, stream>>>(part, dw, grid, D, accumulate);
+  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, 32), dim3(32, 8), 0, stream, part, dw, grid, D, accumulate);
   return (int)cudaGetLastError();
 }
 
