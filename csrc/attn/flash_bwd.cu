@@ -485,12 +485,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
           a.trace[1024 + 3 * t] = (long long)globaltimer();
           a.trace[1024 + 3 * t + 1] = smid;
         }
-        if (tl > 0 && !wait_bar(kv_empty, (tl - 1) & 1, err, 53)) break;
-        trace_at(a.trace, 3, tk, 31);
         const int kcol = (a.H + x.kvh) * HD, vcol = (a.H + a.KV + x.kvh) * HD;
-        bar_arrive_expect_tx(kv_full, 2 * L::TILE);
-        tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, x.row0 + x.k0);
-        tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, x.row0 + x.k0);
         for (int n = 0; n < x.n_items; ++n, ++it) {
           const int s = it & 1;
           const int hq = x.kvh * group + n / x.n_i, i = x.i_start + n % x.n_i;
@@ -504,6 +499,14 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
           bulk_load(smem + L::VEC_OFF + s * 1024 + 512, a.dsum + vbase, vbytes, &q_full[s]);
           tma_load_2d(smem + L::Q_OFF + s * L::TILE, &tm_qkv, &q_full[s], hq * HD, x.row0 + i * kBN);
           tma_load_2d(smem + L::DO_OFF + s * L::TILE, &tm_do, &q_full[s], hq * HD, x.row0 + i * kBN);
+          if (n == 0) {
+            // the tile's first Q / dO are already in flight; K / V wait for the previous tile's MMAs
+            if (tl > 0 && !wait_bar(kv_empty, (tl - 1) & 1, err, 53)) { ok = false; break; }
+            trace_at(a.trace, 3, tk, 31);
+            bar_arrive_expect_tx(kv_full, 2 * L::TILE);
+            tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, x.row0 + x.k0);
+            tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, x.row0 + x.k0);
+          }
         }
       }
     }
