@@ -148,7 +148,8 @@ def run_native(args, rank, world, local):
     if world > 1:
         from llmt.parallel.dp import DataParallel
         dp = DataParallel(world, rank, mode=args.dp_mode)
-    tr = Trainer(cfg, PER_GPU_BATCH, SEQ, device=f"cuda:{local}", cuda_graph=not args.no_graph, dp=dp)
+    tr = Trainer(cfg, PER_GPU_BATCH, SEQ, device=f"cuda:{local}", cuda_graph=not args.no_graph, dp=dp,
+                 linear=args.linear)
     idx, tgt = make_batch(PER_GPU_BATCH, SEQ, cfg.vocab, "cpu", seed=rank)
     idx, tgt = idx.pin_memory(), tgt.pin_memory()
     tr.set_batch(idx.cuda(local), tgt.cuda(local))
@@ -240,7 +241,13 @@ def main():
                    help="data-parallel transport: NCCL (fastest measured at 2 and 8 GPUs), the fused "
                         "peer-memory kernel, or that kernel overlapped with the backward")
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8"],
+                   help="block linears in bf16, or on tensorwise e4m3 operands (every GEMM of qkv, wo, w1||w3, "
+                        "w2; the head stays bf16). With --impl reference, fp8 selects the reference's row "
+                        "'8 + FP8 linears (e4m3)' unless --ref-row is given")
     args = p.parse_args()
+    if args.impl == "reference" and args.linear == "fp8" and args.ref_row == "5 + torch.compile":
+        args.ref_row = "8 + FP8 linears (e4m3)"
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = setup_dist(args.gpus)
@@ -257,10 +264,11 @@ def main():
                 "metric": METRIC, "value": round(res["value"], 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 3),
                 "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": round(res["value"] / BASELINE_TOKS, 3), "dtype": "bf16",
+                "vs_baseline": round(res["value"] / BASELINE_TOKS, 3),
+                "dtype": "bf16" if args.linear == "bf16" else "fp8 e4m3 tensorwise block linears, bf16 rest",
                 "data": "synthetic uniform-random tokens, random-init weights",
                 "config": {"model": MODEL, "global_batch": PER_GPU_BATCH * world, "seq_len": SEQ,
-                           "parallelism": par, "l2": "working set >> 126 MB L2; no flush",
+                           "parallelism": par, "l2": "working set >> 126 MB L2; no flush", "linear": args.linear,
                            "mfu": round(res["mfu"], 4), "tflops_per_gpu": round(res["tflops_per_gpu"], 1)},
                 "clocks": res["clocks"],
             }

@@ -87,6 +87,8 @@ struct GemmArgs {
   void* const* peer;   // PEER_RS: device array of every rank's slot buffer (tp, rows_per_rank, ldo) bf16
   int tp_rank;         // PEER_RS: this rank's slot index in every owner's buffer
   int rows_per_rank;   // PEER_RS: output row r belongs to rank r / rows_per_rank
+  const float* scale_a;  // e4m3 operands: inverse tensorwise scales, acc is multiplied by both
+  const float* scale_b;
   int* err;
 };
 
@@ -96,6 +98,18 @@ struct GemmArgs {
 // fp32 output with accumulate=1 (TMA reduce-add) may also be split along K to fill the SMs.
 cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
                  int epi, int bn, GemmArgs g, cudaStream_t st, int splits = 0);
+// out = a @ b^T with e4m3 a (M x K) and b (N x K), both row-major (K-major): the only layout of
+// the 8-bit GEMM, so the backward passes transposed fp8 copies. g.scale_a / g.scale_b point at
+// the operands' inverse tensorwise scales (device floats). Epilogues: BF16, F32 (reduce-add
+// with accumulate, split-K allowed), SWIGLU, SWIGLU_BWD, ROPE.
+cudaError_t gemm_fp8(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int epi, int bn,
+                     GemmArgs g, cudaStream_t st, int splits = 0);
+// Tensorwise e4m3 quantization: q = e4m3(sat(x * s)), s = 448 / max(amax|x|, 1e-12), optional
+// transposed copy qt (cols x rows), *inv = 1 / s. x is bf16 or fp32 (x_f32), rows x cols with
+// row pitch ld; rows and cols multiples of 16. scratch holds fp8_amax_slots() floats.
+int fp8_amax_slots();
+cudaError_t fp8_quant(const void* x, bool x_f32, int rows, int cols, int64_t ld, void* q, void* qt, float* inv,
+                      float* scratch, cudaStream_t st);
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* splits);
 int gemm_error_code(bool reset);

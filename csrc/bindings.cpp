@@ -214,17 +214,54 @@ void ce_combine(at::Tensor part, at::Tensor tlogit, at::Tensor tgt, at::Tensor l
      "ce_combine");
 }
 
+// ---------------------------------------------------------------- fp8 quantization
+void fp8_quant(at::Tensor x, at::Tensor q, c10::optional<at::Tensor> qt, at::Tensor inv, at::Tensor scratch) {
+  cuda2d(x, "x");
+  CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "fp8_quant: x must be bf16 or fp32");
+  CHECK(x.stride(1) == 1, "fp8_quant: x rows must be contiguous");
+  const int64_t rows = x.size(0), cols = x.size(1);
+  on_device(q, "q");
+  CHECK_DT(q, at::kFloat8_e4m3fn);
+  CHECK(q.is_contiguous() && q.numel() == rows * cols, "fp8_quant: q must be a contiguous rows x cols tensor");
+  void* qtp = nullptr;
+  if (qt.has_value() && qt->defined()) {
+    on_device(*qt, "qt");
+    CHECK_DT((*qt), at::kFloat8_e4m3fn);
+    CHECK(qt->is_contiguous() && qt->numel() == rows * cols, "fp8_quant: qt must be a contiguous cols x rows tensor");
+    qtp = qt->data_ptr();
+  }
+  for (auto* t : {&inv, &scratch}) {
+    on_device(*t, "fp8_quant scale buffer");
+    CHECK_DT((*t), at::kFloat);
+  }
+  CHECK(scratch.numel() >= llmt::fp8_amax_slots(), "fp8_quant: scratch needs fp8_amax_slots() floats");
+  ok(llmt::fp8_quant(x.data_ptr(), x.scalar_type() == at::kFloat, (int)rows, (int)cols, x.stride(0), q.data_ptr(), qtp,
+                     inv.data_ptr<float>(), scratch.data_ptr<float>(), stream()),
+     "fp8_quant");
+}
+
 // ---------------------------------------------------------------- GEMM
 void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor out, bool accumulate,
           c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split, c10::optional<at::Tensor> cos_t,
           c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols, c10::optional<at::Tensor> tgt,
           c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
           c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits, c10::optional<at::Tensor> peer,
-          int64_t tp_rank, int64_t rows_per_rank) {
+          int64_t tp_rank, int64_t rows_per_rank, c10::optional<at::Tensor> scale_a, c10::optional<at::Tensor> scale_b) {
   cuda2d(a, "a");
   cuda2d(b, "b");
-  CHECK_DT(a, at::kBFloat16);
-  CHECK_DT(b, at::kBFloat16);
+  const bool f8 = a.scalar_type() == at::kFloat8_e4m3fn;
+  if (f8) {
+    CHECK_DT(b, at::kFloat8_e4m3fn);
+    CHECK(!ta && tb, "fp8 gemm: both operands K-major (a: M x K, b: N x K)");
+    CHECK(scale_a.has_value() && scale_b.has_value(), "fp8 gemm needs scale_a and scale_b");
+    for (auto* t : {&*scale_a, &*scale_b}) {
+      on_device(*t, "fp8 scale");
+      CHECK_DT((*t), at::kFloat);
+    }
+  } else {
+    CHECK_DT(a, at::kBFloat16);
+    CHECK_DT(b, at::kBFloat16);
+  }
   on_device(out, "out");
   const int M = ta ? a.size(1) : a.size(0);
   const int K = ta ? a.size(0) : a.size(1);
@@ -293,6 +330,14 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
     CHECK(part->numel() >= (int64_t)M * ((N + BN - 1) / BN) * 2, "CE_FWD partial buffer too small");
   }
   if (epi == llmt::EPI_CE_BWD) CHECK(g.tgt && g.lse, "CE_BWD gemm args");
+  if (f8) {
+    g.scale_a = scale_a->data_ptr<float>();
+    g.scale_b = scale_b->data_ptr<float>();
+    ok(llmt::gemm_fp8(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K, (int)epi, (int)bn, g, stream(),
+                      (int)splits),
+       "gemm_fp8");
+    return;
+  }
   ok(llmt::gemm(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), ta, tb, M, N, K, (int)epi, (int)bn, g, stream(),
                 (int)splits),
      "gemm");
@@ -410,7 +455,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "a"_a, "b"_a, "ta"_a, "tb"_a, "epi"_a, "out"_a, "accumulate"_a = false, "aux"_a = py::none(),
         "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
         "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
-        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0, "peer"_a = py::none(), "tp_rank"_a = 0, "rows_per_rank"_a = 0);
+        "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0, "peer"_a = py::none(), "tp_rank"_a = 0, "rows_per_rank"_a = 0,
+        "scale_a"_a = py::none(), "scale_b"_a = py::none());
+  m.def("fp8_amax_slots", &llmt::fp8_amax_slots);
+  m.def("fp8_quant", &fp8_quant, "x"_a, "q"_a, "qt"_a, "inv"_a, "scratch"_a);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);

@@ -68,6 +68,25 @@ int gemm_error_code(bool reset) {
   return v;
 }
 
+// Epilogue output maps: 32x32 boxes, one per epilogue warp and chunk (see Stager).
+static bool make_out_maps(int epi, const GemmArgs& g, int M, int N, GemmMaps* mp) {
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  switch (epi) {
+    case EPI_F32:
+      return make_tmap_2d(&mp->c, g.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, g.ldo, 32, 32,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    case EPI_BF16: case EPI_CE_BWD: case EPI_ROPE:
+      return make_tmap_2d(&mp->c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    case EPI_SWIGLU:
+      return make_tmap_2d(&mp->c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+             make_tmap_3d(&mp->c2, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    case EPI_SWIGLU_BWD:  // c: the saved [g | u] rows (loaded), c2: [dg | du] (stored)
+      return make_tmap_3d(&mp->c, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
+             make_tmap_3d(&mp->c2, g.out2, dt, 2, N, 2, M, N, g.ldo2, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    default: return true;
+  }
+}
+
 cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta, bool tb, int M, int N, int K,
                  int epi, int bn, GemmArgs g, cudaStream_t st, int force_splits) {
   LLMT_REQUIRE(!(ta && tb), "gemm: a^T b^T is not a supported layout");
@@ -119,30 +138,57 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
     set_last_error(msg);
     return cudaErrorInvalidValue;
   }
-  bool ok = true;
-  // Epilogue output maps: 32x32 boxes, one per epilogue warp and chunk (see Stager).
-  switch (epi) {
-    case EPI_F32:
-      ok = make_tmap_2d(&mp.c, g.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, g.ldo, 32, 32,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-      break;
-    case EPI_BF16: case EPI_CE_BWD: case EPI_ROPE:
-      ok = make_tmap_2d(&mp.c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-      break;
-    case EPI_SWIGLU:
-      ok = make_tmap_2d(&mp.c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
-           make_tmap_3d(&mp.c2, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-      break;
-    case EPI_SWIGLU_BWD:  // c: the saved [g | u] rows (loaded), c2: [dg | du] (stored)
-      ok = make_tmap_3d(&mp.c, g.aux, dt, 2, N, 2, M, N, g.ld_aux, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&
-           make_tmap_3d(&mp.c2, g.out2, dt, 2, N, 2, M, N, g.ldo2, 32, 1, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-      break;
-    default: break;
-  }
-  LLMT_REQUIRE(ok, "gemm: output tensor map rejected (pitch/alignment)");
+  LLMT_REQUIRE(make_out_maps(epi, g, M, N, &mp), "gemm: output tensor map rejected (pitch/alignment)");
   if (!ta && tb) return gemm_launch_kk(BN, epi, mp, g, st);
   if (!ta && !tb) return gemm_launch_km(BN, epi, mp, g, st);
   return gemm_launch_mm(BN, epi, mp, g, st);
+}
+
+
+cudaError_t gemm_fp8(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int epi, int bn,
+                     GemmArgs g, cudaStream_t st, int force_splits) {
+  LLMT_REQUIRE(M > 0 && N > 0 && K > 0, "gemm_fp8: empty problem");
+  LLMT_REQUIRE(N % 8 == 0 && K % 16 == 0, "gemm_fp8: N must be a multiple of 8 and K of 16");
+  LLMT_REQUIRE(tma_ok(a, lda, 1) && tma_ok(b, ldb, 1), "gemm_fp8: operands need 16-byte aligned bases and row pitches");
+  LLMT_REQUIRE(g.scale_a && g.scale_b, "gemm_fp8: needs both inverse scales");
+  LLMT_REQUIRE(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD || epi == EPI_ROPE,
+               "gemm_fp8: epilogue not built for e4m3 operands");
+  int BN = bn, splits = 1;
+  const bool can_split = epi == EPI_F32 && g.accumulate;
+  // a k-block is 128 e4m3 elements, the bytes of 64 bf16 ones: plan as K / 2 of bf16
+  if (!BN) gemm_plan(M, N, (K + 1) / 2, epi, can_split, &BN, &splits);
+  if (force_splits > 0) {
+    LLMT_REQUIRE(force_splits == 1 || can_split, "gemm_fp8: split-K needs an fp32 reduce-add output");
+    splits = force_splits;
+  }
+  LLMT_REQUIRE(BN == 128 || BN == 256, "gemm_fp8: BN must be 128 or 256");
+  if (epi == EPI_ROPE)
+    LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm_fp8: bad RoPE epilogue shape");
+  constexpr int KE = 2 * kGemmBK;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.m_blocks = (int)cdiv(M, kGemmBM);
+  g.n_blocks = (int)cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
+  g.k_blocks = (int)cdiv(K, KE);
+  g.k_per_split = (int)cdiv(g.k_blocks, splits);
+  g.splits = (int)cdiv(g.k_blocks, g.k_per_split);
+  g.err = gemm_err_word();
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  alignas(64) GemmMaps mp;
+  memset(&mp, 0, sizeof(mp));
+  const int rows_b = epi == EPI_SWIGLU ? 2 * N : N;
+  const bool ok_a = make_tmap_2d(&mp.a, a, dt, 1, K, M, lda, KE, kGemmBM);
+  const bool ok_b = ok_a && make_tmap_2d(&mp.b, b, dt, 1, K, rows_b, ldb, KE, epi == EPI_SWIGLU ? BN / 2 : BN);
+  if (!ok_a || !ok_b) {
+    char msg[200];
+    snprintf(msg, sizeof(msg), "gemm_fp8: cuTensorMapEncodeTiled rejected operand %s (result %d; M=%d N=%d K=%d)",
+             ok_a ? "B" : "A", last_tmap_result(), M, N, K);
+    set_last_error(msg);
+    return cudaErrorInvalidValue;
+  }
+  LLMT_REQUIRE(make_out_maps(epi, g, M, N, &mp), "gemm_fp8: output tensor map rejected (pitch/alignment)");
+  return gemm_launch_f8(BN, epi, mp, g, st);
 }
 
 namespace {

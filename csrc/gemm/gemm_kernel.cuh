@@ -45,12 +45,12 @@ struct GemmMaps {
 cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // fwd
 cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // dgrad
 cudaError_t gemm_launch_mm(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // wgrad
+cudaError_t gemm_launch_f8(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // e4m3, K-major
 
 namespace gemm_detail {
 
 using namespace sm100;
 
-__device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 // sigmoid on the SFU: 2^(-x log2 e) and a reciprocal, both approximate hardware ops
 __device__ __forceinline__ float sigm(float x) {
   float e, r;
@@ -147,10 +147,15 @@ struct Stager {
 __device__ __forceinline__ bool lane_is_zero(const Stager& st) { return st.lane == 0; }
 
 // row: this thread's accumulator row; wrow: the warp's first row (TMA box origin).
-template <int EPI, int BN>
+// F8: e4m3 operands with tensorwise scales; every accumulator value is multiplied by the two
+// inverse scales before the epilogue's math.
+template <int EPI, int BN, bool F8 = false>
 __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow, int nb, const GemmArgs& a,
                                               const CUtensorMap* tmC, const CUtensorMap* tmC2, Stager& st) {
   const bool rv = row < a.M;
+  float sc = 1.f;
+  if constexpr (F8) sc = __ldg(a.scale_a) * __ldg(a.scale_b);
+  auto cvt = [sc](uint32_t x) { return F8 ? __uint_as_float(x) * sc : __uint_as_float(x); };
   if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_CE_BWD) {
     float l = 0.f, scale = 0.f;
     int64_t t = -1;
@@ -170,7 +175,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       tmem_wait_ld();
       float v[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+      for (int j = 0; j < 32; ++j) v[j] = cvt(r[j]);
       uint8_t* b = st.acquire();
       if constexpr (EPI == EPI_F32) {
         st.put_f32(b, v);
@@ -197,8 +202,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       float g[32], u[32], h[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        g[j] = u2f(rg[j]);
-        u[j] = u2f(ru[j]);
+        g[j] = cvt(rg[j]);
+        u[j] = cvt(ru[j]);
         h[j] = g[j] * sigm(g[j]) * u[j];
       }
       uint8_t* b = st.acquire();
@@ -229,7 +234,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       if (rv) {
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = u2f(r[j]);
+        for (int j = 0; j < 32; ++j) v[j] = cvt(r[j]);
         uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -269,7 +274,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       if (!ok) break;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float d = u2f(r[j]);
+        const float d = cvt(r[j]);
         const float sg = sigm(g[j]);
         dg[j] = d * u[j] * sg * (1.f + g[j] * (1.f - sg));
         du[j] = d * g[j] * sg;
@@ -314,8 +319,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
         float x1[32], x2[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          x1[e] = u2f(r1[e]);
-          x2[e] = u2f(r2[e]);
+          x1[e] = cvt(r1[e]);
+          x2[e] = cvt(r2[e]);
         }
         if (col1 < a.rot_cols) {
 #pragma unroll
@@ -348,7 +353,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       float cm = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float x = u2f(r[j]);
+        const float x = cvt(r[j]);
         if (col0 + j < a.N) cm = fmaxf(cm, x);
         if ((int64_t)(col0 + j) == t) {
           tl = x;
@@ -358,7 +363,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       float cs = 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (col0 + j < a.N) cs += __expf(u2f(r[j]) - cm);
+        if (col0 + j < a.N) cs += __expf(cvt(r[j]) - cm);
       const float nm = fmaxf(m, cm);
       s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + cs * __expf(cm - nm);
       m = nm;
@@ -372,12 +377,14 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool F8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
   pdl_wait();
   constexpr int BM = kGemmBM, BK = kGemmBK;
+  static_assert(!F8 || (!A_MN && !B_MN), "8-bit operands are K-major only");
+  constexpr int KE = F8 ? 2 * BK : BK;  // elements per k-block: one 128-byte swizzled row either way
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -436,7 +443,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           bar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          const int k0 = kb * BK;
+          const int k0 = kb * KE;
           if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full[stage], k0, mb * BM);
           } else {
@@ -463,7 +470,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = F8 ? make_idesc_e4m3(BM, BN) : make_idesc_bf16(BM, BN, A_MN, B_MN);
       int stage = 0, buf = 0;
       uint32_t phase = 0, aphase = 0;
       bool ok = true;
@@ -486,7 +493,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 A_MN ? make_sw128_desc(sa + k * 2048, 8192, 1024) : make_sw128_desc(sa + k * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sw128_desc(sb + k * 2048, 8192, 1024) : make_sw128_desc(sb + k * 32, 16, 1024);
-            mma_f16(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
+            if constexpr (F8) mma_f8(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
+            else mma_f16(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -512,7 +520,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<EPI, BN>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
+      epilogue_tile<EPI, BN, F8>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
       tc_fence_before();
       bar_arrive(&tempty[buf]);
       buf ^= 1;
@@ -529,9 +537,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool F8 = false>
 cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, F8>;
   constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + kEpiStageBytes + 1024 + 256;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr = false;

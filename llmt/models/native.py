@@ -18,6 +18,7 @@ import torch
 import torch.utils.checkpoint
 
 from llmt.models.llama import LlamaModel
+from llmt.ops import fp8 as F8
 from llmt.ops import functions as Fn
 from llmt.ops import native as N
 
@@ -104,6 +105,7 @@ class FlatParams:
                 raise RuntimeError("w1 and w3 must be adjacent in the flat buffer (ffn*d must be a multiple of 64)")
             ffn, d = w1.shape
             w1.w13_16 = shadow[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
+            w1.w13 = self.master[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
             w1.w13_grad = grad[o1:o1 + 2 * ffn * d].view(2 * ffn, d)
             w1.w3_param = w3
 
@@ -121,7 +123,12 @@ class NativeLlama:
     A plain wrapper (not an nn.Module), so model.state_dict() keeps the reference keys."""
 
     def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
-                 nvtx: bool = False, bucket_pad: bool = False):
+                 nvtx: bool = False, bucket_pad: bool = False, linear: str = "bf16"):
+        """linear: "bf16", or "fp8" for the block linears on tensorwise e4m3 operands
+        (llmt.ops.fp8; reference --linear fp8, bench_train.py:33-38); the head stays bf16."""
+        if linear not in ("bf16", "fp8"):
+            raise ValueError(f"linear must be bf16 or fp8, not {linear!r}")
+        self.linear = linear
         self.model = model
         # grad_ready(i) is called from the backward once block i's gradients have all been issued
         # (a hook on the gradient of the block's input): the overlapped data-parallel step uses it
@@ -164,6 +171,11 @@ class NativeLlama:
             n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
         else:
             n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+        if self.linear == "fp8":
+            o = F8.QKVAttentionFP8.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
+            att = F8.LinearFP8.apply(o, blk.attn.wo.weight)
+            n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+            return F8.SwiGLUMLPFP8.apply(n2, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn), s2
         o = Fn.QKVAttention.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
         att = Fn.Linear.apply(o, blk.attn.wo.weight)
         n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)

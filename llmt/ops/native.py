@@ -18,7 +18,7 @@ EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD 
 _KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0, "dp_error_code": 0,
                      "set_reserved_sms": 0, "reserved_sms": 0, "attn_bwd_set_trace": 0,
                      "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "ipc_free": 0, "tensor_from_ptr": 0,
-                     "sm_count": 0}
+                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0}
 
 
 class LaunchCounter:
@@ -186,6 +186,69 @@ def gemm_ce_bwd(h, w, targets, lse, grad_out, scale, out=None, bn=0):
 def gemm_error_code(reset=False) -> int:
     """Sticky code of the first bounded-wait timeout any GEMM launch hit (0 = none)."""
     return ext().gemm_error_code(reset)
+
+
+# ---------------------------------------------------------------- fp8 (tensorwise e4m3)
+E4M3 = torch.float8_e4m3fn
+_AMAX_SLOTS = {}
+
+
+def fp8_quant(x, transpose=True):
+    """Tensorwise e4m3 quantization of a bf16 / fp32 (rows, cols) tensor (reference
+    kernels/lowp.py:51-62): scale = 448 / amax, q = e4m3(sat(x * scale)); returns
+    (q, q^T or None, inv) with inv a 1-element fp32 device tensor holding 1 / scale (bit-identical to
+    llmt.ops.lowp_ref.fp8_quant_ref), so nothing
+    leaves the device (the step stays capturable in a CUDA graph)."""
+    rows, cols = x.shape
+    dev = x.device
+    n = _AMAX_SLOTS.get(dev)
+    if n is None:
+        n = _AMAX_SLOTS[dev] = int(ext().fp8_amax_slots())
+    q = torch.empty((rows, cols), dtype=E4M3, device=dev)
+    qt = torch.empty((cols, rows), dtype=E4M3, device=dev) if transpose else None
+    buf = torch.empty(4 + n, dtype=torch.float32, device=dev)
+    inv = buf[:1]
+    ext().fp8_quant(x, q, qt, inv, buf[4:])
+    return q, qt, inv
+
+
+def gemm_fp8(a, b, sa, sb, out=None, out_dtype=torch.bfloat16, accumulate=False, bn=0, splits=0):
+    """out = (a @ b^T) * sa * sb with e4m3 a (M, K) and b (N, K), fp32 accumulation; bf16 out, or
+    fp32 out (+= with accumulate: weight-gradient accumulation into main_grad)."""
+    M, N = a.shape[0], b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
+    ext().gemm(a, b, False, True, epi, out, accumulate=accumulate, bn=bn, splits=splits, scale_a=sa, scale_b=sb)
+    return out
+
+
+def gemm_fp8_swiglu(xq, w13q, sa, sb, ffn, bn=0):
+    """Merged gate/up GEMM on e4m3 operands with the SwiGLU epilogue: (h, [g | u]) in bf16."""
+    M = xq.shape[0]
+    h = torch.empty((M, ffn), dtype=torch.bfloat16, device=xq.device)
+    gu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=xq.device)
+    ext().gemm(xq, w13q, False, True, EPI_SWIGLU, h, aux=gu, split=ffn, bn=bn, scale_a=sa, scale_b=sb)
+    return h, gu
+
+
+def gemm_fp8_swiglu_bwd(dmq, w2q_t, sa, sb, gu, ffn, bn=0):
+    """w2 dgrad on e4m3 operands (dm and the transposed W2, both K-major) with the SwiGLU
+    backward epilogue: [dg | du] in bf16 from the saved [g | u]."""
+    M = dmq.shape[0]
+    dgu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=dmq.device)
+    ext().gemm(dmq, w2q_t, False, True, EPI_SWIGLU_BWD, dgu, aux=gu, out2=dgu, split=ffn, bn=bn, scale_a=sa,
+               scale_b=sb)
+    return dgu
+
+
+def gemm_fp8_rope(xq, wq, sa, sb, cos, sin, T, hd, rot_cols, bn=0):
+    """qkv GEMM on e4m3 operands with RoPE applied to the first rot_cols columns in the epilogue."""
+    M, N = xq.shape[0], wq.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
+    ext().gemm(xq, wq, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols, bn=bn,
+               scale_a=sa, scale_b=sb)
+    return out
 
 
 # ---------------------------------------------------------------- elementwise

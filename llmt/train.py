@@ -28,7 +28,7 @@ class Trainer:
 
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
                  cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False,
-                 tp_group=None, init: str = "full", nvtx: bool = False):
+                 tp_group=None, init: str = "full", nvtx: bool = False, linear: str = "bf16"):
         self.cfg, self.batch, self.seq = cfg, batch, seq
         self.nvtx = nvtx  # NVTX ranges forward / backward / optimizer per step (eager steps; reference --nvtx)
         self.device = torch.device(device)
@@ -37,6 +37,8 @@ class Trainer:
         self.tp_group = tp_group
         pad_to = dp.world_size if dp is not None else 1
         if tp_group is not None:
+            if linear != "bf16":
+                raise ValueError("fp8 linears are built for the single-shard model only")
             import torch.distributed as dist
             from llmt.parallel.tp import TPNativeLlama, build_local_model
             tp, r = dist.get_world_size(tp_group), dist.get_rank(tp_group)
@@ -46,7 +48,7 @@ class Trainer:
             self.model = build_model(cfg, seq, seed=seed, device=self.device)
             overlap = dp is not None and getattr(dp, "overlap", False)
             self.net = NativeLlama(self.model, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt, nvtx=nvtx,
-                                   bucket_pad=overlap)
+                                   bucket_pad=overlap, linear=linear)
             if overlap:
                 if ckpt:
                     raise ValueError("the overlapped data-parallel step needs ckpt=False")
