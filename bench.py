@@ -241,13 +241,15 @@ def main():
                    help="data-parallel transport: NCCL (fastest measured at 2 and 8 GPUs), the fused "
                         "peer-memory kernel, or that kernel overlapped with the backward")
     p.add_argument("--no-graph", action="store_true")
-    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8"],
-                   help="block linears in bf16, or on tensorwise e4m3 operands (every GEMM of qkv, wo, w1||w3, "
-                        "w2; the head stays bf16). With --impl reference, fp8 selects the reference's row "
-                        "'8 + FP8 linears (e4m3)' unless --ref-row is given")
+    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"],
+                   help="block linears (every GEMM of qkv, wo, w1||w3, w2; the head stays bf16) in bf16, on "
+                        "tensorwise e4m3 operands, or block-scaled MXFP8 / NVFP4. With --impl reference, fp8 "
+                        "and nvfp4 select the reference's rows '8 + FP8 linears (e4m3)' / '9 + NVFP4 linears "
+                        "(e2m1)' unless --ref-row is given")
     args = p.parse_args()
-    if args.impl == "reference" and args.linear == "fp8" and args.ref_row == "5 + torch.compile":
-        args.ref_row = "8 + FP8 linears (e4m3)"
+    if args.impl == "reference" and args.ref_row == "5 + torch.compile":
+        args.ref_row = {"fp8": "8 + FP8 linears (e4m3)", "nvfp4": "9 + NVFP4 linears (e2m1)"}.get(args.linear,
+                                                                                                args.ref_row)
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = setup_dist(args.gpus)
@@ -265,7 +267,9 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 3),
                 "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": round(res["value"] / BASELINE_TOKS, 3),
-                "dtype": "bf16" if args.linear == "bf16" else "fp8 e4m3 tensorwise block linears, bf16 rest",
+                "dtype": {"bf16": "bf16", "fp8": "fp8 e4m3 tensorwise block linears, bf16 rest",
+                          "mxfp8": "mxfp8 (e4m3, ue8m0 per 32) block linears, bf16 rest",
+                          "nvfp4": "nvfp4 (e2m1, ue4m3 per 16) block linears, bf16 rest"}[args.linear],
                 "data": "synthetic uniform-random tokens, random-init weights",
                 "config": {"model": MODEL, "global_batch": PER_GPU_BATCH * world, "seq_len": SEQ,
                            "parallelism": par, "l2": "working set >> 126 MB L2; no flush", "linear": args.linear,

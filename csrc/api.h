@@ -88,7 +88,10 @@ struct GemmArgs {
   int tp_rank;         // PEER_RS: this rank's slot index in every owner's buffer
   int rows_per_rank;   // PEER_RS: output row r belongs to rank r / rows_per_rank
   const float* scale_a;  // e4m3 operands: inverse tensorwise scales, acc is multiplied by both
-  const float* scale_b;
+  const float* scale_b;  // (NVFP4: the two per-tensor decode scales)
+  const uint8_t* sfa;    // block-scaled operands: scale factors of A and B in 512-byte chunks
+  const uint8_t* sfb;    // [row tile of 128][chunk along K][32 x 16 bytes]
+  int sf_chunks;         // chunks per 128-row tile (k-blocks x chunks per k-block)
   int* err;
 };
 
@@ -108,6 +111,24 @@ cudaError_t gemm_fp8(const void* a, int64_t lda, const void* b, int64_t ldb, int
 // transposed copy qt (cols x rows), *inv = 1 / s. x is bf16 or fp32 (x_f32), rows x cols with
 // row pitch ld; rows and cols multiples of 16. scratch holds fp8_amax_slots() floats.
 int fp8_amax_slots();
+// Block-scaled GEMM: out = (a @ b^T) with per-block scales applied by the tensor core.
+// kind 2 = MXFP8 (e4m3 bytes, ue8m0 scale per 32 along K), kind 3 = NVFP4 (e2m1 packed two per
+// byte, ue4m3 scale per 16 along K, g.scale_a / g.scale_b the per-tensor decode scales applied
+// in the epilogue). K counts elements; a and b are row-major (K-major) byte matrices; g.sfa /
+// g.sfb hold the scales in the chunked layout with cdiv(K, elements per 128 bytes) k-blocks.
+// Epilogues: BF16, F32, ROPE, SWIGLU (b rows interleaved 64 of W1, 64 of W3), SWIGLU_BWD.
+cudaError_t gemm_bs(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int epi,
+                    GemmArgs g, cudaStream_t st, int splits = 0);
+// Block-scaled quantization of x (rows x cols, bf16 or fp32) along cols and/or, for x^T, along
+// rows: kind 2 MXFP8, kind 3 NVFP4 (g_out: the per-tensor decode scale amax / (6 * 448), from
+// scratch partials of fp8_amax pass run here). q: (rows, cols) bytes (NVFP4: cols / 2);
+// qt: (cols, rows) (NVFP4: rows / 2); sf / sft: chunked scale layouts. interleave64: the rows
+// of x are [W1; W3] of a merged SwiGLU weight and q is written 64 rows of W1, 64 of W3, ...
+// stochastic: NVFP4 stochastic rounding with a counter-based generator (seed, element index).
+cudaError_t mx_quant(int kind, const void* x, bool x_f32, int rows, int cols, int64_t ld, void* q, void* sf, void* qt,
+                     void* sft, float* g_out, float* scratch, bool interleave64, bool stochastic, uint64_t seed,
+                     const int64_t* seed_dev, cudaStream_t st);
+int64_t mx_sf_bytes(int kind, int rows, int cols);
 cudaError_t fp8_quant(const void* x, bool x_f32, int rows, int cols, int64_t ld, void* q, void* qt, float* inv,
                       float* scratch, cudaStream_t st);
 int gemm_pick_bn(int M, int N, int epi);

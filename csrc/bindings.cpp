@@ -240,17 +240,71 @@ void fp8_quant(at::Tensor x, at::Tensor q, c10::optional<at::Tensor> qt, at::Ten
      "fp8_quant");
 }
 
+void mx_quant(int64_t kind, at::Tensor x, c10::optional<at::Tensor> q, c10::optional<at::Tensor> sf,
+              c10::optional<at::Tensor> qt, c10::optional<at::Tensor> sft, c10::optional<at::Tensor> g,
+              c10::optional<at::Tensor> scratch, bool interleave64, bool stochastic, int64_t seed,
+              c10::optional<at::Tensor> seed_dev) {
+  cuda2d(x, "x");
+  CHECK(x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat, "mx_quant: x must be bf16 or fp32");
+  const int64_t rows = x.size(0), cols = x.size(1);
+  const int64_t per = kind == 3 ? 2 : 1;
+  auto bytes = [&](c10::optional<at::Tensor>& t, int64_t n, const char* name) -> void* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    on_device(*t, name);
+    CHECK(t->element_size() == 1 && t->is_contiguous() && t->numel() >= n, name, ": contiguous bytes, at least ", n);
+    return t->data_ptr();
+  };
+  void* qp = bytes(q, rows * cols / per, "q");
+  void* qtp = bytes(qt, rows * cols / per, "qt");
+  void* sfp = bytes(sf, qp ? llmt::mx_sf_bytes((int)kind, rows, cols) : 0, "sf");
+  void* sftp = bytes(sft, qtp ? llmt::mx_sf_bytes((int)kind, cols, rows) : 0, "sft");
+  float* gp = nullptr;
+  float* sp = nullptr;
+  if (kind == 3) {
+    CHECK(g.has_value() && scratch.has_value(), "mx_quant: NVFP4 needs g and scratch");
+    for (auto* t : {&*g, &*scratch}) {
+      on_device(*t, "mx_quant scale buffer");
+      CHECK_DT((*t), at::kFloat);
+    }
+    CHECK(scratch->numel() >= llmt::fp8_amax_slots(), "mx_quant: scratch too small");
+    gp = g->data_ptr<float>();
+    sp = scratch->data_ptr<float>();
+  }
+  ok(llmt::mx_quant((int)kind, x.data_ptr(), x.scalar_type() == at::kFloat, (int)rows, (int)cols, x.stride(0), qp, sfp, qtp,
+                    sftp, gp, sp, interleave64, stochastic, (uint64_t)seed,
+                    static_cast<const int64_t*>(opt_ptr(seed_dev, "seed_dev")), stream()),
+     "mx_quant");
+}
+
 // ---------------------------------------------------------------- GEMM
 void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor out, bool accumulate,
           c10::optional<at::Tensor> aux, c10::optional<at::Tensor> out2, int64_t split, c10::optional<at::Tensor> cos_t,
           c10::optional<at::Tensor> sin_t, int64_t T, int64_t hd, int64_t rot_cols, c10::optional<at::Tensor> tgt,
           c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
           c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits, c10::optional<at::Tensor> peer,
-          int64_t tp_rank, int64_t rows_per_rank, c10::optional<at::Tensor> scale_a, c10::optional<at::Tensor> scale_b) {
+          int64_t tp_rank, int64_t rows_per_rank, c10::optional<at::Tensor> scale_a, c10::optional<at::Tensor> scale_b,
+          int64_t kind, c10::optional<at::Tensor> sfa, c10::optional<at::Tensor> sfb) {
   cuda2d(a, "a");
   cuda2d(b, "b");
-  const bool f8 = a.scalar_type() == at::kFloat8_e4m3fn;
-  if (f8) {
+  const bool bs = kind == 2 || kind == 3;
+  const bool f8 = !bs && a.scalar_type() == at::kFloat8_e4m3fn;
+  CHECK(kind == 0 || bs, "gemm: kind must be 0 (by dtype), 2 (MXFP8) or 3 (NVFP4)");
+  if (bs) {
+    CHECK(!ta && tb, "block-scaled gemm: both operands K-major (a: M x K, b: N x K)");
+    CHECK(a.element_size() == 1 && b.element_size() == 1, "block-scaled gemm: byte operands");
+    CHECK(sfa.has_value() && sfb.has_value(), "block-scaled gemm needs sfa and sfb");
+    for (auto* t : {&*sfa, &*sfb}) {
+      on_device(*t, "scale factors");
+      CHECK(t->element_size() == 1 && t->is_contiguous(), "scale factors: contiguous bytes");
+    }
+    if (kind == 3) {
+      CHECK(scale_a.has_value() && scale_b.has_value(), "NVFP4 gemm needs the decode scales");
+      for (auto* t : {&*scale_a, &*scale_b}) {
+        on_device(*t, "decode scale");
+        CHECK_DT((*t), at::kFloat);
+      }
+    }
+  } else if (f8) {
     CHECK_DT(b, at::kFloat8_e4m3fn);
     CHECK(!ta && tb, "fp8 gemm: both operands K-major (a: M x K, b: N x K)");
     CHECK(scale_a.has_value() && scale_b.has_value(), "fp8 gemm needs scale_a and scale_b");
@@ -263,10 +317,11 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
     CHECK_DT(b, at::kBFloat16);
   }
   on_device(out, "out");
+  const int kmul = kind == 3 ? 2 : 1;  // NVFP4 bytes hold two elements
   const int M = ta ? a.size(1) : a.size(0);
-  const int K = ta ? a.size(0) : a.size(1);
+  const int K = (ta ? a.size(0) : a.size(1)) * kmul;
   int N = tb ? b.size(0) : b.size(1);
-  const int Kb = tb ? b.size(1) : b.size(0);
+  const int Kb = (tb ? b.size(1) : b.size(0)) * kmul;
   CHECK(K == Kb, "gemm inner dims differ: ", K, " vs ", Kb);
   if (epi == llmt::EPI_SWIGLU) {
     CHECK(tb && b.size(0) == 2 * split, "SWIGLU gemm: b must be W13 (2*ffn, K)");
@@ -330,6 +385,22 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
     CHECK(part->numel() >= (int64_t)M * ((N + BN - 1) / BN) * 2, "CE_FWD partial buffer too small");
   }
   if (epi == llmt::EPI_CE_BWD) CHECK(g.tgt && g.lse, "CE_BWD gemm args");
+  if (bs) {
+    if (kind == 3) {
+      g.scale_a = scale_a->data_ptr<float>();
+      g.scale_b = scale_b->data_ptr<float>();
+    }
+    g.sfa = static_cast<const uint8_t*>(sfa->data_ptr());
+    g.sfb = static_cast<const uint8_t*>(sfb->data_ptr());
+    const int kbytes = K / kmul;
+    const int64_t need_a = llmt::mx_sf_bytes((int)kind, M, K), need_b = llmt::mx_sf_bytes((int)kind, b.size(0), K);
+    CHECK(sfa->numel() >= need_a && sfb->numel() >= need_b, "block-scaled gemm: scale buffers too small");
+    (void)kbytes;
+    ok(llmt::gemm_bs((int)kind, a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), M, N, K, (int)epi, g, stream(),
+                     (int)splits),
+       "gemm_bs");
+    return;
+  }
   if (f8) {
     g.scale_a = scale_a->data_ptr<float>();
     g.scale_b = scale_b->data_ptr<float>();
@@ -456,7 +527,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
         "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
         "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0, "peer"_a = py::none(), "tp_rank"_a = 0, "rows_per_rank"_a = 0,
-        "scale_a"_a = py::none(), "scale_b"_a = py::none());
+        "scale_a"_a = py::none(), "scale_b"_a = py::none(), "kind"_a = 0, "sfa"_a = py::none(), "sfb"_a = py::none());
+  m.def("mx_sf_bytes", &llmt::mx_sf_bytes);
+  m.def("mx_quant", &mx_quant, "kind"_a, "x"_a, "q"_a, "sf"_a, "qt"_a, "sft"_a, "g"_a, "scratch"_a,
+        "interleave64"_a = false, "stochastic"_a = false, "seed"_a = 0, "seed_dev"_a = py::none());
   m.def("fp8_amax_slots", &llmt::fp8_amax_slots);
   m.def("fp8_quant", &fp8_quant, "x"_a, "q"_a, "qt"_a, "inv"_a, "scratch"_a);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);

@@ -253,6 +253,48 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
+// ---- block-scaled MMA (MXFP8: e4m3 data + ue8m0 scale per 32; NVFP4: e2m1 data + ue4m3 scale
+// per 16). Scale factors live in TMEM: a 128-row x 4-scale chunk of shared memory (row m at byte
+// (m % 32) * 16 + (m / 32) * 4, scale k at + k) is copied by one tcgen05.cp 32x128b.warpx4 into 4
+// columns of lanes 0-31, replicated to the other lane quarters. The scale's byte within a
+// 32-bit column is selected by bits 30-31 of the TMEM address and the matching scale-factor id
+// fields of the instruction descriptor.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Shared-memory descriptor without swizzle, K-major: 8-row core matrices of 16-byte rows,
+// sbo_bytes between consecutive 8-row groups.
+__device__ __forceinline__ uint64_t make_plain_desc(uint32_t saddr, uint32_t sbo_bytes) {
+  const uint64_t lo = (saddr & 0x3FFFFu) >> 4;
+  const uint64_t hi = ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14);
+  return lo | (hi << 32);
+}
+__device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// Block-scaled kinds (fp32 accumulator implied): data format of A and B (mxf8f6f4: e4m3 = 0;
+// mxf4nvf4: e2m1 = 1), scale format (ue4m3 = 0, ue8m0 = 1), both K-major. The scale-factor ids
+// (A: bits 29-30, B: bits 4-5) are or-ed in per instruction.
+__host__ __device__ constexpr uint32_t make_idesc_bs(int M, int N, uint32_t ab_fmt, uint32_t sf_fmt) {
+  return (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(N >> 3) << 17) | (sf_fmt << 23) | ((uint32_t)(M >> 4) << 24);
+}
+
 // kind::f8f6f4 with A and B both e4m3 (format code 0), both K-major, fp32 accumulator.
 __host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N) {
   return (1u << 4)                       // D format f32

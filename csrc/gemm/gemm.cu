@@ -191,6 +191,60 @@ cudaError_t gemm_fp8(const void* a, int64_t lda, const void* b, int64_t ldb, int
   return gemm_launch_f8(BN, epi, mp, g, st);
 }
 
+
+cudaError_t gemm_bs(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int epi,
+                    GemmArgs g, cudaStream_t st, int force_splits) {
+  LLMT_REQUIRE(kind == 2 || kind == 3, "gemm_bs: kind must be 2 (MXFP8) or 3 (NVFP4)");
+  LLMT_REQUIRE(M > 0 && N > 0 && K > 0, "gemm_bs: empty problem");
+  LLMT_REQUIRE(N % 8 == 0 && K % 32 == 0, "gemm_bs: N must be a multiple of 8 and K of 32");
+  LLMT_REQUIRE(tma_ok(a, lda, 1) && tma_ok(b, ldb, 1), "gemm_bs: operands need 16-byte aligned bases and row pitches");
+  LLMT_REQUIRE(g.sfa && g.sfb && (reinterpret_cast<uintptr_t>(g.sfa) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(g.sfb) & 15) == 0,
+               "gemm_bs: needs 16-byte aligned scale-factor buffers");
+  LLMT_REQUIRE(kind == 2 || (g.scale_a && g.scale_b), "gemm_bs: NVFP4 needs both per-tensor decode scales");
+  LLMT_REQUIRE(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD || epi == EPI_ROPE,
+               "gemm_bs: epilogue not built for block-scaled operands");
+  constexpr int BN = 128;
+  const int kbytes = kind == 3 ? K / 2 : K;  // row length of a and b in bytes
+  const int k_blocks = (int)cdiv(kbytes, 2 * kGemmBK);
+  int splits = 1;
+  const bool can_split = epi == EPI_F32 && g.accumulate;
+  if (force_splits > 0) {
+    LLMT_REQUIRE(force_splits == 1 || can_split, "gemm_bs: split-K needs an fp32 reduce-add output");
+    splits = force_splits;
+  } else if (can_split) {
+    int bn = 0;
+    gemm_plan(M, N, kbytes / 2, epi, true, &bn, &splits);
+  }
+  if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm_bs: bad RoPE epilogue shape");
+  if (epi == EPI_SWIGLU) LLMT_REQUIRE(N % 64 == 0, "gemm_bs: SwiGLU needs ffn a multiple of 64");
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.m_blocks = (int)cdiv(M, kGemmBM);
+  g.n_blocks = (int)cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
+  g.k_blocks = k_blocks;
+  g.k_per_split = (int)cdiv(k_blocks, splits);
+  g.splits = (int)cdiv(k_blocks, g.k_per_split);
+  g.sf_chunks = k_blocks * (kind == 2 ? 1 : 4);
+  g.err = gemm_err_word();
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  alignas(64) GemmMaps mp;
+  memset(&mp, 0, sizeof(mp));
+  const int rows_b = epi == EPI_SWIGLU ? 2 * N : N;
+  const bool ok_a = make_tmap_2d(&mp.a, a, dt, 1, kbytes, M, lda, 2 * kGemmBK, kGemmBM);
+  const bool ok_b = ok_a && make_tmap_2d(&mp.b, b, dt, 1, kbytes, rows_b, ldb, 2 * kGemmBK, BN);
+  if (!ok_a || !ok_b) {
+    char msg[200];
+    snprintf(msg, sizeof(msg), "gemm_bs: cuTensorMapEncodeTiled rejected operand %s (result %d; M=%d N=%d K=%d)",
+             ok_a ? "B" : "A", last_tmap_result(), M, N, K);
+    set_last_error(msg);
+    return cudaErrorInvalidValue;
+  }
+  LLMT_REQUIRE(make_out_maps(epi, g, M, N, &mp), "gemm_bs: output tensor map rejected (pitch/alignment)");
+  return gemm_launch_bs(kind, epi, mp, g, st);
+}
+
 namespace {
 // Per-row combine of the CE_FWD partials into lse and loss = lse - target logit.
 __global__ void ce_combine_kernel(const float* __restrict__ part, const float* __restrict__ tlogit,

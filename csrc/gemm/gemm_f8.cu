@@ -10,11 +10,11 @@ template <int BN>
 static cudaError_t run_f8(int epi, const GemmMaps& mp, const GemmArgs& g, cudaStream_t st) {
   constexpr int S = stages_for<BN>();
   switch (epi) {
-    case EPI_BF16: return launch<BN, S, false, false, EPI_BF16, true>(mp, g, st);
-    case EPI_F32: return launch<BN, S, false, false, EPI_F32, true>(mp, g, st);
-    case EPI_SWIGLU: return launch<BN, S, false, false, EPI_SWIGLU, true>(mp, g, st);
-    case EPI_SWIGLU_BWD: return launch<BN, S, false, false, EPI_SWIGLU_BWD, true>(mp, g, st);
-    case EPI_ROPE: return launch<BN, S, false, false, EPI_ROPE, true>(mp, g, st);
+    case EPI_BF16: return launch<BN, S, false, false, EPI_BF16, 1>(mp, g, st);
+    case EPI_F32: return launch<BN, S, false, false, EPI_F32, 1>(mp, g, st);
+    case EPI_SWIGLU: return launch<BN, S, false, false, EPI_SWIGLU, 1>(mp, g, st);
+    case EPI_SWIGLU_BWD: return launch<BN, S, false, false, EPI_SWIGLU_BWD, 1>(mp, g, st);
+    case EPI_ROPE: return launch<BN, S, false, false, EPI_ROPE, 1>(mp, g, st);
     default: set_last_error("gemm_fp8: epilogue not built for e4m3 operands"); return cudaErrorInvalidValue;
   }
 }

@@ -46,6 +46,7 @@ cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g
 cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // dgrad
 cudaError_t gemm_launch_mm(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // wgrad
 cudaError_t gemm_launch_f8(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // e4m3, K-major
+cudaError_t gemm_launch_bs(int kind, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // MX / NV
 
 namespace gemm_detail {
 
@@ -147,8 +148,8 @@ struct Stager {
 __device__ __forceinline__ bool lane_is_zero(const Stager& st) { return st.lane == 0; }
 
 // row: this thread's accumulator row; wrow: the warp's first row (TMA box origin).
-// F8: e4m3 operands with tensorwise scales; every accumulator value is multiplied by the two
-// inverse scales before the epilogue's math.
+// SC: e4m3 operands with tensorwise scales (or NVFP4 with per-tensor decode scales); every
+// accumulator value is multiplied by the two scales before the epilogue's math.
 template <int EPI, int BN, bool F8 = false>
 __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow, int nb, const GemmArgs& a,
                                               const CUtensorMap* tmC, const CUtensorMap* tmC2, Stager& st) {
@@ -377,21 +378,29 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool F8 = false>
+// KIND: 0 bf16, 1 e4m3 with tensorwise scales, 2 MXFP8, 3 NVFP4 (2 and 3: block-scaled MMA with
+// the scale-factor chunks of each k-block loaded next to its A / B tiles and copied into TMEM).
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
   pdl_wait();
   constexpr int BM = kGemmBM, BK = kGemmBK;
+  constexpr bool F8 = KIND != 0, BS = KIND >= 2;
   static_assert(!F8 || (!A_MN && !B_MN), "8-bit operands are K-major only");
-  constexpr int KE = F8 ? 2 * BK : BK;  // elements per k-block: one 128-byte swizzled row either way
+  static_assert(!BS || BN == 128, "block-scaled tiles are 128 x 128");
+  constexpr int KX = F8 ? 2 * BK : BK;  // tensor-map units per k-block: one 128-byte swizzled row
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr int NCH = KIND == 2 ? 1 : 4;                // scale chunks per k-block and operand
+  constexpr uint32_t SF_BYTES = BS ? 2 * NCH * 512 : 0;  // A and B chunks of one stage
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr int TMEM_COLS = 2 * BN;
+  constexpr int TMEM_COLS = BS ? 512 : 2 * BN;           // block-scaled: scales at column 256 on
+  constexpr uint32_t SF_COLS = 2 * NCH * 4;              // TMEM columns of one stage's scales
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_out = smem + STAGES * STAGE_BYTES;  // 4 warps x 2 x 4 KB epilogue staging
+  uint8_t* sf_smem = smem + STAGES * STAGE_BYTES;  // per stage: A chunks then B chunks
+  uint8_t* stage_out = sf_smem + STAGES * SF_BYTES;  // 4 warps x 2 x 4 KB epilogue staging
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -442,8 +451,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          bar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          const int k0 = kb * KE;
+          bar_arrive_expect_tx(&full[stage], STAGE_BYTES + SF_BYTES);
+          const int k0 = kb * KX;
+          if constexpr (BS) {
+            uint8_t* sfs = sf_smem + stage * SF_BYTES;
+            const int64_t ck = (int64_t)kb * NCH;
+            bulk_load(sfs, args.sfa + ((int64_t)mb * args.sf_chunks + ck) * 512, NCH * 512, &full[stage]);
+            bulk_load(sfs + NCH * 512, args.sfb + ((int64_t)nb * args.sf_chunks + ck) * 512, NCH * 512, &full[stage]);
+          }
           if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full[stage], k0, mb * BM);
           } else {
@@ -451,7 +466,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             tma_load_2d(sa + 8192, &tmA, &full[stage], mb * BM + 64, k0);
           }
           if constexpr (!B_MN) {
-            if constexpr (EPI == EPI_SWIGLU) {
+            if constexpr (EPI == EPI_SWIGLU && !BS) {
               tma_load_2d(sb, &tmB, &full[stage], k0, nb * (BN / 2));
               tma_load_2d(sb + (BN / 2) * 128, &tmB, &full[stage], k0, args.split + nb * (BN / 2));
             } else {
@@ -470,7 +485,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = F8 ? make_idesc_e4m3(BM, BN) : make_idesc_bf16(BM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = KIND == 3 ? make_idesc_bs(BM, BN, 1, 0)
+                                 : KIND == 2 ? make_idesc_bs(BM, BN, 0, 1)
+                                 : F8        ? make_idesc_e4m3(BM, BN)
+                                             : make_idesc_bf16(BM, BN, A_MN, B_MN);
       int stage = 0, buf = 0;
       uint32_t phase = 0, aphase = 0;
       bool ok = true;
@@ -487,14 +505,38 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+          uint32_t t_sfa = 0, t_sfb = 0;
+          if constexpr (BS) {
+            // this stage's scale chunks into its own TMEM columns (the MMAs that read the
+            // previous contents of these columns completed before the stage was refilled)
+            const uint32_t s_sf = smem_u32(sf_smem + stage * SF_BYTES);
+            t_sfa = tmem_base + 256 + stage * SF_COLS;
+            t_sfb = t_sfa + NCH * 4;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+              tmem_cp_sf(t_sfa + 4 * c, make_plain_desc(s_sf + c * 512, 128));
+              tmem_cp_sf(t_sfb + 4 * c, make_plain_desc(s_sf + (NCH + c) * 512, 128));
+            }
+          }
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad =
                 A_MN ? make_sw128_desc(sa + k * 2048, 8192, 1024) : make_sw128_desc(sa + k * 32, 16, 1024);
             const uint64_t bd =
                 B_MN ? make_sw128_desc(sb + k * 2048, 8192, 1024) : make_sw128_desc(sb + k * 32, 16, 1024);
-            if constexpr (F8) mma_f8(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
-            else mma_f16(d, ad, bd, idesc, (kb > k_lo || k > 0) ? 1u : 0u);
+            const uint32_t acc = (kb > k_lo || k > 0) ? 1u : 0u;
+            if constexpr (KIND == 2) {
+              // one ue8m0 scale per row per K = 32 instruction: byte k of the chunk's columns
+              mma_mxf8(d, ad, bd, idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4), t_sfa | ((uint32_t)k << 30),
+                       t_sfb | ((uint32_t)k << 30), acc);
+            } else if constexpr (KIND == 3) {
+              // four ue4m3 scales per row per K = 64 instruction: chunk k
+              mma_nvf4(d, ad, bd, idesc, t_sfa + 4 * k, t_sfb + 4 * k, acc);
+            } else if constexpr (F8) {
+              mma_f8(d, ad, bd, idesc, acc);
+            } else {
+              mma_f16(d, ad, bd, idesc, acc);
+            }
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -520,7 +562,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<EPI, BN, F8>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
+      epilogue_tile<EPI, BN, KIND == 1 || KIND == 3>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
       tc_fence_before();
       bar_arrive(&tempty[buf]);
       buf ^= 1;
@@ -537,10 +579,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool F8 = false>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0>
 cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, F8>;
-  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2) + kEpiStageBytes + 1024 + 256;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, KIND>;
+  constexpr size_t sf = KIND >= 2 ? 2 * (KIND == 2 ? 1 : 4) * 512 : 0;
+  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2 + sf) + kEpiStageBytes + 1024 + 256;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr = false;
   if (!attr) {

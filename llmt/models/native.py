@@ -19,6 +19,7 @@ import torch.utils.checkpoint
 
 from llmt.models.llama import LlamaModel
 from llmt.ops import fp8 as F8
+from llmt.ops import mx as MX
 from llmt.ops import functions as Fn
 from llmt.ops import native as N
 
@@ -124,10 +125,11 @@ class NativeLlama:
 
     def __init__(self, model: LlamaModel, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
                  nvtx: bool = False, bucket_pad: bool = False, linear: str = "bf16"):
-        """linear: "bf16", or "fp8" for the block linears on tensorwise e4m3 operands
-        (llmt.ops.fp8; reference --linear fp8, bench_train.py:33-38); the head stays bf16."""
-        if linear not in ("bf16", "fp8"):
-            raise ValueError(f"linear must be bf16 or fp8, not {linear!r}")
+        """linear: "bf16"; "fp8" for the block linears on tensorwise e4m3 operands (llmt.ops.fp8;
+        reference --linear fp8, bench_train.py:33-38); "mxfp8" or "nvfp4" (reference --linear fp4)
+        for block-scaled operands (llmt.ops.mx). The head stays bf16."""
+        if linear not in ("bf16", "fp8", "mxfp8", "nvfp4"):
+            raise ValueError(f"linear must be bf16, fp8, mxfp8 or nvfp4, not {linear!r}")
         self.linear = linear
         self.model = model
         # grad_ready(i) is called from the backward once block i's gradients have all been issued
@@ -171,6 +173,12 @@ class NativeLlama:
             n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
         else:
             n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+        if self.linear in ("mxfp8", "nvfp4"):
+            kind = N.MXFP8 if self.linear == "mxfp8" else N.NVFP4
+            o = MX.QKVAttentionMX.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd, kind)
+            att = MX.LinearMX.apply(o, blk.attn.wo.weight, kind)
+            n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+            return MX.SwiGLUMLPMX.apply(n2, blk.mlp.w1.weight, blk.mlp.w2.weight, cfg.ffn, kind), s2
         if self.linear == "fp8":
             o = F8.QKVAttentionFP8.apply(n1, blk.attn.qkv.weight, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd)
             att = F8.LinearFP8.apply(o, blk.attn.wo.weight)

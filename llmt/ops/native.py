@@ -7,6 +7,8 @@ of silently falling back to PyTorch.
 """
 from __future__ import annotations
 
+from typing import NamedTuple, Optional
+
 import torch
 
 _C = None
@@ -18,7 +20,7 @@ EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD 
 _KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0, "dp_error_code": 0,
                      "set_reserved_sms": 0, "reserved_sms": 0, "attn_bwd_set_trace": 0,
                      "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "ipc_free": 0, "tensor_from_ptr": 0,
-                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0}
+                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0}
 
 
 class LaunchCounter:
@@ -248,6 +250,109 @@ def gemm_fp8_rope(xq, wq, sa, sb, cos, sin, T, hd, rot_cols, bn=0):
     out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
     ext().gemm(xq, wq, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols, bn=bn,
                scale_a=sa, scale_b=sb)
+    return out
+
+
+# ---------------------------------------------------------------- block-scaled (MXFP8 / NVFP4)
+MXFP8, NVFP4 = 2, 3
+SR_STEP = {}  # device -> int64 step counter mixed into the stochastic-rounding seed
+
+
+class BlockQ(NamedTuple):
+    """A block-scaled GEMM operand: q (rows, K) e4m3 or (rows, K / 2) packed e2m1 bytes, its
+    scales in the chunked layout, and (NVFP4) the per-tensor decode scale g."""
+    q: torch.Tensor
+    sf: torch.Tensor
+    g: Optional[torch.Tensor]
+
+
+def sr_counter(device):
+    """The device-side step counter of the stochastic rounding (advance it once per step)."""
+    dev = torch.device(device)
+    if dev not in SR_STEP:
+        SR_STEP[dev] = torch.zeros(1, dtype=torch.int64, device=dev)
+    return SR_STEP[dev]
+
+
+_SEEDS = [0]
+
+
+def mx_quant(x, kind, row=True, col=False, interleave64=False, stochastic=False):
+    """Quantize x (rows, cols) for block-scaled GEMMs: `row` along cols (operand of a GEMM that
+    contracts over cols), `col` x^T along rows. Returns (BlockQ | None, BlockQ | None).
+    kind MXFP8 (ue8m0 per 32) or NVFP4 (ue4m3 per 16 + per-tensor scale; reference recipe
+    kernels/lowp.py:110-138, stochastic rounding for gradients). interleave64 writes the row
+    copy of a merged [W1; W3] as 64 rows of W1, 64 of W3, ... (the SwiGLU GEMM's B tiles)."""
+    rows, cols = x.shape
+    dev = x.device
+    per = 2 if kind == NVFP4 else 1
+    qdt = torch.uint8 if kind == NVFP4 else E4M3
+    C = ext()
+    q = sf = qt = sft = None
+    kblk = 256 if kind == NVFP4 else 128  # values per 128-byte k-block
+
+    def scales(r, c):
+        # the kernel writes every scale of the tensor; padding (partial row tiles or k-blocks) is zeroed
+        n = C.mx_sf_bytes(kind, r, c)
+        alloc = torch.empty if (r % 128 == 0 and c % kblk == 0) else torch.zeros
+        return alloc(n, dtype=torch.uint8, device=dev)
+    if row:
+        q = torch.empty((rows, cols // per), dtype=qdt, device=dev)
+        sf = scales(rows, cols)
+    if col:
+        qt = torch.empty((cols, rows // per), dtype=qdt, device=dev)
+        sft = scales(cols, rows)
+    g = scratch = None
+    if kind == NVFP4:
+        n = _AMAX_SLOTS.get(dev)
+        if n is None:
+            n = _AMAX_SLOTS[dev] = int(C.fp8_amax_slots())
+        buf = torch.empty(4 + n, dtype=torch.float32, device=dev)
+        g, scratch = buf[:1], buf[4:]
+    _SEEDS[0] += 1
+    C.mx_quant(kind, x, q, sf, qt, sft, g, scratch, interleave64=interleave64, stochastic=stochastic,
+               seed=_SEEDS[0] * 0x2545F491, seed_dev=sr_counter(dev) if stochastic else None)
+    return (BlockQ(q, sf, g) if row else None), (BlockQ(qt, sft, g) if col else None)
+
+
+def _mx_args(kind, a, b):
+    return dict(kind=kind, sfa=a.sf, sfb=b.sf, scale_a=a.g, scale_b=b.g)
+
+
+def gemm_mx(kind, a, b, out=None, out_dtype=torch.bfloat16, accumulate=False, splits=0):
+    """out = a @ b^T on block-scaled operands (BlockQ, both quantized along K); bf16 out, or fp32
+    (+= with accumulate)."""
+    M, N = a.q.shape[0], b.q.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.q.device)
+    epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
+    ext().gemm(a.q, b.q, False, True, epi, out, accumulate=accumulate, splits=splits, **_mx_args(kind, a, b))
+    return out
+
+
+def gemm_mx_swiglu(kind, x, w13, ffn):
+    """Merged gate/up GEMM with the SwiGLU epilogue; w13 quantized with interleave64."""
+    M = x.q.shape[0]
+    h = torch.empty((M, ffn), dtype=torch.bfloat16, device=x.q.device)
+    gu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=x.q.device)
+    ext().gemm(x.q, w13.q, False, True, EPI_SWIGLU, h, aux=gu, split=ffn, **_mx_args(kind, x, w13))
+    return h, gu
+
+
+def gemm_mx_swiglu_bwd(kind, dm, w2t, gu, ffn):
+    """w2 dgrad (dm along d, W2^T along d) with the SwiGLU backward epilogue -> [dg | du]."""
+    M = dm.q.shape[0]
+    dgu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=dm.q.device)
+    ext().gemm(dm.q, w2t.q, False, True, EPI_SWIGLU_BWD, dgu, aux=gu, out2=dgu, split=ffn, **_mx_args(kind, dm, w2t))
+    return dgu
+
+
+def gemm_mx_rope(kind, x, w, cos, sin, T, hd, rot_cols):
+    """qkv GEMM on block-scaled operands with RoPE on the first rot_cols columns."""
+    M, N = x.q.shape[0], w.q.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.q.device)
+    ext().gemm(x.q, w.q, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols,
+               **_mx_args(kind, x, w))
     return out
 
 

@@ -19,6 +19,7 @@ import torch
 from llmt.config import ModelConfig
 from llmt.models.llama import build_model
 from llmt.models.native import NativeLlama
+from llmt.ops import native
 from llmt.optim.adamw import FusedAdamW
 
 
@@ -30,6 +31,7 @@ class Trainer:
                  cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False,
                  tp_group=None, init: str = "full", nvtx: bool = False, linear: str = "bf16"):
         self.cfg, self.batch, self.seq = cfg, batch, seq
+        self.linear = linear
         self.nvtx = nvtx  # NVTX ranges forward / backward / optimizer per step (eager steps; reference --nvtx)
         self.device = torch.device(device)
         self.microbatches = microbatches
@@ -99,6 +101,8 @@ class Trainer:
             self.opt.step()
         self._end()
         self.loss.copy_(total / self.microbatches)
+        if self.linear == "nvfp4":
+            native.sr_counter(self.device).add_(1)  # new stochastic-rounding noise every step (graph too)
 
     def _capture(self, warmup=2):
         s = torch.cuda.Stream(device=self.device)

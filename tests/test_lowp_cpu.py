@@ -40,3 +40,44 @@ def test_fp8_linear_fwd_dgrad_wgrad(M, N, K):
     assert rel_err(y, xr.detach() @ wr.detach().t()) < 0.06
     assert rel_err(x.grad, xr.grad) < 0.06
     assert rel_err(w.grad, wr.grad) < 0.06
+
+
+def test_mxfp8_oracle_scales_and_error():
+    from llmt.ops.lowp_ref import mxfp8_dequant, mxfp8_quant_ref
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(128, 256, generator=g) * torch.logspace(-3, 3, 256)  # blocks of very different ranges
+    q, s = mxfp8_quant_ref(x)
+    blocks = x.view(128, 8, 32).abs().amax(-1)
+    scale = torch.ldexp(torch.ones_like(blocks), s.long() - 127)
+    # the smallest power of two that keeps each block within the e4m3 range
+    assert bool((blocks <= 448 * scale).all()) and bool((blocks > 224 * scale).all())
+    assert rel_err(mxfp8_dequant(q, s), x) < 0.04
+
+
+def test_nvfp4_oracle_grid_and_stochastic_rounding():
+    from llmt.ops.lowp_ref import FP4_GRID, nvfp4_dequant, nvfp4_quant_ref
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(64, 128, generator=g)
+    p, s8, gs = nvfp4_quant_ref(x)
+    codes = torch.stack([p & 15, p >> 4], -1).flatten(-2)
+    assert int(codes.max()) <= 15 and p.shape == (64, 64)
+    d = nvfp4_dequant(p, s8, gs)
+    assert rel_err(d, x) < 0.12  # reference round-trip bound (kernels/test_lowp.py:43-47)
+    mags = (d.view(64, 8, 16).abs() / (s8.float() * gs)[..., None]).flatten()
+    grid = torch.tensor(FP4_GRID)
+    assert bool(((mags[:, None] - grid).abs().min(-1).values < 1e-5).all())  # on the e2m1 grid
+    acc = torch.zeros_like(x)
+    n = 400
+    for _ in range(n):
+        pp, ss, gg = nvfp4_quant_ref(x, torch.rand(64, 128, generator=g))
+        acc += nvfp4_dequant(pp, ss, gg)
+    assert rel_err(acc / n, x) < 0.02  # unbiased within 2% over 400 draws (test_lowp.py:53-59)
+
+
+def test_chunked_scale_layout():
+    from llmt.ops.lowp_ref import to_chunks
+    sf = torch.arange(256 * 8, dtype=torch.int64).remainder(251).to(torch.uint8).view(256, 8)
+    out = to_chunks(sf, 2, 256)
+    assert out.numel() == 2 * 2 * 512
+    r, c = 37, 5  # tile 0, chunk 1, row 37 -> (37 % 32) * 16 + 1 * 4, scale 5 % 4
+    assert out[(0 * 2 + 1) * 512 + 5 * 16 + 1 * 4 + 1] == sf[r, c]
