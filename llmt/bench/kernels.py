@@ -6,7 +6,7 @@ GEMMs and attention report TFLOP/s and the fraction of the measured bf16 peak; m
 ops report GB/s of algorithmic traffic and the fraction of the measured HBM copy bandwidth
 (MEASURED_PEAKS.json). The PyTorch/cuBLAS/SDPA equivalent of each op runs alongside.
 
-    python -m llmt.bench.kernels --size medium --batch 4 --seq 1024 [--ops gemm,attn,norm,adamw]
+    python -m llmt.bench.kernels --size medium --batch 4 --seq 1024 [--ops gemm,fused,attn,mem,lowp]
 """
 from __future__ import annotations
 
@@ -199,6 +199,56 @@ def bench_memory_ops(cfg, tokens, rows):
     _bw_row(rows, "adamw (+bf16 copy)", f"{n}", ms, time_ms(opt.step), n * (16 + 12 + 2))
 
 
+def bench_lowp(cfg, tokens, rows, reps=10):
+    """The low-precision block-linear GEMMs (all K-major: fwd, dgrad on W^T, wgrad on the
+    transposed activations) per format, and the quantizers (row-wise + transposed copies).
+    fp8 is compared with cuBLAS (torch._scaled_mm, tensorwise scales); the fraction is of twice
+    the measured bf16 peak (the tensor core's 8-bit rate)."""
+    from llmt.ops import native as N
+    peak, hbm = peaks()
+    d, f, qo = cfg.d, cfg.ffn, cfg.qkv_out
+    shapes = [("qkv fwd", tokens, qo, d), ("qkv dgrad", tokens, d, qo), ("qkv wgrad", qo, d, tokens),
+              ("w13 fwd", tokens, 2 * f, d), ("w13 dgrad", tokens, d, 2 * f), ("w2 fwd", tokens, d, f),
+              ("w2 wgrad", d, f, tokens)]
+    for fmt in ("fp8", "mxfp8", "nvfp4"):
+        for name, M, Nn, K in shapes:
+            a = torch.randn(M, K, device="cuda").bfloat16()
+            b = (torch.randn(Nn, K, device="cuda") * 0.05).bfloat16()
+            out = torch.empty(M, Nn, device="cuda", dtype=torch.float32 if "wgrad" in name else torch.bfloat16)
+            ref = None
+            if fmt == "fp8":
+                aq, _, sa = N.fp8_quant(a, transpose=False)
+                bq, _, sb = N.fp8_quant(b, transpose=False)
+                ours = time_ms(lambda: N.gemm_fp8(aq, bq, sa, sb, out=out), reps=reps)
+                try:
+                    ref = time_ms(lambda: torch._scaled_mm(aq, bq.t(), scale_a=sa.reshape(()), scale_b=sb.reshape(()),
+                                                           out_dtype=torch.bfloat16), reps=reps)
+                except Exception:  # noqa: BLE001 - cuBLAS fp8 may be unavailable for a shape
+                    ref = None
+            else:
+                kind = N.MXFP8 if fmt == "mxfp8" else N.NVFP4
+                ar, _ = N.mx_quant(a, kind)
+                br, _ = N.mx_quant(b, kind)
+                ours = time_ms(lambda: N.gemm_mx(kind, ar, br, out=out), reps=reps)
+            fl = 2.0 * M * Nn * K
+            rows.append(dict(op=f"{fmt} {name}", shape=f"{M}x{Nn}x{K}", ms=round(ours, 4),
+                             ref_ms=round(ref, 4) if ref else None, tflops=round(fl / ours / 1e9, 1),
+                             ref_tflops=round(fl / ref / 1e9, 1) if ref else 0.0,
+                             frac_peak=round(fl / ours / 1e9 / (2 * peak), 3)))
+    for fmt in ("fp8", "mxfp8", "nvfp4"):
+        for name, R, C in (("x", tokens, d), ("h", tokens, f), ("dgu", tokens, 2 * f)):
+            x = torch.randn(R, C, device="cuda").bfloat16()
+            if fmt == "fp8":
+                fn = lambda: N.fp8_quant(x)  # noqa: E731
+            else:
+                kind = N.MXFP8 if fmt == "mxfp8" else N.NVFP4
+                fn = lambda: N.mx_quant(x, kind, row=True, col=True, stochastic=kind == N.NVFP4)  # noqa: E731
+            ms = time_ms(fn, reps=reps)
+            per = 0.5 if fmt == "nvfp4" else 1.0
+            nbytes = R * C * 2 + 2 * R * C * per  # read bf16, write two 8-bit (4-bit) copies
+            _bw_row(rows, f"quant {fmt} {name}", f"{R}x{C}", ms, None, nbytes)
+
+
 def sweep_gemm(cfg, tokens, names):
     """Tile width x split-K sweep for the named GEMM shapes (wgrad shapes accumulate in fp32)."""
     from llmt.ops import native as N
@@ -242,6 +292,8 @@ def main():
         bench_attn(cfg, args.batch, args.seq, rows)
     if "mem" in ops:
         bench_memory_ops(cfg, args.batch * args.seq, rows)
+    if "lowp" in ops:
+        bench_lowp(cfg, args.batch * args.seq, rows, args.reps)
     for r in rows:
         extra = (f"{r['tflops']:7.1f} TF/s (ref {r['ref_tflops']:7.1f}) {100 * r['frac_peak']:5.1f}% of peak"
                  if "tflops" in r else f"{r['gbs']:7.1f} GB/s {100 * r['frac_hbm']:5.1f}% of HBM")

@@ -128,6 +128,9 @@ def main():
     p.add_argument("--json", default=None)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile", help="reference ladder row for --impl reference")
+    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"])
+    p.add_argument("--once", action="store_true",
+                   help="run one warm-up step and one step, then exit (a short program for ncu launch lists)")
     args = p.parse_args()
     if args.impl == "reference":
         step = reference_step(args.size, args.batch, args.seq, args.ref_row)
@@ -136,10 +139,16 @@ def main():
         from llmt.models.llama import make_batch
         from llmt.train import Trainer
         cfg = get_config(args.size)
-        tr = Trainer(cfg, args.batch, args.seq, cuda_graph=args.graph)
+        tr = Trainer(cfg, args.batch, args.seq, cuda_graph=args.graph, linear=args.linear)
         idx, tgt = make_batch(args.batch, args.seq, cfg.vocab, "cuda")
         tr.set_batch(idx, tgt)
         step = tr.run_step
+    if args.once:
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        print("two steps done")
+        return
     ms = clean_ms(step)
     res = profile_step(step, args.prof_steps, args.top)
     res["clean_ms_per_step"] = ms
