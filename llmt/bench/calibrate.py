@@ -2,7 +2,7 @@
 
 Measures, with CUDA events after warm-up: dense matmul throughput per precision at 8192^3
 (torch/cuBLAS for fp32, tf32, fp16, bf16; torch._scaled_mm for fp8 e4m3; this framework's
-tcgen05 GEMM for bf16), a 1 GiB device copy (HBM bandwidth, read + write bytes), an L2-resident
+tcgen05 GEMMs for bf16, fp8, MXFP8 and NVFP4), a 1 GiB device copy (HBM bandwidth, read + write bytes), an L2-resident
 copy, the CPU launch cost of an eager kernel and the GPU gap between kernels replayed from a
 CUDA graph. Under torchrun with 2+ ranks it adds NVLink probes: a peer copy between rank 0 and
 rank 1 and the NCCL all-reduce bus bandwidth at 1 GiB. Never records the product name.
@@ -68,6 +68,21 @@ def matmul_tflops(precision, n=8192):
             b = torch.randn(n, n, device="cuda").bfloat16()
             out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
             fn = lambda: N.gemm(a, b, out=out)  # noqa: E731
+        elif precision in ("fp8_llmt", "mxfp8_llmt", "nvfp4_llmt"):
+            # this framework's 8-bit / 4-bit tcgen05 GEMMs (operands quantized once, outside the timing)
+            from llmt.ops import native as N
+            a = torch.randn(n, n, device="cuda").bfloat16()
+            b = torch.randn(n, n, device="cuda").bfloat16()
+            out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
+            if precision == "fp8_llmt":
+                aq, _, sa = N.fp8_quant(a, transpose=False)
+                bq, _, sb = N.fp8_quant(b, transpose=False)
+                fn = lambda: N.gemm_fp8(aq, bq, sa, sb, out=out)  # noqa: E731
+            else:
+                kind = N.MXFP8 if precision == "mxfp8_llmt" else N.NVFP4
+                ar, _ = N.mx_quant(a, kind)
+                br, _ = N.mx_quant(b, kind)
+                fn = lambda: N.gemm_mx(kind, ar, br, out=out)  # noqa: E731
         else:
             raise ValueError(precision)
         sec = _time(fn)
@@ -104,7 +119,8 @@ def launch_us():
 
 def calibrate(label):
     info = env_info(label)
-    mm = {p: matmul_tflops(p) for p in ("fp32", "tf32", "fp16", "bf16", "fp8", "bf16_llmt")}
+    mm = {p: matmul_tflops(p) for p in ("fp32", "tf32", "fp16", "bf16", "fp8", "bf16_llmt", "fp8_llmt", "mxfp8_llmt",
+                                        "nvfp4_llmt")}
     return {**info, "time": time.strftime("%Y-%m-%d %H:%M:%S"), "matmul": mm, "hbm_gbs": copy_gbs(),
             "l2_copy_gbs": copy_gbs(16 << 20), "launch_overhead_us": launch_us(), "gpu_gap_us": graph_gap_us()}
 

@@ -25,9 +25,14 @@ ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 
 
 def native_rows():
+    """Native rows: bf16 (graph, eager, recompute) and the low-precision block linears that match
+    the reference's rows 8 (fp8) and 9 (NVFP4), plus MXFP8."""
     return [("N1 native bf16 (graph)", dict(cuda_graph=True, ckpt=False)),
             ("N2 native bf16 (eager launches)", dict(cuda_graph=False, ckpt=False)),
-            ("N3 native bf16 + per-block recompute", dict(cuda_graph=True, ckpt=True))]
+            ("N3 native bf16 + per-block recompute", dict(cuda_graph=True, ckpt=True)),
+            ("N4 native + fp8 linears (e4m3 tensorwise)", dict(cuda_graph=True, ckpt=False, linear="fp8")),
+            ("N5 native + MXFP8 linears (e4m3, ue8m0 / 32)", dict(cuda_graph=True, ckpt=False, linear="mxfp8")),
+            ("N6 native + NVFP4 linears (e2m1, ue4m3 / 16)", dict(cuda_graph=True, ckpt=False, linear="nvfp4"))]
 
 
 def run_native(size, B, T, opts, warmup, steps):
@@ -38,7 +43,8 @@ def run_native(size, B, T, opts, warmup, steps):
     row = {"name": None, "status": "ok"}
     try:
         torch.cuda.reset_peak_memory_stats()
-        tr = Trainer(cfg, B, T, cuda_graph=opts["cuda_graph"], ckpt=opts.get("ckpt", False))
+        tr = Trainer(cfg, B, T, cuda_graph=opts["cuda_graph"], ckpt=opts.get("ckpt", False),
+                     linear=opts.get("linear", "bf16"))
         idx, tgt = make_batch(B, T, cfg.vocab, "cuda")
         tr.set_batch(idx, tgt)
         for _ in range(warmup):

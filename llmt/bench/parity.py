@@ -33,10 +33,10 @@ def torch_losses(cfg, B, T, steps, bf16):
     return out
 
 
-def native_losses(cfg, B, T, steps, graph):
+def native_losses(cfg, B, T, steps, graph, linear="bf16"):
     from llmt.models.llama import make_batch
     from llmt.train import Trainer
-    tr = Trainer(cfg, B, T, cuda_graph=graph)
+    tr = Trainer(cfg, B, T, cuda_graph=graph, linear=linear)
     idx, tgt = make_batch(B, T, cfg.vocab, "cpu")
     out = []
     if graph:  # the first call runs two eager warm-up steps before capturing: their losses are lost
@@ -55,7 +55,9 @@ def main():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--seq", type=int, default=1024)
     p.add_argument("--steps", type=int, default=100)
-    p.add_argument("--modes", default="torch-fp32,torch-bf16,native-eager,native-graph")
+    p.add_argument("--modes", default="torch-fp32,torch-bf16,native-eager,native-graph",
+                   help="also native-fp8, native-mxfp8, native-nvfp4 (low-precision block linears, CUDA graph; "
+                        "the reference's triton+fp8 / triton+fp4 modes)")
     p.add_argument("--tol", type=float, default=0.05, help="max |gap| / initial loss accepted against torch-fp32")
     p.add_argument("--json", default=None)
     args = p.parse_args()
@@ -65,6 +67,8 @@ def main():
     for mode in args.modes.split(","):
         if mode.startswith("torch"):
             runs[mode] = torch_losses(cfg, args.batch, args.seq, args.steps, bf16=mode == "torch-bf16")
+        elif mode in ("native-fp8", "native-mxfp8", "native-nvfp4"):
+            runs[mode] = native_losses(cfg, args.batch, args.seq, args.steps, graph=True, linear=mode.split("-")[1])
         else:
             runs[mode] = native_losses(cfg, args.batch, args.seq, args.steps, graph=mode == "native-graph")
     ref = runs.get("torch-fp32")
