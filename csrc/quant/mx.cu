@@ -165,16 +165,26 @@ __global__ void __launch_bounds__(kThreads) amax_partial_kernel(const T* __restr
                                                                 float* __restrict__ partial) {
   pdl_wait();
   __shared__ float red[kThreads / 32];
-  const int gpr = cols / 16;
+  const int gpr = cols / 16;  // 16-element groups per row
   const int64_t n = (int64_t)rows * gpr;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
   float m = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
-    const int64_t r = i / gpr;
-    const int c = (int)(i - r * gpr) * 16;
-    float v[16];
-    load16(x + r * ld + c, v);
+  if (ld == cols) {  // contiguous: no row / column split (a 64-bit division per group costs more than the load)
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride) {
+      float v[16];
+      load16(x + i * 16, v);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+      for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+    }
+  } else {
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {  // a row per CTA, its groups over the threads
+      for (int i = threadIdx.x; i < gpr; i += kThreads) {
+        float v[16];
+        load16(x + (int64_t)r * ld + i * 16, v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+      }
+    }
   }
   m = block_max(m, red);
   if (threadIdx.x == 0) partial[blockIdx.x] = m;
