@@ -196,22 +196,27 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
   for (int i = threadIdx.x; i < D; i += kThreads) dw_part[(int64_t)blockIdx.x * D + i] = sdw[i];
 }
 
-// dw[j] (+)= sum_p part[p, j], fixed order over p: 32 columns x 8 row groups per CTA.
-__global__ void dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, int D, int accumulate) {
+// dw[j] (+)= sum_p part[p, j] in a fixed order (deterministic): 4 columns x 64 row groups per CTA,
+// each thread summing every 64th partial (a few independent L2 loads), then a fixed shared-memory
+// tree over the 64 groups. D / 4 CTAs keep the whole GPU busy on the ~1 MB of partials.
+constexpr int kRedCols = 4, kRedGroups = 64;
+__global__ void __launch_bounds__(kRedCols * kRedGroups)
+dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, int D, int accumulate) {
   pdl_wait();
-  __shared__ float acc[8][33];
-  const int col = blockIdx.x * 32 + threadIdx.x;
+  __shared__ float acc[kRedGroups][kRedCols + 1];
+  const int col = blockIdx.x * kRedCols + threadIdx.x;
   float a = 0.f;
   if (col < D)
-    for (int p = threadIdx.y; p < P; p += 8) a += part[(int64_t)p * D + col];
+    for (int p = threadIdx.y; p < P; p += kRedGroups) a += part[(int64_t)p * D + col];
   acc[threadIdx.y][threadIdx.x] = a;
   __syncthreads();
-  if (threadIdx.y == 0 && col < D) {
-    float t = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += acc[i][threadIdx.x];
-    dw[col] = accumulate ? dw[col] + t : t;
+  for (int h = kRedGroups / 2; h > 0; h >>= 1) {
+    if (threadIdx.y < h) acc[threadIdx.y][threadIdx.x] += acc[threadIdx.y + h][threadIdx.x];
+    __syncthreads();
   }
+  if (threadIdx.y == 0 && col < D) dw[col] = accumulate ? dw[col] + acc[0][threadIdx.x] : acc[0][threadIdx.x];
+  pdl_trigger();
 }
 
 template <typename F>
@@ -281,7 +286,7 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
   });
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, 32), dim3(32, 8), 0, st, dw_part, dw, grid, D, accumulate);
+  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, kRedCols), dim3(kRedCols, kRedGroups), 0, st, dw_part, dw, grid, D, accumulate);
   return cudaGetLastError();
 }
 
@@ -349,7 +354,7 @@ extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, con
   });
   e = cudaGetLastError();
   if (e != cudaSuccess) return (int)e;
-  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, 32), dim3(32, 8), 0, stream, part, dw, grid, D, accumulate);
+  launch_pdl(dw_reduce_kernel, (unsigned)cdiv(D, kRedCols), dim3(kRedCols, kRedGroups), 0, stream, part, dw, grid, D, accumulate);
   return (int)cudaGetLastError();
 }
 
