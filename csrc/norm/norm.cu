@@ -176,24 +176,27 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
       }
     }
   }
-  // CTA-level reduction of dw over the row groups, through shared memory (D floats).
+  // CTA-level reduction of dw over the row groups: every row group stores its partial row into
+  // shared memory ([RPC][D] floats), one barrier, then each thread sums whole columns over the
+  // row groups in a fixed order.
   extern __shared__ float sdw[];
-  for (int i = threadIdx.x; i < D; i += kThreads) sdw[i] = 0.f;
-  __syncthreads();
-  for (int rg = 0; rg < RPC; ++rg) {
-    if (rgroup == rg) {
 #pragma unroll
-      for (int c = 0; c < kMaxChunks; ++c) {
-        const int e = (c * TPR + t) * 8;
-        if (e < D) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) sdw[e + j] += dwacc[c][j];
-        }
-      }
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int e = (c * TPR + t) * 8;
+    if (e < D) {
+      float4* dst = reinterpret_cast<float4*>(sdw + (int64_t)rgroup * D + e);
+      dst[0] = make_float4(dwacc[c][0], dwacc[c][1], dwacc[c][2], dwacc[c][3]);
+      dst[1] = make_float4(dwacc[c][4], dwacc[c][5], dwacc[c][6], dwacc[c][7]);
     }
-    __syncthreads();
   }
-  for (int i = threadIdx.x; i < D; i += kThreads) dw_part[(int64_t)blockIdx.x * D + i] = sdw[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += kThreads) {
+    float a = 0.f;
+#pragma unroll
+    for (int rg = 0; rg < RPC; ++rg) a += sdw[rg * D + i];
+    dw_part[(int64_t)blockIdx.x * D + i] = a;
+  }
+  pdl_trigger();
 }
 
 // dw[j] (+)= sum_p part[p, j] in a fixed order (deterministic): 4 columns x 64 row groups per CTA,
@@ -256,10 +259,11 @@ int rmsnorm_bwd_partials(int64_t N, int D) {
   int tpr = D <= 1024 ? 32 : D <= 2048 ? 64 : D <= 4096 ? 128 : 256;
   const int rpc = kThreads / tpr;
   static int per_sm = [] {
-    // 2 CTAs per SM measured fastest at 4096 x 1024 (31.8 us vs 35.8 at 4 or 1); override for tuning
+    // 3 CTAs per SM: the register limit at 80 registers x 256 threads (ncu at 2 per SM: 14.6
+    // warps per SM active, long-scoreboard stalls, 24% of DRAM bandwidth); override for tuning
     const char* e = getenv("LLMT_NORM_BWD_CTAS_PER_SM");
-    const int v = e ? atoi(e) : 2;
-    return v > 0 ? v : 2;
+    const int v = e ? atoi(e) : 3;
+    return v > 0 ? v : 3;
   }();
   return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc), (int64_t)per_sm * sm_count()));
 }
@@ -275,10 +279,13 @@ cudaError_t rmsnorm_bwd(const void* dy_bf16, const float* s, const float* w, con
   const bf16* dy = static_cast<const bf16*>(dy_bf16);
   bf16* d16 = static_cast<bf16*>(ds16);
   const int grid = rmsnorm_bwd_partials(N, D);
-  const size_t smem = D * sizeof(float);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
-    auto launch = [&](auto kern) { launch_pdl(kern, grid, kThreads, smem, st, dy, s, w, rstd, ds_in, ds, d16, dw_part, N, D); };
+    // one partial row per row group: (256 / TPR) x D floats <= 32 KB, as TPR grows with D
+    const size_t smem = (size_t)(kThreads / TPR) * D * sizeof(float);
+    auto launch = [&](auto kern) {
+      launch_pdl(kern, grid, kThreads, smem, st, dy, s, w, rstd, ds_in, ds, d16, dw_part, N, D);
+    };
     if (ds_in && d16) launch(rmsnorm_bwd_kernel<TPR, true, true>);
     else if (ds_in) launch(rmsnorm_bwd_kernel<TPR, true, false>);
     else if (d16) launch(rmsnorm_bwd_kernel<TPR, false, true>);
@@ -341,9 +348,9 @@ extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, con
   const int grid = std::max(1, std::min(rmsnorm_bwd_partials(N, D), LLMT_NOALLOC_SCRATCH_FLOATS / D));
   const bf16* dy = static_cast<const bf16*>(dy_bf16);
   bf16* d16 = static_cast<bf16*>(ds16);
-  const size_t smem = D * sizeof(float);
   dispatch_tpr(D, [&](auto tpr) {
     constexpr int TPR = decltype(tpr)::value;
+    const size_t smem = (size_t)(kThreads / TPR) * D * sizeof(float);
     auto launch = [&](auto kern) {
       launch_pdl(kern, grid, kThreads, smem, stream, dy, s, w, rstd, ds_in, ds, d16, part, N, D);
     };
