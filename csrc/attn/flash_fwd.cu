@@ -43,12 +43,6 @@ struct AttnFwdArgs {
 
 __device__ int g_attn_err = 0;
 
-// Byte offset of 16-byte unit `u` (0..15 over 128 bf16 columns) of row r in a K-major
-// 128-row tile stored as two 64-column SW128 chunks of 16 KB.
-__device__ __forceinline__ uint32_t sw128_row_unit(int r, int u) {
-  return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
-}
-
 template <int HD>
 struct FwdSmem {
   static constexpr int STAGES = HD == 64 ? 2 : 1;

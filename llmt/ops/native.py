@@ -311,7 +311,7 @@ def mx_quant(x, kind, row=True, col=False, interleave64=False, stochastic=False)
         g, scratch = buf[:1], buf[4:]
     _SEEDS[0] += 1
     C.mx_quant(kind, x, q, sf, qt, sft, g, scratch, interleave64=interleave64, stochastic=stochastic,
-               seed=_SEEDS[0] * 0x2545F491, seed_dev=sr_counter(dev) if stochastic else None)
+               seed=(_SEEDS[0] * 0x2545F491) & 0x7FFFFFFFFFFFFFFF, seed_dev=sr_counter(dev) if stochastic else None)
     return (BlockQ(q, sf, g) if row else None), (BlockQ(qt, sft, g) if col else None)
 
 
