@@ -39,10 +39,6 @@ def native_losses(cfg, B, T, steps, graph, linear="bf16"):
     tr = Trainer(cfg, B, T, cuda_graph=graph, linear=linear)
     idx, tgt = make_batch(B, T, cfg.vocab, "cpu")
     out = []
-    if graph:  # the first call runs two eager warm-up steps before capturing: their losses are lost
-        tr.train_step(idx, tgt)
-        out = [float("nan"), float("nan"), float(tr.loss.item())]
-        steps -= 3
     for _ in range(steps):
         out.append(tr.train_step(idx, tgt))
     tr.release()

@@ -18,6 +18,7 @@ from __future__ import annotations
 import torch
 
 from llmt.ops import native as N
+from llmt.ops.functions import first_write_zero
 
 
 class QKVAttentionFP8(torch.autograd.Function):
@@ -41,6 +42,7 @@ class QKVAttentionFP8(torch.autograd.Function):
         dqkv = N.flash_attn_bwd(do.contiguous(), qkv, o, lse, cos, sin, B, T, H, KV, hd, causal=True)
         dq, dqt, sd = N.fp8_quant(dqkv)
         dx = N.gemm_fp8(dq, wqt, sd, sw)
+        first_write_zero(ctx.w.main_grad)
         N.gemm_fp8(dqt, xqt, sd, sx, out=ctx.w.main_grad, accumulate=True)
         return dx, None, None, None, None, None, None, None, None
 
@@ -61,6 +63,7 @@ class LinearFP8(torch.autograd.Function):
         xqt, sx, wqt, sw = ctx.saved_tensors
         dq, dqt, sd = N.fp8_quant(dy.contiguous())
         dx = N.gemm_fp8(dq, wqt, sd, sw)
+        first_write_zero(ctx.w.main_grad)
         N.gemm_fp8(dqt, xqt, sd, sx, out=ctx.w.main_grad, accumulate=True)
         return dx, None
 
@@ -86,8 +89,10 @@ class SwiGLUMLPFP8(torch.autograd.Function):
         w1, w2, ffn = ctx.w1, ctx.w2, ctx.ffn
         dmq, dmqt, sd = N.fp8_quant(dm.contiguous())
         dgu = N.gemm_fp8_swiglu_bwd(dmq, w2qt, sd, s2, gu, ffn)
+        first_write_zero(w2.main_grad)
         N.gemm_fp8(dmqt, hqt, sd, sh, out=w2.main_grad, accumulate=True)
         dgq, dgqt, sg = N.fp8_quant(dgu)
         dx = N.gemm_fp8(dgq, w13qt, sg, s13)
+        first_write_zero(w1.w13_grad)
         N.gemm_fp8(dgqt, xqt, sg, sx, out=w1.w13_grad, accumulate=True)
         return dx, None, None, None

@@ -36,6 +36,12 @@ SWIGLU_EPILOGUE = {"fwd": "fwd" in _sw, "bwd": "bwd" in _sw}
 # recomputes the logit GEMM in its backward, which costs more than writing and re-reading bf16
 # logits while they are small, so logits are materialised up to HEAD_LOGITS_BUDGET bytes and
 # never beyond.
+# First-write gradients: while GRAD["first"] is set (the first micro-batch of a step whose
+# optimizer does not clear the gradient buffer) every weight-gradient writer stores instead of
+# adding, so the buffer is never zeroed and the GEMMs never read the old values back from DRAM.
+# A split-K GEMM (its splits add into one output) and the embedding's atomic scatter zero their
+# own region first.
+GRAD = {"first": False}
 _unf = os.environ.get("LLMT_UNFUSE", "")
 FUSION = {"rope": "rope" not in _unf, "head_ce": False if "head_ce" in _unf else "auto"}
 HEAD_LOGITS_BUDGET = 2 << 30
@@ -51,6 +57,7 @@ class Embed(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dx):
         (idx,) = ctx.saved_tensors
+        first_write_zero(ctx.w.main_grad)  # the scatter adds: rows of absent ids must read zero
         N.embedding_bwd(idx, dx.contiguous(), ctx.w.main_grad)
         return None, None
 
@@ -86,7 +93,7 @@ class RMSNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         x, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, _ = N.rmsnorm_bwd(dy.contiguous(), x, w, rstd, None, w.main_grad, True, write_ds16=False)
+        ds, _ = N.rmsnorm_bwd(dy.contiguous(), x, w, rstd, None, w.main_grad, not GRAD["first"], write_ds16=False)
         return ds, None, None
 
 
@@ -104,7 +111,7 @@ class AddRMSNormFn(torch.autograd.Function):
     def backward(ctx, dy, ds_in):
         s, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, ds_in, w.main_grad, True, write_ds16=True)
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, ds_in, w.main_grad, not GRAD["first"], write_ds16=True)
         return ds16, ds, None, None
 
 
@@ -122,13 +129,31 @@ class FinalNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         s, rstd = ctx.saved_tensors
         w = ctx.w
-        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, None, w.main_grad, True, write_ds16=True)
+        ds, ds16 = N.rmsnorm_bwd(dy.contiguous(), s, w, rstd, None, w.main_grad, not GRAD["first"], write_ds16=True)
         return ds16, ds, None, None
+
+
+def wgrad_into(dy, x, out):
+    """out (M, N) fp32 (+)= dy^T x on the tcgen05 GEMM; on a first write it stores (or zeroes
+    first when the planner splits K)."""
+    if GRAD["first"]:
+        _, splits = N.gemm_plan(dy.shape[1], x.shape[1], dy.shape[0], N.EPI_F32, True)
+        if splits == 1:
+            N.gemm(dy, x, ta=True, tb=False, out=out, accumulate=False)
+            return
+        out.zero_()
+    N.gemm(dy, x, ta=True, tb=False, out=out, accumulate=True)
+
+
+def first_write_zero(out):
+    """Zero `out` if this is the step's first write and the caller can only accumulate."""
+    if GRAD["first"]:
+        out.zero_()
 
 
 def _wgrad(dy, x, p):
     """p.main_grad (out, in) (+)= dy^T x, fp32, on the tcgen05 GEMM."""
-    N.gemm(dy, x, ta=True, tb=False, out=p.main_grad, accumulate=True)
+    wgrad_into(dy, x, p.main_grad)
 
 
 class QKVAttention(torch.autograd.Function):
@@ -214,7 +239,7 @@ class SwiGLUMLP(torch.autograd.Function):
             N.swiglu_bwd(dh, g, u, dg=g, du=u)  # [dg | du] overwrite [g | u] in place
             dgu = gu
         dx = N.gemm(dgu, w1.w13_16, ta=False, tb=False)
-        N.gemm(dgu, x, ta=True, tb=False, out=w1.w13_grad, accumulate=True)
+        wgrad_into(dgu, x, w1.w13_grad)
         return dx, None, None, None, None
 
 
@@ -288,7 +313,7 @@ class HeadCE(torch.autograd.Function):
             dl = ctx.saved_tensors[3]
             N.ce_bwd_rows(dl, targets, lse, g, 1.0 / n)
             dh = N.gemm(dl, w.w16, ta=False, tb=False)
-            N.gemm(dl, h, ta=True, tb=False, out=w.main_grad, accumulate=True)
+            wgrad_into(dl, h, w.main_grad)
             return dh, None, None, None
         dh = torch.empty_like(h)
         for c0 in range(0, n, chunk):
@@ -296,5 +321,8 @@ class HeadCE(torch.autograd.Function):
             hc = h[c0:c1]
             dl = N.gemm_ce_bwd(hc, w.w16, targets[c0:c1], lse[c0:c1], g, 1.0 / n)
             N.gemm(dl, w.w16, ta=False, tb=False, out=dh[c0:c1])
-            N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=True)
+            if c0 == 0:
+                wgrad_into(dl, hc, w.main_grad)
+            else:
+                N.gemm(dl, hc, ta=True, tb=False, out=w.main_grad, accumulate=True)
         return dh, None, None, None

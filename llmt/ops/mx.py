@@ -19,6 +19,7 @@ from __future__ import annotations
 import torch
 
 from llmt.ops import native as N
+from llmt.ops.functions import first_write_zero
 
 
 def _sr(kind):
@@ -44,6 +45,7 @@ class QKVAttentionMX(torch.autograd.Function):
         dqkv = N.flash_attn_bwd(do.contiguous(), qkv, o, lse, cos, sin, B, T, H, KV, hd, causal=True)
         dr, dc = N.mx_quant(dqkv, kind, row=True, col=True, stochastic=_sr(kind))
         dx = N.gemm_mx(kind, dr, ctx.wc)
+        first_write_zero(w.main_grad)
         N.gemm_mx(kind, dc, ctx.xc, out=w.main_grad, accumulate=True)
         ctx.xc = ctx.wc = None
         return dx, None, None, None, None, None, None, None, None, None
@@ -62,6 +64,7 @@ class LinearMX(torch.autograd.Function):
         kind, w = ctx.kind, ctx.w
         dr, dc = N.mx_quant(dy.contiguous(), kind, row=True, col=True, stochastic=_sr(kind))
         dx = N.gemm_mx(kind, dr, ctx.wc)
+        first_write_zero(w.main_grad)
         N.gemm_mx(kind, dc, ctx.xc, out=w.main_grad, accumulate=True)
         ctx.xc = ctx.wc = None
         return dx, None, None
@@ -88,9 +91,11 @@ class SwiGLUMLPMX(torch.autograd.Function):
         w1, w2, ffn, kind = ctx.w1, ctx.w2, ctx.ffn, ctx.kind
         dmr, dmc = N.mx_quant(dm.contiguous(), kind, row=True, col=True, stochastic=_sr(kind))
         dgu = N.gemm_mx_swiglu_bwd(kind, dmr, ctx.w2c, gu, ffn)
+        first_write_zero(w2.main_grad)
         N.gemm_mx(kind, dmc, ctx.hc, out=w2.main_grad, accumulate=True)
         dgr, dgc = N.mx_quant(dgu, kind, row=True, col=True, stochastic=_sr(kind))
         dx = N.gemm_mx(kind, dgr, ctx.w13c)
+        first_write_zero(w1.w13_grad)
         N.gemm_mx(kind, dgc, ctx.xc, out=w1.w13_grad, accumulate=True)
         ctx.xc = ctx.hc = ctx.w2c = ctx.w13c = None
         return dx, None, None, None, None

@@ -20,7 +20,7 @@ EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD 
 _KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0, "dp_error_code": 0,
                      "set_reserved_sms": 0, "reserved_sms": 0, "attn_bwd_set_trace": 0,
                      "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "ipc_free": 0, "tensor_from_ptr": 0,
-                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0}
+                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0, "gemm_plan": 0}
 
 
 class LaunchCounter:
@@ -183,6 +183,11 @@ def gemm_ce_bwd(h, w, targets, lse, grad_out, scale, out=None, bn=0):
         out = torch.empty((M, V), dtype=torch.bfloat16, device=h.device)
     ext().gemm(h, w, False, True, EPI_CE_BWD, out, tgt=targets, lse=lse, grad_out=grad_out, alpha=scale, bn=bn)
     return out
+
+
+def gemm_plan(M, N, K, epi, can_split):
+    """(tile width, split-K factor) the GEMM planner picks for a problem (host only)."""
+    return ext().gemm_plan(int(M), int(N), int(K), int(epi), bool(can_split))
 
 
 def gemm_error_code(reset=False) -> int:

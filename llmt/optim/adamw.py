@@ -2,8 +2,9 @@
 
 Same hyper-parameters and update as the reference's torch.optim.AdamW (bench_train.py:467-469:
 lr 3e-4, betas (0.9, 0.95), weight decay 0.1 on every parameter, eps 1e-8). The kernel
-also writes the bf16 shadow weights that the GEMMs read and zeroes the gradient buffer for
-the next step's accumulation. lr and the step count live on the device, so `step()` can be
+also writes the bf16 shadow weights that the GEMMs read and, unless `zero_grad` is off (the
+gradient writers then store on the step's first write), zeroes the gradient buffer for the next
+step's accumulation. lr and the step count live on the device, so `step()` can be
 captured in a CUDA graph and replayed.
 
 State layout: exp_avg / exp_avg_sq flat fp32 buffers; `state_dict()` returns them per
@@ -19,8 +20,9 @@ from llmt.ops import native as N
 
 class FusedAdamW:
     def __init__(self, master, grad, shadow, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
-                 grad_scale=1.0):
+                 grad_scale=1.0, zero_grad=True):
         self.master, self.grad, self.shadow = master, grad, shadow
+        self.zero_grad = zero_grad
         self.exp_avg = torch.zeros_like(master)
         self.exp_avg_sq = torch.zeros_like(master)
         self.lr_t = torch.full((1,), float(lr), dtype=torch.float32, device=master.device)
@@ -38,7 +40,8 @@ class FusedAdamW:
     def step(self):
         self.step_t.add_(1)
         N.adamw_step(self.master, self.grad, self.exp_avg, self.exp_avg_sq, self.shadow, self.lr_t, self.step_t,
-                     self.betas[0], self.betas[1], self.eps, self.weight_decay, self.grad_scale, zero_grad=True)
+                     self.betas[0], self.betas[1], self.eps, self.weight_decay, self.grad_scale,
+                     zero_grad=self.zero_grad)
 
     def state_dict(self, flat=None):
         """torch.optim.AdamW-style state: {'state': {i: {step, exp_avg, exp_avg_sq}}, 'param_groups': [...]}."""

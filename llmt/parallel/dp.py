@@ -56,6 +56,9 @@ class DataParallel:
         """mode: "nccl" (reduce-scatter / all-gather), "fused" (one peer-memory kernel after the
         backward) or "fused-overlap" (that kernel per bucket, overlapped with the backward)."""
         self.world_size, self.rank, self.mode, self.group = world_size, rank, mode, group
+        # False when the model's gradient writers store on the step's first write (the NCCL
+        # step then skips clearing the buffer; the fused kernels clear what they read anyway)
+        self.zero_grads = True
         self.flat = None
         self.fused = None
 
@@ -121,7 +124,8 @@ class DataParallel:
             self.fused.step()
             return
         dist.reduce_scatter_tensor(opt.grad_shard, f.grad, op=dist.ReduceOp.SUM, group=self.group)
-        f.grad.zero_()  # gradients accumulate into the flat buffer
+        if self.zero_grads:
+            f.grad.zero_()  # gradients accumulate into the flat buffer
         opt.step_local()
         dist.all_gather_into_tensor(f.shadow, f.shadow[opt.lo:opt.hi].clone(), group=self.group)
 

@@ -53,8 +53,7 @@ def main():
         ref = Trainer(cfg, B * world, T, device=f"cuda:{local}", cuda_graph=False, microbatches=world)
         idx = torch.cat([b[0] for b in batches])
         tgt = torch.cat([b[1] for b in batches])
-        # a graph trainer runs two eager warm-up steps before its first replay
-        for _ in range(args.steps + (2 if args.graph else 0)):
+        for _ in range(args.steps):
             ref.train_step(idx, tgt)
         rf = ref.net.flat.master
         rel = ((full - rf).norm() / rf.norm()).item()

@@ -61,7 +61,7 @@ class ParallelTrainer:
             self.pipe = Pipeline1F1B(self.x, s, layout.pp, prev, nxt, g.pp_group, self.device)
         self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
         # whole-step CUDA graph (forward, backward, collectives, optimizer) for layouts without a
-        # pipeline: static token buffers, captured after two eager warm-up steps
+        # pipeline: static token buffers, captured after two eager warm-up steps that are undone
         self.use_graph = cuda_graph and impl == "native" and layout.pp == 1
         self.graph = None
         if self.use_graph:
@@ -118,6 +118,11 @@ class ParallelTrainer:
         self.idx_buf.copy_(idx, non_blocking=True)
         self.tgt_buf.copy_(tgt, non_blocking=True)
         if self.graph is None:
+            # two eager warm-up steps and the capture, then the weights and the optimizer state go
+            # back as they were: the first call is one step like every other
+            flat = self.x.flat
+            state = [flat.master, flat.shadow] + [v for v in vars(self.opt).values() if isinstance(v, torch.Tensor)]
+            saved = [t.detach().to("cpu", copy=True) for t in state]
             s = torch.cuda.Stream(device=self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):
@@ -127,6 +132,9 @@ class ParallelTrainer:
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph):
                 self._body(self.idx_buf, self.tgt_buf)
+            with torch.no_grad():
+                for t, c in zip(state, saved):
+                    t.copy_(c)  # in place: the graph holds these buffers
         self.graph.replay()
 
     def train_step(self, idx, tgt) -> float:

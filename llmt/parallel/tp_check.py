@@ -52,9 +52,7 @@ def main():
     if rank == 0:
         full = unshard_state(gathered, cfg)
         ref = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=False)
-        # a graph trainer runs two eager warm-up steps before its first replay
-        extra = 2 if args.graph else 0
-        ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps + extra)][extra:]
+        ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps)]
         rsd = ref.model.state_dict()
         num = sum(float((full[k].to(rsd[k].device) - rsd[k].float()).norm() ** 2) for k in rsd)
         den = sum(float(rsd[k].float().norm() ** 2) for k in rsd)

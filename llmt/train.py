@@ -19,6 +19,7 @@ import torch
 from llmt.config import ModelConfig
 from llmt.models.llama import build_model
 from llmt.models.native import NativeLlama
+from llmt.ops import functions as Fn
 from llmt.ops import native
 from llmt.optim.adamw import FusedAdamW
 
@@ -56,10 +57,15 @@ class Trainer:
                     raise ValueError("the overlapped data-parallel step needs ckpt=False")
                 self.net.grad_ready = dp.bucket_ready
         flat = self.net.flat
+        # First-write gradients (llmt.ops.functions.GRAD): the first micro-batch's backward stores
+        # every weight gradient, so nothing clears the 4-byte-per-parameter buffer between steps.
+        # Off for the tensor-parallel model, whose collectives' writers always accumulate.
+        self.first_write = tp_group is None
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
+            dp.zero_grads = not self.first_write
         else:
-            self.opt = FusedAdamW(flat.master, flat.grad, flat.shadow, lr=lr)
+            self.opt = FusedAdamW(flat.master, flat.grad, flat.shadow, lr=lr, zero_grad=not self.first_write)
         mb = batch // microbatches
         if mb * microbatches != batch:
             raise ValueError("batch must be a multiple of microbatches")
@@ -89,7 +95,11 @@ class Trainer:
             self._range("backward")
             if self.dp is not None and i == self.microbatches - 1:
                 self.dp.begin_step()  # the last micro-batch's backward releases the buckets
-            (loss / self.microbatches).backward()
+            Fn.GRAD["first"] = self.first_write and i == 0
+            try:
+                (loss / self.microbatches).backward()
+            finally:
+                Fn.GRAD["first"] = False
             self._end()
             total = loss.detach() if total is None else total + loss.detach()
         self._range("optimizer")
@@ -104,7 +114,24 @@ class Trainer:
         if self.linear == "nvfp4":
             native.sr_counter(self.device).add_(1)  # new stochastic-rounding noise every step (graph too)
 
+    def _state_tensors(self):
+        """The tensors one step changes: weights (fp32 master, bf16 shadow) and the optimizer's
+        state (moments, step count). Communication state (barrier epochs) is not included: the
+        peers track it."""
+        flat = self.net.flat
+        ts = [flat.master, flat.shadow]
+        ts += [v for v in vars(self.opt).values() if isinstance(v, torch.Tensor)]
+        return ts
+
     def _capture(self, warmup=2):
+        """Warm up (allocator, tensor maps, NCCL communicators) with `warmup` eager steps, capture
+        one step, then put the weights and the optimizer state back as they were, so the first
+        train_step is one step like every other."""
+        state = self._state_tensors()
+        need = sum(t.numel() * t.element_size() for t in state)
+        free, _ = torch.cuda.mem_get_info(self.device)
+        where = self.device if free > 2 * need + (4 << 30) else torch.device("cpu")
+        saved = [t.detach().to(where, copy=True) for t in state]
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -115,6 +142,10 @@ class Trainer:
         with torch.cuda.graph(g):
             self._body()
         self.graph = g
+        with torch.no_grad():
+            for t, c in zip(state, saved):
+                t.copy_(c)  # in place: the graph holds these buffers
+        del saved
 
     def set_batch(self, idx, tgt):
         """Copy one step's tokens (B, T) into the static device buffers (async from pinned memory)."""
