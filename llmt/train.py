@@ -30,7 +30,8 @@ class Trainer:
 
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, device="cuda", seed: int = 0, lr: float = 3e-4,
                  cuda_graph: bool = True, microbatches: int = 1, dp=None, ce_chunk: int = 8192, ckpt: bool = False,
-                 tp_group=None, init: str = "full", nvtx: bool = False, linear: str = "bf16"):
+                 tp_group=None, init: str = "full", nvtx: bool = False, linear: str = "bf16",
+                 first_write: bool = True):
         self.cfg, self.batch, self.seq = cfg, batch, seq
         self.linear = linear
         self.nvtx = nvtx  # NVTX ranges forward / backward / optimizer per step (eager steps; reference --nvtx)
@@ -60,7 +61,7 @@ class Trainer:
         # First-write gradients (llmt.ops.functions.GRAD): the first micro-batch's backward stores
         # every weight gradient, so nothing clears the 4-byte-per-parameter buffer between steps.
         # Off for the tensor-parallel model, whose collectives' writers always accumulate.
-        self.first_write = tp_group is None
+        self.first_write = first_write and tp_group is None
         if dp is not None:
             self.opt = dp.make_optimizer(flat, lr=lr)
             dp.zero_grads = not self.first_write
