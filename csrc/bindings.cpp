@@ -534,6 +534,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_amax_slots", &llmt::fp8_amax_slots);
   m.def("fp8_quant", &fp8_quant, "x"_a, "q"_a, "qt"_a, "inv"_a, "scratch"_a);
   m.def("gemm_error_code", &llmt::gemm_error_code, "reset"_a = false);
+  m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K, int64_t epi, bool can_split) {
+    int bn = 0, splits = 1;
+    llmt::gemm_plan((int)M, (int)N, (int)K, (int)epi, can_split, &bn, &splits);
+    return std::make_tuple(bn, splits);
+  });
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("attn_error_code", &llmt::attn_error_code, "reset"_a = false);
