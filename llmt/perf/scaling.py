@@ -18,6 +18,7 @@ Per layout (dp, tp, pp, micro-batch mb; m = G / (dp * mb) micro-batches):
             dp, activations in flight; must fit 90% of the GPU
 
     python -m llmt.perf.scaling --models medium,llama3-8b --gpus 8,64,1024 --system b200_nvl8_ib
+    python -m llmt.perf.scaling --fit <single-stage runs> --holdout <pipelined runs> --json out.json
 """
 from __future__ import annotations
 
@@ -97,7 +98,9 @@ class StageCompute:
 
 
 def evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp: StageCompute, links, system, ckpt=False, fused_tp=True,
-             overlap_dp=True, overlap_pp=True):
+             overlap_dp=True, overlap_pp=True, compute_scale=1.0, comm_scale=1.0):
+    """compute_scale multiplies the roofline compute of a micro-batch (and so the pipeline
+    bubble); comm_scale the tensor-parallel collective time (both fitted by `calibrate`)."""
     if dp * tp * pp != n or G % (dp * mb) or cfg.L % pp or cfg.H % tp or cfg.kvh % tp:
         return None
     m = G // (dp * mb)
@@ -117,10 +120,11 @@ def evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp: StageCompute, links, system, 
     if mem > 0.9 * sysd["gpu_memory_gb"] * 1e9:
         return None
     t_mb, t_mb_bwd = comp.get(tp, mb, ckpt)
+    t_mb, t_mb_bwd = t_mb * compute_scale, t_mb_bwd * compute_scale
     t_stage, t_stage_bwd = t_mb / pp, t_mb_bwd / pp
     act_bytes = mb * seq * cfg.d * 2
     tp_link = intra
-    t_tp_raw = 8 * (cfg.L / pp) * reduce_scatter_s(act_bytes, tp, tp_link) if tp > 1 else 0.0
+    t_tp_raw = comm_scale * 8 * (cfg.L / pp) * reduce_scatter_s(act_bytes, tp, tp_link) if tp > 1 else 0.0
     t_tp = max(0.0, t_tp_raw - 0.8 * t_stage) if fused_tp else t_tp_raw
     pp_link = intra if tp * pp <= g else inter
     t_send = p2p_s(act_bytes, pp_link) if pp > 1 else 0.0
@@ -138,6 +142,92 @@ def evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp: StageCompute, links, system, 
             "breakdown_s": {"compute": m * t_stage, "pipeline bubble": (pp - 1) * t_stage, "tp comm (exposed)": slots * t_tp,
                             "pp sends": (2 * t_send * pp if overlap_pp else slots * 2 * t_send),
                             "dp comm (exposed)": t_dp - hidden, "optimizer": t_opt}}
+
+
+# ---------------------------------------------------------------- calibration against real runs
+# The runs here are the bench JSON lines of llmt.bench.parallel_bench (results/par_*.json). Their
+# collectives ran on NCCL, which the step neither fuses into the GEMMs nor overlaps with the
+# backward, so they are modeled exposed (fused_tp=False, overlap_dp=False).
+RUN_KW = dict(fused_tp=False, overlap_dp=False)
+
+
+def run_layout(run):
+    """(dp, tp, pp, micro-batch size, global batch) of a parallel-bench result."""
+    kv = {p[:2]: int(p[2:]) for p in run["layout"].split()}
+    G, m = run["global_batch"], run["microbatches"]
+    return kv["dp"], kv["tp"], kv["pp"], G // (kv["dp"] * m), G
+
+
+def _terms(run, comp, links, system):
+    cfg, seq = comp.cfg, comp.seq
+    dp, tp, pp, mb, G = run_layout(run)
+    r = evaluate(cfg, seq, G, dp * tp * pp, dp, tp, pp, mb, comp, links, system, **RUN_KW)
+    b = r["breakdown_s"]
+    scaled_c = b["compute"] + b["pipeline bubble"]
+    scaled_t = b["tp comm (exposed)"]
+    fixed = b["pp sends"] + b["dp comm (exposed)"] + b["optimizer"]
+    return scaled_c, scaled_t, fixed
+
+
+def calibrate(fit_runs, comp, links, system):
+    """Least-squares (compute_scale, comm_scale) so that measured = a * compute + c * tp comm +
+    the unscaled terms (pipeline sends, data-parallel collectives, optimizer) on `fit_runs`."""
+    rows, rhs = [], []
+    for run in fit_runs:
+        c, t, fixed = _terms(run, comp, links, system)
+        rows.append((c, t))
+        rhs.append(run["ms_per_step"] / 1e3 - fixed)
+    # normal equations of the 2-parameter fit (no numpy needed)
+    saa = sum(c * c for c, _ in rows)
+    sab = sum(c * t for c, t in rows)
+    sbb = sum(t * t for _, t in rows)
+    sya = sum(c * y for (c, _), y in zip(rows, rhs))
+    syb = sum(t * y for (_, t), y in zip(rows, rhs))
+    det = saa * sbb - sab * sab
+    if abs(det) < 1e-30:  # no tensor-parallel run: fit the compute scale alone
+        return sya / saa, 1.0
+    return (sya * sbb - syb * sab) / det, (syb * saa - sya * sab) / det
+
+
+def predict_run(run, comp, links, system, compute_scale=1.0, comm_scale=1.0):
+    dp, tp, pp, mb, G = run_layout(run)
+    r = evaluate(comp.cfg, comp.seq, G, dp * tp * pp, dp, tp, pp, mb, comp, links, system,
+                 compute_scale=compute_scale, comm_scale=comm_scale, **RUN_KW)
+    return r["step_s"] * 1e3
+
+
+def validate(fit_paths, holdout_paths, machine, links, system="b200_nvl8_ib", shape_times=None):
+    """Fit the two scales on `fit_paths` (single-stage runs) and report the error of every run,
+    the held-out ones (pipelined / hybrid layouts) separately."""
+    def load(ps):
+        out = []
+        for p in ps:
+            with open(p) as f:
+                d = json.load(f)
+            d["path"] = p
+            out.append(d)
+        return out
+    fit, hold = load(fit_paths), load(holdout_paths)
+    model = {r["model"] for r in fit + hold}
+    if len(model) != 1:
+        raise ValueError(f"one model per validation, got {sorted(model)}")
+    run0 = (fit + hold)[0]
+    comp = StageCompute(SIZES[run0["model"]], run0["seq"], machine, shape_times)
+    a, c = calibrate(fit, comp, links, system)
+    res = {"model": run0["model"], "seq": run0["seq"], "system": system, "compute_scale": a, "comm_scale": c,
+           "fit": [], "holdout": []}
+    for key, runs in (("fit", fit), ("holdout", hold)):
+        for r in runs:
+            raw = predict_run(r, comp, links, system)
+            cal = predict_run(r, comp, links, system, a, c)
+            res[key].append({"run": os.path.basename(r["path"]), "layout": r["layout"],
+                             "microbatches": r["microbatches"], "global_batch": r["global_batch"],
+                             "measured_ms": r["ms_per_step"], "roofline_ms": round(raw, 2),
+                             "calibrated_ms": round(cal, 2), "error": round(cal / r["ms_per_step"] - 1, 4)})
+    for key in ("fit", "holdout"):
+        errs = [abs(x["error"]) for x in res[key]]
+        res[f"{key}_mae"] = round(sum(errs) / len(errs), 4) if errs else None
+    return res
 
 
 def divisors(x, cap):
@@ -181,10 +271,28 @@ def main():
     ap.add_argument("--layout", default=None, help="evaluate one layout, e.g. 'dp2,tp2,pp2,mb1' (needs one --gpus)")
     ap.add_argument("--global-batch", type=int, default=None)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--fit", default=None,
+                    help="comma list of single-stage parallel-bench results (results/par_*.json) to fit the "
+                         "compute and tensor-parallel scales on")
+    ap.add_argument("--holdout", default="", help="comma list of results predicted with the fitted scales")
     args = ap.parse_args()
     links = load_links(args.links)
     m = Machine.from_peaks()
     st = load_shape_times(args.shape_times)
+    if args.fit:
+        res = validate(args.fit.split(","), [p for p in args.holdout.split(",") if p], m, links, args.system, st)
+        print(f"{res['model']}: compute x{res['compute_scale']:.3f} of the roofline, tensor-parallel collectives "
+              f"x{res['comm_scale']:.3f} of the ring model")
+        for key in ("fit", "holdout"):
+            for x in res[key]:
+                print(f"  {key:8s} {x['layout']:12s} m{x['microbatches']:<2d} measured {x['measured_ms']:8.1f} ms  "
+                      f"roofline {x['roofline_ms']:8.1f}  calibrated {x['calibrated_ms']:8.1f}  "
+                      f"error {100 * x['error']:+6.1f}%")
+            print(f"  {key} mean absolute error {100 * res[key + '_mae']:.1f}%" if res[key + "_mae"] is not None else "")
+        if args.json:
+            with open(args.json, "w") as f:
+                json.dump(res, f, indent=1)
+        return
     res = []
     for name in args.models.split(","):
         size, seq, G = WORKLOADS[name]
