@@ -19,6 +19,7 @@ Per layout (dp, tp, pp, micro-batch mb; m = G / (dp * mb) micro-batches):
 
     python -m llmt.perf.scaling --models medium,llama3-8b --gpus 8,64,1024 --system b200_nvl8_ib
     python -m llmt.perf.scaling --fit <single-stage runs> --holdout <pipelined runs> --json out.json
+    python -m llmt.perf.scaling --models llama3-8b --gpus 8,64 --calibration out.json
 """
 from __future__ import annotations
 
@@ -275,6 +276,9 @@ def main():
                     help="comma list of single-stage parallel-bench results (results/par_*.json) to fit the "
                          "compute and tensor-parallel scales on")
     ap.add_argument("--holdout", default="", help="comma list of results predicted with the fitted scales")
+    ap.add_argument("--calibration", default=None,
+                    help="a --fit result (JSON): search / evaluate layouts with its compute and "
+                         "tensor-parallel scales and NCCL's exposed collectives")
     args = ap.parse_args()
     links = load_links(args.links)
     m = Machine.from_peaks()
@@ -293,6 +297,11 @@ def main():
             with open(args.json, "w") as f:
                 json.dump(res, f, indent=1)
         return
+    kw = {}
+    if args.calibration:
+        with open(args.calibration) as f:
+            cal = json.load(f)
+        kw = dict(RUN_KW, compute_scale=cal["compute_scale"], comm_scale=cal["comm_scale"])
     res = []
     for name in args.models.split(","):
         size, seq, G = WORKLOADS[name]
@@ -302,10 +311,10 @@ def main():
         for n in (int(x) for x in args.gpus.split(",")):
             if args.layout:
                 kv = dict((p[:2], int(p[2:])) for p in args.layout.split(","))
-                r = evaluate(cfg, seq, G, n, kv["dp"], kv["tp"], kv["pp"], kv["mb"], comp, links, args.system)
+                r = evaluate(cfg, seq, G, n, kv["dp"], kv["tp"], kv["pp"], kv["mb"], comp, links, args.system, **kw)
                 rows = [r] if r else []
             else:
-                rows = all_layouts(cfg, seq, G, n, comp, links, args.system)[: args.show_top]
+                rows = all_layouts(cfg, seq, G, n, comp, links, args.system, **kw)[: args.show_top]
             for r in rows:
                 print(f"{name:10s} {n:5d} GPUs  {layout_str(r):22s} {r['step_s'] * 1e3:9.2f} ms "
                       f"{r['tokens_per_s'] / 1e6:8.3f} M tok/s  MFU {100 * r['mfu']:5.1f}%  mem {r['mem_gb']:.1f} GB")

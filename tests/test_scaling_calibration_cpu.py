@@ -20,3 +20,17 @@ def test_calibrated_scaling_model_predicts_held_out_layouts():
         assert abs(x["error"]) < 0.08, x
     # the uncalibrated roofline is far off on the same runs
     assert all(x["roofline_ms"] < 0.8 * x["measured_ms"] for x in res["holdout"])
+
+
+def test_search_with_calibration_matches_validation():
+    """The layout search / evaluation with the fitted scales gives the validated prediction."""
+    from llmt.config import SIZES
+    from llmt.perf.scaling import RUN_KW, StageCompute, evaluate
+    fit = [str(R / f) for f in ("par_8b_tp2_nccl.json", "par_8b_tp4.json", "par_8b_tp8_nccl.json")]
+    hold = [str(R / "par_8b_dp2tp2pp2.json")]
+    m, links = Machine.from_peaks(), load_links()
+    res = validate(fit, hold, m, links)
+    comp = StageCompute(SIZES["llama3-8b"], 4096, m)
+    r = evaluate(SIZES["llama3-8b"], 4096, 16, 8, 2, 2, 2, 2, comp, links, "b200_nvl8_ib",
+                 compute_scale=res["compute_scale"], comm_scale=res["comm_scale"], **RUN_KW)
+    assert abs(r["step_s"] * 1e3 - res["holdout"][0]["calibrated_ms"]) < 0.01
