@@ -143,8 +143,6 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
                            const float* cos_t, const float* sin_t, void* dqkv, float* dsum, float* dq_acc, int B,
                            int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st);
 int attn_error_code(bool reset);
-// Event trace of the hd-64 attention backward: 1024 int64 on the device, or nullptr (off).
-void attn_bwd_set_trace(long long* buf);
 
 // ---------------------------------------------------------------- tensor-parallel row collectives
 // Over NVLink peer memory (CUDA IPC mappings of every rank's buffers). `dst` / `slots` are

@@ -44,15 +44,7 @@ struct AttnBwdArgs {
   float scale, scale_log2;
   int causal;
   int* err;
-  long long* trace;  // optional event log of CTA (0, 0): 4 regions of 256 (clock64 << 8 | event id)
 };
-
-// Timestamped event of CTA (0, 0) into slot `region` of the trace (plain stores, no atomics).
-__device__ __forceinline__ void trace_at(long long* tr, int region, int& k, int id) {
-  if (tr == nullptr || blockIdx.x != 0 || blockIdx.y != 0) return;
-  if (k < 255) tr[region * 256 + k] = (clock64() << 8) | id;
-  ++k;
-}
 
 __device__ __forceinline__ uint32_t sw_unit(int r, int u) {
   return (uint32_t)((u >> 3) * 16384 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
@@ -425,7 +417,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
   const int n_tiles = n_bk * nqb;
   const int G = gridDim.x;
   int* err = a.err;
-  int tk = 0;  // trace slot of this thread
 
   if (threadIdx.x == 0) {
     bar_init(kv_full, 1);
@@ -470,7 +461,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 
   if (warp == 0) {
     if (lane == 0) {
-      trace_at(a.trace, 3, tk, 0);
       prefetch_tmap(&tm_qkv);
       prefetch_tmap(&tm_do);
       int it = 0, tl = 0;
@@ -479,18 +469,11 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const int t = snake_tile(r, blockIdx.x, G);
         if (t >= n_tiles) break;
         const Tile x = tile_of(t);
-        if (a.trace != nullptr && t < 1024) {
-          uint32_t smid;
-          asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-          a.trace[1024 + 3 * t] = (long long)globaltimer();
-          a.trace[1024 + 3 * t + 1] = smid;
-        }
         const int kcol = (a.H + x.kvh) * HD, vcol = (a.H + a.KV + x.kvh) * HD;
         for (int n = 0; n < x.n_items; ++n, ++it) {
           const int s = it & 1;
           const int hq = x.kvh * group + n / x.n_i, i = x.i_start + n % x.n_i;
           if (!wait_bar(&q_empty[s], ((it >> 1) & 1) ^ 1, err, 41)) { ok = false; break; }
-          trace_at(a.trace, 3, tk, 30);
           const int nq = min(kBN, a.T - i * kBN);
           const uint32_t vbytes = (uint32_t)(((nq + 3) & ~3) * 4);
           bar_arrive_expect_tx(&q_full[s], 2 * L::TILE + 2 * vbytes);
@@ -502,7 +485,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
           if (n == 0) {
             // the tile's first Q / dO are already in flight; K / V wait for the previous tile's MMAs
             if (tl > 0 && !wait_bar(kv_empty, (tl - 1) & 1, err, 53)) { ok = false; break; }
-            trace_at(a.trace, 3, tk, 31);
             bar_arrive_expect_tx(kv_full, 2 * L::TILE);
             tma_load_2d(smem + L::K_OFF, &tm_qkv, kv_full, kcol, x.row0 + x.k0);
             tma_load_2d(smem + L::V_OFF, &tm_qkv, kv_full, vcol, x.row0 + x.k0);
@@ -536,20 +518,16 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         if (t >= n_tiles) break;
         const Tile x = tile_of(t);
         if (!wait_bar(kv_full, tl & 1, err, 42)) break;
-        trace_at(a.trace, 0, tk, 7);
         if (!wait_bar(&q_full[it & 1], (it >> 1) & 1, err, 43)) break;
-        trace_at(a.trace, 0, tk, 8);
         tc_fence_after();
         issue_sdp(it & 1);
         for (int n = 0; n < x.n_items; ++n) {
           const int g = it + n;
           const int s = g & 1, pb = g & 1;
           if (!wait_bar(pds_full, g & 1, err, 44)) { ok = false; break; }
-          trace_at(a.trace, 0, tk, 1);
           tc_fence_after();
           if (n + 1 < x.n_items) {  // S^T / dP^T columns were read out before pds_full arrived
             if (!wait_bar(&q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, err, 45)) { ok = false; break; }
-            trace_at(a.trace, 0, tk, 2);
             issue_sdp((g + 1) & 1);
           }
           // the previous tile's dK / dV must be out of TMEM before they are overwritten
@@ -569,9 +547,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
                     make_sw128_desc(q_addr + offm, 16384, 1024), id_kv, (n > 0 || k > 0) ? 1u : 0u);
           }
           mma_commit(&q_empty[s]);  // dQ reads no Q / dO: the stage can refill as soon as dV / dK are done
-          trace_at(a.trace, 0, tk, 4);
           if (g > 0 && !wait_bar(dq_free, (g - 1) & 1, err, 46)) { ok = false; break; }
-          trace_at(a.trace, 0, tk, 5);
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kBM / 16; ++k)  // contraction over keys
@@ -579,7 +555,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
                     make_sw128_desc(k_addr + k * 2048, 16384, 1024), id_q, k > 0);
           mma_commit(dq_full);
           mma_commit(&pds_empty[pb]);
-          trace_at(a.trace, 0, tk, 6);
         }
         if (!ok) break;
         mma_commit(dkv_full);  // this tile's dK / dV are final
@@ -592,8 +567,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     const int half = (warp - 2) >> 2;  // column half handled by this warp (2 warps per lane quadrant)
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const bool tr_thread = lane == 0 && (warp == 2 || warp == 9);
-    const int tr_region = warp == 2 ? 1 : 2;
     bool ok = true;
     int it = 0, tl = 0;
     for (int rr = 0; ok; ++rr, ++tl) {
@@ -606,7 +579,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
       auto drain_dq = [&](int n) -> bool {
         const int g = it + n;
         if (!wait_bar(dq_full, g & 1, err, 47)) return false;
-        if (tr_thread) trace_at(a.trace, tr_region, tk, 13);
         tc_fence_after();
         const int hq = x.kvh * group + n / x.n_i, qb = (x.i_start + n % x.n_i) * kBN;
         const int col = half * 32;
@@ -638,7 +610,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (g & 1) * 1024);
         const float* d_s = lse_s + 128;
         if (!wait_bar(s_full, g & 1, err, 48)) { ok = false; break; }
-        if (tr_thread) trace_at(a.trace, tr_region, tk, 10);
         if (!wait_bar(&pds_empty[pb], ((g >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
         if (g >= 2) {
           // buffer pb staged dQ(g - 2) for every warp's TMA reduce: all of them must have read it
@@ -688,18 +659,15 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
             *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
           }
         }
-        if (tr_thread) trace_at(a.trace, tr_region, tk, 12);
         tc_fence_before();
         fence_proxy_async_smem();
         bar_arrive(pds_full);
         if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
-        if (tr_thread) trace_at(a.trace, tr_region, tk, 14);
       }
       if (ok && x.n_items > 0) ok = drain_dq(x.n_items - 1);
       // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second; column
       // pairs (e, e + 32) are handled 16 at a time to keep registers low
       if (ok && wait_bar(dkv_full, tl & 1, err, 50)) {
-        if (tr_thread) trace_at(a.trace, tr_region, tk, 15);
         tc_fence_after();
         const uint32_t col = half == 0 ? C_DK : C_DV;
         const float sc = half == 0 ? a.scale : 1.f;
@@ -748,7 +716,6 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
       } else {
         ok = false;
       }
-      if (tr_thread && warp == 2 && a.trace != nullptr && t < 1024) a.trace[1024 + 3 * t + 2] = (long long)globaltimer();
       it += x.n_items;
     }
     if (lane == 0) bulk_wait<0>();  // this warp's dQ reductions are complete before exit
@@ -861,12 +828,6 @@ cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, 
 
 }  // namespace
 
-// Event tracing of the pipelined backward (for profiling): a zeroed device buffer of 4096
-// int64 (4 regions of 256 events of CTA (0, 0): MMA thread, compute warps 2 and 9, TMA
-// thread; then per CTA (up to 1024) its start time, SM and end time in ns), or nullptr.
-static long long* g_bwd_trace = nullptr;
-void attn_bwd_set_trace(long long* buf) { g_bwd_trace = buf; }
-
 // dqkv (B*T, ld_qkv) bf16 receives the gradient w.r.t. the packed *pre-RoPE* qkv rows.
 // dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
 cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
@@ -904,7 +865,6 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   args.scale_log2 = scale * 1.4426950408889634f;
   args.causal = causal ? 1 : 0;
   args.err = attn_err_word();
-  args.trace = hd == 64 ? g_bwd_trace : nullptr;
   alignas(64) CUtensorMap tq, tdo, tdq;
   const bool ok =
       make_tmap_2d(&tq, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows, ld_qkv, 64, 128) &&

@@ -353,11 +353,8 @@ cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb, 
 }  // namespace
 
 int* attn_err_word() {
-  static int* p[64] = {nullptr};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!p[dev]) cudaGetSymbolAddress(reinterpret_cast<void**>(&p[dev]), g_attn_err);
-  return p[dev];
+  static std::atomic<int*> slots[64];
+  return device_symbol_address(slots, g_attn_err);
 }
 
 int attn_error_code(bool reset) {

@@ -566,15 +566,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     ok(llmt::tp_sum_slots(slots.data_ptr(), out.data_ptr(), (int)tp, out.size(0), (int)out.size(1), stream()),
        "tp_sum_slots");
   });
-  m.def("attn_bwd_set_trace", [](c10::optional<at::Tensor> buf) {
-    if (buf && buf->defined()) {
-      CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->numel() >= 4096,
-            "trace buffer: 4096 int64 on the GPU");
-      llmt::attn_bwd_set_trace(reinterpret_cast<long long*>(buf->data_ptr<int64_t>()));
-    } else {
-      llmt::attn_bwd_set_trace(nullptr);
-    }
-  }, "buf"_a = py::none());
   m.def("sm_count", &llmt::sm_count);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

@@ -135,11 +135,8 @@ cudaError_t ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr); }
 cudaError_t ipc_free(void* ptr) { return cudaFree(ptr); }
 
 int* dp_err_word() {
-  static int* p[64] = {nullptr};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!p[dev]) cudaGetSymbolAddress(reinterpret_cast<void**>(&p[dev]), g_dp_err);
-  return p[dev];
+  static std::atomic<int*> slots[64];
+  return device_symbol_address(slots, g_dp_err);
 }
 
 int dp_error_code(bool reset) {

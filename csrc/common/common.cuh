@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "../api.h"
 
@@ -68,6 +69,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 }
 
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Device address of a file-scope __device__ variable on the current device, looked up once per
+// device and kept in `slots` (atomics: several host threads may make the first lookup at once;
+// they store the same address).
+template <typename T>
+inline T* device_symbol_address(std::atomic<T*> (&slots)[64], const T& symbol) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  T* p = slots[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    void* q = nullptr;
+    if (cudaGetSymbolAddress(&q, symbol) != cudaSuccess) return nullptr;
+    p = static_cast<T*>(q);
+    slots[dev].store(p, std::memory_order_relaxed);
+  }
+  return p;
+}
 
 // ---------------------------------------------------------------- programmatic dependent launch
 // Kernels on the training path are launched with programmatic stream serialisation: a kernel's

@@ -2,6 +2,7 @@
 // Host-side runtime helpers shared by all launchers: last-error message, SM count.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <string>
 
 #include "../api.h"
@@ -15,19 +16,23 @@ const char* last_error() { return g_last_error.c_str(); }
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
 int sm_count() {
-  static int n[64] = {0};
+  static std::atomic<int> n[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev];
+  int v = n[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
 }
 
 // SMs left to the persistent kernels (GEMM, attention backward): all of them unless some are
 // reserved for kernels that run beside them (the overlapped data-parallel step). A persistent
 // kernel sized to every SM waits, whole, for any SM another stream holds.
-static int g_reserved_sms = 0;
-void set_reserved_sms(int n) { g_reserved_sms = n < 0 ? 0 : n; }
-int reserved_sms() { return g_reserved_sms; }
-int persistent_sms() { return std::max(1, sm_count() - g_reserved_sms); }
+static std::atomic<int> g_reserved_sms{0};
+void set_reserved_sms(int n) { g_reserved_sms.store(n < 0 ? 0 : n); }
+int reserved_sms() { return g_reserved_sms.load(); }
+int persistent_sms() { return std::max(1, sm_count() - g_reserved_sms.load()); }
 }  // namespace llmt

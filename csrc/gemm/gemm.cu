@@ -13,11 +13,8 @@ namespace {
 __device__ int g_gemm_err = 0;  // sticky: first bounded-wait timeout code seen by any GEMM launch
 
 int* gemm_err_word() {
-  static int* p[64] = {nullptr};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!p[dev]) cudaGetSymbolAddress(reinterpret_cast<void**>(&p[dev]), g_gemm_err);
-  return p[dev];
+  static std::atomic<int*> slots[64];
+  return device_symbol_address(slots, g_gemm_err);
 }
 }  // namespace
 

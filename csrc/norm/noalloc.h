@@ -26,7 +26,9 @@
 //    ordering) race on it: serialise them, for example on one stream.
 //  * The first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that first call
-//    before any CUDA stream capture on that device.
+//    before any CUDA stream capture on that device. A first call made while its stream is
+//    capturing is refused (cudaErrorStreamCaptureUnsupported, with a message). First calls
+//    from several host threads at once are safe: the cache slots are atomics.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>

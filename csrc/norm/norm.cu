@@ -1,4 +1,6 @@
 #include <stdlib.h>
+
+#include <atomic>
 // Fused residual-add + RMSNorm, forward and backward (sm_100a).
 //
 // Contract (same math as the reference's add+RMSNorm, kernels/cuda_ext/add_rmsnorm.cu:78-178
@@ -308,9 +310,12 @@ namespace {
 static __device__ __align__(256) float g_rmsnorm_noalloc_scratch[LLMT_NOALLOC_SCRATCH_FLOATS];
 
 // Device address of the scratch array for the current device, looked up once per device
-// (host code cannot use the array's name as a device pointer).
-float* noalloc_scratch_ptr(cudaError_t* err) {
-  static float* ptrs[64] = {nullptr};
+// (host code cannot use the array's name as a device pointer). The per-device slots are
+// atomics, so first calls from several host threads at once are safe; they all store the
+// same address. A lookup cannot run inside a stream capture (it may load the module), so a
+// first call made while the stream is capturing is refused with a message.
+float* noalloc_scratch_ptr(cudaStream_t stream, cudaError_t* err) {
+  static std::atomic<float*> ptrs[64];
   int dev = 0;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -318,13 +323,20 @@ float* noalloc_scratch_ptr(cudaError_t* err) {
     *err = cudaErrorInvalidDevice;
     return nullptr;
   }
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    *err = cudaGetSymbolAddress(&p, g_rmsnorm_noalloc_scratch);
-    if (*err != cudaSuccess) return nullptr;
-    ptrs[dev] = static_cast<float*>(p);
+  float* cached = ptrs[dev].load(std::memory_order_relaxed);
+  if (cached) return cached;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone) {
+    llmt::set_last_error("llmt_rmsnorm_bwd_noalloc: the first call on a device must come before any stream "
+                         "capture (it looks up the scratch array's device address)");
+    *err = cudaErrorStreamCaptureUnsupported;
+    return nullptr;
   }
-  return ptrs[dev];
+  void* p = nullptr;
+  *err = cudaGetSymbolAddress(&p, g_rmsnorm_noalloc_scratch);
+  if (*err != cudaSuccess) return nullptr;
+  ptrs[dev].store(static_cast<float*>(p), std::memory_order_relaxed);
+  return static_cast<float*>(p);
 }
 }  // namespace
 
@@ -342,7 +354,7 @@ extern "C" int llmt_rmsnorm_bwd_noalloc(const void* dy_bf16, const float* s, con
   }
   if (N == 0) return (int)cudaSuccess;
   cudaError_t e = cudaSuccess;
-  float* part = noalloc_scratch_ptr(&e);
+  float* part = noalloc_scratch_ptr(stream, &e);
   if (!part) return (int)e;
   // One partial row per CTA; the scratch holds LLMT_NOALLOC_SCRATCH_FLOATS / D of them.
   const int grid = std::max(1, std::min(rmsnorm_bwd_partials(N, D), LLMT_NOALLOC_SCRATCH_FLOATS / D));

@@ -16,25 +16,26 @@ import argparse
 import json
 import os
 import platform
+import statistics
 import time
 
 import torch
 
 
 def _time(fn, warmup=3, iters=20, repeats=3):
+    """Seconds per call of `fn`: median over `iters * repeats` launches, each bracketed by its own
+    pair of CUDA events on the current stream (events are read after one final synchronize)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    best = float("inf")
-    for _ in range(repeats):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(iters * repeats)]
+    for a, b in marks:
         a.record()
-        for _ in range(iters):
-            fn()
+        fn()
         b.record()
-        torch.cuda.synchronize()
-        best = min(best, a.elapsed_time(b) / 1e3 / iters)
-    return best
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in marks) / 1e3
 
 
 def env_info(label):
@@ -45,52 +46,63 @@ def env_info(label):
             "gpu_mem_gb": round(p.total_memory / 1e9, 1)}
 
 
+def _square(n, dtype):
+    return torch.randn(n, n, device="cuda").to(dtype)
+
+
+def _torch_mm(dtype, tf32=False):
+    def make(n):
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        a, b = _square(n, dtype), _square(n, dtype)
+        return lambda: torch.mm(a, b)
+    return make
+
+
+def _torch_fp8(n):
+    # torch._scaled_mm wants the second operand column-major: a transposed row-major matrix
+    a, bt = _square(n, torch.float8_e4m3fn), _square(n, torch.float8_e4m3fn)
+    unit = torch.ones((), device="cuda")
+    return lambda: torch._scaled_mm(a, bt.t(), scale_a=unit, scale_b=unit, out_dtype=torch.bfloat16)
+
+
+def _llmt_gemm(kind):
+    """This framework's tcgen05 GEMMs; operands are quantized once, outside the timed calls."""
+    def make(n):
+        from llmt.ops import native as N
+        a, b = _square(n, torch.bfloat16), _square(n, torch.bfloat16)
+        out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
+        if kind == "bf16":
+            return lambda: N.gemm(a, b, out=out)
+        if kind == "fp8":
+            (aq, _, sa), (bq, _, sb) = N.fp8_quant(a, transpose=False), N.fp8_quant(b, transpose=False)
+            return lambda: N.gemm_fp8(aq, bq, sa, sb, out=out)
+        fmt = {"mxfp8": N.MXFP8, "nvfp4": N.NVFP4}[kind]
+        ar, br = N.mx_quant(a, fmt)[0], N.mx_quant(b, fmt)[0]
+        return lambda: N.gemm_mx(fmt, ar, br, out=out)
+    return make
+
+
+# precision name -> builder(n) returning the call to time (torch / cuBLAS rows first, then ours)
+MATMULS = {
+    "fp32": _torch_mm(torch.float32), "tf32": _torch_mm(torch.float32, tf32=True),
+    "fp16": _torch_mm(torch.float16), "bf16": _torch_mm(torch.bfloat16), "fp8": _torch_fp8,
+    "bf16_llmt": _llmt_gemm("bf16"), "fp8_llmt": _llmt_gemm("fp8"), "mxfp8_llmt": _llmt_gemm("mxfp8"),
+    "nvfp4_llmt": _llmt_gemm("nvfp4"),
+}
+
+
 def matmul_tflops(precision, n=8192):
-    flops = 2.0 * n ** 3
-    old = torch.backends.cuda.matmul.allow_tf32
+    """Dense n^3 matmul throughput of one precision, {"status", "tflops", "ms"}; a precision that
+    fails to build or run is reported with its error and does not stop the calibration."""
+    saved_tf32 = torch.backends.cuda.matmul.allow_tf32
     try:
-        if precision in ("fp32", "tf32"):
-            torch.backends.cuda.matmul.allow_tf32 = precision == "tf32"
-            a, b = torch.randn(n, n, device="cuda"), torch.randn(n, n, device="cuda")
-            fn = lambda: a @ b  # noqa: E731
-        elif precision in ("fp16", "bf16"):
-            dt = torch.float16 if precision == "fp16" else torch.bfloat16
-            a, b = torch.randn(n, n, device="cuda", dtype=dt), torch.randn(n, n, device="cuda", dtype=dt)
-            fn = lambda: a @ b  # noqa: E731
-        elif precision == "fp8":
-            a = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn)
-            b = torch.randn(n, n, device="cuda").to(torch.float8_e4m3fn).t()
-            one = torch.tensor(1.0, device="cuda")
-            fn = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)  # noqa: E731
-        elif precision == "bf16_llmt":
-            from llmt.ops import native as N
-            a = torch.randn(n, n, device="cuda").bfloat16()
-            b = torch.randn(n, n, device="cuda").bfloat16()
-            out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
-            fn = lambda: N.gemm(a, b, out=out)  # noqa: E731
-        elif precision in ("fp8_llmt", "mxfp8_llmt", "nvfp4_llmt"):
-            # this framework's 8-bit / 4-bit tcgen05 GEMMs (operands quantized once, outside the timing)
-            from llmt.ops import native as N
-            a = torch.randn(n, n, device="cuda").bfloat16()
-            b = torch.randn(n, n, device="cuda").bfloat16()
-            out = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
-            if precision == "fp8_llmt":
-                aq, _, sa = N.fp8_quant(a, transpose=False)
-                bq, _, sb = N.fp8_quant(b, transpose=False)
-                fn = lambda: N.gemm_fp8(aq, bq, sa, sb, out=out)  # noqa: E731
-            else:
-                kind = N.MXFP8 if precision == "mxfp8_llmt" else N.NVFP4
-                ar, _ = N.mx_quant(a, kind)
-                br, _ = N.mx_quant(b, kind)
-                fn = lambda: N.gemm_mx(kind, ar, br, out=out)  # noqa: E731
-        else:
-            raise ValueError(precision)
-        sec = _time(fn)
-        return {"status": "ok", "tflops": round(flops / sec / 1e12, 1), "ms": round(sec * 1e3, 3)}
-    except Exception as e:  # noqa: BLE001 - keep calibrating the other precisions
-        return {"status": "error", "error": f"{type(e).__name__}: {e}"[:300]}
+        call = MATMULS[precision](n)
+        sec = _time(call)
+        return {"status": "ok", "tflops": round(2.0 * n ** 3 / sec / 1e12, 1), "ms": round(sec * 1e3, 3)}
+    except Exception as e:  # noqa: BLE001
+        return {"status": "error", "error": (type(e).__name__ + ": " + str(e))[:300]}
     finally:
-        torch.backends.cuda.matmul.allow_tf32 = old
+        torch.backends.cuda.matmul.allow_tf32 = saved_tf32
         torch.cuda.empty_cache()
 
 

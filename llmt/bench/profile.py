@@ -48,32 +48,33 @@ def short_name(name: str, n=110) -> str:
 
 
 def union_us(intervals):
-    total, cur_s, cur_e = 0.0, None, None
-    for s, e in sorted(intervals):
-        if cur_e is None or s > cur_e:
-            if cur_e is not None:
-                total += cur_e - cur_s
-            cur_s, cur_e = s, e
-        else:
-            cur_e = max(cur_e, e)
-    if cur_e is not None:
-        total += cur_e - cur_s
-    return total
+    """Time during which at least one interval is open (kernels on concurrent streams overlap and
+    must not be counted twice): a sweep over the start (+1) and end (-1) boundaries, summing the
+    stretches where the open count is positive."""
+    edges = sorted([(s, 1) for s, _ in intervals] + [(e, -1) for _, e in intervals],
+                   key=lambda t: (t[0], -t[1]))
+    busy, depth, opened = 0.0, 0, 0.0
+    for t, step in edges:
+        if depth == 0 and step > 0:
+            opened = t
+        depth += step
+        if depth == 0:
+            busy += t - opened
+    return busy
 
 
 def clean_ms(step, warmup=3, steps=10):
+    """Median ms of one step with no profiler attached (an event pair per step, read at the end)."""
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    times = []
-    for _ in range(steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record()
+    for i in range(steps):
         step()
-        b.record()
-        torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    return statistics.median(times)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    return statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(steps))
 
 
 def profile_step(step, prof_steps=3, top=25):

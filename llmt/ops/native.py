@@ -18,7 +18,7 @@ EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD 
 
 # Kernels launched per call of an extension entry point (1 unless listed).
 _KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0, "dp_error_code": 0,
-                     "set_reserved_sms": 0, "reserved_sms": 0, "attn_bwd_set_trace": 0,
+                     "set_reserved_sms": 0, "reserved_sms": 0,
                      "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "ipc_free": 0, "tensor_from_ptr": 0,
                      "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0, "gemm_plan": 0}
 

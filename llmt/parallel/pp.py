@@ -30,8 +30,6 @@ from llmt.export.trace import schedule_1f1b
 from llmt.models.llama import Block, RMSNorm, build_model, rope_tables
 from llmt.parallel.collectives import gather_rows, scatter_rows
 
-_DEBUG = bool(int(__import__("os").environ.get("LLMT_PP_DEBUG", "0")))
-
 
 def stage_layers(L: int, pp: int, s: int):
     """Blocks [l0, l1) of stage s; the first L % pp stages take one extra block."""
@@ -251,11 +249,6 @@ class Pipeline1F1B:
             if self.last:
                 outputs[i].backward()
             else:
-                if _DEBUG:
-                    for name, t in (("out", outputs[i]), ("grad", grads)):
-                        print(f"[pp stage {self.s} mb {i}] {name}: " + ", ".join(
-                            f"{tuple(x.shape)}/{x.stride()}/{x.dtype}/{x.device}/ptr%256={x.data_ptr() % 256}"
-                            f"/off={x.storage_offset()}" for x in t), flush=True)
                 torch.autograd.backward(list(outputs[i]), list(grads))
             g_in = None if self.first else [t.grad for t in inputs[i]]
             inputs[i] = outputs[i] = None

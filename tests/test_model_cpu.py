@@ -83,8 +83,14 @@ def test_tiny256_step_matches_reference_fp32():
     o2 = torch.optim.AdamW(ours.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
     o1.step()
     o2.step()
+    # The two implementations order their fp32 operations differently, so gradients agree to
+    # rounding (about 1e-8 absolute). Adam's first step maps g to about lr * g / (|g| + eps), which
+    # amplifies a rounding difference where |g| is near eps = 1e-8; compare the updated weights
+    # tightly where the gradient is well above eps, and everywhere within one step's bound.
     for p1, p2 in zip(ref.parameters(), ours.parameters()):
-        assert torch.allclose(p1, p2, rtol=1e-5, atol=1e-7)
+        big = p1.grad.abs() > 1e-6
+        assert torch.allclose(p1[big], p2[big], rtol=1e-5, atol=1e-7)
+        assert (p1 - p2).abs().max() <= 2 * 3e-4
 
 
 def test_gqa_model_runs_on_cpu():

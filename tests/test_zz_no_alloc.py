@@ -37,7 +37,9 @@ def _call(so, dy, s, w, rstd, ds_in, ds, ds16, dw, accumulate):
                                        int(accumulate), stream)
 
 
-@pytest.mark.parametrize("N,D", [(4096, 1024), (300, 768), (64, 8192)])
+# (4096, 4096) and (4096, 8192) want more partial rows than the fixed scratch holds, so the grid is
+# cut to 256 and 128 CTAs and each CTA walks more rows.
+@pytest.mark.parametrize("N,D", [(4096, 1024), (300, 768), (64, 8192), (4096, 4096), (4096, 8192)])
 def test_noalloc_matches_regular_entry_point_twice(lib, N, D):
     so, native = lib
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -59,6 +61,26 @@ def test_noalloc_matches_regular_entry_point_twice(lib, N, D):
         assert rel_err(ds, ds_ref) < 1e-5
         assert rel_err(ds16, ds16_ref) < 1e-2
         assert rel_err(dw, dw_ref) < 1e-4
+
+
+def test_noalloc_without_optional_inputs(lib):
+    """ds_in and ds16 are optional (NULL): no incoming residual gradient, no bf16 copy of ds."""
+    so, native = lib
+    N, D = 1000, 2048
+    g = torch.Generator(device="cuda").manual_seed(1)
+    r = torch.randn(N, D, device="cuda", generator=g)
+    a = torch.randn(N, D, device="cuda", generator=g).bfloat16()
+    w = 1 + 0.1 * torch.randn(D, device="cuda", generator=g)
+    _, s, rstd = native.add_rmsnorm_fwd(a, r, w, 1e-5)
+    dy = torch.randn(N, D, device="cuda", generator=g).bfloat16()
+    dw_ref, dw = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+    ds_ref, _ = native.rmsnorm_bwd(dy, s, w, rstd, None, dw_ref, accumulate=False, write_ds16=False)
+    ds = torch.empty_like(s)
+    rc = _call(so, dy, s, w, rstd, None, ds, None, dw, accumulate=False)
+    torch.cuda.synchronize()
+    assert rc == 0, so.llmt_noalloc_last_error()
+    assert rel_err(ds, ds_ref) < 1e-5
+    assert rel_err(dw, dw_ref) < 1e-4
 
 
 def test_noalloc_rejects_oversized_width(lib):
