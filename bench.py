@@ -260,7 +260,7 @@ def main():
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile",
                    help="reference ladder row (default: its fastest bf16 row on B200)")
-    p.add_argument("--dp-mode", default="nccl", choices=["fused", "nccl", "fused-overlap"],
+    p.add_argument("--dp-mode", default="nccl", choices=["nvls", "fused", "nccl", "fused-overlap"],
                    help="data-parallel transport: NCCL (fastest measured at 2 and 8 GPUs), the fused "
                         "peer-memory kernel, or that kernel overlapped with the backward")
     p.add_argument("--no-graph", action="store_true")

@@ -171,5 +171,9 @@ cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, fl
                            int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
                            cudaStream_t st, int max_blocks = 0);
 int dp_error_code(bool reset);
+// NVLS data-parallel step (comm/dp_nvls.cu): g_mc / w_mc are the NVLink multicast addresses of
+// the flat bf16 gradient and weight buffers; reduce, AdamW on [lo, lo + n), multicast store.
+cudaError_t dp_nvls_adamw(const void* g_mc, void* w_mc, float* master, float* m, float* v, int64_t lo, int64_t n,
+                          const float* lr, const int* step, AdamHyper h, cudaStream_t st, int max_blocks = 0);
 
 }  // namespace llmt

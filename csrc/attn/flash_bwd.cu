@@ -408,7 +408,8 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
   uint64_t* stage_free = bars + 12;  // 8 arrivals: every compute warp's dQ reduce has read its staging
   uint64_t* kv_empty = bars + 13;    // the tile's MMAs have finished reading K / V
   uint64_t* dkv_free = bars + 14;    // 256 arrivals: the tile's dK / dV are out of TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* st_read = bars + 15;     // 256 arrivals: S^T / dP^T of the block are in registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int group = a.H / a.KV;
@@ -433,6 +434,7 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     bar_init(stage_free, 8);
     bar_init(kv_empty, 1);
     bar_init(dkv_free, kComputeThreads);
+    bar_init(st_read, kComputeThreads);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
@@ -524,12 +526,16 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         for (int n = 0; n < x.n_items; ++n) {
           const int g = it + n;
           const int s = g & 1, pb = g & 1;
-          if (!wait_bar(pds_full, g & 1, err, 44)) { ok = false; break; }
-          tc_fence_after();
-          if (n + 1 < x.n_items) {  // S^T / dP^T columns were read out before pds_full arrived
+          // the next block's S^T / dP^T as soon as this block's are in the compute warps'
+          // registers, so those MMAs run under this block's softmax
+          if (n + 1 < x.n_items) {
+            if (!wait_bar(st_read, g & 1, err, 55)) { ok = false; break; }
             if (!wait_bar(&q_full[(g + 1) & 1], ((g + 1) >> 1) & 1, err, 45)) { ok = false; break; }
+            tc_fence_after();
             issue_sdp((g + 1) & 1);
           }
+          if (!wait_bar(pds_full, g & 1, err, 44)) { ok = false; break; }
+          tc_fence_after();
           // the previous tile's dK / dV must be out of TMEM before they are overwritten
           if (n == 0 && tl > 0 && !wait_bar(dkv_free, (tl - 1) & 1, err, 54)) { ok = false; break; }
           tc_fence_after();
@@ -629,13 +635,21 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const bool key_ok = kk < a.T;
         const int q_lo = (a.causal && qbase < x.k0 + kBM) ? kk - qbase : 0;
         const int q_hi = key_ok ? min(kBN, a.T - qbase) : 0;
-#pragma unroll 1
+        // this warp's 64 columns of S^T and dP^T into registers, then the columns are released
+        uint32_t sv2[2][32], dv2[2][32];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          tmem_ld32(tmem + lane_off + C_S + (half * 2 + cc) * 32, sv2[cc]);
+          tmem_ld32(tmem + lane_off + C_DP + (half * 2 + cc) * 32, dv2[cc]);
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        bar_arrive(st_read);
+#pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int c = half * 2 + cc;
-          uint32_t sv[32], dv[32];
-          tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
-          tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
-          tmem_wait_ld();
+          const uint32_t(&sv)[32] = sv2[cc];
+          const uint32_t(&dv)[32] = dv2[cc];
           const int lo = q_lo - c * 32, hi = q_hi - c * 32;
           const float4* l4 = reinterpret_cast<const float4*>(lse_s + c * 32);
           const float4* d4 = reinterpret_cast<const float4*>(d_s + c * 32);

@@ -5,17 +5,27 @@
 // packed post-RoPE qkv rows (B*T, (H + 2*KV) * hd) and o is written as (B*T, H*hd), the layout
 // the wo GEMM consumes. Online softmax (Milakov & Gimelshein 2018; FlashAttention, Dao et al.).
 //
-// Persistent: two CTAs per SM (so one CTA's softmax overlaps the other's MMAs) walk the
-// (batch*head, 128-query block) tiles, heaviest causal blocks first, in a snake order:
-//   warp 0     TMA producer: each tile's Q (double-buffered at head dim 64, so the next tile's
-//              Q lands during this one), K/V blocks of 128 keys through a STAGES-deep ring
-//   warp 1     TMEM allocator + single-thread MMA issuer:
-//                S_j  = Q K_j^T   (SS form, M=128, N=128, K=hd)    -> TMEM cols [0, 128)
-//                O'_j = P_j V_j   (TS form: P_j read from TMEM)    -> TMEM cols [128, 128+hd)
-//   warps 2-5  one thread per query row: row max of S_j (tree reduction, diagonal block
-//              masked branch-free), P = 2^(S*scale*log2e - m) on the SFU, row sum, P packed to
-//              bf16 and stored back over the consumed S columns with tcgen05.st; O is kept in
-//              registers, O = O * 2^(m_old - m_new) + O'_j.
+// One persistent CTA per SM walks (batch*head, 256-query) tiles, heaviest causal tiles first, in
+// a snake order. A tile is two 128-row query blocks, A and B, that share every K/V block; each
+// has its own softmax warpgroup, so one block's softmax runs while the tensor core works on the
+// other's ("ping-pong"):
+//   warp 0     TMA producer: the tile's Q pair (double-buffered at head dim 64, so the next
+//              tile's Q lands during this one) and 128-key K / V blocks through a ring
+//   warp 1     TMEM allocator and single-thread MMA issuer, per key block j:
+//                S_A = Q_A K_j^T, S_B = Q_B K_j^T      (SS form, M=128, N=128, K=hd)
+//                O_A += P_A V_j,  O_B += P_B V_j       (TS form: P read from TMEM)
+//              the next block's S is issued as soon as the softmax has read this block's S
+//              out of TMEM, so score MMAs run ahead of the softmax
+//   warps 2-5  softmax of block A, warps 6-9 of block B: one thread per query row holds the
+//              row's 128 scores in registers; row max, P = 2^(S*scale*log2e - m) split
+//              between the SFU (ex2.approx) and an FMA-pipe polynomial, row sum, P packed to
+//              bf16 into TMEM. O stays in TMEM: the running max is only moved (and O, l
+//              rescaled in place) when it grows by more than 2^8, so most blocks skip the
+//              rescale; O and l always refer to the same max, so the result is exact.
+//              After a tile's last block the same warps normalise O and write o and lse.
+// TMEM (512 columns): S_A, S_B 128 each; O_A, O_B hd each; at hd 64 P_A, P_B 64 each (bf16
+// pairs), at hd 128 P is written over the block's own S columns (the next S then waits for the
+// P.V that reads them).
 // GQA: query head h reads key/value head h / (H / KV). Keys past T or past the query
 // (causal) are masked. Saves lse (B, H, T) in natural-log units for the backward.
 #include "../common/common.cuh"
@@ -28,9 +38,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBlockM = 128;
-constexpr int kBlockN = 128;
-constexpr int kAttnThreads = 192;
+constexpr int kBlockM = 128;   // query rows per softmax warpgroup
+constexpr int kBlockN = 128;   // keys per K/V block
+constexpr int kTileM = 256;    // query rows per tile (blocks A and B)
+// TMA warp, MMA warp, two softmax warpgroups. Ten warps leave 168 registers a thread (three warps
+// share a 16K-register SM sub-partition), enough for a row of 128 scores plus its P.
+constexpr int kAttnThreads = 320;
+constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
 
 struct AttnFwdArgs {
   bf16* o;
@@ -45,54 +59,62 @@ __device__ int g_attn_err = 0;
 
 template <int HD>
 struct FwdSmem {
-  static constexpr int STAGES = HD == 64 ? 2 : 1;
-  static constexpr int QST = HD == 64 ? 2 : 1;  // Q buffers: the next tile's Q loads during this one
-  static constexpr uint32_t Q_BYTES = kBlockM * HD * 2;
+  static constexpr int QST = HD == 64 ? 2 : 1;   // Q pair buffers
+  static constexpr int KVST = HD == 64 ? 3 : 2;  // K / V ring stages
+  static constexpr uint32_t QB_BYTES = kBlockM * HD * 2;  // one 128-row Q block
   static constexpr uint32_t KV_BYTES = kBlockN * HD * 2;
   static constexpr uint32_t Q_OFF = 0;
-  static constexpr uint32_t K_OFF = Q_OFF + QST * Q_BYTES;
-  static constexpr uint32_t V_OFF = K_OFF + STAGES * KV_BYTES;
-  static constexpr uint32_t BAR_OFF = V_OFF + STAGES * KV_BYTES;
-  static constexpr uint32_t TOTAL = BAR_OFF + 128 + 1024;
+  static constexpr uint32_t K_OFF = Q_OFF + QST * 2 * QB_BYTES;
+  static constexpr uint32_t V_OFF = K_OFF + KVST * KV_BYTES;
+  static constexpr uint32_t BAR_OFF = V_OFF + KVST * KV_BYTES;
+  static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
 };
 
-// Tiles are (batch x head, 128-query block) pairs; a persistent CTA (two per SM) walks its share in
-// a snake order over rounds, query blocks with the most key blocks first. Every barrier phase runs on
-// counters that continue across tiles, so TMEM, barriers and the K/V ring persist, and the next
-// tile's Q (double-buffered at hd 64) loads while this tile runs.
 __device__ __forceinline__ int fwd_snake(int r, int i, int G) { return r * G + ((r & 1) ? (G - 1 - i) : i); }
 
+// Number of 128-key blocks block `half` (0 = A, 1 = B) of a tile starting at query q0 reads.
+__device__ __forceinline__ int fwd_nkv(int q0, int half, int T, int causal) {
+  const int qb0 = q0 + half * kBlockM;
+  if (qb0 >= T) return 0;
+  const int nall = (int)cdiv(T, kBlockN);
+  return causal ? min(qb0 / kBlockN + 1, nall) : nall;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
   pdl_wait();
   using L = FwdSmem<HD>;
-  constexpr int ST = L::STAGES;
   constexpr int QST = L::QST;
-  constexpr int TMEM_COLS = 256;        // S/P at [0, 128), O' at [128, 128 + HD)
-  constexpr uint32_t C_O = 128;
+  constexpr int KVST = L::KVST;
+  constexpr bool kSepP = HD == 64;  // P in its own TMEM columns (else over S)
+  // TMEM columns of half w: S, O and P
+  auto c_s = [](int w) -> uint32_t { return w ? 128u : 0u; };
+  auto c_o = [](int w) -> uint32_t { return w ? 256u + HD : 256u; };
+  auto c_p = [](int w) -> uint32_t { return kSepP ? (w ? 448u : 384u) : (w ? 128u : 0u); };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* k_full = bars + 0;       // [ST]
-  uint64_t* v_full = bars + 2;       // [ST]
-  uint64_t* kv_empty = bars + 4;     // [ST]
-  uint64_t* s_full = bars + 6;
-  uint64_t* p_full = bars + 7;       // 128 arrivals
-  uint64_t* o_full = bars + 8;
-  uint64_t* q_full = bars + 9;       // [QST]
-  uint64_t* q_empty = bars + 11;     // [QST]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* k_full = bars + 0;        // [KVST]
+  uint64_t* v_full = bars + 3;        // [KVST]
+  uint64_t* kv_empty = bars + 6;      // [KVST]
+  uint64_t* q_full = bars + 9;        // [QST]
+  uint64_t* q_empty = bars + 11;      // [QST]
+  uint64_t* s_full = bars + 13;       // [2] S of block A / B in TMEM
+  uint64_t* s_free = bars + 15;       // [2] 128 arrivals: the softmax has read S (separate-P mode)
+  uint64_t* p_full = bars + 17;       // [2] 128 arrivals: P written (and O rescaled)
+  uint64_t* o_done = bars + 19;       // [2] the P.V of the last issued block has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_bh = a.B * a.H;
-  const int nqb = (int)cdiv(a.T, kBlockM);
-  const int n_tiles = n_bh * nqb;
+  const int npair = (int)cdiv(a.T, kTileM);
+  const int n_tiles = n_bh * npair;
   const int G = gridDim.x;
   int* err = a.err;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < KVST; ++s) {
       bar_init(&k_full[s], 1);
       bar_init(&v_full[s], 1);
       bar_init(&kv_empty[s], 1);
@@ -101,29 +123,33 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       bar_init(&q_full[s], 1);
       bar_init(&q_empty[s], 1);
     }
-    bar_init(s_full, 1);
-    bar_init(p_full, 128);
-    bar_init(o_full, 1);
+    for (int w = 0; w < 2; ++w) {
+      bar_init(&s_full[w], 1);
+      bar_init(&s_free[w], 128);
+      bar_init(&p_full[w], 128);
+      bar_init(&o_done[w], 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  if (warp == 1) tmem_alloc<512>(tmem_slot);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   struct Tile {
-    int b, h, q0, kvh, nkv, row0;
+    int b, h, q0, kvh, n[2], row0;
   };
   auto tile_of = [&](int t) {
     Tile x;
-    const int qb = nqb - 1 - t / n_bh;  // most key blocks first
+    const int pr = npair - 1 - t / n_bh;  // most key blocks first
     const int bh = t % n_bh;
     x.b = bh / a.H;
     x.h = bh % a.H;
-    x.q0 = qb * kBlockM;
+    x.q0 = pr * kTileM;
     x.kvh = x.h / (a.H / a.KV);
-    x.nkv = a.causal ? min(qb + 1, (int)cdiv(a.T, kBlockN)) : (int)cdiv(a.T, kBlockN);
+    x.n[0] = fwd_nkv(x.q0, 0, a.T, a.causal);
+    x.n[1] = fwd_nkv(x.q0, 1, a.T, a.causal);
     x.row0 = x.b * a.T;  // first packed row of this sequence
     return x;
   };
@@ -140,14 +166,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
         const int qs = tl % QST;
         if (!wait_bar(&q_empty[qs], ((tl / QST) & 1) ^ 1, err, 10)) break;
         const int qcol = x.h * HD, kcol = (a.H + x.kvh) * HD, vcol = (a.H + a.KV + x.kvh) * HD;
-        bar_arrive_expect_tx(&q_full[qs], L::Q_BYTES);
+        bar_arrive_expect_tx(&q_full[qs], 2 * L::QB_BYTES);
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c)
-          tma_load_2d(smem + L::Q_OFF + qs * L::Q_BYTES + c * 16384, &tm_qkv, &q_full[qs], qcol + c * 64,
-                      x.row0 + x.q0);
-        for (int j = 0; j < x.nkv; ++j, ++jj) {
-          const int s = jj % ST;
-          if (!wait_bar(&kv_empty[s], ((jj / ST) & 1) ^ 1, err, 11)) { ok = false; break; }
+        for (int hb = 0; hb < 2; ++hb)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(smem + L::Q_OFF + (qs * 2 + hb) * L::QB_BYTES + c * 16384, &tm_qkv, &q_full[qs],
+                        qcol + c * 64, x.row0 + x.q0 + hb * kBlockM);
+        const int nmax = max(x.n[0], x.n[1]);
+        for (int j = 0; j < nmax; ++j, ++jj) {
+          const int s = jj % KVST;
+          if (!wait_bar(&kv_empty[s], ((jj / KVST) & 1) ^ 1, err, 11)) { ok = false; break; }
           bar_arrive_expect_tx(&k_full[s], L::KV_BYTES);
 #pragma unroll
           for (int c = 0; c < HD / 64; ++c)
@@ -166,164 +195,217 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       constexpr uint32_t idesc_s = make_idesc_bf16(kBlockM, kBlockN, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(kBlockM, HD, false, true);
       int jj = 0, tl = 0;
+      int cnt[2] = {0, 0};  // blocks issued per half, over all tiles (barrier phases)
       bool ok = true;
+      // S_w = Q_w K^T into S columns of half w; waits until the half's previous S was read
+      // (separate P) or its previous P.V completed (P over S).
+      // g: the half's global block index of this S
+      auto issue_s = [&](int w, int g, uint32_t q_addr, uint32_t k_addr) -> bool {
+        if (g > 0) {
+          if (kSepP) {
+            if (!wait_bar(&s_free[w], (g - 1) & 1, err, 15)) return false;
+          } else {
+            if (!wait_bar(&o_done[w], (g - 1) & 1, err, 15)) return false;
+          }
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          mma_f16(tmem + c_s(w), make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024),
+                  idesc_s, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[w]);
+        return true;
+      };
       for (int r = 0; ok; ++r, ++tl) {
         const int t = fwd_snake(r, blockIdx.x, G);
         if (t >= n_tiles) break;
         const Tile x = tile_of(t);
         const int qs = tl % QST;
         if (!wait_bar(&q_full[qs], (tl / QST) & 1, err, 12)) break;
-        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + qs * L::Q_BYTES);
-        for (int j = 0; j < x.nkv; ++j, ++jj) {
-          const int s = jj % ST;
-          if (!wait_bar(&k_full[s], (jj / ST) & 1, err, 16)) { ok = false; break; }
-          // P_{jj-1} (aliasing S) must have been read by PV_{jj-1} before S_jj overwrites it.
-          if (jj > 0 && !wait_bar(o_full, (jj - 1) & 1, err, 17)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + L::K_OFF + s * L::KV_BYTES);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-            mma_f16(tmem, make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024), idesc_s,
-                    k > 0 ? 1u : 0u);
+        const uint32_t q_addr0 = smem_u32(smem + L::Q_OFF + (qs * 2) * L::QB_BYTES);
+        const uint32_t q_addr1 = q_addr0 + L::QB_BYTES;
+        const int nmax = max(x.n[0], x.n[1]);
+        // S of key block 0
+        {
+          const int s0 = jj % KVST;
+          if (!wait_bar(&k_full[s0], (jj / KVST) & 1, err, 16)) break;
+          const uint32_t k_addr = smem_u32(smem + L::K_OFF + s0 * L::KV_BYTES);
+          if (x.n[0] > 0) ok = issue_s(0, cnt[0], q_addr0, k_addr);
+          if (ok && x.n[1] > 0) ok = issue_s(1, cnt[1], q_addr1, k_addr);
+          if (!ok) break;
+          if (nmax == 1) mma_commit(&q_empty[qs]);
+        }
+        for (int j = 0; j < nmax && ok; ++j, ++jj) {
+          const int s = jj % KVST;
+          if (kSepP && j + 1 < nmax) {  // run the next block's scores ahead of this block's P.V
+            const int s1 = (jj + 1) % KVST;
+            if (!wait_bar(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
+            const uint32_t k_addr = smem_u32(smem + L::K_OFF + s1 * L::KV_BYTES);
+            if (j + 1 < x.n[0]) ok = issue_s(0, cnt[0] + 1, q_addr0, k_addr);
+            if (ok && j + 1 < x.n[1]) ok = issue_s(1, cnt[1] + 1, q_addr1, k_addr);
+            if (!ok) break;
+            if (j + 2 == nmax) mma_commit(&q_empty[qs]);  // the tile's last S has read its Q
           }
-          mma_commit(s_full);
-          if (j == x.nkv - 1) mma_commit(&q_empty[qs]);  // the tile's last S has read its Q
-          if (!wait_bar(&v_full[s], (jj / ST) & 1, err, 13)) { ok = false; break; }
-          if (!wait_bar(p_full, jj & 1, err, 14)) { ok = false; break; }
-          tc_fence_after();
+          if (!wait_bar(&v_full[s], (jj / KVST) & 1, err, 13)) { ok = false; break; }
           const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
 #pragma unroll
-          for (int k = 0; k < kBlockN / 16; ++k)
-            mma_f16_ts(tmem + C_O, tmem + k * 8, make_sw128_desc(v_addr + k * 2048, 16384, 1024), idesc_o,
-                       k > 0 ? 1u : 0u);
-          mma_commit(o_full);
+          for (int w = 0; w < 2; ++w) {
+            if (j >= (w ? x.n[1] : x.n[0])) continue;
+            if (!wait_bar(&p_full[w], cnt[w] & 1, err, 14)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < kBlockN / 16; ++k)
+              mma_f16_ts(tmem + c_o(w), tmem + c_p(w) + k * 8, make_sw128_desc(v_addr + k * 2048, 16384, 1024),
+                         idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+            mma_commit(&o_done[w]);
+            ++cnt[w];
+          }
+          if (!ok) break;
           mma_commit(&kv_empty[s]);
+          if (!kSepP && j + 1 < nmax) {  // P over S: the next S waits for this block's P.V
+            const int s1 = (jj + 1) % KVST;
+            if (!wait_bar(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
+            const uint32_t k_addr = smem_u32(smem + L::K_OFF + s1 * L::KV_BYTES);
+            if (j + 1 < x.n[0]) ok = issue_s(0, cnt[0], q_addr0, k_addr);
+            if (ok && j + 1 < x.n[1]) ok = issue_s(1, cnt[1], q_addr1, k_addr);
+            if (!ok) break;
+            if (j + 2 == nmax) mma_commit(&q_empty[qs]);
+          }
         }
       }
     }
   } else {
+    // softmax warpgroups: warps 2-5 -> half A, 6-9 -> half B; TMEM lane quadrant = warp % 4
+    const int w = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row within the block
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t t_s = tmem + lane_off;
+    const uint32_t t_s = tmem + lane_off + c_s(w);
+    const uint32_t t_o = tmem + lane_off + c_o(w);
+    const uint32_t t_p = tmem + lane_off + c_p(w);
     const float sl2 = a.scale_log2;
-    int jj = 0;
+    int cnt = 0;  // blocks of this half processed, over all tiles
     bool ok = true;
     for (int rr = 0; ok; ++rr) {
       const int t = fwd_snake(rr, blockIdx.x, G);
       if (t >= n_tiles) break;
       const Tile x = tile_of(t);
-      const int q = x.q0 + r;
-      const int q0 = x.q0;
-      float o_acc[HD];
-#pragma unroll
-      for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
-      float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-      for (int j = 0; j < x.nkv && ok; ++j, ++jj) {
-        if (!wait_bar(s_full, jj & 1, err, 19)) { ok = false; break; }
+      const int nkv = w ? x.n[1] : x.n[0];
+      if (nkv == 0) continue;
+      const int qb0 = x.q0 + w * kBlockM;
+      const int q = qb0 + r;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv; ++j, ++cnt) {
+        if (!wait_bar(&s_full[w], cnt & 1, err, 19)) { ok = false; break; }
         tc_fence_after();
+        uint32_t su[kBlockN];  // the row's scores (fp32 bits)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+        tmem_wait_ld();
+        if (kSepP) {
+          tc_fence_before();
+          bar_arrive(&s_free[w]);  // the next block's S may be computed now
+        }
         const int k0 = j * kBlockN;
         // keys allowed for this row: key < lim (causal: key <= q; always key < T)
         const int lim = a.causal ? min(q + 1, a.T) : a.T;
-        const bool need_mask = k0 + kBlockN > (a.causal ? q0 + 1 : a.T) || k0 + kBlockN > a.T;
-        // pass 1: row max, 8 independent chains
+        const bool need_mask = k0 + kBlockN > (a.causal ? qb0 + 1 : a.T) || k0 + kBlockN > a.T;
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < kBlockN; ++e)
+            if (k0 + e >= lim) su[e] = 0xff800000u;  // -inf
+        }
         float mx8[8];
-  #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
-  #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_s + c * 32, v);
-          tmem_wait_ld();
-          if (need_mask) {
-  #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = (k0 + c * 32 + e < lim) ? __uint_as_float(v[e]) : -INFINITY;
-              mx8[e & 7] = fmaxf(mx8[e & 7], x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(su[i]);
+#pragma unroll
+        for (int e = 8; e < kBlockN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(su[e]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+        // move the running max (and rescale O and l) only if it grew by more than 2^8 in some row
+        const bool grow = mx > m_used + kRescaleLog2;
+        const bool rescale = __any_sync(0xffffffffu, grow);
+        float alpha = 1.f;
+        if (rescale) {
+          const float m_new = fmaxf(m_used, mx);
+          alpha = ex2_approx(m_used - m_new);  // m_used = -inf on the first block -> 0
+          m_used = m_new;
+        }
+        const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+        // P = 2^(s * scale_log2 - m): three of every four on the SFU, one on the FMA pipe
+        float sum8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+        uint32_t pk[kBlockN / 2];
+#pragma unroll
+        for (int e = 0; e < kBlockN; e += 2) {
+          const float x0 = fmaf(__uint_as_float(su[e]), sl2, -msub), x1 = fmaf(__uint_as_float(su[e + 1]), sl2, -msub);
+          float p0, p1;
+          if ((e & 7) == 6) {
+            p0 = ex2_poly(x0);
+            p1 = ex2_poly(x1);
+            if (need_mask) {  // the polynomial does not map -inf to 0
+              p0 = su[e] == 0xff800000u ? 0.f : p0;
+              p1 = su[e + 1] == 0xff800000u ? 0.f : p1;
             }
           } else {
-  #pragma unroll
-            for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(v[e]));
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
           }
+          sum8[(e >> 1) & 7] += p0 + p1;
+          pk[e >> 1] = pack_bf16x2(p0, p1);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-        const float m_new = fmaxf(m, mx * sl2);
-        const float msub = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = ex2_approx(m - msub);  // m = -inf on the first block -> 0
-        // O'_{j-1} finished before S_j started (same MMA issue order), fold it in now.
-        if (j > 0) {
-          if (!wait_bar(o_full, (jj - 1) & 1, err, 18)) { ok = false; break; }
-          tc_fence_after();
-  #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(t_s + C_O + c * 32, v);
+        // The previous block's P.V has completed before O is rescaled or P rewritten: with P over S
+        // this block's S was issued after it; with separate P it is waited for here.
+        if (kSepP && j > 0 && !wait_bar(&o_done[w], (cnt - 1) & 1, err, 18)) { ok = false; break; }
+        tc_fence_after();
+        if (rescale && j > 0) {
+#pragma unroll
+          for (int c = 0; c < HD / 16; ++c) {
+            uint32_t v[16];
+            tmem_ld16(t_o + c * 16, v);
             tmem_wait_ld();
-  #pragma unroll
-            for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st16(t_o + c * 16, v);
           }
         }
-        // pass 2: P = 2^(s * scale_log2 - m_new) as bf16 over the consumed S columns, row sum
-        float sum8[8];
-  #pragma unroll
-        for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
-  #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_s + c * 32, v);
-          tmem_wait_ld();
-          float p[32];
-          if (need_mask) {
-  #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              p[e] = (k0 + c * 32 + e < lim) ? ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -msub)) : 0.f;
-          } else {
-  #pragma unroll
-            for (int e = 0; e < 32; ++e) p[e] = ex2_approx(fmaf(__uint_as_float(v[e]), sl2, -msub));
-          }
-          uint32_t pk[16];
-  #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            sum8[e & 7] += p[2 * e] + p[2 * e + 1];
-            pk[e] = pack_bf16x2(p[2 * e], p[2 * e + 1]);
-          }
-          tmem_st16(t_s + c * 16, pk);
-        }
+        l *= alpha;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_st16(t_p + c * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + c * 16));
         tmem_wait_st();
         tc_fence_before();
-        bar_arrive(p_full);
-        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
-        l = l * alpha + sum;
-        m = m_new;
-        alpha_prev = alpha;
+        bar_arrive(&p_full[w]);
+        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       }
-      // the tile's last O' is folded in after its PV
-      if (ok && x.nkv >= 1 && wait_bar(o_full, (jj - 1) & 1, err, 18)) {
-        tc_fence_after();
+      if (!ok) break;
+      // epilogue: the last P.V of the tile, then o = O / l and lse
+      if (!wait_bar(&o_done[w], (cnt - 1) & 1, err, 20)) { ok = false; break; }
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      bf16* orow = a.o + (int64_t)(x.row0 + min(q, a.T - 1)) * a.ld_o + x.h * HD;
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_s + C_O + c * 32, v);
-          tmem_wait_ld();
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_o + c * 32, v);
+        tmem_wait_ld();
+        if (q < a.T) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, __uint_as_float(v[e]));
+          for (int u = 0; u < 4; ++u) {
+            float tt[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) tt[e] = __uint_as_float(v[u * 8 + e]) * inv;
+            *reinterpret_cast<BF16x8*>(orow + c * 32 + u * 8) = float_to_bf16x8(tt);
+          }
         }
       }
-      if (ok && q < a.T) {
-        const float inv = (l > 0.f) ? 1.f / l : 0.f;
-        bf16* orow = a.o + (int64_t)(x.row0 + q) * a.ld_o + x.h * HD;
-#pragma unroll
-        for (int c = 0; c < HD / 8; ++c) {
-          float tt[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) tt[e] = o_acc[c * 8 + e] * inv;
-          *reinterpret_cast<BF16x8*>(orow + c * 8) = float_to_bf16x8(tt);
-        }
-        // natural-log lse of the scaled scores: (m + log2 l) / log2(e)
-        a.lse[((int64_t)x.b * a.H + x.h) * a.T + q] = (l > 0.f) ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
-      }
+      tc_fence_before();  // O may be overwritten by the next tile's first P.V after p_full
+      // natural-log lse of the scaled scores: (m + log2 l) / log2(e)
+      if (q < a.T)
+        a.lse[((int64_t)x.b * a.H + x.h) * a.T + q] = (l > 0.f) ? (m_used + log2f(l)) * 0.69314718055994530942f
+                                                               : -INFINITY;
     }
   }
   pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
@@ -331,12 +413,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<TMEM_COLS>(tmem);
+    tmem_dealloc<512>(tmem);
   }
 }
 
 template <int HD>
-cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb, cudaStream_t st) {
+cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
   auto kern = flash_fwd_kernel<HD>;
   constexpr size_t smem = FwdSmem<HD>::TOTAL;
   static bool attr = false;
@@ -345,8 +427,8 @@ cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, int nqb, 
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = args.B * args.H * nqb;
-  launch_pdl(kern, std::min(tiles, 2 * persistent_sms()), kAttnThreads, smem, st, tm, args);
+  const int tiles = args.B * args.H * (int)cdiv(args.T, kTileM);
+  launch_pdl(kern, std::min(tiles, persistent_sms()), kAttnThreads, smem, st, tm, args);
   return cudaGetLastError();
 }
 
@@ -390,8 +472,7 @@ cudaError_t flash_attn_fwd(const void* qkv, int64_t ld_qkv, void* o, float* lse,
   LLMT_REQUIRE(make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd,
                             (uint64_t)B * T, ld_qkv, 64, 128),
                "flash_attn_fwd: tensor map rejected");
-  const int nqb = (int)cdiv(T, kBlockM);
-  return hd == 64 ? launch_fwd<64>(tm, args, nqb, st) : launch_fwd<128>(tm, args, nqb, st);
+  return hd == 64 ? launch_fwd<64>(tm, args, st) : launch_fwd<128>(tm, args, st);
 }
 
 }  // namespace llmt

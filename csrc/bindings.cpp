@@ -502,6 +502,21 @@ void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor mas
      "dp_fused_adamw");
 }
 
+void dp_nvls_adamw(int64_t g_mc, int64_t w_mc, at::Tensor master, at::Tensor m, at::Tensor v, int64_t lo, int64_t n,
+                   at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale,
+                   int64_t max_blocks) {
+  on_device(master, "master");
+  on_device(m, "m");
+  on_device(v, "v");
+  CHECK(g_mc != 0 && w_mc != 0, "dp_nvls_adamw: multicast addresses are null (no NVLS support)");
+  CHECK(m.numel() >= n && v.numel() >= n && master.numel() >= lo + n, "shard bounds exceed the buffers");
+  llmt::AdamHyper h{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
+  ok(llmt::dp_nvls_adamw(reinterpret_cast<const void*>(g_mc), reinterpret_cast<void*>(w_mc), master.data_ptr<float>(),
+                         m.data_ptr<float>(), v.data_ptr<float>(), lo, n, lr.data_ptr<float>(), step.data_ptr<int>(), h,
+                         stream(), (int)max_blocks),
+     "dp_nvls_adamw");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -576,4 +591,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_fused_adamw", &dp_fused_adamw, "grads_dev"_a, "shadows_dev"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a,
         "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "world"_a, "max_blocks"_a = 0);
   m.def("dp_error_code", &llmt::dp_error_code, "reset"_a = false);
+  m.def("dp_nvls_adamw", &dp_nvls_adamw, "g_mc"_a, "w_mc"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a, "lr"_a, "step"_a,
+        "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "max_blocks"_a = 0);
 }

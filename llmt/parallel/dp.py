@@ -10,11 +10,14 @@ Here it runs. Per step, after the backward:
   3. all-gather the bf16 shadow shards -> every rank has the full bf16 weights for the next
      forward (this is the bf16 "parameter all-gather"; fp32 masters stay sharded)
 
-Two transports, same math:
-  mode="nccl"   NCCL reduce_scatter_tensor / all_gather_into_tensor (the baseline path);
+Transports, same math:
+  mode="nvls"   the gradient cast to bf16, then one sm_100a kernel that reduces this rank's
+                shard inside the NVSwitch (multimem.ld_reduce), applies AdamW and multicasts the
+                new bf16 weights to every rank (multimem.st) (llmt.parallel.nvls_dp);
   mode="fused"  one sm_100a kernel per step over NVLink peer memory that reads every peer's
-                gradient shard, sums, applies AdamW and stores the new bf16 shard into every
-                peer's shadow buffer (llmt.parallel.fused_dp), with bounded device-side waits.
+                fp32 gradient shard, sums, applies AdamW and stores the new bf16 shard into
+                every peer's shadow buffer (llmt.parallel.fused_dp), with bounded device-side waits;
+  mode="nccl"   NCCL reduce_scatter_tensor / all_gather_into_tensor (the baseline path).
 
 Every rank takes the same collective steps in the same order (warm-up, capture and replay).
 """
@@ -53,8 +56,9 @@ class ShardedAdamW:
 
 class DataParallel:
     def __init__(self, world_size: int, rank: int, mode: str = "nccl", group=None):
-        """mode: "nccl" (reduce-scatter / all-gather), "fused" (one peer-memory kernel after the
-        backward) or "fused-overlap" (that kernel per bucket, overlapped with the backward)."""
+        """mode: "nvls" (bf16 cast + one multicast kernel after the backward), "nccl"
+        (reduce-scatter / all-gather), "fused" (one peer-memory kernel after the backward) or
+        "fused-overlap" (that kernel per bucket, overlapped with the backward)."""
         self.world_size, self.rank, self.mode, self.group = world_size, rank, mode, group
         # False when the model's gradient writers store on the step's first write (the NCCL
         # step then skips clearing the buffer; the fused kernels clear what they read anyway)
@@ -92,6 +96,9 @@ class DataParallel:
         if self.mode == "fused":
             from llmt.parallel.fused_dp import FusedDP
             self.fused = FusedDP(flat, opt, self.rank, self.world_size, self.group)
+        elif self.mode == "nvls":
+            from llmt.parallel.nvls_dp import NvlsDP
+            self.fused = NvlsDP(flat, opt, self.rank, self.world_size, self.group)
         return opt
 
     def begin_step(self):

@@ -1,0 +1,81 @@
+"""Data-parallel step on NVLink multicast (host side of csrc/comm/dp_nvls.cu).
+
+Replaces NCCL reduce_scatter + sharded AdamW + all_gather (llmt.parallel.dp, mode "nccl") by
+a bf16 cast of the gradient and one fused kernel per step:
+
+  cast      the flat fp32 gradient the backward wrote -> a symmetric bf16 buffer (local)
+  barrier   every rank's cast is complete (flag barrier over peer memory, bounded)
+  fused     multimem.ld_reduce of this rank's gradient shard (summed in the NVSwitch, fp32
+            accumulation), AdamW on the fp32 master shard, multimem.st of the new bf16 weights
+            into every rank's weight buffer
+  barrier   every rank's weights are written before any rank's next forward reads them
+
+Set-up uses PyTorch's symmetric memory (torch.distributed._symmetric_memory) for the plumbing:
+the bf16 gradient buffer, the bf16 weight buffer (which becomes the model's shadow weights) and
+a small flag pad are symmetric allocations, and the rendezvous binds the first two to NVLink
+multicast objects; the kernel only receives their multicast addresses. Ranks that cannot get a
+multicast address (no NVSwitch, or a single GPU) raise at set-up.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from llmt.ops import native as N
+
+
+def _symm():
+    import torch.distributed._symmetric_memory as symm
+    return symm
+
+
+class NvlsDP:
+    def __init__(self, flat, opt, rank: int, world: int, group=None):
+        self.flat, self.opt, self.rank, self.world = flat, opt, rank, world
+        self.group = group if group is not None else dist.group.WORLD
+        symm = _symm()
+        dev = flat.master.device
+        self.device = dev
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            try:
+                symm.enable_symm_mem_for_group(self.group.group_name)
+            except Exception:  # noqa: BLE001 - newer releases need no registration
+                pass
+        self.g16 = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
+        shadow = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
+        shadow.copy_(flat.shadow)
+        flat.rebind(grad=flat.grad, shadow=shadow)
+        self.pad = symm.empty(64 * world, dtype=torch.int32, device=dev)
+        self.pad.zero_()
+        torch.cuda.synchronize(dev)
+        self.h_g = symm.rendezvous(self.g16, self.group)
+        self.h_w = symm.rendezvous(flat.shadow, self.group)
+        self.h_p = symm.rendezvous(self.pad, self.group)
+        if not self.h_g.multicast_ptr or not self.h_w.multicast_ptr:
+            raise RuntimeError("NVLS data parallelism needs NVLink multicast (symmetric memory reported none)")
+        self.g_mc = self.h_g.multicast_ptr + (self.g16.data_ptr() - self.h_g.buffer_ptrs[rank])
+        self.w_mc = self.h_w.multicast_ptr + (flat.shadow.data_ptr() - self.h_w.buffer_ptrs[rank])
+        off = self.pad.data_ptr() - self.h_p.buffer_ptrs[rank]
+        self.pads_dev = torch.tensor([p + off for p in self.h_p.buffer_ptrs], dtype=torch.int64, device=dev)
+        self.my_pad = self.pad.data_ptr()
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    @torch.no_grad()
+    def step(self):
+        C, o, f = N.ext(), self.opt, self.flat
+        C.cast_bf16(f.grad, self.g16)
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 300)
+        o.step_t.add_(1)
+        b1, b2 = o.betas
+        C.dp_nvls_adamw(self.g_mc, self.w_mc, f.master, o.exp_avg, o.exp_avg_sq, o.lo, o.hi - o.lo, o.lr_t, o.step_t,
+                        b1, b2, o.eps, o.weight_decay, o.grad_scale)
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 400)
+
+    def error_code(self, reset=False) -> int:
+        return N.ext().dp_error_code(reset)
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)

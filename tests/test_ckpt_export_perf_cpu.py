@@ -132,3 +132,24 @@ def test_astra_inputs_and_acceptance(tmp_path):
     assert ok and ticks == {0: 100, 1: 100}
     ok, _ = accept("sys[0] finished, 100 cycles\nsys[1] finished, 90 cycles", 2)
     assert not ok
+
+
+def test_execution_trace_cross_check_matches_inventory(tmp_path):
+    """A real PyTorch execution trace of one step (tiny256, CPU fp32) has the GEMM shapes, the
+    forward GEMM order and the attention calls that the step inventory lists."""
+    from llmt.config import get_config
+    from llmt.export.observe import cross_check
+    res = cross_check(get_config("tiny256"), 2, 64, "cpu", et_path=str(tmp_path / "et.json"))
+    assert res["gemm_multiset_match"], res
+    assert res["forward_order_match"]
+    assert res["attention"]["trace"] == res["attention"]["inventory"] == [4, 4]
+    assert res["pass"]
+
+
+def test_official_chakra_decoder_check_skips_or_passes(tmp_path):
+    from llmt.config import get_config
+    from llmt.export.observe import official_decode
+    from llmt.export.trace import export
+    export(get_config("tiny256"), 1, 64, 2, 1, 2, 2, outdir=str(tmp_path))
+    res = official_decode(str(tmp_path))
+    assert res["status"] in ("skipped", "pass"), res
