@@ -28,6 +28,10 @@ __global__ void swiglu_fwd_kernel(const bf16* __restrict__ g, const bf16* __rest
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / vec_per_row;
     const int c = (int)(i % vec_per_row) * 8;
+    // the last row ends F columns after its start: extents of the strided g / u / h views
+    if (!LLMT_IN(r * ldgu + c, r * ldgu + c + 8, (rows - 1) * ldgu + F, 201) ||
+        !LLMT_IN(r * ldh + c, r * ldh + c + 8, (rows - 1) * ldh + F, 202))
+      continue;
     float gf[8], uf[8], o[8];
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(g + r * ldgu + c), gf);
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(u + r * ldgu + c), uf);
@@ -46,6 +50,10 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dh, int64_t lddh, con
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / vec_per_row;
     const int c = (int)(i % vec_per_row) * 8;
+    if (!LLMT_IN(r * ldgu + c, r * ldgu + c + 8, (rows - 1) * ldgu + F, 203) ||
+        !LLMT_IN(r * lddh + c, r * lddh + c + 8, (rows - 1) * lddh + F, 204) ||
+        !LLMT_IN(r * lddgu + c, r * lddgu + c + 8, (rows - 1) * lddgu + F, 205))
+      continue;
     float gf[8], uf[8], d[8], og[8], ou[8];
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(g + r * ldgu + c), gf);
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(u + r * ldgu + c), uf);
@@ -76,6 +84,12 @@ __global__ void rope_kernel(bf16* __restrict__ qkv, const float* __restrict__ co
     const int64_t n = rest / n_rot_heads;
     const int t = (int)(n % T);
     bf16* base = qkv + n * ld + (int64_t)h * hd;
+    // the rotated heads of the last row end n_rot_heads * hd columns after its start; the
+    // tables hold T rows of hd
+    if (!LLMT_IN(n * ld + (int64_t)h * hd + c, n * ld + (int64_t)h * hd + half + c + 8,
+                 (N - 1) * ld + (int64_t)n_rot_heads * hd, 210) ||
+        !LLMT_IN((int64_t)t * hd + c, (int64_t)t * hd + half + c + 8, (int64_t)T * hd, 211))
+      continue;
     float x1[8], x2[8], y1[8], y2[8];
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(base + c), x1);
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(base + half + c), x2);
@@ -117,6 +131,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const floa
       if (err) atomicExch(err, 1);  // record and clamp instead of reading out of bounds
       tok = 0;
     }
+    if (!LLMT_IN(tok * d + c, tok * d + c + 4, V * d, 220) || !LLMT_IN(n * d + c, n * d + c + 4, N * d, 221)) continue;
     st_f4(x + n * d + c, ld_f4(W + tok * d + c));
   }
 }
@@ -131,6 +146,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const floa
     const int c = (int)(i % vpr) * 4;
     const int64_t tok = idx[n] - v0;
     if (tok < 0 || tok >= V) continue;
+    if (!LLMT_IN(tok * d + c, tok * d + c + 4, V * d, 222) || !LLMT_IN(n * d + c, n * d + c + 4, N * d, 223)) continue;
     atomicAdd(reinterpret_cast<float4*>(dW + tok * d + c), ld_f4(dx + n * d + c));
   }
 }

@@ -18,6 +18,15 @@ int sm_count();
 void set_reserved_sms(int n);
 int reserved_sms();
 int persistent_sms();
+// Bounds-checked build: each translation unit registers the reader of its out-of-range record;
+// bounds_error() returns the first non-zero record (bit 63 | site << 40 | index) or 0, and
+// bounds_checking() says whether this module was built with the checks.
+int register_bounds_reader(unsigned long long (*reader)(bool reset));
+unsigned long long bounds_error(bool reset);
+bool bounds_checking();
+#ifdef LLMT_DEBUG_BOUNDS
+cudaError_t bounds_probe(float* buf, int64_t n, int64_t i, cudaStream_t st);  // common/bounds_probe.cu
+#endif
 
 // ---------------------------------------------------------------- RMSNorm
 cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, void* y_bf16, float* s, float* rstd,

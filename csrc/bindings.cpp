@@ -517,6 +517,17 @@ void dp_nvls_adamw(int64_t g_mc, int64_t w_mc, at::Tensor master, at::Tensor m, 
      "dp_nvls_adamw");
 }
 
+#ifdef LLMT_DEBUG_BOUNDS
+// Self-test of the bounds-checked build: a store at index `i` of an n-float buffer, guarded by
+// LLMT_IN. With i >= n the guard records the site and skips the store (nothing is written out
+// of bounds); the record is read back with bounds_error(). Only this build has it.
+void bounds_probe(at::Tensor buf, int64_t i) {
+  on_device(buf, "buf");
+  CHECK_DT(buf, at::kFloat);
+  ok(llmt::bounds_probe(buf.data_ptr<float>(), buf.numel(), i, stream()), "bounds_probe");
+}
+#endif
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -591,6 +602,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_fused_adamw", &dp_fused_adamw, "grads_dev"_a, "shadows_dev"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a,
         "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "world"_a, "max_blocks"_a = 0);
   m.def("dp_error_code", &llmt::dp_error_code, "reset"_a = false);
+  m.def("bounds_error", &llmt::bounds_error, "reset"_a = false);
+  m.def("bounds_checking", &llmt::bounds_checking);
+#ifdef LLMT_DEBUG_BOUNDS
+  m.def("bounds_probe", &bounds_probe, "buf"_a, "i"_a);
+#endif
   m.def("dp_nvls_adamw", &dp_nvls_adamw, "g_mc"_a, "w_mc"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a, "lr"_a, "step"_a,
         "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "max_blocks"_a = 0);
 }

@@ -45,6 +45,7 @@ ce_fwd_rows_kernel(const bf16* __restrict__ logits, int64_t ld, const int64_t* _
   const bf16* row = logits + r * ld;
   float m = -INFINITY, s = 0.f;
   for (int c = threadIdx.x * 8; c < V; c += kCeThreads * 8) {
+    if (!LLMT_IN(r * ld + c, r * ld + c + 8, (int64_t)(gridDim.x - 1) * ld + V, 301)) continue;
     float f[8];
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(row + c), f);
     float mx = f[0];
@@ -74,6 +75,7 @@ ce_bwd_rows_kernel(bf16* __restrict__ logits, int64_t ld, const int64_t* __restr
   const float g = scale * (grad_out ? *grad_out : 1.f);
   const int64_t t = tgt[r];
   for (int c = threadIdx.x * 8; c < V; c += kCeThreads * 8) {
+    if (!LLMT_IN(r * ld + c, r * ld + c + 8, (int64_t)(gridDim.x - 1) * ld + V, 302)) continue;
     float f[8];
     bf16x8_to_float(*reinterpret_cast<const BF16x8*>(row + c), f);
 #pragma unroll

@@ -39,6 +39,10 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const uint4* __restri
     const int64_t r = i / d16;
     const int c = (int)(i - r * d16);
     const int64_t q = r / n;
+    // every slot buffer holds tp * n rows: the same extent as the source
+    if (!LLMT_IN(((int64_t)rank * n + (r - q * n)) * d16 + c, ((int64_t)rank * n + (r - q * n)) * d16 + c + 1,
+                 total16, 501))
+      continue;
     uint4* dst = reinterpret_cast<uint4*>(slots[q]) + ((int64_t)rank * n + (r - q * n)) * d16 + c;
     __stcg(dst, __ldg(src + i));
   }

@@ -88,6 +88,39 @@ inline T* device_symbol_address(std::atomic<T*> (&slots)[64], const T& symbol) {
   return p;
 }
 
+// ---------------------------------------------------------------- bounds-checked debug build
+// Built with -DLLMT_DEBUG_BOUNDS=1 (the llmt._C_bounds module), every guarded global access
+// first checks that the element range [lo, hi) it touches lies inside [0, n) of the buffer
+// the launcher described. A range outside records the site and the first index in this
+// translation unit's device word (first failure wins) and the access is skipped: nothing is
+// read or written out of bounds, nothing traps, and the host reads the record with
+// bounds_error(). In the release build LLMT_IN is `true` and compiles away.
+#ifdef LLMT_DEBUG_BOUNDS
+namespace bounds_detail {
+static __device__ unsigned long long g_record = 0;  // one per translation unit
+// bit 63 set | site << 40 | low 40 bits of the first index
+static unsigned long long read_record(bool reset) {
+  unsigned long long v = 0;
+  cudaMemcpyFromSymbol(&v, g_record, sizeof(v));
+  if (reset && v) {
+    const unsigned long long z = 0;
+    cudaMemcpyToSymbol(g_record, &z, sizeof(z));
+  }
+  return v;
+}
+static const int registered = ::llmt::register_bounds_reader(&read_record);
+}  // namespace bounds_detail
+__device__ __forceinline__ bool llmt_in_bounds(int64_t lo, int64_t hi, int64_t n, int site) {
+  if (lo >= 0 && hi <= n && lo <= hi) return true;
+  atomicCAS(&bounds_detail::g_record, 0ull,
+            (1ull << 63) | ((unsigned long long)(site & 0x7fffff) << 40) | ((unsigned long long)lo & 0xffffffffffull));
+  return false;
+}
+#define LLMT_IN(lo, hi, n, site) ::llmt::llmt_in_bounds((int64_t)(lo), (int64_t)(hi), (int64_t)(n), (site))
+#else
+#define LLMT_IN(lo, hi, n, site) true
+#endif
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Kernels on the training path are launched with programmatic stream serialisation: a kernel's
 // CTAs may be scheduled while the previous kernel in the stream drains, and each kernel calls

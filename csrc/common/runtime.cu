@@ -35,4 +35,31 @@ static std::atomic<int> g_reserved_sms{0};
 void set_reserved_sms(int n) { g_reserved_sms.store(n < 0 ? 0 : n); }
 int reserved_sms() { return g_reserved_sms.load(); }
 int persistent_sms() { return std::max(1, sm_count() - g_reserved_sms.load()); }
+
+namespace {
+std::atomic<int> g_n_readers{0};
+unsigned long long (*g_readers[64])(bool) = {nullptr};
+}  // namespace
+// Called during static initialisation of each instrumented translation unit.
+int register_bounds_reader(unsigned long long (*reader)(bool)) {
+  const int i = g_n_readers.fetch_add(1);
+  if (i < 64) g_readers[i] = reader;
+  return i;
+}
+unsigned long long bounds_error(bool reset) {
+  unsigned long long first = 0;
+  const int n = std::min(64, g_n_readers.load());
+  for (int i = 0; i < n; ++i) {
+    const unsigned long long v = g_readers[i](reset);
+    if (v && !first) first = v;
+  }
+  return first;
+}
+bool bounds_checking() {
+#ifdef LLMT_DEBUG_BOUNDS
+  return true;
+#else
+  return false;
+#endif
+}
 }  // namespace llmt

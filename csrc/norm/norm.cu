@@ -59,7 +59,7 @@ add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, 
 #pragma unroll
   for (int c = 0; c < kMaxChunks; ++c) {
     const int e = (c * TPR + t) * 8;
-    if (valid && e < D) {
+    if (valid && e < D && LLMT_IN(row * D + e, row * D + e + 8, N * D, 101)) {
       const int64_t off = row * D + e;
       float4 r0 = ld_f4(r + off), r1 = ld_f4(r + off + 4);
       v[c][0] = r0.x; v[c][1] = r0.y; v[c][2] = r0.z; v[c][3] = r0.w;
@@ -80,7 +80,7 @@ add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, 
 #pragma unroll
   for (int c = 0; c < kMaxChunks; ++c) {
     const int e = (c * TPR + t) * 8;
-    if (e < D) {
+    if (e < D && LLMT_IN(row * D + e, row * D + e + 8, N * D, 102) && LLMT_IN(e, e + 8, D, 103)) {
       const int64_t off = row * D + e;
       if constexpr (WRITE_S) {
         st_f4(s_out + off, make_float4(v[c][0], v[c][1], v[c][2], v[c][3]));
@@ -94,7 +94,7 @@ add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, 
       *reinterpret_cast<BF16x8*>(y + off) = float_to_bf16x8(o);
     }
   }
-  if (t == 0) rstd_out[row] = rstd;
+  if (t == 0 && LLMT_IN(row, row + 1, N, 104)) rstd_out[row] = rstd;
 }
 
 // dy bf16, s fp32, ds_in fp32 (optional); ds fp32 and ds16 bf16 (optional) out.
@@ -124,11 +124,11 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
     const int64_t row = it * stride + (int64_t)blockIdx.x * RPC + rgroup;
     const bool valid = row < N;
     float dot = 0.f;
-    const float rs = valid ? rstd_in[row] : 0.f;
+    const float rs = (valid && LLMT_IN(row, row + 1, N, 110)) ? rstd_in[row] : 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       const int e = (c * TPR + t) * 8;
-      if (valid && e < D) {
+      if (valid && e < D && LLMT_IN(row * D + e, row * D + e + 8, N * D, 111) && LLMT_IN(e, e + 8, D, 112)) {
         const int64_t off = row * D + e;
         if constexpr (HAS_DSIN) {
           // the second pass adds ds_in after the row reduction: start its DRAM fetch now so that
@@ -155,7 +155,7 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
 #pragma unroll
       for (int c = 0; c < kMaxChunks; ++c) {
         const int e = (c * TPR + t) * 8;
-        if (e < D) {
+        if (e < D && LLMT_IN(row * D + e, row * D + e + 8, N * D, 113) && LLMT_IN(e, e + 8, D, 114)) {
           const int64_t off = row * D + e;
           float dyf[8];
           bf16x8_to_float(*reinterpret_cast<const BF16x8*>(dy + off), dyf);
@@ -196,7 +196,8 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
     float a = 0.f;
 #pragma unroll
     for (int rg = 0; rg < RPC; ++rg) a += sdw[rg * D + i];
-    dw_part[(int64_t)blockIdx.x * D + i] = a;
+    if (LLMT_IN((int64_t)blockIdx.x * D + i, (int64_t)blockIdx.x * D + i + 1, (int64_t)gridDim.x * D, 115))
+      dw_part[(int64_t)blockIdx.x * D + i] = a;
   }
   pdl_trigger();
 }
@@ -212,7 +213,8 @@ dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, 
   const int col = blockIdx.x * kRedCols + threadIdx.x;
   float a = 0.f;
   if (col < D)
-    for (int p = threadIdx.y; p < P; p += kRedGroups) a += part[(int64_t)p * D + col];
+    for (int p = threadIdx.y; p < P; p += kRedGroups)
+      if (LLMT_IN((int64_t)p * D + col, (int64_t)p * D + col + 1, (int64_t)P * D, 120)) a += part[(int64_t)p * D + col];
   acc[threadIdx.y][threadIdx.x] = a;
   __syncthreads();
 #pragma unroll
@@ -220,7 +222,7 @@ dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int P, 
     if (threadIdx.y < h) acc[threadIdx.y][threadIdx.x] += acc[threadIdx.y + h][threadIdx.x];
     __syncthreads();
   }
-  if (threadIdx.y == 0 && col < D) dw[col] = accumulate ? dw[col] + acc[0][threadIdx.x] : acc[0][threadIdx.x];
+  if (threadIdx.y == 0 && col < D && LLMT_IN(col, col + 1, D, 121)) dw[col] = accumulate ? dw[col] + acc[0][threadIdx.x] : acc[0][threadIdx.x];
   pdl_trigger();
 }
 

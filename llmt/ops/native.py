@@ -7,6 +7,7 @@ of silently falling back to PyTorch.
 """
 from __future__ import annotations
 
+import os
 from typing import NamedTuple, Optional
 
 import torch
@@ -20,7 +21,7 @@ EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_BWD, EPI_ROPE, EPI_CE_FWD, EPI_CE_BWD 
 _KERNELS_PER_CALL = {"flash_attn_bwd": 3, "gemm_error_code": 0, "attn_error_code": 0, "dp_error_code": 0,
                      "set_reserved_sms": 0, "reserved_sms": 0,
                      "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0, "ipc_free": 0, "tensor_from_ptr": 0,
-                     "sm_count": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0, "gemm_plan": 0}
+                     "sm_count": 0, "bounds_error": 0, "bounds_checking": 0, "fp8_quant": 2, "fp8_amax_slots": 0, "mx_sf_bytes": 0, "gemm_plan": 0}
 
 
 class LaunchCounter:
@@ -63,7 +64,10 @@ def ext():
     global _C
     if _C is None:
         try:
-            from llmt import _C as c  # noqa: PLC0415
+            if os.environ.get("LLMT_BOUNDS") == "1":  # the bounds-checked build (debug)
+                from llmt import _C_bounds as c  # noqa: PLC0415
+            else:
+                from llmt import _C as c  # noqa: PLC0415
         except ImportError as e:  # pragma: no cover - depends on the build
             raise RuntimeError(
                 "llmt native extension is not built; run `python setup.py build_ext --inplace` "
