@@ -12,7 +12,9 @@ and runs the same 1F1B order (llmt.export.trace.schedule_1f1b, shared with the e
 
 A forward send and the backward receive that follows it (and a backward send with the next
 forward receive) go out as one batched NCCL group (batch_isend_irecv): issued one after the
-other, two neighbouring stages would each block in a send to the other. The stage boundary
+other, two neighbouring stages would each block in a send to the other. Groups that only send
+(the warm-up forwards, the last backward) are not waited for on the compute stream: the next
+micro-batch's compute overlaps the transfer, and the step waits for them at its end. The stage boundary
 carries what the block stack carries: the native path's (pending branch output bf16, fp32
 residual) pair, the reference-math path's fp32 residual. Tensor parallelism composes: each
 stage is itself sharded over its tensor-parallel group and sends its sequence rows to the
@@ -210,16 +212,33 @@ class Pipeline1F1B:
         self.x, self.s, self.pp = executor, stage_idx, pp
         self.prev, self.next, self.group, self.device = prev, nxt, pp_group, torch.device(device)
         self.first, self.last = stage_idx == 0, stage_idx == pp - 1
+        self._inflight = []  # send-only groups not waited for yet: (requests, tensors)
 
     def _empty(self, rows):
         return [torch.empty(shape, dtype=dt, device=self.device) for shape, dt in self.x.act_specs(rows)]
 
     def _batch(self, sends, recvs, peer_send, peer_recv):
-        ops = [dist.P2POp(dist.isend, t.contiguous(), peer_send, self.group) for t in sends]
+        """One NCCL group of sends to peer_send and receives from peer_recv. A group with receives
+        is waited for (the compute stream needs their data next); a send-only group is not: the
+        compute stream goes on with the next micro-batch while the transfer runs, and the group
+        is waited for at the end of the step (its tensors are kept alive until then)."""
+        sends = [t.contiguous() for t in sends]
+        ops = [dist.P2POp(dist.isend, t, peer_send, self.group) for t in sends]
         ops += [dist.P2POp(dist.irecv, t, peer_recv, self.group) for t in recvs]
-        if ops:
-            for req in dist.batch_isend_irecv(ops):
+        if not ops:
+            return
+        reqs = dist.batch_isend_irecv(ops)
+        if recvs:
+            for req in reqs:
                 req.wait()
+        else:
+            self._inflight.append((reqs, sends))
+
+    def _drain(self):
+        for reqs, _ in self._inflight:
+            for req in reqs:
+                req.wait()
+        self._inflight.clear()
 
     def step(self, idx, tgt):
         """idx, tgt: (m, mb, T) micro-batches of this data-parallel rank."""
@@ -315,4 +334,5 @@ class Pipeline1F1B:
             self.order.append(("B", j))
             send_bwd(bwd(j, recv_bwd()))
         assert self.order == schedule_1f1b(self.s, self.pp, m_count)
+        self._drain()
         return torch.stack(losses).mean() if self.last else None
