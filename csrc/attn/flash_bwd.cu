@@ -635,21 +635,19 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const bool key_ok = kk < a.T;
         const int q_lo = (a.causal && qbase < x.k0 + kBM) ? kk - qbase : 0;
         const int q_hi = key_ok ? min(kBN, a.T - qbase) : 0;
-        // this warp's 64 columns of S^T and dP^T into registers, then the columns are released
-        uint32_t sv2[2][32], dv2[2][32];
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          tmem_ld32(tmem + lane_off + C_S + (half * 2 + cc) * 32, sv2[cc]);
-          tmem_ld32(tmem + lane_off + C_DP + (half * 2 + cc) * 32, dv2[cc]);
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        bar_arrive(st_read);
-#pragma unroll
+        // this warp's 64 columns of S^T and dP^T, 32 at a time; after the second chunk is in
+        // registers the columns are released, so the next block's S^T / dP^T MMAs can start
+#pragma unroll 1
         for (int cc = 0; cc < 2; ++cc) {
           const int c = half * 2 + cc;
-          const uint32_t(&sv)[32] = sv2[cc];
-          const uint32_t(&dv)[32] = dv2[cc];
+          uint32_t sv[32], dv[32];
+          tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
+          tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
+          tmem_wait_ld();
+          if (cc == 1) {
+            tc_fence_before();
+            bar_arrive(st_read);
+          }
           const int lo = q_lo - c * 32, hi = q_hi - c * 32;
           const float4* l4 = reinterpret_cast<const float4*>(lse_s + c * 32);
           const float4* d4 = reinterpret_cast<const float4*>(d_s + c * 32);
