@@ -381,6 +381,10 @@ static_assert(BwdSmemP::TOTAL <= 232448, "pipelined attention backward exceeds 2
 // run while the compute warps finish the previous tile's dK / dV epilogue.
 __device__ __forceinline__ int snake_tile(int r, int i, int G) { return r * G + ((r & 1) ? (G - 1 - i) : i); }
 
+// VARIANT 0: the kernel; 2: a timing skeleton with the P / dS arithmetic replaced by copies
+// (wrong results; it measures the MMA / TMA / barrier structure alone), chosen at run time with
+// LLMT_ATTN_VARIANT for measurements only.
+template <int VARIANT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                            const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
@@ -659,6 +663,11 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int e = 4 * g4 + q;
+              if (VARIANT == 2) {
+                p[e] = __uint_as_float(sv[e]);
+                ds[e] = __uint_as_float(dv[e]);
+                continue;
+              }
               float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -la[q] * kLog2e));
               pe = (e >= lo && e < hi) ? pe : 0.f;
               p[e] = pe;
@@ -823,19 +832,30 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
-                                 const AttnBwdArgs& args, cudaStream_t st) {
+template <int VARIANT>
+cudaError_t launch_bwd_pipelined_v(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
+                                   const AttnBwdArgs& args, cudaStream_t st) {
   constexpr size_t smem = BwdSmemP::TOTAL;
+  auto kern = flash_bwd_pipelined_kernel<VARIANT>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(flash_bwd_pipelined_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   const int tiles = args.B * args.KV * (int)cdiv(args.T, kBM);
-  launch_pdl(flash_bwd_pipelined_kernel, std::min(tiles, persistent_sms()), kBwdThreads, smem, st, tq, tdo, tdq, args);
+  launch_pdl(kern, std::min(tiles, persistent_sms()), kBwdThreads, smem, st, tq, tdo, tdq, args);
   return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
+                                 const AttnBwdArgs& args, cudaStream_t st) {
+  static const int variant = [] {
+    const char* e = getenv("LLMT_ATTN_VARIANT");
+    return e ? atoi(e) : 0;
+  }();
+  return variant == 2 ? launch_bwd_pipelined_v<2>(tq, tdo, tdq, args, st)
+                      : launch_bwd_pipelined_v<0>(tq, tdo, tdq, args, st);
 }
 
 }  // namespace

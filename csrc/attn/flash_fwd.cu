@@ -17,9 +17,9 @@
 //              the next block's S is issued as soon as the softmax has read this block's S
 //              out of TMEM, so score MMAs run ahead of the softmax
 //   warps 2-5  softmax of block A, warps 6-9 of block B: one thread per query row holds the
-//              row's 128 scores in registers; row max, P = 2^(S*scale*log2e - m) split
-//              between the SFU (ex2.approx) and an FMA-pipe polynomial, row sum, P packed to
-//              bf16 into TMEM. O stays in TMEM: the running max is only moved (and O, l
+//              row's 128 scores in registers; row max (three-input max), P = 2^(S*scale*log2e
+//              - m) on the SFU with the scaling and the row sum as packed fp32 pairs, P packed
+//              to bf16 into TMEM 32 keys at a time. O stays in TMEM: the running max is only moved (and O, l
 //              rescaled in place) when it grows by more than 2^8, so most blocks skip the
 //              rescale; O and l always refer to the same max, so the result is exact.
 //              After a tile's last block the same warps normalise O and write o and lse.
@@ -45,6 +45,10 @@ constexpr int kTileM = 256;    // query rows per tile (blocks A and B)
 // share a 16K-register SM sub-partition), enough for a row of 128 scores plus its P.
 constexpr int kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
+// One exponential pair in kPolyEvery runs as the FMA-pipe polynomial (ex2_poly), 0 = none. ncu of
+// the medium forward showed the SFU pipe at 10% and issue slots as the limit, so all
+// exponentials stay on the SFU, where each costs one issue slot.
+constexpr int kPolyEvery = 0;
 
 struct AttnFwdArgs {
   bf16* o;
@@ -80,7 +84,11 @@ __device__ __forceinline__ int fwd_nkv(int q0, int half, int T, int causal) {
   return causal ? min(qb0 / kBlockN + 1, nall) : nall;
 }
 
-template <int HD>
+// VARIANT 0: the kernel. 1: the scaling FMA and the row sum as packed fp32 pairs (fewer
+// instructions, more register pressure). 2: a timing skeleton with the softmax arithmetic
+// replaced by constants (wrong results; it measures the MMA / TMA / barrier structure alone).
+// Chosen at run time with LLMT_ATTN_VARIANT for measurements only.
+template <int HD, int VARIANT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
   pdl_wait();
@@ -317,13 +325,17 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
           for (int e = 0; e < kBlockN; ++e)
             if (k0 + e >= lim) su[e] = 0xff800000u;  // -inf
         }
-        float mx8[8];
+        // row max: three-input max over key pairs, four independent chains
+        auto sf = [&](int e) { return __uint_as_float(su[e]); };
+        float mx4[4] = {sf(0), sf(1), sf(2), sf(3)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(su[i]);
-#pragma unroll
-        for (int e = 8; e < kBlockN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(su[e]));
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+        for (int e = 4; e < kBlockN; e += 8) {
+          mx4[0] = max3f(mx4[0], sf(e), sf(e + 1));
+          mx4[1] = max3f(mx4[1], sf(e + 2), sf(e + 3));
+          mx4[2] = max3f(mx4[2], sf(e + 4), sf(e + 5));
+          mx4[3] = max3f(mx4[3], sf(e + 6), sf(e + 7));
+        }
+        const float mx = VARIANT == 2 ? 0.f : fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
         // move the running max (and rescale O and l) only if it grew by more than 2^8 in some row
         const bool grow = mx > m_used + kRescaleLog2;
         const bool rescale = __any_sync(0xffffffffu, grow);
@@ -334,33 +346,45 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
           m_used = m_new;
         }
         const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-        // P = 2^(s * scale_log2 - m): three of every four on the SFU, one on the FMA pipe
-        float sum8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
-        uint32_t pk[kBlockN / 2];
-#pragma unroll
-        for (int e = 0; e < kBlockN; e += 2) {
-          const float x0 = fmaf(__uint_as_float(su[e]), sl2, -msub), x1 = fmaf(__uint_as_float(su[e + 1]), sl2, -msub);
-          float p0, p1;
-          if ((e & 7) == 6) {
-            p0 = ex2_poly(x0);
-            p1 = ex2_poly(x1);
-            if (need_mask) {  // the polynomial does not map -inf to 0
-              p0 = su[e] == 0xff800000u ? 0.f : p0;
-              p1 = su[e + 1] == 0xff800000u ? 0.f : p1;
-            }
-          } else {
-            p0 = ex2_approx(x0);
-            p1 = ex2_approx(x1);
-          }
-          sum8[(e >> 1) & 7] += p0 + p1;
-          pk[e >> 1] = pack_bf16x2(p0, p1);
-        }
         // The previous block's P.V has completed before O is rescaled or P rewritten: with P over S
         // this block's S was issued after it; with separate P it is waited for here.
         if (kSepP && j > 0 && !wait_bar(&o_done[w], (cnt - 1) & 1, err, 18)) { ok = false; break; }
         tc_fence_after();
+        // P = 2^(s * scale_log2 - m) on the SFU, 32 keys at a time straight into TMEM; the scaling
+        // and the row sum run as packed fp32 pairs
+        const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
+        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 xx = VARIANT == 1 ? fma2(make_float2(sf(c * 32 + e), sf(c * 32 + e + 1)), sl2x2, negm)
+                                     : make_float2(fmaf(sf(c * 32 + e), sl2, -msub), fmaf(sf(c * 32 + e + 1), sl2, -msub));
+            float2 pp;
+            if (VARIANT == 2) {
+              pp = xx;
+            } else if (kPolyEvery > 0 && (e >> 1) % kPolyEvery == kPolyEvery - 1) {
+              pp.x = ex2_poly(xx.x);
+              pp.y = ex2_poly(xx.y);
+              if (need_mask) {  // the polynomial does not map -inf to 0
+                pp.x = su[c * 32 + e] == 0xff800000u ? 0.f : pp.x;
+                pp.y = su[c * 32 + e + 1] == 0xff800000u ? 0.f : pp.y;
+              }
+            } else {
+              pp.x = ex2_approx(xx.x);
+              pp.y = ex2_approx(xx.y);
+            }
+            if (VARIANT == 1) {
+              sum2[(e >> 1) & 3] = add2(sum2[(e >> 1) & 3], pp);
+            } else {
+              sum2[(e >> 1) & 3].x += pp.x;
+              sum2[(e >> 1) & 3].y += pp.y;
+            }
+            pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
+          }
+          tmem_st16(t_p + c * 16, pk);
+        }
         if (rescale && j > 0) {
 #pragma unroll
           for (int c = 0; c < HD / 16; ++c) {
@@ -372,13 +396,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
             tmem_st16(t_o + c * 16, v);
           }
         }
-        l *= alpha;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_st16(t_p + c * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + c * 16));
         tmem_wait_st();
         tc_fence_before();
         bar_arrive(&p_full[w]);
-        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+        const float2 s01 = add2(sum2[0], sum2[1]), s23 = add2(sum2[2], sum2[3]);
+        l = l * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
       }
       if (!ok) break;
       // epilogue: the last P.V of the tile, then o = O / l and lse
@@ -417,9 +439,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
   }
 }
 
-template <int HD>
-cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
-  auto kern = flash_fwd_kernel<HD>;
+template <int HD, int VARIANT>
+cudaError_t launch_fwd_v(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
+  auto kern = flash_fwd_kernel<HD, VARIANT>;
   constexpr size_t smem = FwdSmem<HD>::TOTAL;
   static bool attr = false;
   if (!attr) {
@@ -430,6 +452,17 @@ cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStrea
   const int tiles = args.B * args.H * (int)cdiv(args.T, kTileM);
   launch_pdl(kern, std::min(tiles, persistent_sms()), kAttnThreads, smem, st, tm, args);
   return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
+  static const int variant = [] {
+    const char* e = getenv("LLMT_ATTN_VARIANT");
+    return e ? atoi(e) : 0;
+  }();
+  if (variant == 1) return launch_fwd_v<HD, 1>(tm, args, st);
+  if (variant == 2) return launch_fwd_v<HD, 2>(tm, args, st);
+  return launch_fwd_v<HD, 0>(tm, args, st);
 }
 
 }  // namespace
