@@ -11,15 +11,16 @@
 // other's ("ping-pong"):
 //   warp 0     TMA producer: the tile's Q pair (double-buffered at head dim 64, so the next
 //              tile's Q lands during this one) and 128-key K / V blocks through a ring
-//   warp 1     TMEM allocator and single-thread MMA issuer, per key block j:
+//   warp 1     TMEM allocator and MMA issuer (the warp runs the loop, one elected lane
+//              issues), per key block j:
 //                S_A = Q_A K_j^T, S_B = Q_B K_j^T      (SS form, M=128, N=128, K=hd)
 //                O_A += P_A V_j,  O_B += P_B V_j       (TS form: P read from TMEM)
 //              the next block's S is issued as soon as the softmax has read this block's S
 //              out of TMEM, so score MMAs run ahead of the softmax
 //   warps 2-5  softmax of block A, warps 6-9 of block B: one thread per query row holds the
 //              row's 128 scores in registers; row max (three-input max), P = 2^(S*scale*log2e
-//              - m) on the SFU with the scaling and the row sum as packed fp32 pairs, P packed
-//              to bf16 into TMEM 32 keys at a time. O stays in TMEM: the running max is only moved (and O, l
+//              - m) split between the SFU and an FMA-pipe polynomial, row sum, P packed to
+//              bf16 in registers before the wait for the previous P.V, then stored to TMEM. O stays in TMEM: the running max is only moved (and O, l
 //              rescaled in place) when it grows by more than 2^8, so most blocks skip the
 //              rescale; O and l always refer to the same max, so the result is exact.
 //              After a tile's last block the same warps normalise O and write o and lse.
@@ -45,10 +46,11 @@ constexpr int kTileM = 256;    // query rows per tile (blocks A and B)
 // share a 16K-register SM sub-partition), enough for a row of 128 scores plus its P.
 constexpr int kAttnThreads = 320;
 constexpr float kRescaleLog2 = 8.f;  // move the running max only when it grows by more than 2^8
-// One exponential pair in kPolyEvery runs as the FMA-pipe polynomial (ex2_poly), 0 = none. ncu of
-// the medium forward showed the SFU pipe at 10% and issue slots as the limit, so all
-// exponentials stay on the SFU, where each costs one issue slot.
-constexpr int kPolyEvery = 0;
+// One exponential pair in kPolyEvery runs as the FMA-pipe polynomial (ex2_poly), 0 = none. At head
+// dim 64 the softmax is bound by the SFU (an event trace of one CTA: about 2,400 cycles per
+// 128-key block with every exponential on the SFU); a quarter on the FMA pipe balances the SFU
+// against the extra issue slots the polynomial costs.
+constexpr int kPolyEvery = 4;
 
 struct AttnFwdArgs {
   bf16* o;
@@ -87,6 +89,7 @@ __device__ __forceinline__ int fwd_nkv(int q0, int half, int T, int causal) {
 // VARIANT 0: the kernel. 1: the scaling FMA and the row sum as packed fp32 pairs (fewer
 // instructions, more register pressure). 2: a timing skeleton with the softmax arithmetic
 // replaced by constants (wrong results; it measures the MMA / TMA / barrier structure alone).
+// 3: as 2, and the softmax warps do not touch TMEM either.
 // Chosen at run time with LLMT_ATTN_VARIANT for measurements only.
 template <int HD, int VARIANT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -199,9 +202,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issue loop; one elected lane issues each MMA
       constexpr uint32_t idesc_s = make_idesc_bf16(kBlockM, kBlockN, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(kBlockM, HD, false, true);
+      // TMEM base and shared-memory descriptors as warp-uniform values (kept in uniform registers,
+      // which the MMA instructions read directly); per-MMA descriptors are the base plus an offset
+      const uint32_t tm = __shfl_sync(0xffffffffu, tmem, 0);
       int jj = 0, tl = 0;
       int cnt[2] = {0, 0};  // blocks issued per half, over all tiles (barrier phases)
       bool ok = true;
@@ -211,19 +217,19 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       auto issue_s = [&](int w, int g, uint32_t q_addr, uint32_t k_addr) -> bool {
         if (g > 0) {
           if (kSepP) {
-            if (!wait_bar(&s_free[w], (g - 1) & 1, err, 15)) return false;
+            if (!wait_bar_w(&s_free[w], (g - 1) & 1, err, 15)) return false;
           } else {
-            if (!wait_bar(&o_done[w], (g - 1) & 1, err, 15)) return false;
+            if (!wait_bar_w(&o_done[w], (g - 1) & 1, err, 15)) return false;
           }
         }
         tc_fence_after();
+        const uint64_t qd = make_sw128_desc(q_addr, 16, 1024), kd = make_sw128_desc(k_addr, 16, 1024);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          mma_f16(tmem + c_s(w), make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024),
-                  idesc_s, k > 0 ? 1u : 0u);
+          const uint32_t off = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
+          umma_f16(tm + c_s(w), qd + off, kd + off, idesc_s, k > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[w]);
+        umma_commit(&s_full[w]);
         return true;
       };
       for (int r = 0; ok; ++r, ++tl) {
@@ -231,55 +237,56 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
         if (t >= n_tiles) break;
         const Tile x = tile_of(t);
         const int qs = tl % QST;
-        if (!wait_bar(&q_full[qs], (tl / QST) & 1, err, 12)) break;
+        if (!wait_bar_w(&q_full[qs], (tl / QST) & 1, err, 12)) break;
         const uint32_t q_addr0 = smem_u32(smem + L::Q_OFF + (qs * 2) * L::QB_BYTES);
         const uint32_t q_addr1 = q_addr0 + L::QB_BYTES;
         const int nmax = max(x.n[0], x.n[1]);
         // S of key block 0
         {
           const int s0 = jj % KVST;
-          if (!wait_bar(&k_full[s0], (jj / KVST) & 1, err, 16)) break;
+          if (!wait_bar_w(&k_full[s0], (jj / KVST) & 1, err, 16)) break;
           const uint32_t k_addr = smem_u32(smem + L::K_OFF + s0 * L::KV_BYTES);
           if (x.n[0] > 0) ok = issue_s(0, cnt[0], q_addr0, k_addr);
           if (ok && x.n[1] > 0) ok = issue_s(1, cnt[1], q_addr1, k_addr);
           if (!ok) break;
-          if (nmax == 1) mma_commit(&q_empty[qs]);
+          if (nmax == 1) umma_commit(&q_empty[qs]);
         }
         for (int j = 0; j < nmax && ok; ++j, ++jj) {
           const int s = jj % KVST;
           if (kSepP && j + 1 < nmax) {  // run the next block's scores ahead of this block's P.V
             const int s1 = (jj + 1) % KVST;
-            if (!wait_bar(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
+            if (!wait_bar_w(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
             const uint32_t k_addr = smem_u32(smem + L::K_OFF + s1 * L::KV_BYTES);
             if (j + 1 < x.n[0]) ok = issue_s(0, cnt[0] + 1, q_addr0, k_addr);
             if (ok && j + 1 < x.n[1]) ok = issue_s(1, cnt[1] + 1, q_addr1, k_addr);
             if (!ok) break;
-            if (j + 2 == nmax) mma_commit(&q_empty[qs]);  // the tile's last S has read its Q
+            if (j + 2 == nmax) umma_commit(&q_empty[qs]);  // the tile's last S has read its Q
           }
-          if (!wait_bar(&v_full[s], (jj / KVST) & 1, err, 13)) { ok = false; break; }
+          if (!wait_bar_w(&v_full[s], (jj / KVST) & 1, err, 13)) { ok = false; break; }
           const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
 #pragma unroll
           for (int w = 0; w < 2; ++w) {
             if (j >= (w ? x.n[1] : x.n[0])) continue;
-            if (!wait_bar(&p_full[w], cnt[w] & 1, err, 14)) { ok = false; break; }
+            if (!wait_bar_w(&p_full[w], cnt[w] & 1, err, 14)) { ok = false; break; }
             tc_fence_after();
+            const uint64_t vd = make_sw128_desc(v_addr, 16384, 1024);
 #pragma unroll
             for (int k = 0; k < kBlockN / 16; ++k)
-              mma_f16_ts(tmem + c_o(w), tmem + c_p(w) + k * 8, make_sw128_desc(v_addr + k * 2048, 16384, 1024),
-                         idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-            mma_commit(&o_done[w]);
+              umma_f16_ts(tm + c_o(w), tm + c_p(w) + k * 8, vd + (uint64_t)(k * 2048 >> 4), idesc_o,
+                          (j > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&o_done[w]);
             ++cnt[w];
           }
           if (!ok) break;
-          mma_commit(&kv_empty[s]);
+          umma_commit(&kv_empty[s]);
           if (!kSepP && j + 1 < nmax) {  // P over S: the next S waits for this block's P.V
             const int s1 = (jj + 1) % KVST;
-            if (!wait_bar(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
+            if (!wait_bar_w(&k_full[s1], ((jj + 1) / KVST) & 1, err, 16)) { ok = false; break; }
             const uint32_t k_addr = smem_u32(smem + L::K_OFF + s1 * L::KV_BYTES);
             if (j + 1 < x.n[0]) ok = issue_s(0, cnt[0], q_addr0, k_addr);
             if (ok && j + 1 < x.n[1]) ok = issue_s(1, cnt[1], q_addr1, k_addr);
             if (!ok) break;
-            if (j + 2 == nmax) mma_commit(&q_empty[qs]);
+            if (j + 2 == nmax) umma_commit(&q_empty[qs]);
           }
         }
       }
@@ -310,7 +317,14 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
         tc_fence_after();
         uint32_t su[kBlockN];  // the row's scores (fp32 bits)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+        for (int c = 0; c < 4; ++c) {
+          if (VARIANT == 3) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) su[c * 32 + e] = __float_as_uint((float)(e + c));
+          } else {
+            tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+          }
+        }
         tmem_wait_ld();
         if (kSepP) {
           tc_fence_before();
@@ -335,7 +349,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
           mx4[2] = max3f(mx4[2], sf(e + 4), sf(e + 5));
           mx4[3] = max3f(mx4[3], sf(e + 6), sf(e + 7));
         }
-        const float mx = VARIANT == 2 ? 0.f : fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+        const float mx = VARIANT >= 2 ? 0.f : fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
         // move the running max (and rescale O and l) only if it grew by more than 2^8 in some row
         const bool grow = mx > m_used + kRescaleLog2;
         const bool rescale = __any_sync(0xffffffffu, grow);
@@ -346,45 +360,48 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
           m_used = m_new;
         }
         const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+        // P = 2^(s * scale_log2 - m): one exponential pair in kPolyEvery on the FMA pipe, the rest
+        // on the SFU; packed to bf16 pairs in registers
+        const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
+        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        uint32_t pk[kBlockN / 2];
+#pragma unroll
+        for (int e = 0; e < kBlockN; e += 2) {
+          const float2 xx = VARIANT == 1 ? fma2(make_float2(sf(e), sf(e + 1)), sl2x2, negm)
+                                         : make_float2(fmaf(sf(e), sl2, -msub), fmaf(sf(e + 1), sl2, -msub));
+          float2 pp;
+          if (VARIANT >= 2) {
+            pp = xx;
+          } else if (kPolyEvery > 0 && (e >> 1) % kPolyEvery == kPolyEvery - 1) {
+            pp.x = ex2_poly(xx.x);
+            pp.y = ex2_poly(xx.y);
+            if (need_mask) {  // the polynomial does not map -inf to 0
+              pp.x = su[e] == 0xff800000u ? 0.f : pp.x;
+              pp.y = su[e + 1] == 0xff800000u ? 0.f : pp.y;
+            }
+          } else {
+            pp.x = ex2_approx(xx.x);
+            pp.y = ex2_approx(xx.y);
+          }
+          if (VARIANT == 1) {
+            sum2[(e >> 1) & 3] = add2(sum2[(e >> 1) & 3], pp);
+          } else {
+            sum2[(e >> 1) & 3].x += pp.x;
+            sum2[(e >> 1) & 3].y += pp.y;
+          }
+          pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
+        }
+        // P must exist before the wait below: the compiler would otherwise sink this arithmetic past
+        // the wait, and the softmax would idle for the previous P.V before doing its work
+#pragma unroll
+        for (int i = 0; i < kBlockN / 2; ++i) asm volatile("" ::"r"(pk[i]));
         // The previous block's P.V has completed before O is rescaled or P rewritten: with P over S
         // this block's S was issued after it; with separate P it is waited for here.
         if (kSepP && j > 0 && !wait_bar(&o_done[w], (cnt - 1) & 1, err, 18)) { ok = false; break; }
         tc_fence_after();
-        // P = 2^(s * scale_log2 - m) on the SFU, 32 keys at a time straight into TMEM; the scaling
-        // and the row sum run as packed fp32 pairs
-        const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-msub, -msub);
-        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 xx = VARIANT == 1 ? fma2(make_float2(sf(c * 32 + e), sf(c * 32 + e + 1)), sl2x2, negm)
-                                     : make_float2(fmaf(sf(c * 32 + e), sl2, -msub), fmaf(sf(c * 32 + e + 1), sl2, -msub));
-            float2 pp;
-            if (VARIANT == 2) {
-              pp = xx;
-            } else if (kPolyEvery > 0 && (e >> 1) % kPolyEvery == kPolyEvery - 1) {
-              pp.x = ex2_poly(xx.x);
-              pp.y = ex2_poly(xx.y);
-              if (need_mask) {  // the polynomial does not map -inf to 0
-                pp.x = su[c * 32 + e] == 0xff800000u ? 0.f : pp.x;
-                pp.y = su[c * 32 + e + 1] == 0xff800000u ? 0.f : pp.y;
-              }
-            } else {
-              pp.x = ex2_approx(xx.x);
-              pp.y = ex2_approx(xx.y);
-            }
-            if (VARIANT == 1) {
-              sum2[(e >> 1) & 3] = add2(sum2[(e >> 1) & 3], pp);
-            } else {
-              sum2[(e >> 1) & 3].x += pp.x;
-              sum2[(e >> 1) & 3].y += pp.y;
-            }
-            pk[e >> 1] = pack_bf16x2(pp.x, pp.y);
-          }
-          tmem_st16(t_p + c * 16, pk);
-        }
+        for (int c = 0; c < 4; ++c)
+          if (VARIANT != 3) tmem_st16(t_p + c * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + c * 16));
         if (rescale && j > 0) {
 #pragma unroll
           for (int c = 0; c < HD / 16; ++c) {
@@ -462,6 +479,7 @@ cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStrea
   }();
   if (variant == 1) return launch_fwd_v<HD, 1>(tm, args, st);
   if (variant == 2) return launch_fwd_v<HD, 2>(tm, args, st);
+  if (variant == 3) return launch_fwd_v<HD, 3>(tm, args, st);
   return launch_fwd_v<HD, 0>(tm, args, st);
 }
 

@@ -64,6 +64,12 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* er
   }
 }
 
+// wait_bar for a whole warp that runs an issue loop (MMA warps): the result is warp-uniform, so
+// the compiler keeps the loop's control flow, and the values it computes, uniform.
+__device__ __forceinline__ bool wait_bar_w(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, err, code));
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (tensor core / TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -153,7 +159,7 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      );
 }
 // 8-bit operands (both e4m3 here), K = 32 per instruction: the same 32 bytes of a 128-byte
 // swizzled row as one K = 16 step of bf16, so the shared-memory descriptors are unchanged.
@@ -164,7 +170,7 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      );
 }
 
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread has completed.
@@ -231,6 +237,44 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      );
+}
+
+// The MMA helpers carry no "memory" clobber: a clobber makes the compiler reload every value it
+// keeps in memory (local copies, captured variables) after each MMA, which in a loop of small
+// MMAs costs more than the MMAs take to run. Ordering against the mbarrier waits and commits
+// (volatile asm with a memory clobber) is kept by volatile-asm order.
+//
+// Warp-collective MMA issue: the whole warp executes these with warp-uniform operands and one
+// lane, chosen by elect.sync, issues the instruction. Issuing from a lane-0-only branch makes
+// the operands divergent values that the tcgen05 instructions must first move to uniform
+// registers; measured on the attention forward, that cost about 100 cycles per MMA, more than
+// a 128 x 64 x 16 MMA takes to run.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      );
+}
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      );
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
 
@@ -359,7 +403,7 @@ __device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint6
       "setp.ne.b32 p, %6, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
-      : "memory");
+      );
 }
 __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
@@ -368,7 +412,7 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint6
       "setp.ne.b32 p, %6, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
-      : "memory");
+      );
 }
 
 // Block-scaled kinds (fp32 accumulator implied): data format of A and B (mxf8f6f4: e4m3 = 0;
