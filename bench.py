@@ -151,8 +151,8 @@ def run_native(args, rank, world, local):
     cfg = get_config(MODEL)
     dp = None
     if world > 1:
-        from llmt.parallel.dp import DataParallel
-        dp = DataParallel(world, rank, mode=args.dp_mode)
+        from llmt.parallel.dp import DataParallel, pick_mode
+        dp = DataParallel(world, rank, mode=pick_mode(args.dp_mode, local))
     tr = Trainer(cfg, PER_GPU_BATCH, SEQ, device=f"cuda:{local}", cuda_graph=not args.no_graph, dp=dp,
                  linear=args.linear)
     idx, tgt = make_batch(PER_GPU_BATCH, SEQ, cfg.vocab, "cpu", seed=rank)
@@ -260,9 +260,11 @@ def main():
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile",
                    help="reference ladder row (default: its fastest bf16 row on B200)")
-    p.add_argument("--dp-mode", default="nccl", choices=["nvls", "fused", "nccl", "fused-overlap"],
-                   help="data-parallel transport: NCCL (fastest measured at 2 and 8 GPUs), the fused "
-                        "peer-memory kernel, or that kernel overlapped with the backward")
+    p.add_argument("--dp-mode", default="auto", choices=["auto", "nvls", "fused", "nccl", "fused-overlap"],
+                   help="data-parallel transport: auto = nvls where the GPUs support NVLink multicast, else "
+                        "nccl; nvls = bf16 gradient cast + one kernel reducing in the NVSwitch, AdamW and "
+                        "multicasting the weights; fused = peer-memory kernel; nccl = reduce-scatter / "
+                        "all-gather")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"],
                    help="block linears (every GEMM of qkv, wo, w1||w3, w2; the head stays bf16) in bf16, on "

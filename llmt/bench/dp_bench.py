@@ -2,11 +2,15 @@
 step on a flat buffer of a model's parameter count, timed with CUDA events between barriers,
 max over ranks, against their NVLink roofline.
 
-The roofline of one step is the larger of two link directions of one GPU (the measured peer
-copy bandwidth per direction, from llmt/perf/links.json):
-  egress   the reduce-scatter: every gradient byte of the other ranks' shards leaves this GPU
-           once, (N - 1) / N x P x bytes-per-gradient
-  ingress  the all-gather: the other ranks' new bf16 weights arrive once, (N - 1) / N x P x 2
+The roofline of one step is the slowest of three resources of one GPU:
+  egress   NVLink, the reduce-scatter: every gradient byte of the other ranks' shards leaves this
+           GPU once, (N - 1) / N x P x bytes-per-gradient, at the measured peer-copy bandwidth
+           per direction (llmt/perf/links.json)
+  ingress  NVLink, the all-gather: the other ranks' new bf16 weights arrive once,
+           (N - 1) / N x P x 2
+  HBM      the local passes: the gradient cast (NVLS: read 4 B, write 2 B per parameter), AdamW on
+           the shard (master, m, v read and written: 24 B per shard parameter) and the arriving
+           bf16 weights (2 B per parameter), at the measured copy bandwidth (MEASURED_PEAKS.json)
 The NVLS kernel moves bf16 gradients (its cast is part of the timed step); the NCCL step
 reduce-scatters the fp32 gradients as the "nccl" mode does.
 
@@ -58,7 +62,10 @@ def main():
     numel = (total + unit - 1) // unit * unit
     with open(os.path.join(os.path.dirname(os.path.dirname(__file__)), "perf", "links.json")) as f:
         link_gbs = float(json.load(f)["links"]["nvlink5"]["p2p_gbs"])
-    out = {"model": args.model, "params": numel, "world": world, "link_gbs_per_direction": link_gbs, "modes": {}}
+    from llmt.bench.kernels import peaks
+    hbm_gbs = peaks()[1]
+    out = {"model": args.model, "params": numel, "world": world, "link_gbs_per_direction": link_gbs,
+           "hbm_gbs": hbm_gbs, "modes": {}}
     for mode in args.modes.split(","):
         flat = _Flat(numel, f"cuda:{local}")
         dp = DataParallel(world, rank, mode=mode)
@@ -79,9 +86,12 @@ def main():
         gbytes = 2 if mode == "nvls" else 4
         egress = (world - 1) / world * numel * gbytes
         ingress = (world - 1) / world * numel * 2
-        roof_ms = max(egress, ingress) / (link_gbs * 1e9) * 1e3
+        hbm = (6 * numel if mode == "nvls" else 4 * numel) + 24 * numel / world + 2 * numel
+        roof_ms = max(max(egress, ingress) / (link_gbs * 1e9), hbm / (hbm_gbs * 1e9)) * 1e3
         err = dp.fused.error_code() if dp.fused is not None and hasattr(dp.fused, "error_code") else 0
         out["modes"][mode] = {"ms_per_step": round(ms.item(), 4), "roofline_ms": round(roof_ms, 4),
+                              "nvlink_ms": round(max(egress, ingress) / (link_gbs * 1e9) * 1e3, 4),
+                              "hbm_ms": round(hbm / (hbm_gbs * 1e9) * 1e3, 4),
                               "fraction_of_roofline": round(roof_ms / ms.item(), 3),
                               "gradient_bytes_per_param": gbytes, "dp_error_code": err}
         dp.close()

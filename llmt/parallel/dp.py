@@ -29,6 +29,19 @@ import torch.distributed as dist
 from llmt.ops import native as N
 
 
+def pick_mode(mode: str, device_index: int) -> str:
+    """"auto" -> "nvls" when the device supports NVLink multicast (every rank of one box answers
+    the same), else "nccl"; any other mode is returned as given."""
+    if mode != "auto":
+        return mode
+    try:
+        import torch.distributed._symmetric_memory as symm
+        ok = symm._SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, device_index)
+    except Exception:  # noqa: BLE001 - no symmetric memory in this build
+        ok = False
+    return "nvls" if ok else "nccl"
+
+
 class ShardedAdamW:
     """AdamW state for one contiguous shard [lo, hi) of the flat buffers."""
 

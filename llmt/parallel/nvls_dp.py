@@ -36,11 +36,6 @@ class NvlsDP:
         symm = _symm()
         dev = flat.master.device
         self.device = dev
-        if hasattr(symm, "enable_symm_mem_for_group"):
-            try:
-                symm.enable_symm_mem_for_group(self.group.group_name)
-            except Exception:  # noqa: BLE001 - newer releases need no registration
-                pass
         self.g16 = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
         shadow = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
         shadow.copy_(flat.shadow)
