@@ -18,6 +18,15 @@ int* gemm_err_word() {
 }
 }  // namespace
 
+// CTA-pair tiles are on unless LLMT_GEMM_PAIRS=0 (kept for measurements).
+static bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LLMT_GEMM_PAIRS");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Estimated time ~ waves x tile width; ties go to the wider (more efficient) tile.
 int gemm_pick_bn(int M, int N, int epi) {
   if (epi == EPI_SWIGLU) return N >= 512 ? 256 : 128;
@@ -103,10 +112,12 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
                      !ta,
                  "gemm: PEER_RS needs peer slots, M a multiple of the rows per rank, N a multiple of 32");
   if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm: bad RoPE epilogue shape");
+  // 256 x 256 tiles on CTA pairs wherever the planner picked 256-wide tiles and M fills them
+  const bool pair = BN == 256 && M > kGemmBM && epi != EPI_PEER_RS && gemm_pairs_enabled();
   g.M = M;
   g.N = N;
   g.K = K;
-  g.m_blocks = (int)cdiv(M, kGemmBM);
+  g.m_blocks = (int)cdiv(M, pair ? 2 * kGemmBM : kGemmBM);
   g.n_blocks = (int)cdiv(N, epi == EPI_SWIGLU ? BN / 2 : BN);
   g.k_blocks = (int)cdiv(K, kGemmBK);
   g.k_per_split = (int)cdiv(g.k_blocks, splits);
@@ -121,7 +132,7 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   bool ok_b;
   if (tb) {
     const int rows = epi == EPI_SWIGLU ? 2 * N : N;
-    ok_b = make_tmap_2d(&mp.b, b, dt, 2, K, rows, ldb, kGemmBK, epi == EPI_SWIGLU ? BN / 2 : BN);
+    ok_b = make_tmap_2d(&mp.b, b, dt, 2, K, rows, ldb, kGemmBK, (epi == EPI_SWIGLU || pair) ? BN / 2 : BN);
   } else {
     ok_b = make_tmap_2d(&mp.b, b, dt, 2, N, K, ldb, 64, kGemmBK);
   }
@@ -136,9 +147,9 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
     return cudaErrorInvalidValue;
   }
   LLMT_REQUIRE(make_out_maps(epi, g, M, N, &mp), "gemm: output tensor map rejected (pitch/alignment)");
-  if (!ta && tb) return gemm_launch_kk(BN, epi, mp, g, st);
-  if (!ta && !tb) return gemm_launch_km(BN, epi, mp, g, st);
-  return gemm_launch_mm(BN, epi, mp, g, st);
+  if (!ta && tb) return gemm_launch_kk(BN, epi, mp, g, st, pair);
+  if (!ta && !tb) return gemm_launch_km(BN, epi, mp, g, st, pair);
+  return gemm_launch_mm(BN, epi, mp, g, st, pair);
 }
 
 

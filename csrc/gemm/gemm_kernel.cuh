@@ -42,9 +42,10 @@ constexpr int kEpiStageBytes = 4 * 2 * 4096;
 struct GemmMaps {
   CUtensorMap a, b, c, c2;  // operands, main output, auxiliary output
 };
-cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // fwd
-cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // dgrad
-cudaError_t gemm_launch_mm(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // wgrad
+// pair: 256 x 256 tiles on CTA pairs (cta_group::2), BN must be 256
+cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st, bool pair);  // fwd
+cudaError_t gemm_launch_km(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st, bool pair);  // dgrad
+cudaError_t gemm_launch_mm(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st, bool pair);  // wgrad
 cudaError_t gemm_launch_f8(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // e4m3, K-major
 cudaError_t gemm_launch_bs(int kind, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st);  // MX / NV
 
@@ -380,7 +381,11 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
 
 // KIND: 0 bf16, 1 e4m3 with tensorwise scales, 2 MXFP8, 3 NVFP4 (2 and 3: block-scaled MMA with
 // the scale-factor chunks of each k-block loaded next to its A / B tiles and copied into TMEM).
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0>
+// PAIR: a cluster of two CTAs computes each 256 x BN tile with cta_group::2 MMAs (bf16, BN =
+// 256): each CTA loads its 128 rows of A and its BN/2 columns of B and holds its 128 rows of the
+// accumulator; the leader issues the MMAs. Per SM that halves the B operand traffic from L2,
+// which bounds the one-CTA kernel at BN = 256.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
@@ -390,8 +395,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   static_assert(!F8 || (!A_MN && !B_MN), "8-bit operands are K-major only");
   static_assert(!BS || BN == 128, "block-scaled tiles are 128 x 128");
   constexpr int KX = F8 ? 2 * BK : BK;  // tensor-map units per k-block: one 128-byte swizzled row
+  static_assert(!PAIR || (KIND == 0 && BN == 256), "CTA pairs: bf16 operands, 256-wide tiles");
   constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;  // PAIR: this CTA's half of B
   constexpr int NCH = KIND == 2 ? 1 : 4;                // scale chunks per k-block and operand
   constexpr uint32_t SF_BYTES = BS ? 2 * NCH * 512 : 0;  // A and B chunks of one stage
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -410,6 +416,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   int* err = args.err;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the leader (issues the MMAs)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       bar_init(&full[s], 1);
@@ -417,7 +424,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     for (int b = 0; b < 2; ++b) {
       bar_init(&tfull[b], 1);
-      bar_init(&tempty[b], 128);
+      bar_init(&tempty[b], PAIR ? 8 : 128);  // PAIR: one arrival per epilogue warp of both CTAs
     }
     for (int b = 0; b < 8; ++b) bar_init(&ebar[b], 1);
     fence_barrier_init();
@@ -426,21 +433,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_slot);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_alloc_pair<TMEM_COLS>(tmem_slot);
+    else tmem_alloc<TMEM_COLS>(tmem_slot);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int mn_tiles = args.m_blocks * args.n_blocks;
   const int num_tiles = mn_tiles * args.splits;
   const int kpb = args.k_per_split;  // k-blocks per split (splits > 1 only with reduce-add output)
+  // persistent unit: one CTA, or one CTA pair (tiles of 2 x BM rows)
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int TM = PAIR ? 2 * BM : BM;  // rows of one tile
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += units) {
         const int rest = tile % mn_tiles, ks = tile / mn_tiles;
         const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
         const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
@@ -451,6 +466,35 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
+          if constexpr (PAIR) {
+            // both CTAs' halves land on the leader's barrier; the leader expects them all
+            if (rank == 0) bar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+            const uint32_t fb = cluster_map(&full[stage], 0);
+            const int k0 = kb * KX;
+            const int row = mb * TM + (int)rank * BM;
+            if constexpr (!A_MN) {
+              tma_load_2d_pair(sa, &tmA, fb, k0, row);
+            } else {
+              tma_load_2d_pair(sa, &tmA, fb, row, k0);
+              tma_load_2d_pair(sa + 8192, &tmA, fb, row + 64, k0);
+            }
+            if constexpr (!B_MN) {
+              if constexpr (EPI == EPI_SWIGLU) {  // leader: W1 rows, peer: the same W3 rows
+                tma_load_2d_pair(sb, &tmB, fb, k0, (rank ? args.split : 0) + nb * (BN / 2));
+              } else {
+                tma_load_2d_pair(sb, &tmB, fb, k0, nb * BN + (int)rank * (BN / 2));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_2d_pair(sb + j * 8192, &tmB, fb, nb * BN + (int)rank * (BN / 2) + j * 64, k0);
+            }
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           bar_arrive_expect_tx(&full[stage], STAGE_BYTES + SF_BYTES);
           const int k0 = kb * KX;
           if constexpr (BS) {
@@ -484,15 +528,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = KIND == 3 ? make_idesc_bs(BM, BN, 1, 0)
                                  : KIND == 2 ? make_idesc_bs(BM, BN, 0, 1)
                                  : F8        ? make_idesc_e4m3(BM, BN)
-                                             : make_idesc_bf16(BM, BN, A_MN, B_MN);
+                                             : make_idesc_bf16(TM, BN, A_MN, B_MN);
       int stage = 0, buf = 0;
       uint32_t phase = 0, aphase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit0; tile < num_tiles && ok; tile += units) {
         const int ks = tile / mn_tiles;
         const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
         if (!wait_bar(&tempty[buf], aphase ^ 1, err, 2)) break;
@@ -534,18 +578,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               mma_nvf4(d, ad, bd, idesc, t_sfa + 4 * k, t_sfb + 4 * k, acc);
             } else if constexpr (F8) {
               mma_f8(d, ad, bd, idesc, acc);
+            } else if constexpr (PAIR) {
+              mma_f16_pair(d, ad, bd, idesc, acc);
             } else {
               mma_f16(d, ad, bd, idesc, acc);
             }
           }
-          mma_commit(&empty[stage]);
+          if constexpr (PAIR) mma_commit_pair(&empty[stage]);
+          else mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[buf]);
+        if constexpr (PAIR) mma_commit_pair(&tfull[buf]);
+        else mma_commit(&tfull[buf]);
         buf ^= 1;
         if (buf == 0) aphase ^= 1;
       }
@@ -556,15 +604,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     Stager st{stage_out + (warp - 2) * 8192, 0, lane, &ebar[(warp - 2) * 2], 0u};
     int buf = 0;
     uint32_t aphase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = unit0; tile < num_tiles; tile += units) {
       const int rest = tile % mn_tiles;
       const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<EPI, BN, KIND == 1 || KIND == 3>(taddr, mb * BM + row_in_tile, mb * BM + q * 32, nb, args, &tmC, &tmC2, st);
+      const int row0 = mb * TM + (int)rank * BM;  // first row of this CTA's accumulator
+      epilogue_tile<EPI, BN, KIND == 1 || KIND == 3>(taddr, row0 + row_in_tile, row0 + q * 32, nb, args, &tmC, &tmC2, st);
       tc_fence_before();
-      bar_arrive(&tempty[buf]);
+      if constexpr (PAIR) {
+        __syncwarp();
+        if (lane == 0) bar_arrive_cluster(cluster_map(&tempty[buf], 0));
+      } else {
+        bar_arrive(&tempty[buf]);
+      }
       buf ^= 1;
       if (buf == 0) aphase ^= 1;
     }
@@ -572,18 +626,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
   pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the pair's MMAs have read both CTAs' shared memory
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<TMEM_COLS>(tmem_base);
+    if constexpr (PAIR) tmem_dealloc_pair<TMEM_COLS>(tmem_base);
+    else tmem_dealloc<TMEM_COLS>(tmem_base);
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0, bool PAIR = false>
 cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, KIND>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, KIND, PAIR>;
   constexpr size_t sf = KIND >= 2 ? 2 * (KIND == 2 ? 1 : 4) * 512 : 0;
-  constexpr size_t smem = STAGES * (kGemmBM * kGemmBK * 2 + BN * kGemmBK * 2 + sf) + kEpiStageBytes + 1024 + 256;
+  constexpr size_t smem =
+      STAGES * (kGemmBM * kGemmBK * 2 + (PAIR ? BN / 2 : BN) * kGemmBK * 2 + sf) + kEpiStageBytes + 1024 + 256;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr = false;
   if (!attr) {
@@ -592,6 +649,26 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     attr = true;
   }
   const int tiles = args.m_blocks * args.n_blocks * args.splits;
+  if constexpr (PAIR) {
+    const int pairs = std::min(tiles, persistent_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp.a, mp.b, mp.c, mp.c2, args);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+  }
   const int grid = std::min(tiles, persistent_sms());
   launch_pdl(kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();
@@ -601,6 +678,8 @@ template <int BN>
 constexpr int stages_for() {
   return BN == 256 ? 4 : 6;
 }
+// CTA pairs hold half of B per stage (32 KB stages): six fit beside the epilogue staging.
+constexpr int kPairStages = 6;
 
 }  // namespace gemm_detail
 }  // namespace llmt
