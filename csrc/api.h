@@ -101,6 +101,7 @@ struct GemmArgs {
   const uint8_t* sfa;    // block-scaled operands: scale factors of A and B in 512-byte chunks
   const uint8_t* sfb;    // [row tile of 128][chunk along K][32 x 16 bytes]
   int sf_chunks;         // chunks per 128-row tile (k-blocks x chunks per k-block)
+  int n_fastest;         // tile order: 1 = consecutive tiles walk N (A blocks reused), 0 = walk M
   int* err;
 };
 

@@ -123,6 +123,9 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   g.k_per_split = (int)cdiv(g.k_blocks, splits);
   g.splits = (int)cdiv(g.k_blocks, g.k_per_split);
   g.err = gemm_err_word();
+  // consecutive tiles share the larger operand's block: A (M x K) larger -> walk N, else walk M,
+  // so the larger operand streams from DRAM once while the smaller stays in L2
+  g.n_fastest = M > N ? 1 : 0;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   alignas(64) GemmMaps mp;
   memset(&mp, 0, sizeof(mp));
@@ -182,6 +185,9 @@ cudaError_t gemm_fp8(const void* a, int64_t lda, const void* b, int64_t ldb, int
   g.k_per_split = (int)cdiv(g.k_blocks, splits);
   g.splits = (int)cdiv(g.k_blocks, g.k_per_split);
   g.err = gemm_err_word();
+  // consecutive tiles share the larger operand's block: A (M x K) larger -> walk N, else walk M,
+  // so the larger operand streams from DRAM once while the smaller stays in L2
+  g.n_fastest = M > N ? 1 : 0;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   alignas(64) GemmMaps mp;
   memset(&mp, 0, sizeof(mp));
@@ -236,6 +242,9 @@ cudaError_t gemm_bs(int kind, const void* a, int64_t lda, const void* b, int64_t
   g.splits = (int)cdiv(k_blocks, g.k_per_split);
   g.sf_chunks = k_blocks * (kind == 2 ? 1 : 4);
   g.err = gemm_err_word();
+  // consecutive tiles share the larger operand's block: A (M x K) larger -> walk N, else walk M,
+  // so the larger operand streams from DRAM once while the smaller stays in L2
+  g.n_fastest = M > N ? 1 : 0;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   alignas(64) GemmMaps mp;
   memset(&mp, 0, sizeof(mp));

@@ -457,7 +457,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       bool ok = true;
       for (int tile = unit0; tile < num_tiles && ok; tile += units) {
         const int rest = tile % mn_tiles, ks = tile / mn_tiles;
-        const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
+        const int mb = args.n_fastest ? rest / args.n_blocks : rest % args.m_blocks;
+        const int nb = args.n_fastest ? rest % args.n_blocks : rest / args.m_blocks;
         const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
         for (int kb = k_lo; kb < k_hi; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, err, 1)) {
@@ -606,7 +607,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint32_t aphase = 0;
     for (int tile = unit0; tile < num_tiles; tile += units) {
       const int rest = tile % mn_tiles;
-      const int mb = rest % args.m_blocks, nb = rest / args.m_blocks;
+      const int mb = args.n_fastest ? rest / args.n_blocks : rest % args.m_blocks;
+        const int nb = args.n_fastest ? rest % args.n_blocks : rest / args.m_blocks;
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
