@@ -622,9 +622,11 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         if (!wait_bar(s_full, g & 1, err, 48)) { ok = false; break; }
         if (!wait_bar(&pds_empty[pb], ((g >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
         if (g >= 2) {
-          // buffer pb staged dQ(g - 2) for every warp's TMA reduce: all of them must have read it
+          // buffer pb staged dQ(g - 2) for every warp's TMA reduce: all of them must have read it.
+          // Each warp issued one reduce per block since, dQ(g - 1)'s from the other buffer, which
+          // may still be in flight (waiting for it cost about 1,400 cycles per block).
           if (lane == 0) {
-            bulk_wait_read<0>();
+            bulk_wait_read<1>();
             bar_arrive(stage_free);
           }
           __syncwarp();
