@@ -260,11 +260,12 @@ def main():
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile",
                    help="reference ladder row (default: its fastest bf16 row on B200)")
-    p.add_argument("--dp-mode", default="auto", choices=["auto", "nvls", "fused", "nccl", "fused-overlap"],
+    p.add_argument("--dp-mode", default="auto",
+                   choices=["auto", "nvls", "nvls-overlap", "fused", "fused-overlap", "nccl"],
                    help="data-parallel transport: auto = nvls where the GPUs support NVLink multicast, else "
                         "nccl; nvls = bf16 gradient cast + one kernel reducing in the NVSwitch, AdamW and "
-                        "multicasting the weights; fused = peer-memory kernel; nccl = reduce-scatter / "
-                        "all-gather")
+                        "multicasting the weights; nvls-overlap = the same per bucket during the backward; "
+                        "fused = peer-memory kernel; nccl = reduce-scatter / all-gather")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"],
                    help="block linears (every GEMM of qkv, wo, w1||w3, w2; the head stays bf16) in bf16, on "

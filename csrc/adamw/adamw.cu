@@ -74,6 +74,28 @@ __global__ void cast_bf16_kernel(const float* __restrict__ x, bf16* __restrict__
     y[i] = __float2bfloat16_rn(x[i]);
 }
 
+// 8 elements per thread and iteration (two 16-byte loads, one 16-byte store), two iterations'
+// loads issued before either store: enough bytes in flight per SM for a grid of a few SMs (the
+// overlapped data-parallel step casts on the SMs the backward leaves free).
+__global__ void cast_bf16_x8_kernel(const float* __restrict__ x, bf16* __restrict__ y, int64_t n8) {
+  pdl_wait();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
+    const int64_t j = i + stride;
+    const float4 a0 = ld_f4(x + 8 * i), a1 = ld_f4(x + 8 * i + 4);
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (j < n8) {
+      b0 = ld_f4(x + 8 * j);
+      b1 = ld_f4(x + 8 * j + 4);
+    }
+    *reinterpret_cast<uint4*>(y + 8 * i) = make_uint4(pack_bf16x2(a0.x, a0.y), pack_bf16x2(a0.z, a0.w),
+                                                      pack_bf16x2(a1.x, a1.y), pack_bf16x2(a1.z, a1.w));
+    if (j < n8)
+      *reinterpret_cast<uint4*>(y + 8 * j) = make_uint4(pack_bf16x2(b0.x, b0.y), pack_bf16x2(b0.z, b0.w),
+                                                        pack_bf16x2(b1.x, b1.y), pack_bf16x2(b1.z, b1.w));
+  }
+}
+
 }  // namespace
 
 // zero_grad: also reset g to 0 after reading it (the next step's gradients accumulate into it).
@@ -92,10 +114,17 @@ cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_
   return cudaGetLastError();
 }
 
-cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st) {
+// max_blocks > 0 caps the grid (a side stream that must leave the rest of the GPU to others).
+cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st, int max_blocks) {
   if (n == 0) return cudaSuccess;
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), sm_count() * 8));
-  launch_pdl(cast_bf16_kernel, grid, 256, 0, st, x, static_cast<bf16*>(y), n);
+  const int64_t cap = max_blocks > 0 ? max_blocks : sm_count() * 8;
+  if (n % 8 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0) {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 8, 512), cap));
+    launch_pdl(cast_bf16_x8_kernel, grid, 256, 0, st, x, static_cast<bf16*>(y), n / 8);
+  } else {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), cap));
+    launch_pdl(cast_bf16_kernel, grid, 256, 0, st, x, static_cast<bf16*>(y), n);
+  }
   return cudaGetLastError();
 }
 

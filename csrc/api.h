@@ -56,7 +56,7 @@ struct AdamHyper {
 };
 cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
                        const int* step, AdamHyper h, bool zero_grad, cudaStream_t st);
-cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st);
+cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st, int max_blocks = 0);
 
 // ---------------------------------------------------------------- cross entropy rows
 cudaError_t ce_fwd_rows(const void* logits, int64_t ld, const int64_t* tgt, float* lse, float* loss, int64_t R, int V,

@@ -177,13 +177,13 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
      "adamw_step");
 }
 
-void cast_bf16(at::Tensor x, at::Tensor y) {
+void cast_bf16(at::Tensor x, at::Tensor y, int64_t max_blocks) {
   CHECK_DT(x, at::kFloat);
   CHECK_DT(y, at::kBFloat16);
   on_device(x, "x");
   on_device(y, "y");
   CHECK(x.numel() == y.numel() && x.is_contiguous() && y.is_contiguous(), "cast_bf16: bad args");
-  ok(llmt::cast_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream()), "cast_bf16");
+  ok(llmt::cast_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), stream(), (int)max_blocks), "cast_bf16");
 }
 
 // ---------------------------------------------------------------- cross entropy
@@ -545,7 +545,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &embedding_bwd, "idx"_a, "dx"_a, "dW"_a, "v0"_a = 0);
   m.def("adamw_step", &adamw_step, "p"_a, "g"_a, "m"_a, "v"_a, "p16"_a, "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a,
         "wd"_a, "grad_scale"_a, "zero_grad"_a = false);
-  m.def("cast_bf16", &cast_bf16);
+  m.def("cast_bf16", &cast_bf16, "x"_a, "y"_a, "max_blocks"_a = 0);
   m.def("ce_fwd_rows", &ce_fwd_rows);
   m.def("ce_bwd_rows", &ce_bwd_rows);
   m.def("ce_combine", &ce_combine);

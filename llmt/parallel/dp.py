@@ -18,6 +18,8 @@ Transports, same math:
                 fp32 gradient shard, sums, applies AdamW and stores the new bf16 shard into
                 every peer's shadow buffer (llmt.parallel.fused_dp), with bounded device-side waits;
   mode="nccl"   NCCL reduce_scatter_tensor / all_gather_into_tensor (the baseline path).
+"nvls-overlap" and "fused-overlap" run their kernel per bucket on a side stream while the backward
+of the earlier blocks computes (bucket-sharded optimizer state).
 
 Every rank takes the same collective steps in the same order (warm-up, capture and replay).
 """
@@ -69,9 +71,10 @@ class ShardedAdamW:
 
 class DataParallel:
     def __init__(self, world_size: int, rank: int, mode: str = "nccl", group=None):
-        """mode: "nvls" (bf16 cast + one multicast kernel after the backward), "nccl"
-        (reduce-scatter / all-gather), "fused" (one peer-memory kernel after the backward) or
-        "fused-overlap" (that kernel per bucket, overlapped with the backward)."""
+        """mode: "nvls" (bf16 cast + one multicast kernel after the backward), "nvls-overlap"
+        (the same per bucket, overlapped with the backward), "nccl" (reduce-scatter /
+        all-gather), "fused" (one peer-memory kernel after the backward) or "fused-overlap"
+        (that kernel per bucket, overlapped with the backward)."""
         self.world_size, self.rank, self.mode, self.group = world_size, rank, mode, group
         # False when the model's gradient writers store on the step's first write (the NCCL
         # step then skips clearing the buffer; the fused kernels clear what they read anyway)
@@ -81,7 +84,7 @@ class DataParallel:
 
     @property
     def overlap(self):
-        return self.mode == "fused-overlap"
+        return self.mode in ("fused-overlap", "nvls-overlap")
 
     def make_optimizer(self, flat, lr=3e-4, **kw):
         if flat.numel % self.world_size:
@@ -94,8 +97,12 @@ class DataParallel:
             src = dist.get_global_rank(self.group, 0) if self.group is not None else 0
             dist.broadcast(flat.master, src, group=self.group)
             flat.refresh_shadow()
-            from llmt.parallel.fused_dp import OverlappedFusedDP
-            self.fused = OverlappedFusedDP(flat, opt, self.rank, self.world_size, self.group)
+            if self.mode == "nvls-overlap":
+                from llmt.parallel.nvls_dp import NvlsOverlapDP
+                self.fused = NvlsOverlapDP(flat, opt, self.rank, self.world_size, self.group)
+            else:
+                from llmt.parallel.fused_dp import OverlappedFusedDP
+                self.fused = OverlappedFusedDP(flat, opt, self.rank, self.world_size, self.group)
             return opt
         shard = flat.numel // self.world_size
         self.flat = flat

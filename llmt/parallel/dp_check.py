@@ -21,7 +21,7 @@ import torch.distributed as dist
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--mode", default="fused", choices=["fused", "nccl", "fused-overlap", "nvls"])
+    p.add_argument("--mode", default="fused", choices=["fused", "nccl", "fused-overlap", "nvls", "nvls-overlap"])
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--graph", action="store_true")
     args = p.parse_args()

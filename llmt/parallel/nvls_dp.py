@@ -15,8 +15,15 @@ the bf16 gradient buffer, the bf16 weight buffer (which becomes the model's shad
 a small flag pad are symmetric allocations, and the rendezvous binds the first two to NVLink
 multicast objects; the kernel only receives their multicast addresses. Ranks that cannot get a
 multicast address (no NVSwitch, or a single GPU) raise at set-up.
+
+NvlsOverlapDP runs the same three parts per bucket (a block's parameters, or the trailing
+emb / norm_f / head group) on a side stream as soon as the backward has issued the bucket's
+gradients, so the reductions and the weight multicasts cross NVLink while the backward of the
+earlier blocks computes.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -74,3 +81,70 @@ class NvlsDP:
     def close(self):
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
+
+
+class NvlsOverlapDP(NvlsDP):
+    """The NVLS data-parallel step one bucket at a time, overlapped with the rest of the backward.
+
+    Needs the bucket-sharded optimizer (llmt.parallel.dp.BucketShardedAdamW): rank r owns chunk r
+    of every bucket. When a block's backward has been issued (a hook on the gradient of the
+    block's input), a side stream waits for that point and, on `sms` SMs that the persistent
+    GEMM / attention grids leave free:
+      cast      the bucket's fp32 gradients -> the symmetric bf16 buffer
+      barrier   every rank's cast of the bucket is complete (so every rank's backward has also
+                finished reading the bucket's weights)
+      fused     multimem.ld_reduce + AdamW + multimem.st of this rank's chunk of the bucket
+    After the backward the trailing bucket follows, then a final barrier (every rank's new
+    weights are in every rank's buffer) that the main stream joins before the next forward.
+    `sms` defaults to LLMT_DP_SMS or 16."""
+
+    def __init__(self, flat, opt, rank: int, world: int, group=None, sms: int | None = None):
+        super().__init__(flat, opt, rank, world, group)
+        self.sms = int(os.environ.get("LLMT_DP_SMS", "16")) if sms is None else int(sms)
+        # the side kernels run 4 CTAs of 256 threads per reserved SM; one more SM for the barrier
+        self.blocks = 4 * max(1, self.sms)
+        N.ext().set_reserved_sms(self.sms + 1)
+        self.side = torch.cuda.Stream(device=self.device, priority=-1)
+        self.armed = False
+        self.started = False
+        self.done = set()
+
+    def begin_step(self):
+        """Arm the bucket hooks for the backward that follows (the last micro-batch's)."""
+        self.armed, self.started, self.done = True, False, set()
+
+    def _bucket(self, b):
+        C, o, f = N.ext(), self.opt, self.flat
+        blo, bhi = f.buckets[b]
+        lo, hi = o.ranges[b]
+        moff, n = o.moffs[b], hi - lo
+        if not self.started:
+            o.step_t.add_(1)
+            self.started = True
+        C.cast_bf16(f.grad[blo:bhi], self.g16[blo:bhi], self.blocks)
+        C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 500)
+        b1, b2 = o.betas
+        C.dp_nvls_adamw(self.g_mc, self.w_mc, f.master, o.exp_avg[moff:moff + n], o.exp_avg_sq[moff:moff + n], lo, n,
+                        o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay, o.grad_scale, self.blocks)
+
+    def bucket_ready(self, b):
+        """Called (from the backward's hooks) when bucket b's gradients have all been issued."""
+        if not self.armed or b in self.done:
+            return
+        self.done.add(b)
+        self.side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.side):
+            self._bucket(b)
+
+    @torch.no_grad()
+    def finish_step(self):
+        for b in range(len(self.opt.ranges)):  # the trailing bucket, and any a hook did not reach
+            self.bucket_ready(b)
+        with torch.cuda.stream(self.side):
+            N.ext().dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 600)
+        torch.cuda.current_stream(self.device).wait_stream(self.side)
+        self.armed = False
+
+    def close(self):
+        N.ext().set_reserved_sms(0)
+        super().close()

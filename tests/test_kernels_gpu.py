@@ -114,6 +114,18 @@ def test_adamw_matches_torch(nat):
     assert rel_err(p16, p_ref.detach()) < 1e-2
 
 
+@pytest.mark.parametrize("n,blocks", [(8, 0), (1 << 20, 0), (1 << 20, 3), (1000 * 8 + 8, 5), (1001, 2)])
+def test_cast_bf16_matches_torch(nat, n, blocks):
+    """Vector path (n a multiple of 8, 16-byte aligned) and scalar path, with and without a grid cap
+    (the overlapped data-parallel step casts on a few SMs)."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(n + 8, device="cuda", generator=g)
+    y = torch.full((n + 16,), 7.0, device="cuda", dtype=torch.bfloat16)
+    nat.ext().cast_bf16(x[:n], y[8:8 + n], blocks)
+    assert torch.equal(y[8:8 + n], x[:n].bfloat16())
+    assert bool((y[:8] == 7).all() and (y[8 + n:] == 7).all())
+
+
 def test_ce_rows(nat):
     g = torch.Generator(device="cuda").manual_seed(5)
     R, V = 333, 32000
