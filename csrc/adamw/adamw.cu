@@ -99,13 +99,15 @@ __global__ void cast_bf16_x8_kernel(const float* __restrict__ x, bf16* __restric
 }  // namespace
 
 // zero_grad: also reset g to 0 after reading it (the next step's gradients accumulate into it).
+// max_blocks > 0 caps the grid (a side stream sharing the GPU with the backward).
 cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
-                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st) {
+                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st, int max_blocks) {
   if (n == 0) return cudaSuccess;
   LLMT_REQUIRE(((uintptr_t)p | (uintptr_t)g | (uintptr_t)m | (uintptr_t)v) % 16 == 0,
                "adamw: fp32 buffers must be 16-byte aligned");
   LLMT_REQUIRE(p16 == nullptr || (uintptr_t)p16 % 8 == 0, "adamw: bf16 copy must be 8-byte aligned");
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4 + 1, 256), sm_count() * 8));
+  const int64_t cap = max_blocks > 0 ? max_blocks : sm_count() * 8;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4 + 1, 256), cap));
   bf16* q = static_cast<bf16*>(p16);
   if (p16 && zero_grad) launch_pdl(adamw_kernel<true, true>, grid, 256, 0, st, p, g, m, v, q, n, lr, step, h);
   else if (p16) launch_pdl(adamw_kernel<true, false>, grid, 256, 0, st, p, g, m, v, q, n, lr, step, h);

@@ -55,7 +55,7 @@ struct AdamHyper {
   float b1, b2, eps, wd, grad_scale;
 };
 cudaError_t adamw_step(float* p, float* g, float* m, float* v, void* p16, int64_t n, const float* lr,
-                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st);
+                       const int* step, AdamHyper h, bool zero_grad, cudaStream_t st, int max_blocks = 0);
 cudaError_t cast_bf16(const float* x, void* y, int64_t n, cudaStream_t st, int max_blocks = 0);
 
 // ---------------------------------------------------------------- cross entropy rows
@@ -148,7 +148,7 @@ int gemm_error_code(bool reset);
 // ---------------------------------------------------------------- attention
 cudaError_t flash_attn_fwd(const void* qkv, int64_t ld_qkv, void* o, float* lse, int B, int T, int H, int KV, int hd,
                            bool causal, float scale, cudaStream_t st);
-// dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
+// dsum (2*B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
 cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
                            const float* cos_t, const float* sin_t, void* dqkv, float* dsum, float* dq_acc, int B,
                            int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st);

@@ -32,6 +32,9 @@ constexpr int kBN = 128;  // queries per step
 constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 compute warps (2 per TMEM lane quadrant)
 constexpr int kComputeThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
+// One exponential pair in kBwdPolyEvery runs as the FMA-pipe polynomial (ex2_poly), 0 = none: the
+// SFU issues 16 exponentials per clock per SM, the four schedulers 128 FMA-pipe lanes.
+constexpr int kBwdPolyEvery = 4;
 
 struct AttnBwdArgs {
   const float* lse;   // (B, H, T) natural log
@@ -387,7 +390,8 @@ __device__ __forceinline__ int snake_tile(int r, int i, int G) { return r * G + 
 template <int VARIANT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                           const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
+                           const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
+                           const AttnBwdArgs a) {
   pdl_wait();
   using L = BwdSmemP;
   constexpr int HD = 64;
@@ -578,13 +582,14 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     bool ok = true;
+    bool epi_pending = false;  // this warp's last dK / dV TMA store may still be reading its staging
     int it = 0, tl = 0;
     for (int rr = 0; ok; ++rr, ++tl) {
       const int t = snake_tile(rr, blockIdx.x, G);
       if (t >= n_tiles) break;
       const Tile x = tile_of(t);
       const int kk = x.k0 + r;  // this thread's key (S^T / dP^T phase)
-      // dQ of item n of this tile: TMEM -> registers -> scaled, staged as one 32 x 32 fp32 box per
+      // dQ of item n of this tile: TMEM -> registers, staged as one 32 x 32 fp32 box per
       // warp (SW128) in the item's P buffer (its MMAs are done) -> TMA reduce-add into dq_acc
       auto drain_dq = [&](int n) -> bool {
         const int g = it + n;
@@ -601,8 +606,8 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
-                          __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+              make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]), __uint_as_float(v[4 * u + 2]),
+                          __uint_as_float(v[4 * u + 3]));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -617,18 +622,18 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const int pb = g & 1;
         const int i = x.i_start + n % x.n_i;
         const int qbase = i * kBN;
-        const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (g & 1) * 1024);
-        const float* d_s = lse_s + 128;
+        const float* nl_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (g & 1) * 1024);  // -lse log2(e)
+        const float* nd_s = nl_s + 128;                                                           // -scale D
         if (!wait_bar(s_full, g & 1, err, 48)) { ok = false; break; }
         if (!wait_bar(&pds_empty[pb], ((g >> 1) & 1) ^ 1, err, 49)) { ok = false; break; }
         if (g >= 2) {
-          // buffer pb staged dQ(g - 2) for every warp's TMA reduce: all of them must have read it.
-          // Each warp issued one reduce per block since, dQ(g - 1)'s from the other buffer, which
-          // may still be in flight (waiting for it cost about 1,400 cycles per block).
+          // buffer pb staged dQ(g - 2) for every warp's TMA reduce (issued at the end of the
+          // previous block, this warp's latest bulk group): all of them must have read it.
           if (lane == 0) {
-            bulk_wait_read<1>();
+            bulk_wait_read<0>();
             bar_arrive(stage_free);
           }
+          epi_pending = false;
           __syncwarp();
           if (!wait_bar(stage_free, (g - 2) & 1, err, 52)) { ok = false; break; }
         }
@@ -642,9 +647,14 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
         const int q_lo = (a.causal && qbase < x.k0 + kBM) ? kk - qbase : 0;
         const int q_hi = key_ok ? min(kBN, a.T - qbase) : 0;
         // this warp's 64 columns of S^T and dP^T, 32 at a time; after the second chunk is in
-        // registers the columns are released, so the next block's S^T / dP^T MMAs can start
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
+        // registers the columns are released, so the next block's S^T / dP^T MMAs can start.
+        // Per pair of queries: x = scale log2(e) S - lse log2(e) (one packed FMA, the lse term
+        // negated and scaled by the pre-pass), P = 2^x (one pair in kBwdPolyEvery on the FMA
+        // pipe), dS = P (scale dP - scale D) (a packed FMA and a packed multiply): dS carries the
+        // softmax scale, so dK and dQ need no scaling. Blocks with no masked query in this key row
+        // (all but the diagonal block, and keys past T) skip the mask.
+        auto chunk = [&](int cc, auto masked_tag) {
+          constexpr bool MASKED = decltype(masked_tag)::value;
           const int c = half * 2 + cc;
           uint32_t sv[32], dv[32];
           tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
@@ -655,25 +665,43 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
             bar_arrive(st_read);
           }
           const int lo = q_lo - c * 32, hi = q_hi - c * 32;
-          const float4* l4 = reinterpret_cast<const float4*>(lse_s + c * 32);
-          const float4* d4 = reinterpret_cast<const float4*>(d_s + c * 32);
+          const float4* l4 = reinterpret_cast<const float4*>(nl_s + c * 32);
+          const float4* d4 = reinterpret_cast<const float4*>(nd_s + c * 32);
+          const float2 sl2 = make_float2(a.scale_log2, a.scale_log2), sc2 = make_float2(a.scale, a.scale);
           float p[32], ds[32];
 #pragma unroll
           for (int g4 = 0; g4 < 8; ++g4) {
             const float4 lv = l4[g4], dd = d4[g4];
-            const float la[4] = {lv.x, lv.y, lv.z, lv.w}, da[4] = {dd.x, dd.y, dd.z, dd.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int e = 4 * g4 + q;
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int e = 4 * g4 + 2 * h2;
+              const float2 s2 = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+              const float2 d2 = make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1]));
               if (VARIANT == 2) {
-                p[e] = __uint_as_float(sv[e]);
-                ds[e] = __uint_as_float(dv[e]);
+                p[e] = s2.x;
+                p[e + 1] = s2.y;
+                ds[e] = d2.x;
+                ds[e + 1] = d2.y;
                 continue;
               }
-              float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -la[q] * kLog2e));
-              pe = (e >= lo && e < hi) ? pe : 0.f;
-              p[e] = pe;
-              ds[e] = pe * (__uint_as_float(dv[e]) - da[q]);
+              const float2 x = fma2(s2, sl2, h2 ? make_float2(lv.z, lv.w) : make_float2(lv.x, lv.y));
+              float2 pe;
+              if (kBwdPolyEvery > 0 && (e >> 1) % kBwdPolyEvery == kBwdPolyEvery - 1) {
+                pe.x = ex2_poly(x.x);
+                pe.y = ex2_poly(x.y);
+              } else {
+                pe.x = ex2_approx(x.x);
+                pe.y = ex2_approx(x.y);
+              }
+              if (MASKED) {
+                pe.x = (e >= lo && e < hi) ? pe.x : 0.f;
+                pe.y = (e + 1 >= lo && e + 1 < hi) ? pe.y : 0.f;
+              }
+              const float2 dsv = mul2(pe, fma2(d2, sc2, h2 ? make_float2(dd.z, dd.w) : make_float2(dd.x, dd.y)));
+              p[e] = pe.x;
+              p[e + 1] = pe.y;
+              ds[e] = dsv.x;
+              ds[e + 1] = dsv.y;
             }
           }
 #pragma unroll
@@ -681,60 +709,119 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
             *reinterpret_cast<BF16x8*>(pt + sw_unit(r, c * 4 + u)) = float_to_bf16x8(p + u * 8);
             *reinterpret_cast<BF16x8*>(dst + sw_unit(r, c * 4 + u)) = float_to_bf16x8(ds + u * 8);
           }
+        };
+        // warp-uniform choice: tcgen05.ld is a warp-collective instruction, so the whole warp
+        // takes one path (the diagonal block's first key row alone would need no mask)
+        if (__all_sync(0xffffffffu, q_lo <= 0 && q_hi >= kBN)) {
+          chunk(0, std::false_type{});
+          chunk(1, std::false_type{});
+        } else {
+          chunk(0, std::true_type{});
+          chunk(1, std::true_type{});
         }
         tc_fence_before();
         fence_proxy_async_smem();
         bar_arrive(pds_full);
         if (n > 0 && !drain_dq(n - 1)) { ok = false; break; }
       }
+      // The RoPE table slices of this warp's dK column pairs (16 * half + [0, 16) and + 32): cos
+      // loaded before the last dQ drain, sin after it, so that their latency passes under the
+      // drain and the dK / dV wait (both before would spill).
+      float4 pc[8], ps[8];
+      const int64_t toff = (int64_t)min(kk, a.T - 1) * HD + half * 16;
+#pragma unroll
+      for (int e4 = 0; e4 < 4; ++e4) {
+        pc[e4] = ld_f4(a.cos_t + toff + 4 * e4);
+        pc[4 + e4] = ld_f4(a.cos_t + toff + 32 + 4 * e4);
+      }
       if (ok && x.n_items > 0) ok = drain_dq(x.n_items - 1);
-      // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second; column
-      // pairs (e, e + 32) are handled 16 at a time to keep registers low
+#pragma unroll
+      for (int e4 = 0; e4 < 4; ++e4) {
+        ps[e4] = ld_f4(a.sin_t + toff + 4 * e4);
+        ps[4 + e4] = ld_f4(a.sin_t + toff + 32 + 4 * e4);
+      }
+      // dK (RoPE backward; dS carried the scale) by the first warp of each quadrant, dV by the
+      // second; column pairs (e, e + 32) are handled 16 at a time to keep registers low
+      // dK (RoPE backward; dS carried the scale) and dV: the two warps of a lane quadrant each take
+      // 16 of the 32 column pairs (e, e + 32) of both. A quadrant's 32 full rows leave through one
+      // TMA store per matrix of a 32 x 64 bf16 box staged (128B swizzle) in dS^T buffer 0, which no
+      // MMA reads any more: per-thread stores, each a 16-byte piece of 32 different rows, took about
+      // 25 times as long. A ragged last key block keeps per-thread stores (its rows past T would
+      // fall into the next sequence).
       if (ok && wait_bar(dkv_full, tl & 1, err, 50)) {
         tc_fence_after();
-        const uint32_t col = half == 0 ? C_DK : C_DV;
-        const float sc = half == 0 ? a.scale : 1.f;
-        bf16* drow = a.dqkv + (int64_t)(x.row0 + min(kk, a.T - 1)) * a.ld_qkv +
-                     (half == 0 ? (a.H + x.kvh) : (a.H + a.KV + x.kvh)) * HD;
-#pragma unroll 1
-        for (int j = 0; j < 2; ++j) {
-          uint32_t v1[16], v2[16];
-          tmem_ld16(tmem + lane_off + col + j * 16, v1);
-          tmem_ld16(tmem + lane_off + col + 32 + j * 16, v2);
-          tmem_wait_ld();
-          if (j == 1) {
-            tc_fence_before();
-            bar_arrive(dkv_free);  // the next tile's dV / dK may overwrite these columns now
+        const bool box = x.k0 + quad * 32 + 32 <= a.T;  // uniform across the quadrant's two warps
+        uint8_t* stg_k = smem + L::DS_OFF + quad * 8192;
+        uint8_t* stg_v = stg_k + 4096;
+        if (box && epi_pending) {  // the quadrant's previous TMA stores must have read the boxes
+          if (lane == 0) bulk_wait_read<0>();
+          named_bar_sync(1 + quad, 64);
+        }
+        const int64_t grow = (int64_t)(x.row0 + min(kk, a.T - 1)) * a.ld_qkv;
+        bf16* krow = a.dqkv + grow + (a.H + x.kvh) * HD;
+        bf16* vrow = a.dqkv + grow + (a.H + a.KV + x.kvh) * HD;
+        const int sw = lane & 7;
+        // columns 16 * half + [0, 16) -> 16-byte units 2 half, 2 half + 1; + 32 -> units 4 + 2 half, 5 + 2 half
+        auto put = [&](uint8_t* stg, bf16* grow_ptr, const float* x1, const float* x2) {
+          if (box) {
+            uint8_t* row = stg + lane * 128;
+            *reinterpret_cast<BF16x8*>(row + (((2 * half) ^ sw) << 4)) = float_to_bf16x8(x1);
+            *reinterpret_cast<BF16x8*>(row + (((2 * half + 1) ^ sw) << 4)) = float_to_bf16x8(x1 + 8);
+            *reinterpret_cast<BF16x8*>(row + (((4 + 2 * half) ^ sw) << 4)) = float_to_bf16x8(x2);
+            *reinterpret_cast<BF16x8*>(row + (((5 + 2 * half) ^ sw) << 4)) = float_to_bf16x8(x2 + 8);
+          } else if (kk < a.T) {
+            *reinterpret_cast<BF16x8*>(grow_ptr + half * 16) = float_to_bf16x8(x1);
+            *reinterpret_cast<BF16x8*>(grow_ptr + half * 16 + 8) = float_to_bf16x8(x1 + 8);
+            *reinterpret_cast<BF16x8*>(grow_ptr + 32 + half * 16) = float_to_bf16x8(x2);
+            *reinterpret_cast<BF16x8*>(grow_ptr + 32 + half * 16 + 8) = float_to_bf16x8(x2 + 8);
           }
+        };
+        {
+          uint32_t v1[16], v2[16];
+          tmem_ld16(tmem + lane_off + C_DV + half * 16, v1);
+          tmem_ld16(tmem + lane_off + C_DV + 32 + half * 16, v2);
+          tmem_wait_ld();
           float x1[16], x2[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            x1[e] = __uint_as_float(v1[e]) * sc;
-            x2[e] = __uint_as_float(v2[e]) * sc;
+            x1[e] = __uint_as_float(v1[e]);
+            x2[e] = __uint_as_float(v2[e]);
           }
-          if (kk < a.T) {
-            if (half == 0) {
-              const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD + j * 16);
-              const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD + j * 16);
+          put(stg_v, vrow, x1, x2);
+        }
+        {
+          uint32_t v1[16], v2[16];
+          tmem_ld16(tmem + lane_off + C_DK + half * 16, v1);
+          tmem_ld16(tmem + lane_off + C_DK + 32 + half * 16, v2);
+          tmem_wait_ld();
+          tc_fence_before();
+          bar_arrive(dkv_free);  // the next tile's dV / dK may overwrite these columns now
+          float x1[16], x2[16];
 #pragma unroll
-              for (int e4 = 0; e4 < 4; ++e4) {
-                const float4 c1 = cr[e4], c2 = cr[e4 + 8], s1 = sr[e4], s2 = sr[e4 + 8];
-                const float cl[4] = {c1.x, c1.y, c1.z, c1.w}, ch[4] = {c2.x, c2.y, c2.z, c2.w};
-                const float sl[4] = {s1.x, s1.y, s1.z, s1.w}, sh[4] = {s2.x, s2.y, s2.z, s2.w};
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float cl[4] = {pc[e4].x, pc[e4].y, pc[e4].z, pc[e4].w};
+            const float ch[4] = {pc[4 + e4].x, pc[4 + e4].y, pc[4 + e4].z, pc[4 + e4].w};
+            const float sl[4] = {ps[e4].x, ps[e4].y, ps[e4].z, ps[e4].w};
+            const float sh[4] = {ps[4 + e4].x, ps[4 + e4].y, ps[4 + e4].z, ps[4 + e4].w};
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const int e = e4 * 4 + q;
-                  const float a1 = x1[e], a2 = x2[e];
-                  x1[e] = a1 * cl[q] + a2 * sh[q];
-                  x2[e] = a2 * ch[q] - a1 * sl[q];
-                }
-              }
+            for (int q = 0; q < 4; ++q) {
+              const int e = e4 * 4 + q;
+              const float a1 = __uint_as_float(v1[e]), a2 = __uint_as_float(v2[e]);
+              x1[e] = a1 * cl[q] + a2 * sh[q];
+              x2[e] = a2 * ch[q] - a1 * sl[q];
             }
-            *reinterpret_cast<BF16x8*>(drow + j * 16) = float_to_bf16x8(x1);
-            *reinterpret_cast<BF16x8*>(drow + j * 16 + 8) = float_to_bf16x8(x1 + 8);
-            *reinterpret_cast<BF16x8*>(drow + 32 + j * 16) = float_to_bf16x8(x2);
-            *reinterpret_cast<BF16x8*>(drow + 32 + j * 16 + 8) = float_to_bf16x8(x2 + 8);
           }
+          put(stg_k, krow, x1, x2);
+        }
+        if (box) {
+          fence_proxy_async_smem();
+          named_bar_sync(1 + quad, 64);  // both halves of both boxes are staged
+          if (lane == 0) {
+            const int gcol = (half == 0 ? (a.H + x.kvh) : (a.H + a.KV + x.kvh)) * HD;
+            tma_store_2d(&tm_dkv, half == 0 ? stg_k : stg_v, gcol, x.row0 + x.k0 + quad * 32);
+            bulk_commit();
+          }
+          epi_pending = true;
         }
       } else {
         ok = false;
@@ -755,9 +842,12 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 
 // D = rowsum(dO * O) per (b, h, t); also zeroes the fp32 dQ accumulator row slice.
 // One thread per 8-wide chunk; the HD/8 threads of a (row, head) reduce with shuffles.
+// With nlse2 set (the pipelined kernel) it writes -D * dscale and -lse * log2(e) instead, the two
+// addends of that kernel's packed FMAs (dS = P (scale dP - scale D), P = 2^(scale log2e S - lse log2e)).
 template <int HD>
 __global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dO, float* __restrict__ dsum,
-                                    float* __restrict__ dq_acc, int BT, int T, int H) {
+                                    float* __restrict__ dq_acc, int BT, int T, int H, const float* __restrict__ lse,
+                                    float* __restrict__ nlse2, float dscale) {
   pdl_wait();
   constexpr int G = HD / 8;  // threads per (row, head): 8 or 16, divides the warp
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -782,7 +872,13 @@ __global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __re
     const int64_t row = rh / H;
     const int h = (int)(rh % H);
     const int b = (int)(row / T), t = (int)(row % T);
-    dsum[((int64_t)b * H + h) * T + t] = acc;
+    const int64_t i = ((int64_t)b * H + h) * T + t;
+    if (nlse2) {
+      dsum[i] = -acc * dscale;
+      nlse2[i] = -lse[i] * kLog2e;
+    } else {
+      dsum[i] = acc;
+    }
   }
 }
 
@@ -836,7 +932,7 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
 
 template <int VARIANT>
 cudaError_t launch_bwd_pipelined_v(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
-                                   const AttnBwdArgs& args, cudaStream_t st) {
+                                   const CUtensorMap& tdkv, const AttnBwdArgs& args, cudaStream_t st) {
   constexpr size_t smem = BwdSmemP::TOTAL;
   auto kern = flash_bwd_pipelined_kernel<VARIANT>;
   static bool attr = false;
@@ -846,24 +942,24 @@ cudaError_t launch_bwd_pipelined_v(const CUtensorMap& tq, const CUtensorMap& tdo
     attr = true;
   }
   const int tiles = args.B * args.KV * (int)cdiv(args.T, kBM);
-  launch_pdl(kern, std::min(tiles, persistent_sms()), kBwdThreads, smem, st, tq, tdo, tdq, args);
+  launch_pdl(kern, std::min(tiles, persistent_sms()), kBwdThreads, smem, st, tq, tdo, tdq, tdkv, args);
   return cudaGetLastError();
 }
 
 cudaError_t launch_bwd_pipelined(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
-                                 const AttnBwdArgs& args, cudaStream_t st) {
+                                 const CUtensorMap& tdkv, const AttnBwdArgs& args, cudaStream_t st) {
   static const int variant = [] {
     const char* e = getenv("LLMT_ATTN_VARIANT");
     return e ? atoi(e) : 0;
   }();
-  return variant == 2 ? launch_bwd_pipelined_v<2>(tq, tdo, tdq, args, st)
-                      : launch_bwd_pipelined_v<0>(tq, tdo, tdq, args, st);
+  return variant == 2 ? launch_bwd_pipelined_v<2>(tq, tdo, tdq, tdkv, args, st)
+                      : launch_bwd_pipelined_v<0>(tq, tdo, tdq, tdkv, args, st);
 }
 
 }  // namespace
 
 // dqkv (B*T, ld_qkv) bf16 receives the gradient w.r.t. the packed *pre-RoPE* qkv rows.
-// dsum (B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
+// dsum (2*B*H*T floats) and dq_acc (B*T*H*hd floats) are caller-provided scratch.
 cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, const void* o, const float* lse,
                            const float* cos_t, const float* sin_t, void* dqkv, float* dsum, float* dq_acc, int B,
                            int T, int H, int KV, int hd, bool causal, float scale, cudaStream_t st) {
@@ -877,13 +973,14 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   {
     const int64_t n = rows * H * (hd / 8);
     auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
-    launch_pdl(k, (unsigned)cdiv(n, 256), 256, 0, st, static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum, dq_acc,
-                                              (int)rows, T, H);
+    float* nlse2 = hd == 64 ? dsum + rows * H : nullptr;
+    launch_pdl(k, (unsigned)cdiv(n, 256), 256, 0, st, static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum,
+               dq_acc, (int)rows, T, H, lse, nlse2, scale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   AttnBwdArgs args{};
-  args.lse = lse;
+  args.lse = hd == 64 ? dsum + rows * H : lse;  // hd 64: -lse log2(e) and -scale D (see the pre-pass)
   args.dsum = dsum;
   args.dq_acc = dq_acc;
   args.dqkv = static_cast<bf16*>(dqkv);
@@ -906,7 +1003,18 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
       make_tmap_2d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * hd, rows, (uint64_t)H * hd, 32, 32,
                    CU_TENSOR_MAP_SWIZZLE_128B);
   LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
-  cudaError_t e = hd == 64 ? launch_bwd_pipelined(tq, tdo, tdq, args, st) : launch_bwd<128>(tq, tdo, tdq, args, st);
+  cudaError_t e;
+  if (hd == 64) {
+    // dK / dV boxes of 32 key rows x one head for the pipelined kernel's TMA-store epilogue
+    alignas(64) CUtensorMap tdkv;
+    LLMT_REQUIRE(tma_ok(dqkv, ld_qkv, 2) &&
+                     make_tmap_2d(&tdkv, dqkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows,
+                                  ld_qkv, 64, 32),
+                 "flash_attn_bwd: dqkv tensor map rejected");
+    e = launch_bwd_pipelined(tq, tdo, tdq, tdkv, args, st);
+  } else {
+    e = launch_bwd<128>(tq, tdo, tdq, args, st);
+  }
   if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);

@@ -157,7 +157,8 @@ void embedding_bwd(at::Tensor idx, at::Tensor dx, at::Tensor dW, int64_t v0) {
 
 // ---------------------------------------------------------------- optimizer
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16, at::Tensor lr,
-                at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale, bool zero_grad) {
+                at::Tensor step, double b1, double b2, double eps, double wd, double grad_scale, bool zero_grad,
+                int64_t max_blocks) {
   for (auto* t : {&p, &g, &m, &v, &lr, &step}) on_device(*t, "adamw operand");
   for (auto* t : {&p, &g, &m, &v}) {
     CHECK_DT((*t), at::kFloat);
@@ -173,7 +174,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
   }
   llmt::AdamHyper h{(float)b1, (float)b2, (float)eps, (float)wd, (float)grad_scale};
   ok(llmt::adamw_step(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p16p,
-                      p.numel(), lr.data_ptr<float>(), step.data_ptr<int>(), h, zero_grad, stream()),
+                      p.numel(), lr.data_ptr<float>(), step.data_ptr<int>(), h, zero_grad, stream(), (int)max_blocks),
      "adamw_step");
 }
 
@@ -443,7 +444,7 @@ at::Tensor flash_attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tenso
   CHECK(cos_t.size(0) >= T && cos_t.size(1) == hd && cos_t.is_contiguous() && sin_t.is_contiguous(),
         "flash_attn_bwd: rope tables");
   auto dqkv = at::empty_like(qkv);
-  auto dsum = at::empty({B, H, T}, lse.options());
+  auto dsum = at::empty({2, B, H, T}, lse.options());
   auto dq_acc = at::empty({B * T, H * hd}, lse.options());
   ok(llmt::flash_attn_bwd(dO.data_ptr(), qkv.data_ptr(), qkv.stride(0), o.data_ptr(), lse.data_ptr<float>(),
                           cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), dqkv.data_ptr(), dsum.data_ptr<float>(),
@@ -544,7 +545,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "partial"_a = false);
   m.def("embedding_bwd", &embedding_bwd, "idx"_a, "dx"_a, "dW"_a, "v0"_a = 0);
   m.def("adamw_step", &adamw_step, "p"_a, "g"_a, "m"_a, "v"_a, "p16"_a, "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a,
-        "wd"_a, "grad_scale"_a, "zero_grad"_a = false);
+        "wd"_a, "grad_scale"_a, "zero_grad"_a = false, "max_blocks"_a = 0);
   m.def("cast_bf16", &cast_bf16, "x"_a, "y"_a, "max_blocks"_a = 0);
   m.def("ce_fwd_rows", &ce_fwd_rows);
   m.def("ce_bwd_rows", &ce_bwd_rows);

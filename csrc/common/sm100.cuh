@@ -320,6 +320,11 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   return o;
 }
 // max of three (sm_100 three-input max)
+// Named barrier `id` (1..15; 0 is __syncthreads) across `nthreads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

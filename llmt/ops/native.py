@@ -401,13 +401,13 @@ def embedding_bwd(idx, dx, dW, v0=0):
     ext().embedding_bwd(idx.reshape(-1), dx, dW, int(v0))
 
 
-def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0, zero_grad=False):
+def adamw_step(p, g, m, v, p16, lr, step, b1, b2, eps, wd, grad_scale=1.0, zero_grad=False, max_blocks=0):
     ext().adamw_step(p, g, m, v, p16, lr, step, float(b1), float(b2), float(eps), float(wd), float(grad_scale),
-                     bool(zero_grad))
+                     bool(zero_grad), int(max_blocks))
 
 
-def cast_bf16(x, y):
-    ext().cast_bf16(x, y)
+def cast_bf16(x, y, max_blocks=0):
+    ext().cast_bf16(x, y, int(max_blocks))
 
 
 def ce_fwd_rows(logits, targets, lse, loss):
