@@ -72,8 +72,11 @@ struct FwdSmem {
   static constexpr uint32_t Q_OFF = 0;
   static constexpr uint32_t K_OFF = Q_OFF + QST * 2 * QB_BYTES;
   static constexpr uint32_t V_OFF = K_OFF + KVST * KV_BYTES;
-  static constexpr uint32_t BAR_OFF = V_OFF + KVST * KV_BYTES;
+  // O staging: one 32-row x 64-column bf16 box (4 KB, 128B swizzle) per softmax warp
+  static constexpr uint32_t OST_OFF = V_OFF + KVST * KV_BYTES;
+  static constexpr uint32_t BAR_OFF = OST_OFF + 8 * 4096;
   static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;
+  static_assert(TOTAL <= 232448, "attention forward shared memory exceeds the per-CTA limit");
 };
 
 __device__ __forceinline__ int fwd_snake(int r, int i, int G) { return r * G + ((r & 1) ? (G - 1 - i) : i); }
@@ -93,7 +96,8 @@ __device__ __forceinline__ int fwd_nkv(int q0, int half, int T, int causal) {
 // Chosen at run time with LLMT_ATTN_VARIANT for measurements only.
 template <int HD, int VARIANT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a) {
+flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_o,
+                 const AttnFwdArgs a) {
   pdl_wait();
   using L = FwdSmem<HD>;
   constexpr int QST = L::QST;
@@ -424,13 +428,40 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
       if (!wait_bar(&o_done[w], (cnt - 1) & 1, err, 20)) { ok = false; break; }
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      // A warp's 32 full rows leave through TMA stores of 32 x 64 bf16 boxes staged (128B swizzle)
+      // in its own 4 KB slot: per-thread stores of 16-byte row pieces, 32 rows per instruction,
+      // are many times slower. Rows of a ragged last block keep per-thread stores (rows past T
+      // belong to the next sequence).
+      const bool box = qb0 + quad * 32 + 32 <= a.T;  // warp-uniform
+      uint8_t* stg = smem + L::OST_OFF + (warp - 2) * 4096;
       bf16* orow = a.o + (int64_t)(x.row0 + min(q, a.T - 1)) * a.ld_o + x.h * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
         tmem_ld32(t_o + c * 32, v);
         tmem_wait_ld();
-        if (q < a.T) {
+        if (box) {
+          if ((c & 1) == 0) {  // the slot's previous box must have been read by its TMA store
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float tt[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) tt[e] = __uint_as_float(v[u * 8 + e]) * inv;
+            const int unit = (c & 1) * 4 + u;
+            *reinterpret_cast<BF16x8*>(stg + lane * 128 + ((unit ^ (lane & 7)) << 4)) = float_to_bf16x8(tt);
+          }
+          if (c & 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_o, stg, x.h * HD + (c >> 1) * 64, x.row0 + qb0 + quad * 32);
+              bulk_commit();
+            }
+          }
+        } else if (q < a.T) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             float tt[8];
@@ -447,6 +478,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
                                                                : -INFINITY;
     }
   }
+  if (warp >= 2) {  // the softmax warps' O stores are complete before the CTA exits
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
   pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled
   tc_fence_before();
   __syncthreads();
@@ -457,7 +492,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnFwdArgs a
 }
 
 template <int HD, int VARIANT>
-cudaError_t launch_fwd_v(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
+cudaError_t launch_fwd_v(const CUtensorMap& tm, const CUtensorMap& tmo, const AttnFwdArgs& args, cudaStream_t st) {
   auto kern = flash_fwd_kernel<HD, VARIANT>;
   constexpr size_t smem = FwdSmem<HD>::TOTAL;
   static bool attr = false;
@@ -467,20 +502,20 @@ cudaError_t launch_fwd_v(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStr
     attr = true;
   }
   const int tiles = args.B * args.H * (int)cdiv(args.T, kTileM);
-  launch_pdl(kern, std::min(tiles, persistent_sms()), kAttnThreads, smem, st, tm, args);
+  launch_pdl(kern, std::min(tiles, persistent_sms()), kAttnThreads, smem, st, tm, tmo, args);
   return cudaGetLastError();
 }
 
 template <int HD>
-cudaError_t launch_fwd(const CUtensorMap& tm, const AttnFwdArgs& args, cudaStream_t st) {
+cudaError_t launch_fwd(const CUtensorMap& tm, const CUtensorMap& tmo, const AttnFwdArgs& args, cudaStream_t st) {
   static const int variant = [] {
     const char* e = getenv("LLMT_ATTN_VARIANT");
     return e ? atoi(e) : 0;
   }();
-  if (variant == 1) return launch_fwd_v<HD, 1>(tm, args, st);
-  if (variant == 2) return launch_fwd_v<HD, 2>(tm, args, st);
-  if (variant == 3) return launch_fwd_v<HD, 3>(tm, args, st);
-  return launch_fwd_v<HD, 0>(tm, args, st);
+  if (variant == 1) return launch_fwd_v<HD, 1>(tm, tmo, args, st);
+  if (variant == 2) return launch_fwd_v<HD, 2>(tm, tmo, args, st);
+  if (variant == 3) return launch_fwd_v<HD, 3>(tm, tmo, args, st);
+  return launch_fwd_v<HD, 0>(tm, tmo, args, st);
 }
 
 }  // namespace
@@ -523,7 +558,11 @@ cudaError_t flash_attn_fwd(const void* qkv, int64_t ld_qkv, void* o, float* lse,
   LLMT_REQUIRE(make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd,
                             (uint64_t)B * T, ld_qkv, 64, 128),
                "flash_attn_fwd: tensor map rejected");
-  return hd == 64 ? launch_fwd<64>(tm, args, st) : launch_fwd<128>(tm, args, st);
+  alignas(64) CUtensorMap tmo;  // 32-row x 64-column boxes of o for the TMA-store epilogue
+  LLMT_REQUIRE(tma_ok(o, (int64_t)H * hd, 2) && make_tmap_2d(&tmo, o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                                             (uint64_t)H * hd, (uint64_t)B * T, (uint64_t)H * hd, 64, 32),
+               "flash_attn_fwd: output tensor map rejected");
+  return hd == 64 ? launch_fwd<64>(tm, tmo, args, st) : launch_fwd<128>(tm, tmo, args, st);
 }
 
 }  // namespace llmt
