@@ -359,8 +359,8 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
 //   compute warps:     P, dS of block n (S^T/dP^T(n) already in TMEM) -> drain dQ(n-1)
 // so block n+1's S^T/dP^T and block n's dV/dK/dQ run while the compute warps turn block
 // n+1 into P/dS. P and dS are double-buffered in shared memory; dQ leaves TMEM one block
-// late as vector fp32 reductions straight from registers (red.global.add.v4.f32), with no
-// staging buffer. TMEM: S^T 0-127, dP^T 128-255, dV 256-319, dK 320-383, dQ 384-447.
+// late, staged in the block's P buffer (its dV MMAs are done) and reduced into the fp32 dQ
+// accumulator by TMA. TMEM: S^T 0-127, dP^T 128-255, dV 256-319, dK 320-383, dQ 384-447.
 struct BwdSmemP {
   static constexpr uint32_t TILE = 128 * 64 * 2;  // one 128 x 64 bf16 tile (16 KB)
   static constexpr uint32_t K_OFF = 0;

@@ -31,7 +31,8 @@ def main():
     p.add_argument("--microbatches", type=int, default=1)
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--dp-mode", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--dp-mode", default="auto", choices=["auto", "nvls", "nccl", "fused"],
+                   help="data-parallel transport (auto: nvls where NVLink multicast exists, else nccl)")
     p.add_argument("--json", default=None)
     p.add_argument("--calibrate", action="store_true",
                    help="also predict from this rank's GEMM / attention shapes timed on the GPU")
@@ -49,8 +50,10 @@ def main():
     cfg = get_config(args.model)
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     B = args.global_batch // args.dp
+    from llmt.parallel.dp import pick_mode
+    dp_mode = pick_mode(args.dp_mode, local)
     tr = ParallelTrainer(cfg, B, args.seq, lay, microbatches=args.microbatches, device=f"cuda:{local}",
-                         init="local", dp_mode=args.dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
+                         init="local", dp_mode=dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
     g = torch.Generator().manual_seed(1 + tr.groups.dp_rank)
     idx = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
     tgt = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
@@ -73,7 +76,7 @@ def main():
     tokens = args.global_batch * args.seq
     res = {"model": args.model, "seq": args.seq, "global_batch": args.global_batch,
            "layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches, "n_gpus": world,
-           "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm,
+           "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm, "dp_mode": dp_mode if args.dp > 1 else None,
            "ms_per_step": round(ms.item(), 3), "tokens_per_s": round(tokens / step_s, 1),
            "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2), "dtype": "bf16",
            "data": "synthetic uniform-random tokens, random-init weights", "timing": "CUDA events, max over ranks"}
