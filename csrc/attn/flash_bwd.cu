@@ -73,7 +73,8 @@ struct BwdSmem {
 template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdArgs a) {
+                 const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dkv,
+                 const AttnBwdArgs a) {
   pdl_wait();
   using L = BwdSmem<HD>;
   constexpr int ST = L::STAGES;
@@ -197,6 +198,7 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
           mma_f16(tmem + C_DK, make_sw128_desc(ds_addr + offk, 16, 1024), make_sw128_desc(q_addr + offm, 16384, 1024),
                   id_kv, (n > 0 || k > 0) ? 1u : 0u);
         }
+        mma_commit(&q_empty[s]);  // dQ reads no Q / dO: the stage can refill once dV / dK are done
 #pragma unroll
         for (int k = 0; k < kBM / 16; ++k) {  // contraction over keys
           mma_f16(tmem + C_DQ, make_sw128_desc(ds_addr + k * 2048, 16384, 1024),
@@ -204,7 +206,6 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
         }
         mma_commit(dq_full);
         mma_commit(pds_empty);
-        mma_commit(&q_empty[s]);
       }
       if (ok) mma_commit(dkv_full);
     }
@@ -220,9 +221,9 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
     for (int n = 0; n < n_items; ++n) {
       const int hq = kvh * group + n / n_i, i = i_start + n % n_i;
       const int qbase = i * kBN;
-      // s_full implies this item's Q/dO stage (and its lse / D vectors) has landed
-      const float* lse_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n % ST) * 1024);
-      const float* d_s = lse_s + 128;
+      // s_full implies this item's Q/dO stage (and its -lse log2(e) / -scale D vectors) has landed
+      const float* nl_s = reinterpret_cast<const float*>(smem + L::VEC_OFF + (n % ST) * 1024);
+      const float* nd_s = nl_s + 128;
       if (!wait_bar(s_full, n & 1, err, 36)) { ok = false; break; }
       if (!wait_bar(pds_empty, (n & 1) ^ 1, err, 37)) { ok = false; break; }
       tc_fence_after();
@@ -238,23 +239,40 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
         tmem_ld32(tmem + lane_off + C_S + c * 32, sv);
         tmem_ld32(tmem + lane_off + C_DP + c * 32, dv);
         tmem_wait_ld();
+        // the same packed form as the pipelined kernel: x = scale log2(e) S - lse log2(e),
+        // dS = P (scale dP - scale D) with both addends prepared by the pre-pass
         float p[32], ds[32];
-        if (diag || !key_ok || q_tail) {
+        const bool masked = diag || !key_ok || q_tail;
+        const float4* l4 = reinterpret_cast<const float4*>(nl_s + c * 32);
+        const float4* d4 = reinterpret_cast<const float4*>(nd_s + c * 32);
+        const float2 sl2 = make_float2(a.scale_log2, a.scale_log2), sc2 = make_float2(a.scale, a.scale);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qi = c * 32 + e;
-            const bool valid = key_ok && (!diag || qbase + qi >= kk) && qbase + qi < a.T;
-            const float pe = valid ? ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e)) : 0.f;
-            p[e] = pe;
-            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
-          }
-        } else {
+        for (int g4 = 0; g4 < 8; ++g4) {
+          const float4 lv = l4[g4], dd = d4[g4];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qi = c * 32 + e;
-            const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), a.scale_log2, -lse_s[qi] * kLog2e));
-            p[e] = pe;
-            ds[e] = pe * (__uint_as_float(dv[e]) - d_s[qi]);
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int e = 4 * g4 + 2 * h2;
+            const float2 x = fma2(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), sl2,
+                                  h2 ? make_float2(lv.z, lv.w) : make_float2(lv.x, lv.y));
+            float2 pe;
+            if (kBwdPolyEvery > 0 && (e >> 1) % kBwdPolyEvery == kBwdPolyEvery - 1) {
+              pe.x = ex2_poly(x.x);
+              pe.y = ex2_poly(x.y);
+            } else {
+              pe.x = ex2_approx(x.x);
+              pe.y = ex2_approx(x.y);
+            }
+            if (masked) {
+              const int qi = qbase + c * 32 + e;
+              pe.x = (key_ok && (!diag || qi >= kk) && qi < a.T) ? pe.x : 0.f;
+              pe.y = (key_ok && (!diag || qi + 1 >= kk) && qi + 1 < a.T) ? pe.y : 0.f;
+            }
+            const float2 dsv = mul2(pe, fma2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), sc2,
+                                             h2 ? make_float2(dd.z, dd.w) : make_float2(dd.x, dd.y)));
+            p[e] = pe.x;
+            p[e + 1] = pe.y;
+            ds[e] = dsv.x;
+            ds[e + 1] = dsv.y;
           }
         }
 #pragma unroll
@@ -266,7 +284,7 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
       tc_fence_before();
       fence_proxy_async_smem();
       bar_arrive(pds_full);
-      // dQ rows (thread = query row of this block): scale, stage as 32x32 fp32 boxes, TMA reduce-add
+      // dQ rows (thread = query row of this block): stage as 32x32 fp32 boxes, TMA reduce-add
       if (!wait_bar(dq_full, n & 1, err, 38)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll 1
@@ -282,8 +300,8 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
-                          __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+              make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]), __uint_as_float(v[4 * u + 2]),
+                          __uint_as_float(v[4 * u + 3]));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -296,30 +314,39 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
-    // dK (scaled, RoPE backward) by the first warp of each quadrant, dV by the second; column
-    // pairs (e, e + HD/2) 16 at a time, so no HD-wide row is held in registers
+    // dK (RoPE backward; dS carried the scale) and dV: the two warps of a lane quadrant each take
+    // HD/4 of the HD/2 column pairs (e, e + HD/2) of both, 16 at a time. A quadrant's 32 full rows
+    // leave through TMA stores of 32 x 64 bf16 boxes (HD/64 per matrix) staged with the 128B
+    // swizzle in the P / dS buffers, which no MMA reads any more; per-thread stores of 16-byte
+    // pieces of 32 rows are many times slower. A ragged last key block keeps per-thread stores.
     if (ok && wait_bar(dkv_full, 0, err, 39)) {
       tc_fence_after();
-      const uint32_t col = half == 0 ? C_DK : C_DV;
-      const float sc = half == 0 ? a.scale : 1.f;
-      bf16* drow = a.dqkv + (int64_t)(row0 + min(kk, a.T - 1)) * a.ld_qkv +
-                   (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+      constexpr int NB = HD / 64;  // boxes per matrix and quadrant
+      const bool box = k0 + quad * 32 + 32 <= a.T;  // uniform across the quadrant's two warps
+      uint8_t* stg = smem + L::P_OFF + quad * (2 * NB * 4096);  // dK boxes, then dV boxes
+      const int64_t grow = (int64_t)(row0 + min(kk, a.T - 1)) * a.ld_qkv;
+      const int sw = lane & 7;
 #pragma unroll 1
-      for (int j = 0; j < HD / 32; ++j) {
-        uint32_t v1[16], v2[16];
-        tmem_ld16(tmem + lane_off + col + j * 16, v1);
-        tmem_ld16(tmem + lane_off + col + HD / 2 + j * 16, v2);
-        tmem_wait_ld();
-        float x1[16], x2[16];
+      for (int m = 0; m < 2; ++m) {  // 0: dV, 1: dK
+        const uint32_t col = m ? C_DK : C_DV;
+        bf16* drow = a.dqkv + grow + (m ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+        uint8_t* mst = stg + (m ? 0 : NB * 4096);
+#pragma unroll 1
+        for (int jj = 0; jj < HD / 64; ++jj) {
+          const int e0 = half * (HD / 4) + jj * 16;  // first column of this step's pairs
+          uint32_t v1[16], v2[16];
+          tmem_ld16(tmem + lane_off + col + e0, v1);
+          tmem_ld16(tmem + lane_off + col + HD / 2 + e0, v2);
+          tmem_wait_ld();
+          float x1[16], x2[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          x1[e] = __uint_as_float(v1[e]) * sc;
-          x2[e] = __uint_as_float(v2[e]) * sc;
-        }
-        if (kk < a.T) {
-          if (half == 0) {
-            const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD + j * 16);
-            const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD + j * 16);
+          for (int e = 0; e < 16; ++e) {
+            x1[e] = __uint_as_float(v1[e]);
+            x2[e] = __uint_as_float(v2[e]);
+          }
+          if (m == 1 && kk < a.T) {
+            const float4* cr = reinterpret_cast<const float4*>(a.cos_t + (int64_t)kk * HD + e0);
+            const float4* sr = reinterpret_cast<const float4*>(a.sin_t + (int64_t)kk * HD + e0);
 #pragma unroll
             for (int e4 = 0; e4 < 4; ++e4) {
               const float4 c1 = cr[e4], c2 = cr[e4 + HD / 8], s1 = sr[e4], s2 = sr[e4 + HD / 8];
@@ -334,11 +361,36 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
               }
             }
           }
-          *reinterpret_cast<BF16x8*>(drow + j * 16) = float_to_bf16x8(x1);
-          *reinterpret_cast<BF16x8*>(drow + j * 16 + 8) = float_to_bf16x8(x1 + 8);
-          *reinterpret_cast<BF16x8*>(drow + HD / 2 + j * 16) = float_to_bf16x8(x2);
-          *reinterpret_cast<BF16x8*>(drow + HD / 2 + j * 16 + 8) = float_to_bf16x8(x2 + 8);
+          if (box) {
+            // columns e0 .. e0 + 15 and e0 + HD/2 ..: box (c / 64), 16-byte unit (c % 64) / 8
+            const int u0 = (e0 % 64) / 8;
+            uint8_t* r1 = mst + (e0 / 64) * 4096 + lane * 128;
+            uint8_t* r2 = mst + ((e0 + HD / 2) / 64) * 4096 + lane * 128;
+            *reinterpret_cast<BF16x8*>(r1 + ((u0 ^ sw) << 4)) = float_to_bf16x8(x1);
+            *reinterpret_cast<BF16x8*>(r1 + (((u0 + 1) ^ sw) << 4)) = float_to_bf16x8(x1 + 8);
+            *reinterpret_cast<BF16x8*>(r2 + ((u0 ^ sw) << 4)) = float_to_bf16x8(x2);
+            *reinterpret_cast<BF16x8*>(r2 + (((u0 + 1) ^ sw) << 4)) = float_to_bf16x8(x2 + 8);
+          } else if (kk < a.T) {
+            *reinterpret_cast<BF16x8*>(drow + e0) = float_to_bf16x8(x1);
+            *reinterpret_cast<BF16x8*>(drow + e0 + 8) = float_to_bf16x8(x1 + 8);
+            *reinterpret_cast<BF16x8*>(drow + HD / 2 + e0) = float_to_bf16x8(x2);
+            *reinterpret_cast<BF16x8*>(drow + HD / 2 + e0 + 8) = float_to_bf16x8(x2 + 8);
+          }
         }
+      }
+      if (box) {
+        fence_proxy_async_smem();
+        named_bar_sync(1 + quad, 64);  // both warps' halves of the quadrant's boxes are staged
+        if (lane == 0) {
+          // the first warp stores the dK boxes, the second the dV boxes
+          const int gcol = (half == 0 ? (a.H + kvh) : (a.H + a.KV + kvh)) * HD;
+          uint8_t* src = stg + (half == 0 ? 0 : NB * 4096);
+#pragma unroll
+          for (int bx = 0; bx < NB; ++bx) tma_store_2d(&tm_dkv, src + bx * 4096, gcol + bx * 64, row0 + k0 + quad * 32);
+          bulk_commit();
+          bulk_wait<0>();  // the boxes are read (and written) before the CTA's shared memory goes away
+        }
+        __syncwarp();
       }
     }
   }
@@ -842,8 +894,8 @@ flash_bwd_pipelined_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __g
 
 // D = rowsum(dO * O) per (b, h, t); also zeroes the fp32 dQ accumulator row slice.
 // One thread per 8-wide chunk; the HD/8 threads of a (row, head) reduce with shuffles.
-// With nlse2 set (the pipelined kernel) it writes -D * dscale and -lse * log2(e) instead, the two
-// addends of that kernel's packed FMAs (dS = P (scale dP - scale D), P = 2^(scale log2e S - lse log2e)).
+// With nlse2 set (both backward kernels) it writes -D * dscale and -lse * log2(e) instead, the two
+// addends of their packed FMAs (dS = P (scale dP - scale D), P = 2^(scale log2e S - lse log2e)).
 template <int HD>
 __global__ void attn_bwd_pre_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dO, float* __restrict__ dsum,
                                     float* __restrict__ dq_acc, int BT, int T, int H, const float* __restrict__ lse,
@@ -915,8 +967,8 @@ __global__ void attn_bwd_post_kernel(const float* __restrict__ dq_acc, bf16* __r
 }
 
 template <int HD>
-cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq, const AttnBwdArgs& args,
-                       cudaStream_t st) {
+cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq, const CUtensorMap& tdkv,
+                       const AttnBwdArgs& args, cudaStream_t st) {
   auto kern = flash_bwd_kernel<HD>;
   constexpr size_t smem = BwdSmem<HD>::TOTAL;
   static bool attr = false;
@@ -926,7 +978,7 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
     attr = true;
   }
   dim3 grid((unsigned)cdiv(args.T, kBM), args.B * args.KV);
-  launch_pdl(kern, grid, kBwdThreads, smem, st, tq, tdo, tdq, args);
+  launch_pdl(kern, grid, kBwdThreads, smem, st, tq, tdo, tdq, tdkv, args);
   return cudaGetLastError();
 }
 
@@ -973,14 +1025,14 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
   {
     const int64_t n = rows * H * (hd / 8);
     auto k = hd == 64 ? attn_bwd_pre_kernel<64> : attn_bwd_pre_kernel<128>;
-    float* nlse2 = hd == 64 ? dsum + rows * H : nullptr;
+    float* nlse2 = dsum + rows * H;
     launch_pdl(k, (unsigned)cdiv(n, 256), 256, 0, st, static_cast<const bf16*>(o), static_cast<const bf16*>(dO), dsum,
                dq_acc, (int)rows, T, H, lse, nlse2, scale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   AttnBwdArgs args{};
-  args.lse = hd == 64 ? dsum + rows * H : lse;  // hd 64: -lse log2(e) and -scale D (see the pre-pass)
+  args.lse = dsum + rows * H;  // -lse log2(e); args.dsum holds -scale D (see the pre-pass)
   args.dsum = dsum;
   args.dq_acc = dq_acc;
   args.dqkv = static_cast<bf16*>(dqkv);
@@ -1003,18 +1055,14 @@ cudaError_t flash_attn_bwd(const void* dO, const void* qkv, int64_t ld_qkv, cons
       make_tmap_2d(&tdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)H * hd, rows, (uint64_t)H * hd, 32, 32,
                    CU_TENSOR_MAP_SWIZZLE_128B);
   LLMT_REQUIRE(ok, "flash_attn_bwd: tensor map rejected");
-  cudaError_t e;
-  if (hd == 64) {
-    // dK / dV boxes of 32 key rows x one head for the pipelined kernel's TMA-store epilogue
-    alignas(64) CUtensorMap tdkv;
-    LLMT_REQUIRE(tma_ok(dqkv, ld_qkv, 2) &&
-                     make_tmap_2d(&tdkv, dqkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows,
-                                  ld_qkv, 64, 32),
-                 "flash_attn_bwd: dqkv tensor map rejected");
-    e = launch_bwd_pipelined(tq, tdo, tdq, tdkv, args, st);
-  } else {
-    e = launch_bwd<128>(tq, tdo, tdq, args, st);
-  }
+  // dK / dV boxes of 32 key rows x 64 columns for the TMA-store epilogues
+  alignas(64) CUtensorMap tdkv;
+  LLMT_REQUIRE(tma_ok(dqkv, ld_qkv, 2) &&
+                   make_tmap_2d(&tdkv, dqkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)(H + 2 * KV) * hd, rows,
+                                ld_qkv, 64, 32),
+               "flash_attn_bwd: dqkv tensor map rejected");
+  cudaError_t e = hd == 64 ? launch_bwd_pipelined(tq, tdo, tdq, tdkv, args, st)
+                           : launch_bwd<128>(tq, tdo, tdq, tdkv, args, st);
   if (e != cudaSuccess) return e;
   {
     const int64_t n = rows * H * (hd / 16);
