@@ -52,8 +52,11 @@ void gemm_plan(int M, int N, int K, int epi, bool can_split, int* bn, int* split
     for (int s = 1; s <= smax; ++s) {
       const int64_t kps = cdiv(kb, s);
       const int64_t units = tiles * cdiv(kb, kps);
-      // BN=128 tiles reach ~70% of the BN=256 per-FLOP rate (operand smem bandwidth)
-      const double cost = (double)cdiv(units, sms) * (double)(kps + 3) * (BN == 256 ? 2.0 : 1.45) * (s > 1 ? 1.15 : 1.0);
+      // BN=128 tiles reach ~70% of the BN=256 per-FLOP rate (operand smem bandwidth). A split
+      // pays for its reduce-add traffic and for clearing the output first: measured on the
+      // medium weight gradients (K 4096), 1.3x per unit plus a fixed 10 units (~2 us)
+      const double cost = (double)cdiv(units, sms) * (double)(kps + 3) * (BN == 256 ? 2.0 : 1.45) * (s > 1 ? 1.3 : 1.0) +
+                          (s > 1 ? 10.0 : 0.0);
       if (cost < best - 1e-9) {
         best = cost;
         *bn = BN;
