@@ -2,15 +2,19 @@
 step on a flat buffer of a model's parameter count, timed with CUDA events between barriers,
 max over ranks, against their NVLink roofline.
 
-The roofline of one step is the slowest of three resources of one GPU:
-  egress   NVLink, the reduce-scatter: every gradient byte of the other ranks' shards leaves this
-           GPU once, (N - 1) / N x P x bytes-per-gradient, at the measured peer-copy bandwidth
-           per direction (llmt/perf/links.json)
-  ingress  NVLink, the all-gather: the other ranks' new bf16 weights arrive once,
-           (N - 1) / N x P x 2
-  HBM      the local passes: the gradient cast (NVLS: read 4 B, write 2 B per parameter), AdamW on
-           the shard (master, m, v read and written: 24 B per shard parameter) and the arriving
-           bf16 weights (2 B per parameter), at the measured copy bandwidth (MEASURED_PEAKS.json)
+The roofline of one step, per GPU (P parameters, N ranks):
+  nccl     reduce-scatter of fp32 gradients and all-gather of bf16 weights: (N - 1) / N x P x 4
+           bytes leave (and (N - 1) / N x P x 2 arrive) at the measured peer-copy bandwidth per
+           direction (llmt/perf/links.json); HBM for the cast, the AdamW shard (master, m, v read
+           and written: 24 B per shard parameter) and the arriving weights in parallel
+  nvls     the bf16 cast first (read 4 B, write 2 B per parameter: HBM, in series), then the
+           multicast kernel, bound by the larger of its NVLink bytes and its HBM bytes. Through
+           the switch every rank's whole bf16 gradient is read once for the ld_reduce of all
+           shards (P x 2 leave, this GPU's own shard included) and every shard's new weights
+           land in every rank, this one included (P x 2 arrive), plus the shard's reduced
+           gradient (P / N x 2 in) and its multicast stores (P / N x 2 out): (1 + 1 / N) x P x 2
+           each way. Kernel HBM: the gradient read by the switch (2 B), the AdamW shard
+           (24 B / N) and the arriving weights (2 B) per parameter
 The NVLS kernel moves bf16 gradients (its cast is part of the timed step); the NCCL step
 reduce-scatters the fp32 gradients as the "nccl" mode does.
 
@@ -84,14 +88,22 @@ def main():
         ms = torch.tensor([a.elapsed_time(b) / args.iters], device="cuda")
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         gbytes = 2 if mode == "nvls" else 4
-        egress = (world - 1) / world * numel * gbytes
-        ingress = (world - 1) / world * numel * 2
-        hbm = (6 * numel if mode == "nvls" else 4 * numel) + 24 * numel / world + 2 * numel
-        roof_ms = max(max(egress, ingress) / (link_gbs * 1e9), hbm / (hbm_gbs * 1e9)) * 1e3
+        if mode == "nvls":
+            link = (1 + 1 / world) * numel * 2
+            serial_hbm = 6 * numel                                  # the cast, before the kernel
+            hbm = 2 * numel + 24 * numel / world + 2 * numel        # inside the kernel
+        else:
+            link = (world - 1) / world * numel * 4
+            serial_hbm = 0
+            hbm = 4 * numel + 24 * numel / world + 2 * numel
+        link_ms = link / (link_gbs * 1e9) * 1e3
+        hbm_ms = hbm / (hbm_gbs * 1e9) * 1e3
+        serial_ms = serial_hbm / (hbm_gbs * 1e9) * 1e3
+        roof_ms = serial_ms + max(link_ms, hbm_ms)
         err = dp.fused.error_code() if dp.fused is not None and hasattr(dp.fused, "error_code") else 0
         out["modes"][mode] = {"ms_per_step": round(ms.item(), 4), "roofline_ms": round(roof_ms, 4),
-                              "nvlink_ms": round(max(egress, ingress) / (link_gbs * 1e9) * 1e3, 4),
-                              "hbm_ms": round(hbm / (hbm_gbs * 1e9) * 1e3, 4),
+                              "nvlink_ms": round(link_ms, 4), "hbm_ms": round(hbm_ms, 4),
+                              "serial_hbm_ms": round(serial_ms, 4),
                               "fraction_of_roofline": round(roof_ms / ms.item(), 3),
                               "gradient_bytes_per_param": gbytes, "dp_error_code": err}
         dp.close()
