@@ -151,8 +151,8 @@ def run_native(args, rank, world, local):
     cfg = get_config(MODEL)
     dp = None
     if world > 1:
-        from llmt.parallel.dp import DataParallel, pick_mode
-        dp = DataParallel(world, rank, mode=pick_mode(args.dp_mode, local))
+        from llmt.parallel.dp import DataParallel
+        dp = DataParallel(world, rank, mode=args.dp_mode)  # "auto": NVLS where multicast exists
     tr = Trainer(cfg, PER_GPU_BATCH, SEQ, device=f"cuda:{local}", cuda_graph=not args.no_graph, dp=dp,
                  linear=args.linear)
     idx, tgt = make_batch(PER_GPU_BATCH, SEQ, cfg.vocab, "cpu", seed=rank)
@@ -177,9 +177,10 @@ def run_native(args, rank, world, local):
     tflops = model_flops_per_token(cfg, SEQ) * tok_s / world / 1e12
     err = native.gemm_error_code() | native.attn_error_code() | native.ext().dp_error_code(False)
     tr.release()
+    dp_mode = dp.mode if dp is not None else None
     if dp is not None:
         dp.close()
-    return dict(value=tok_s, ms_per_step=ms_step, mfu=tflops / peak_tflops(), tflops_per_gpu=tflops,
+    return dict(value=tok_s, ms_per_step=ms_step, mfu=tflops / peak_tflops(), tflops_per_gpu=tflops, dp_mode=dp_mode,
                 e2e=dict(value=round(e2e_tok_s, 1), unit="tokens/s", h2d_bytes_per_step=2 * idx.numel() * 8,
                          d2h_bytes_per_step=4, wall_ms_per_step=round(e2e_wall / args.steps, 3)),
                 gpu_launches=launches_per_step * args.steps, final_loss=losses[-1] if losses else None,
@@ -299,7 +300,8 @@ def main():
                 "data": "synthetic uniform-random tokens, random-init weights",
                 "config": {"model": MODEL, "global_batch": PER_GPU_BATCH * world, "seq_len": SEQ,
                            "parallelism": par, "l2": "working set >> 126 MB L2; no flush", "linear": args.linear,
-                           "mfu": round(res["mfu"], 4), "tflops_per_gpu": round(res["tflops_per_gpu"], 1)},
+                           "mfu": round(res["mfu"], 4), "tflops_per_gpu": round(res["tflops_per_gpu"], 1),
+                           "dp_transport": res.get("dp_mode")},
                 "clocks": res["clocks"],
             }
             line["e2e"] = res["e2e"]

@@ -50,10 +50,9 @@ def main():
     cfg = get_config(args.model)
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     B = args.global_batch // args.dp
-    from llmt.parallel.dp import pick_mode
-    dp_mode = pick_mode(args.dp_mode, local)
     tr = ParallelTrainer(cfg, B, args.seq, lay, microbatches=args.microbatches, device=f"cuda:{local}",
-                         init="local", dp_mode=dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
+                         init="local", dp_mode=args.dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
+    dp_mode = tr.dp.mode if tr.dp is not None else None  # what "auto" resolved to
     g = torch.Generator().manual_seed(1 + tr.groups.dp_rank)
     idx = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
     tgt = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
@@ -76,7 +75,7 @@ def main():
     tokens = args.global_batch * args.seq
     res = {"model": args.model, "seq": args.seq, "global_batch": args.global_batch,
            "layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches, "n_gpus": world,
-           "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm, "dp_mode": dp_mode if args.dp > 1 else None,
+           "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm, "dp_mode": dp_mode,
            "ms_per_step": round(ms.item(), 3), "tokens_per_s": round(tokens / step_s, 1),
            "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2), "dtype": "bf16",
            "data": "synthetic uniform-random tokens, random-init weights", "timing": "CUDA events, max over ranks"}

@@ -45,14 +45,17 @@ def pick_mode(mode: str, device_index: int) -> str:
 
 
 class ShardedAdamW:
-    """AdamW state for one contiguous shard [lo, hi) of the flat buffers."""
+    """AdamW state for one contiguous shard [lo, hi) of the flat buffers. grad_shard (the
+    reduce-scatter output) only exists for the NCCL transport; the fused kernels read the
+    gradients where the backward left them."""
 
-    def __init__(self, flat, lo, hi, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, grad_scale=1.0):
+    def __init__(self, flat, lo, hi, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, grad_scale=1.0,
+                 grad_shard=True):
         self.flat, self.lo, self.hi = flat, lo, hi
         dev = flat.master.device
         self.exp_avg = torch.zeros(hi - lo, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros(hi - lo, dtype=torch.float32, device=dev)
-        self.grad_shard = torch.zeros(hi - lo, dtype=torch.float32, device=dev)
+        self.grad_shard = torch.zeros(hi - lo, dtype=torch.float32, device=dev) if grad_shard else None
         self.lr_t = torch.full((1,), float(lr), dtype=torch.float32, device=dev)
         self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
         self.betas, self.eps, self.weight_decay, self.grad_scale = betas, eps, weight_decay, grad_scale
@@ -71,11 +74,16 @@ class ShardedAdamW:
 
 class DataParallel:
     def __init__(self, world_size: int, rank: int, mode: str = "nccl", group=None):
-        """mode: "nvls" (bf16 cast + one multicast kernel after the backward), "nvls-overlap"
+        """mode: "auto" (NVLS where the GPUs have NVLink multicast and every rank can allocate its
+        buffers, else NCCL), "nvls" (bf16 cast + one multicast kernel after the backward), "nvls-overlap"
         (the same per bucket, overlapped with the backward), "nccl" (reduce-scatter /
         all-gather), "fused" (one peer-memory kernel after the backward) or "fused-overlap"
         (that kernel per bucket, overlapped with the backward)."""
         self.world_size, self.rank, self.mode, self.group = world_size, rank, mode, group
+        self.requested = mode  # "auto" resolves here: NVLS where multicast exists, NCCL otherwise
+        self.fallback_reason = None
+        if mode == "auto":
+            self.mode = pick_mode(mode, torch.cuda.current_device() if torch.cuda.is_available() else 0)
         # False when the model's gradient writers store on the step's first write (the NCCL
         # step then skips clearing the buffer; the fused kernels clear what they read anyway)
         self.zero_grads = True
@@ -107,7 +115,8 @@ class DataParallel:
         shard = flat.numel // self.world_size
         self.flat = flat
         lo, hi = self.rank * shard, (self.rank + 1) * shard
-        opt = ShardedAdamW(flat, lo, hi, lr=lr, grad_scale=1.0 / self.world_size, **kw)
+        opt = ShardedAdamW(flat, lo, hi, lr=lr, grad_scale=1.0 / self.world_size, grad_shard=self.mode == "nccl",
+                           **kw)
         # all ranks start from rank 0's weights (the same seed already makes them equal; this
         # makes it a guarantee)
         src = dist.get_global_rank(self.group, 0) if self.group is not None else 0
@@ -117,8 +126,16 @@ class DataParallel:
             from llmt.parallel.fused_dp import FusedDP
             self.fused = FusedDP(flat, opt, self.rank, self.world_size, self.group)
         elif self.mode == "nvls":
-            from llmt.parallel.nvls_dp import NvlsDP
-            self.fused = NvlsDP(flat, opt, self.rank, self.world_size, self.group)
+            from llmt.parallel.nvls_dp import NvlsDP, NvlsUnavailable
+            try:
+                self.fused = NvlsDP(flat, opt, self.rank, self.world_size, self.group)
+            except NvlsUnavailable as e:
+                if self.requested != "auto":
+                    raise
+                # "auto" falls back to the NCCL step (every rank took the same decision)
+                self.fallback_reason = str(e)
+                self.mode = "nccl"
+                opt.grad_shard = torch.zeros(hi - lo, dtype=torch.float32, device=flat.master.device)
         return opt
 
     def begin_step(self):

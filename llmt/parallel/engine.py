@@ -62,7 +62,9 @@ class ParallelTrainer:
         self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
         # whole-step CUDA graph (forward, backward, collectives, optimizer) for layouts without a
         # pipeline: static token buffers, captured after two eager warm-up steps that are undone
-        self.use_graph = cuda_graph and impl == "native" and layout.pp == 1
+        # (the peer-memory tensor-parallel path is not capturable: it runs eager, recorded as
+        # cuda_graph false in the bench output)
+        self.use_graph = cuda_graph and impl == "native" and layout.pp == 1 and tp_comm != "p2p"
         self.graph = None
         if self.use_graph:
             self.idx_buf = torch.zeros((batch, seq), dtype=torch.long, device=self.device)

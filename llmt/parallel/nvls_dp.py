@@ -36,6 +36,10 @@ def _symm():
     return symm
 
 
+class NvlsUnavailable(RuntimeError):
+    """Some rank of the group could not allocate the symmetric buffers (every rank raises it)."""
+
+
 class NvlsDP:
     def __init__(self, flat, opt, rank: int, world: int, group=None):
         self.flat, self.opt, self.rank, self.world = flat, opt, rank, world
@@ -43,11 +47,25 @@ class NvlsDP:
         symm = _symm()
         dev = flat.master.device
         self.device = dev
-        self.g16 = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
-        shadow = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
-        shadow.copy_(flat.shadow)
+        # The symmetric buffers come from their own allocator; where one rank cannot get them
+        # (device memory) every rank learns it before the collective rendezvous and raises.
+        why = ""
+        try:
+            self.g16 = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
+            shadow = symm.empty(flat.numel, dtype=torch.bfloat16, device=dev)
+            self.pad = symm.empty(64 * world, dtype=torch.int32, device=dev)
+        except RuntimeError as e:  # torch.OutOfMemoryError, CUDA driver errors
+            why = str(e).splitlines()[0][:200]
+            self.g16 = shadow = self.pad = None
+            torch.cuda.empty_cache()
+        ok = torch.tensor([0 if why else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if not int(ok.item()):
+            self.g16 = shadow = self.pad = None
+            torch.cuda.empty_cache()
+            raise NvlsUnavailable("NVLS buffers could not be allocated on every rank" + (f": {why}" if why else ""))
         flat.rebind(grad=flat.grad, shadow=shadow)
-        self.pad = symm.empty(64 * world, dtype=torch.int32, device=dev)
+        flat.refresh_shadow()  # bf16 copy of the (broadcast) masters
         self.pad.zero_()
         torch.cuda.synchronize(dev)
         self.h_g = symm.rendezvous(self.g16, self.group)

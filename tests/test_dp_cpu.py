@@ -52,3 +52,11 @@ def test_auto_mode_without_multicast_is_nccl():
     assert pick_mode("nvls-overlap", 0) == "nvls-overlap"
     if not torch.cuda.is_available():
         assert pick_mode("auto", 0) == "nccl"
+
+
+def test_auto_mode_resolves_in_data_parallel():
+    from llmt.parallel.dp import DataParallel
+    dp = DataParallel(2, 0, mode="auto")
+    assert dp.requested == "auto"
+    if not torch.cuda.is_available():
+        assert dp.mode == "nccl"
