@@ -98,9 +98,12 @@ add_rmsnorm_fwd_kernel(const bf16* __restrict__ a, const float* __restrict__ r, 
 }
 
 // dy bf16, s fp32, ds_in fp32 (optional); ds fp32 and ds16 bf16 (optional) out.
-// Two passes over each row's registers-free chunks (the second re-reads dy and s from L1),
-// so the kernel keeps only the dw partial in registers and runs several CTAs per SM.
-// Each CTA writes one (D) dw partial row; dw_reduce_kernel sums them in a fixed order.
+// Two passes over each row's registers-free chunks (the second re-reads dy and s from L1).
+// The dw partial of a row group lives in its own shared-memory row (each thread owns its 8-column
+// pieces, so no synchronisation), not in registers: the kernel then fits five CTAs per SM and
+// one wave covers the 4096 rows of a medium step (a second, mostly idle wave cost a whole
+// dependent DRAM round trip). Each CTA writes one (D) dw partial row; dw_reduce_kernel sums
+// them in a fixed order.
 template <int TPR, bool HAS_DSIN, bool WRITE_DS16>
 __global__ void __launch_bounds__(kThreads)
 rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, const float* __restrict__ w,
@@ -108,14 +111,19 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
                    float* __restrict__ ds, bf16* __restrict__ ds16, float* __restrict__ dw_part, int64_t N, int D) {
   pdl_wait();
   __shared__ float red[kThreads / 32];
+  extern __shared__ float sdw[];  // [RPC][D] dw partials, one row per row group
   constexpr int RPC = kThreads / TPR;
   const int t = threadIdx.x % TPR;
   const int rgroup = threadIdx.x / TPR;
-  float dwacc[kMaxChunks][8];
+  float* my_dw = sdw + (int64_t)rgroup * D;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dwacc[c][j] = 0.f;
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int e = (c * TPR + t) * 8;
+    if (e < D) {
+      reinterpret_cast<float4*>(my_dw + e)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4*>(my_dw + e)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   const int64_t stride = (int64_t)gridDim.x * RPC;
   // Every row group runs the same number of iterations so the block-wide barriers in
   // row_sum line up; rows past N are masked.
@@ -141,11 +149,17 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
         const float4 w0 = ld_f4(w + e), w1 = ld_f4(w + e + 4);
         const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float4* acc = reinterpret_cast<float4*>(my_dw + e);
+        float4 a0 = acc[0], a1 = acc[1];
+        float* av0 = reinterpret_cast<float*>(&a0);
+        float* av1 = reinterpret_cast<float*>(&a1);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           dot += dyf[j] * wv[j] * sv[j];
-          dwacc[c][j] += dyf[j] * sv[j] * rs;
+          (j < 4 ? av0[j] : av1[j - 4]) += dyf[j] * sv[j] * rs;
         }
+        acc[0] = a0;
+        acc[1] = a1;
       }
     }
     dot = row_sum<TPR>(dot, red);
@@ -178,19 +192,8 @@ rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const float* __restrict__ s, con
       }
     }
   }
-  // CTA-level reduction of dw over the row groups: every row group stores its partial row into
-  // shared memory ([RPC][D] floats), one barrier, then each thread sums whole columns over the
-  // row groups in a fixed order.
-  extern __shared__ float sdw[];
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int e = (c * TPR + t) * 8;
-    if (e < D) {
-      float4* dst = reinterpret_cast<float4*>(sdw + (int64_t)rgroup * D + e);
-      dst[0] = make_float4(dwacc[c][0], dwacc[c][1], dwacc[c][2], dwacc[c][3]);
-      dst[1] = make_float4(dwacc[c][4], dwacc[c][5], dwacc[c][6], dwacc[c][7]);
-    }
-  }
+  // CTA-level reduction of dw over the row groups' shared-memory rows: one barrier, then each
+  // thread sums whole columns over the row groups in a fixed order.
   __syncthreads();
   for (int i = threadIdx.x; i < D; i += kThreads) {
     float a = 0.f;
@@ -262,13 +265,32 @@ cudaError_t add_rmsnorm_fwd(const void* a_bf16, const float* r, const float* w, 
 int rmsnorm_bwd_partials(int64_t N, int D) {
   int tpr = D <= 1024 ? 32 : D <= 2048 ? 64 : D <= 4096 ? 128 : 256;
   const int rpc = kThreads / tpr;
-  static int per_sm = [] {
-    // 3 CTAs per SM: the register limit at 80 registers x 256 threads (ncu at 2 per SM: 14.6
-    // warps per SM active, long-scoreboard stalls, 24% of DRAM bandwidth); override for tuning
+  // CTAs per SM: what the registers and the [rows per CTA][D] dw slots allow for the largest
+  // variant (ds_in and the bf16 copy), so that as many rows as possible are in flight in one wave;
+  // LLMT_NORM_BWD_CTAS_PER_SM overrides it for tuning
+  static int env = [] {
     const char* e = getenv("LLMT_NORM_BWD_CTAS_PER_SM");
-    const int v = e ? atoi(e) : 3;
-    return v > 0 ? v : 3;
+    return e ? atoi(e) : 0;
   }();
+  static std::atomic<int> cached[4] = {0, 0, 0, 0};  // per threads-per-row choice (D sets the slot size)
+  const int slot = tpr == 32 ? 0 : tpr == 64 ? 1 : tpr == 128 ? 2 : 3;
+  int per_sm = env > 0 ? env : cached[slot].load();
+  if (per_sm <= 0) {
+    per_sm = 1;
+    dispatch_tpr(D, [&](auto t) {
+      constexpr int TPR = decltype(t)::value;
+      int n = 0;
+      // the slot size at this TPR's largest width, so that the answer holds for every D it serves
+      const size_t smem = (size_t)(kThreads / TPR) * (TPR * 8 * kMaxChunks) * sizeof(float);
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rmsnorm_bwd_kernel<TPR, true, true>, kThreads, smem) ==
+              cudaSuccess &&
+          n > 0)
+        per_sm = n;
+      else
+        (void)cudaGetLastError();
+    });
+    cached[slot].store(per_sm);
+  }
   return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(N, rpc), (int64_t)per_sm * sm_count()));
 }
 
