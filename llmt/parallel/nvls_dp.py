@@ -68,11 +68,23 @@ class NvlsDP:
         flat.refresh_shadow()  # bf16 copy of the (broadcast) masters
         self.pad.zero_()
         torch.cuda.synchronize(dev)
-        self.h_g = symm.rendezvous(self.g16, self.group)
-        self.h_w = symm.rendezvous(flat.shadow, self.group)
-        self.h_p = symm.rendezvous(self.pad, self.group)
-        if not self.h_g.multicast_ptr or not self.h_w.multicast_ptr:
-            raise RuntimeError("NVLS data parallelism needs NVLink multicast (symmetric memory reported none)")
+        # the rendezvous binds the buffers to multicast objects (collective); a rank that gets no
+        # multicast address reports it and every rank raises together
+        why = ""
+        try:
+            self.h_g = symm.rendezvous(self.g16, self.group)
+            self.h_w = symm.rendezvous(flat.shadow, self.group)
+            self.h_p = symm.rendezvous(self.pad, self.group)
+            if not self.h_g.multicast_ptr or not self.h_w.multicast_ptr:
+                why = "symmetric memory reported no NVLink multicast address"
+        except RuntimeError as e:
+            why = str(e).splitlines()[0][:200]
+        ok = torch.tensor([0 if why else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if not int(ok.item()):
+            self.g16 = None
+            torch.cuda.empty_cache()
+            raise NvlsUnavailable("NVLS multicast set-up failed on some rank" + (f": {why}" if why else ""))
         self.g_mc = self.h_g.multicast_ptr + (self.g16.data_ptr() - self.h_g.buffer_ptrs[rank])
         self.w_mc = self.h_w.multicast_ptr + (flat.shadow.data_ptr() - self.h_w.buffer_ptrs[rank])
         off = self.pad.data_ptr() - self.h_p.buffer_ptrs[rank]
