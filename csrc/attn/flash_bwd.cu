@@ -96,8 +96,11 @@ flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kb = blockIdx.x;             // key block
-  const int bk = blockIdx.y;             // b * KV + kv head
+  // blocks launch x-fastest: every (batch, kv head) of key block 0 first, so the longest causal
+  // CTAs (low key blocks walk the most query blocks) start in the first wave and the short ones
+  // fill in behind them
+  const int bk = blockIdx.x;             // b * KV + kv head
+  const int kb = blockIdx.y;             // key block
   const int b = bk / a.KV, kvh = bk % a.KV;
   const int group = a.H / a.KV;
   const int nqb = (int)cdiv(a.T, kBN);
@@ -977,7 +980,7 @@ cudaError_t launch_bwd(const CUtensorMap& tq, const CUtensorMap& tdo, const CUte
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((unsigned)cdiv(args.T, kBM), args.B * args.KV);
+  dim3 grid((unsigned)(args.B * args.KV), (unsigned)cdiv(args.T, kBM));
   launch_pdl(kern, grid, kBwdThreads, smem, st, tq, tdo, tdq, tdkv, args);
   return cudaGetLastError();
 }
