@@ -84,7 +84,9 @@ static bool make_out_maps(int epi, const GemmArgs& g, int M, int N, GemmMaps* mp
     case EPI_F32:
       return make_tmap_2d(&mp->c, g.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, g.ldo, 32, 32,
                           CU_TENSOR_MAP_SWIZZLE_128B);
-    case EPI_BF16: case EPI_CE_BWD: case EPI_ROPE:
+    case EPI_BF16: case EPI_CE_BWD:  // 32 rows x 64 columns (128-byte rows)
+      return make_tmap_2d(&mp->c, g.out, dt, 2, N, M, g.ldo, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    case EPI_ROPE:
       return make_tmap_2d(&mp->c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
     case EPI_SWIGLU:
       return make_tmap_2d(&mp->c, g.out, dt, 2, N, M, g.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B) &&

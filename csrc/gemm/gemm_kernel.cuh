@@ -117,6 +117,13 @@ struct Stager {
     for (int u = 0; u < 4; ++u)
       *reinterpret_cast<BF16x8*>(b + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = float_to_bf16x8(v + u * 8);
   }
+  // 32 rows x 64 bf16 columns (128-byte rows, 128B swizzle): unit u (columns 8u .. 8u + 7) of row
+  // `lane` at unit u ^ (lane & 7); v holds the row's 64 values
+  __device__ __forceinline__ void put_bf16x64(uint8_t* b, const float* v) const {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      *reinterpret_cast<BF16x8*>(b + lane * 128 + ((u ^ (lane & 7)) << 4)) = float_to_bf16x8(v + u * 8);
+  }
   __device__ __forceinline__ void put_f32(uint8_t* b, const float* v) const {
 #pragma unroll
     for (int u = 0; u < 8; ++u)
@@ -158,7 +165,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
   float sc = 1.f;
   if constexpr (F8) sc = __ldg(a.scale_a) * __ldg(a.scale_b);
   auto cvt = [sc](uint32_t x) { return F8 ? __uint_as_float(x) * sc : __uint_as_float(x); };
-  if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_CE_BWD) {
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_CE_BWD) {
+    // 64 columns per staged box and TMA store (half the stores, fences and buffer waits of 32)
     float l = 0.f, scale = 0.f;
     int64_t t = -1;
     if constexpr (EPI == EPI_CE_BWD) {
@@ -168,6 +176,29 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       }
       scale = a.alpha * (a.grad_out ? *a.grad_out : 1.f);
     }
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      const int col0 = nb * BN + c * 64;
+      if (col0 >= a.N) break;  // uniform across the warp
+      uint32_t r0[32], r1[32];
+      tmem_ld32(taddr + c * 64, r0);
+      tmem_ld32(taddr + c * 64 + 32, r1);
+      tmem_wait_ld();
+      float v[64];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = cvt(r0[j]);
+        v[32 + j] = cvt(r1[j]);
+      }
+      if constexpr (EPI == EPI_CE_BWD) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) v[j] = (__expf(v[j] - l) - ((int64_t)(col0 + j) == t ? 1.f : 0.f)) * scale;
+      }
+      uint8_t* b = st.acquire();
+      st.put_bf16x64(b, v);
+      st.store2d(tmC, b, col0, wrow);
+    }
+  } else if constexpr (EPI == EPI_F32) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col0 = nb * BN + c * 32;
@@ -179,17 +210,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = cvt(r[j]);
       uint8_t* b = st.acquire();
-      if constexpr (EPI == EPI_F32) {
-        st.put_f32(b, v);
-        st.store2d(tmC, b, col0, wrow, a.accumulate != 0);
-      } else {
-        if constexpr (EPI == EPI_CE_BWD) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = (__expf(v[j] - l) - ((int64_t)(col0 + j) == t ? 1.f : 0.f)) * scale;
-        }
-        st.put_bf16(b, v);
-        st.store2d(tmC, b, col0, wrow);
-      }
+      st.put_f32(b, v);
+      st.store2d(tmC, b, col0, wrow, a.accumulate != 0);
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     const int F = a.split;
