@@ -141,6 +141,33 @@ inline bool pdl_enabled() {
   }();
   return on;
 }
+// GEMM launches are programmatic by default (LLMT_PDL=0 turns them off, =1 makes every launch
+// programmatic): the GEMM waits for its predecessor after its own set-up (barriers, TMEM,
+// tensor-map prefetch), so that set-up overlaps the previous kernel's tail. Measured on the medium
+// step in back-to-back pairs on one box: 14.39 / 14.31 / 14.40 ms against 14.51 / 14.48 / 14.49 ms.
+inline bool pdl_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("LLMT_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_if(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

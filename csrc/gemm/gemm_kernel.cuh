@@ -411,7 +411,6 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0, bool 
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
-  pdl_wait();
   constexpr int BM = kGemmBM, BK = kGemmBK;
   constexpr bool F8 = KIND != 0, BS = KIND >= 2;
   static_assert(!F8 || (!A_MN && !B_MN), "8-bit operands are K-major only");
@@ -463,6 +462,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrival
   else __syncthreads();
   tc_fence_after();
+  // with a programmatic launch the set-up above overlaps the previous kernel's tail; nothing of
+  // global memory is touched before that kernel has completed
+  pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int mn_tiles = args.m_blocks * args.n_blocks;
   const int num_tiles = mn_tiles * args.splits;
@@ -688,13 +690,13 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cfg.numAttrs = pdl_gemm_enabled() ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp.a, mp.b, mp.c, mp.c2, args);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
   const int grid = std::min(tiles, persistent_sms());
-  launch_pdl(kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, args);
+  launch_pdl_if(pdl_gemm_enabled(), kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, args);
   return cudaGetLastError();
 }
 
