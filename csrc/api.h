@@ -103,7 +103,22 @@ struct GemmArgs {
   int sf_chunks;         // chunks per 128-row tile (k-blocks x chunks per k-block)
   int n_fastest;         // tile order: 1 = consecutive tiles walk N (A blocks reused), 0 = walk M
   int* err;
+  // Tensor-parallel all-gather fused into the A loads (bf16, K-major A). A (M x K, row pitch
+  // ag_ldd) is this rank's gather buffer of M = ag_tp * rows_per_rank rows; rank q owns rows
+  // [q rows_per_rank, (q + 1) rows_per_rank). The kernel's epilogue warps first store this
+  // rank's rows (ag_src, pitch ag_lds) into every rank's buffer (ag_dst[p], peer-mapped) in
+  // 16-row pieces and count each piece in the flag of its 128-row block on the destination
+  // (ag_flags[p][block], red.release.sys); the TMA producer loads an A tile only once this
+  // rank's flag of the tile's row block has reached ag_expect (bounded wait, error code 8).
+  const void* ag_src;           // nullptr: no fused all-gather
+  int64_t ag_lds, ag_ldd;
+  void* const* ag_dst;          // device array [ag_tp] of every rank's gather buffer
+  uint32_t* const* ag_flags;    // device array [ag_tp] of every rank's flags (one per 128-row block)
+  uint32_t ag_expect;           // calls of this gather site so far x kAgPieces
+  int ag_tp;
 };
+// 16-row pieces per 128-row block of a fused all-gather: each adds one to the block's flag.
+constexpr int kAgPieces = 8;
 
 // out = op(a) @ op(b); a: (ta ? K x M : M x K) row pitch lda, b: (tb ? N x K : K x N) row pitch ldb.
 // The epilogue fields of `g` (out, ldo, accumulate, split, aux, ...) are set by the caller;
@@ -179,7 +194,7 @@ cudaError_t dp_barrier(uint32_t* const* pads_dev, uint32_t* my_pad, uint32_t* ep
                        cudaStream_t st);
 cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, float* master, float* m, float* v,
                            int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
-                           cudaStream_t st, int max_blocks = 0);
+                           cudaStream_t st, int max_blocks = 0, bool clear = true);
 int dp_error_code(bool reset);
 // NVLS data-parallel step (comm/dp_nvls.cu): g_mc / w_mc are the NVLink multicast addresses of
 // the flat bf16 gradient and weight buffers; reduce, AdamW on [lo, lo + n), multicast store.

@@ -284,7 +284,8 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
           c10::optional<at::Tensor> lse, c10::optional<at::Tensor> grad_out, c10::optional<at::Tensor> part,
           c10::optional<at::Tensor> tlogit, double alpha, int64_t bn, int64_t splits, c10::optional<at::Tensor> peer,
           int64_t tp_rank, int64_t rows_per_rank, c10::optional<at::Tensor> scale_a, c10::optional<at::Tensor> scale_b,
-          int64_t kind, c10::optional<at::Tensor> sfa, c10::optional<at::Tensor> sfb) {
+          int64_t kind, c10::optional<at::Tensor> sfa, c10::optional<at::Tensor> sfb, c10::optional<at::Tensor> ag_src,
+          c10::optional<at::Tensor> ag_dst, c10::optional<at::Tensor> ag_flags, int64_t ag_expect, int64_t ag_tp) {
   cuda2d(a, "a");
   cuda2d(b, "b");
   const bool bs = kind == 2 || kind == 3;
@@ -377,6 +378,25 @@ void gemm(at::Tensor a, at::Tensor b, bool ta, bool tb, int64_t epi, at::Tensor 
   g.peer = reinterpret_cast<void* const*>(const_cast<void*>(opt_ptr(peer, "peer")));
   g.tp_rank = (int)tp_rank;
   g.rows_per_rank = (int)rows_per_rank;
+  if (ag_src.has_value() && ag_src->defined()) {
+    // fused all-gather: this rank's rows (rows_per_rank, K) bf16; a is this rank's gather buffer
+    cuda2d(*ag_src, "ag_src");
+    CHECK(kind == 0 && !f8, "fused all-gather: bf16 operands only");
+    CHECK_DT((*ag_src), at::kBFloat16);
+    CHECK(!ta && ag_src->size(0) == rows_per_rank && ag_src->size(1) == a.size(1) && ag_src->stride(1) == 1,
+          "ag_src must be this rank's (rows_per_rank, K) rows of a row-major A");
+    CHECK(ag_dst.has_value() && ag_flags.has_value() && ag_dst->scalar_type() == at::kLong &&
+              ag_flags->scalar_type() == at::kLong && ag_dst->numel() == ag_tp && ag_flags->numel() == ag_tp,
+          "fused all-gather needs ag_dst and ag_flags: int64 device arrays of ag_tp pointers");
+    on_device(*ag_dst, "ag_dst");
+    on_device(*ag_flags, "ag_flags");
+    g.ag_src = ag_src->data_ptr();
+    g.ag_lds = ag_src->stride(0);
+    g.ag_dst = reinterpret_cast<void* const*>(ag_dst->data_ptr());
+    g.ag_flags = reinterpret_cast<uint32_t* const*>(ag_flags->data_ptr());
+    g.ag_expect = (uint32_t)ag_expect;
+    g.ag_tp = (int)ag_tp;
+  }
   if (epi == llmt::EPI_ROPE) CHECK(g.cos_t && g.sin_t && T > 0, "ROPE gemm needs rope tables and T");
   if (epi == llmt::EPI_SWIGLU) CHECK(g.aux && aux->stride(0) % 8 == 0, "SWIGLU gemm needs the gu save buffer");
   if (epi == llmt::EPI_SWIGLU_BWD) CHECK(g.aux && g.out2 && split == N, "SWIGLU_BWD gemm args");
@@ -490,7 +510,7 @@ void dp_barrier(at::Tensor pads_dev, int64_t my_pad, at::Tensor epoch, int64_t r
 
 void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor master, at::Tensor m, at::Tensor v,
                     int64_t lo, int64_t n, at::Tensor lr, at::Tensor step, double b1, double b2, double eps, double wd,
-                    double grad_scale, int64_t world, int64_t max_blocks) {
+                    double grad_scale, int64_t world, int64_t max_blocks, bool clear) {
   CHECK_DT(grads_dev, at::kLong);
   CHECK_DT(shadows_dev, at::kLong);
   CHECK(grads_dev.numel() == world && shadows_dev.numel() == world, "peer pointer arrays must have world entries");
@@ -499,7 +519,7 @@ void dp_fused_adamw(at::Tensor grads_dev, at::Tensor shadows_dev, at::Tensor mas
   ok(llmt::dp_fused_adamw(reinterpret_cast<float* const*>(grads_dev.data_ptr<int64_t>()),
                           reinterpret_cast<void* const*>(shadows_dev.data_ptr<int64_t>()), master.data_ptr<float>(),
                           m.data_ptr<float>(), v.data_ptr<float>(), lo, n, lr.data_ptr<float>(), step.data_ptr<int>(),
-                          h, (int)world, stream(), (int)max_blocks),
+                          h, (int)world, stream(), (int)max_blocks, clear),
      "dp_fused_adamw");
 }
 
@@ -554,7 +574,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "out2"_a = py::none(), "split"_a = 0, "cos_t"_a = py::none(), "sin_t"_a = py::none(), "T"_a = 0, "hd"_a = 0,
         "rot_cols"_a = 0, "tgt"_a = py::none(), "lse"_a = py::none(), "grad_out"_a = py::none(), "part"_a = py::none(),
         "tlogit"_a = py::none(), "alpha"_a = 1.0, "bn"_a = 0, "splits"_a = 0, "peer"_a = py::none(), "tp_rank"_a = 0, "rows_per_rank"_a = 0,
-        "scale_a"_a = py::none(), "scale_b"_a = py::none(), "kind"_a = 0, "sfa"_a = py::none(), "sfb"_a = py::none());
+        "scale_a"_a = py::none(), "scale_b"_a = py::none(), "kind"_a = 0, "sfa"_a = py::none(), "sfb"_a = py::none(),
+        "ag_src"_a = py::none(), "ag_dst"_a = py::none(), "ag_flags"_a = py::none(), "ag_expect"_a = 0, "ag_tp"_a = 0);
   m.def("mx_sf_bytes", &llmt::mx_sf_bytes);
   m.def("mx_quant", &mx_quant, "kind"_a, "x"_a, "q"_a, "sf"_a, "qt"_a, "sft"_a, "g"_a, "scratch"_a,
         "interleave64"_a = false, "stochastic"_a = false, "seed"_a = 0, "seed_dev"_a = py::none());
@@ -601,7 +622,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("dp_barrier", &dp_barrier);
   m.def("dp_fused_adamw", &dp_fused_adamw, "grads_dev"_a, "shadows_dev"_a, "master"_a, "m"_a, "v"_a, "lo"_a, "n"_a,
-        "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "world"_a, "max_blocks"_a = 0);
+        "lr"_a, "step"_a, "b1"_a, "b2"_a, "eps"_a, "wd"_a, "grad_scale"_a, "world"_a, "max_blocks"_a = 0,
+        "clear"_a = true);
   m.def("dp_error_code", &llmt::dp_error_code, "reset"_a = false);
   m.def("bounds_error", &llmt::bounds_error, "reset"_a = false);
   m.def("bounds_checking", &llmt::bounds_checking);

@@ -7,7 +7,8 @@
 // buffers are CUDA-IPC mapped into every other rank (plain P2P loads/stores through NVSwitch,
 // no multicast). For its shard [lo, lo + n) rank r:
 //   g   = sum_p grad_p[lo + i]                 (P2P loads, 16 B per access)
-//   grad_p[lo + i] = 0 for every p             (the reader clears: next step accumulates)
+//   grad_p[lo + i] = 0 for every p             (the reader clears when the next step accumulates;
+//                                               skipped when its first write stores)
 //   AdamW on master[lo + i], m[i], v[i]        (local, same math as adamw.cu)
 //   shadow_p[lo + i] = bf16(master[lo + i])    (P2P stores: the parameter all-gather)
 // Ordering across ranks uses a flag barrier before (all gradients complete) and after (all
@@ -64,6 +65,8 @@ struct DpArgs {
   const int* step;
   AdamHyper h;
   int world;
+  int clear;             // zero every rank's gradient shard after reading it (0: the next step's
+                         // first micro-batch stores its gradients instead of adding)
 };
 
 template <int WORLD>
@@ -88,8 +91,10 @@ __global__ void __launch_bounds__(256) dp_fused_adamw_kernel(DpArgs a) {
       gs.z += x.z;
       gs.w += x.w;
     }
+    if (a.clear) {
 #pragma unroll 8
-    for (int p = 0; p < world; ++p) __stcg(reinterpret_cast<float4*>(a.grads[p] + gi), make_float4(0.f, 0.f, 0.f, 0.f));
+      for (int p = 0; p < world; ++p) __stcg(reinterpret_cast<float4*>(a.grads[p] + gi), make_float4(0.f, 0.f, 0.f, 0.f));
+    }
     float4 pp = ld_f4(a.master + gi), mm = ld_f4(a.m + 4 * i), vv = ld_f4(a.v + 4 * i);
     float* pe = &pp.x;
     const float* ge = &gs.x;
@@ -157,10 +162,10 @@ cudaError_t dp_barrier(uint32_t* const* pads_dev, uint32_t* my_pad, uint32_t* ep
 
 cudaError_t dp_fused_adamw(float* const* grads_dev, void* const* shadows_dev, float* master, float* m, float* v,
                            int64_t lo, int64_t n, const float* lr, const int* step, AdamHyper h, int world,
-                           cudaStream_t st, int max_blocks) {
+                           cudaStream_t st, int max_blocks, bool clear) {
   LLMT_REQUIRE(n % 4 == 0 && lo % 4 == 0, "dp_fused_adamw: shard bounds must be multiples of 4");
   if (n == 0) return cudaSuccess;
-  DpArgs a{grads_dev, reinterpret_cast<bf16* const*>(shadows_dev), master, m, v, lo, n, lr, step, h, world};
+  DpArgs a{grads_dev, reinterpret_cast<bf16* const*>(shadows_dev), master, m, v, lo, n, lr, step, h, world, clear ? 1 : 0};
   // max_blocks > 0 keeps the kernel to a few SMs when it runs beside the backward
   const int64_t cap = max_blocks > 0 ? max_blocks : sm_count() * 4;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n / 4, 256), cap));

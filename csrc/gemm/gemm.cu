@@ -117,6 +117,17 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
                      !ta,
                  "gemm: PEER_RS needs peer slots, M a multiple of the rows per rank, N a multiple of 32");
   if (epi == EPI_ROPE) LLMT_REQUIRE(g.hd % 64 == 0 && BN % g.hd == 0 && N % g.hd == 0, "gemm: bad RoPE epilogue shape");
+  if (g.ag_src) {
+    LLMT_REQUIRE(!ta && (epi == EPI_BF16 || epi == EPI_ROPE || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD),
+                 "gemm: a fused all-gather needs a K-major A and a bf16 epilogue");
+    LLMT_REQUIRE(g.ag_dst && g.ag_flags && g.ag_tp >= 1 && g.ag_tp <= 8 && g.tp_rank >= 0 && g.tp_rank < g.ag_tp,
+                 "gemm: fused all-gather needs gather buffers, flags and 0 <= rank < tp <= 8");
+    LLMT_REQUIRE(g.rows_per_rank > 0 && g.rows_per_rank % 128 == 0 && (int64_t)g.ag_tp * g.rows_per_rank == M,
+                 "gemm: fused all-gather needs M = tp x rows per rank, rows per rank a multiple of 128");
+    LLMT_REQUIRE(K % 8 == 0 && g.ag_lds % 8 == 0 && lda % 8 == 0 && (reinterpret_cast<uintptr_t>(g.ag_src) & 15) == 0,
+                 "gemm: fused all-gather rows must be 16-byte aligned");
+    g.ag_ldd = lda;
+  }
   // 256 x 256 tiles on CTA pairs wherever the planner picked 256-wide tiles and M fills them
   const bool pair = BN == 256 && M > kGemmBM && epi != EPI_PEER_RS && gemm_pairs_enabled();
   g.M = M;

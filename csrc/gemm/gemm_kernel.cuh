@@ -401,6 +401,93 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
   }
 }
 
+// ---------------------------------------------------------------- fused tensor-parallel all-gather
+// (GemmArgs::ag_*). The copy runs on the epilogue warps before their first tile, so it overlaps
+// the first tiles' MMAs; the producer waits, per 128-row block of A, for the pieces of the
+// owning rank (acquire at system scope, then a proxy fence: the rows were written by generic
+// stores, local or through NVLink, and are read by TMA).
+// 1 s: below the 2 s of the pipeline's own mbarrier waits, so a missing peer is what runs out first
+// (the MMA warp waiting on the stalled producer would otherwise record its own timeout)
+constexpr uint64_t kAgWaitLimitNs = 1000000000ull;
+constexpr int kAgWaitCode = 8;
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Epilogue warps of every CTA (t = 0..127): this rank's rows into every rank's gather buffer,
+// own buffer first, then the peers in rank order, in 16-row pieces strided over the grid.
+__device__ __forceinline__ void ag_store_rows(const GemmArgs& a, int t) {
+  constexpr int PR = 128 / kAgPieces;  // rows per piece
+  constexpr int U = 8;                 // 16-byte loads in flight per thread
+  const int k16 = a.K / 8;
+  const int blocks = a.rows_per_rank / 128;
+  const int per_dest = blocks * kAgPieces;
+  const int units = per_dest * a.ag_tp;
+  const int n16 = PR * k16;
+  const int64_t ls = a.ag_lds / 8, ld = a.ag_ldd / 8;
+  const int gblk0 = a.tp_rank * blocks;  // this rank's first 128-row block of A
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int j = u / per_dest, r = u - j * per_dest;
+    const int p = (a.tp_rank + j) % a.ag_tp;
+    const int lrow0 = r * PR;
+    const uint4* src = reinterpret_cast<const uint4*>(a.ag_src) + (int64_t)lrow0 * ls;
+    uint4* dst = reinterpret_cast<uint4*>(a.ag_dst[p]) + ((int64_t)a.tp_rank * a.rows_per_rank + lrow0) * ld;
+    for (int i0 = t; i0 < n16; i0 += 128 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int e = 0; e < U; ++e) {
+        const int i = i0 + e * 128;
+        if (i < n16) {
+          const int rr = i / k16;
+          v[e] = __ldg(src + rr * ls + (i - rr * k16));
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < U; ++e) {
+        const int i = i0 + e * 128;
+        if (i < n16) {
+          const int rr = i / k16;
+          __stcg(dst + rr * ld + (i - rr * k16), v[e]);
+        }
+      }
+    }
+    __threadfence_system();  // this thread's stores are visible system-wide before the count
+    named_bar_sync(1, 128);  // every epilogue thread has stored and fenced its part of the piece
+    if (t == 0) red_release_sys_add(a.ag_flags[p] + gblk0 + r / kAgPieces, 1u);
+  }
+}
+
+// Producer: wait until 128-row block `blk` of A holds its owner's rows for this call. A wait that
+// runs out records kAgWaitCode and stops waiting for the rest of the launch (no hang).
+__device__ __forceinline__ void ag_wait_block(const GemmArgs& a, const uint32_t* flags, int blk, bool& give_up) {
+  if (!give_up) {
+    const uint64_t t0 = globaltimer();
+    uint32_t spin = 0;
+    while ((int32_t)(ld_acquire_sys_u32(flags + blk) - a.ag_expect) < 0) {
+      if ((++spin & 63u) == 0 && globaltimer() - t0 > kAgWaitLimitNs) {
+        atomicCAS(a.err, 0, kAgWaitCode);
+        give_up = true;
+        break;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Output tile of a linear tile index; a fused all-gather starts at this rank's own row blocks
+// (available first) by rotating the row-block index.
+__device__ __forceinline__ void tile_mn(const GemmArgs& g, int rest, int rot, int& mb, int& nb) {
+  mb = g.n_fastest ? rest / g.n_blocks : rest % g.m_blocks;
+  nb = g.n_fastest ? rest % g.n_blocks : rest / g.m_blocks;
+  if (rot) mb = (mb + rot) % g.m_blocks;
+}
+
 // KIND: 0 bf16, 1 e4m3 with tensorwise scales, 2 MXFP8, 3 NVFP4 (2 and 3: block-scaled MMA with
 // the scale-factor chunks of each k-block loaded next to its A / B tiles and copied into TMEM).
 // PAIR: a cluster of two CTAs computes each 256 x BN tile with cta_group::2 MMAs (bf16, BN =
@@ -474,16 +561,30 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr int TM = PAIR ? 2 * BM : BM;  // rows of one tile
 
+  // fused all-gather (bf16 only): this rank's row blocks first
+  const bool ag = KIND == 0 && args.ag_src != nullptr;
+  const int ag_rot = ag ? (args.tp_rank * args.rows_per_rank) / TM : 0;
+
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int ag_ready = -1;
+      bool ag_give_up = false;
+      const uint32_t* ag_my_flags = ag ? args.ag_flags[args.tp_rank] : nullptr;
       for (int tile = unit0; tile < num_tiles && ok; tile += units) {
         const int rest = tile % mn_tiles, ks = tile / mn_tiles;
-        const int mb = args.n_fastest ? rest / args.n_blocks : rest % args.m_blocks;
-        const int nb = args.n_fastest ? rest % args.n_blocks : rest / args.m_blocks;
+        int mb, nb;
+        tile_mn(args, rest, ag_rot, mb, nb);
         const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
+        if constexpr (KIND == 0) {
+          const int arow = mb * TM + (int)rank * BM;  // first row of this CTA's A tile
+          if (ag && arow < args.M && arow / BM != ag_ready) {
+            ag_wait_block(args, ag_my_flags, arow / BM, ag_give_up);
+            ag_ready = arow / BM;
+          }
+        }
         for (int kb = k_lo; kb < k_hi; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, err, 1)) {
             ok = false;
@@ -629,10 +730,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     Stager st{stage_out + (warp - 2) * 8192, 0, lane, &ebar[(warp - 2) * 2], 0u};
     int buf = 0;
     uint32_t aphase = 0;
+    if constexpr (KIND == 0) {
+      if (ag) ag_store_rows(args, (int)threadIdx.x - 64);
+    }
     for (int tile = unit0; tile < num_tiles; tile += units) {
       const int rest = tile % mn_tiles;
-      const int mb = args.n_fastest ? rest / args.n_blocks : rest % args.m_blocks;
-        const int nb = args.n_fastest ? rest % args.n_blocks : rest / args.m_blocks;
+      int mb, nb;
+      tile_mn(args, rest, ag_rot, mb, nb);
       if (!wait_bar(&tfull[buf], aphase, err, 4)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + buf * BN + ((uint32_t)(q * 32) << 16);
@@ -676,7 +780,7 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
   }
   const int tiles = args.m_blocks * args.n_blocks * args.splits;
   if constexpr (PAIR) {
-    const int pairs = std::min(tiles, persistent_sms() / 2);
+    int pairs = std::min(tiles, persistent_sms() / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(kGemmThreads);
@@ -691,6 +795,18 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_gemm_enabled() ? 2 : 1;
+    if (args.ag_src) {
+      // a fused all-gather needs every pair resident at once (the producers wait for rows that
+      // other CTAs' epilogue warps store): no more pairs than the clusters that fit together
+      static int fit = 0;
+      if (!fit) {
+        cfg.gridDim = dim3(2 * pairs);
+        cudaError_t e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
+        if (e != cudaSuccess || fit < 1) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
+      }
+      pairs = std::min(pairs, fit);
+      cfg.gridDim = dim3(2 * pairs);
+    }
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp.a, mp.b, mp.c, mp.c2, args);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();

@@ -115,6 +115,24 @@ def rmsnorm_bwd(dy, s, w, rstd, ds_in, dw, accumulate, write_ds16=True):
 
 
 # ---------------------------------------------------------------- GEMM
+def _take_ag(a, ta=False):
+    """Keyword arguments of an all-gather fused into this GEMM's A loads.
+
+    A tensor returned by the peer-memory tensor-parallel all-gather (TPPeerComm with fused
+    gathers) carries the gather it still owes as `_llmt_pending_ag`: its rows are stored into
+    every rank's buffer by the first GEMM that reads it with a K-major A. A consumer that cannot
+    fuse (an MN-major A, i.e. a weight gradient reading it first) has the gather run on its own
+    before it. Either way the pending gather is consumed once."""
+    pending = getattr(a, "_llmt_pending_ag", None)
+    if pending is None:
+        return {}
+    del a._llmt_pending_ag
+    if ta:
+        pending.run_unfused()
+        return {}
+    return pending.kwargs()
+
+
 def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate=False, bn=0, splits=0):
     """out = op(a) @ op(b) on the tcgen05 GEMM (bf16 operands, fp32 accumulation).
 
@@ -130,7 +148,8 @@ def gemm(a, b, ta=False, tb=True, out=None, out_dtype=torch.bfloat16, accumulate
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
     epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
-    ext().gemm(a, b, ta, tb, epi, out, accumulate=accumulate, bn=bn, splits=splits)
+    _take_ag(b, True)  # a pending gather read as B first runs on its own
+    ext().gemm(a, b, ta, tb, epi, out, accumulate=accumulate, bn=bn, splits=splits, **_take_ag(a, ta))
     return out
 
 
@@ -141,7 +160,7 @@ def gemm_swiglu(x, w13, ffn, h=None, gu=None, bn=0):
         h = torch.empty((M, ffn), dtype=torch.bfloat16, device=x.device)
     if gu is None:
         gu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=x.device)
-    ext().gemm(x, w13, False, True, EPI_SWIGLU, h, aux=gu, split=ffn, bn=bn)
+    ext().gemm(x, w13, False, True, EPI_SWIGLU, h, aux=gu, split=ffn, bn=bn, **_take_ag(x))
     return h, gu
 
 
@@ -150,7 +169,7 @@ def gemm_swiglu_bwd(dm, w2, gu, ffn, dgu=None, bn=0):
     M = dm.shape[0]
     if dgu is None:
         dgu = torch.empty((M, 2 * ffn), dtype=torch.bfloat16, device=dm.device)
-    ext().gemm(dm, w2, False, False, EPI_SWIGLU_BWD, dgu, aux=gu, out2=dgu, split=ffn, bn=bn)
+    ext().gemm(dm, w2, False, False, EPI_SWIGLU_BWD, dgu, aux=gu, out2=dgu, split=ffn, bn=bn, **_take_ag(dm))
     return dgu
 
 
@@ -159,7 +178,8 @@ def gemm_rope(x, wqkv, cos, sin, T, hd, rot_cols, out=None, bn=0):
     M, N = x.shape[0], wqkv.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
-    ext().gemm(x, wqkv, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols, bn=bn)
+    ext().gemm(x, wqkv, False, True, EPI_ROPE, out, cos_t=cos, sin_t=sin, T=T, hd=hd, rot_cols=rot_cols, bn=bn,
+               **_take_ag(x))
     return out
 
 

@@ -85,7 +85,7 @@ class DataParallel:
         if mode == "auto":
             self.mode = pick_mode(mode, torch.cuda.current_device() if torch.cuda.is_available() else 0)
         # False when the model's gradient writers store on the step's first write (the NCCL
-        # step then skips clearing the buffer; the fused kernels clear what they read anyway)
+        # step then skips clearing the buffer, and so does the peer-memory kernel)
         self.zero_grads = True
         self.flat = None
         self.fused = None
@@ -161,6 +161,8 @@ class DataParallel:
     @torch.no_grad()
     def reduce_and_step(self, opt: ShardedAdamW):
         f = self.flat
+        if self.fused is not None and hasattr(self.fused, "clear_grads"):
+            self.fused.clear_grads = self.zero_grads  # used from this step's kernels on
         if self.overlap:
             self.fused.finish_step()
             return

@@ -54,6 +54,10 @@ class FusedDP:
         self.pads_dev = torch.tensor(pptr, dtype=torch.int64, device=dev)
         self.my_pad = pp
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        # zero the gradient shards after reading them; off when the model's first gradient
+        # write of a step stores (DataParallel.zero_grads), which saves world x 4 bytes of
+        # NVLink stores per parameter
+        self.clear_grads = True
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
@@ -64,7 +68,8 @@ class FusedDP:
         o.step_t.add_(1)
         b1, b2 = o.betas
         C.dp_fused_adamw(self.grads_dev, self.shadows_dev, f.master, o.exp_avg, o.exp_avg_sq, o.lo, o.hi - o.lo,
-                         o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay, o.grad_scale, self.world)
+                         o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay, o.grad_scale, self.world,
+                         clear=self.clear_grads)
         C.dp_barrier(self.pads_dev, self.my_pad, self.epoch, self.rank, self.world, 200)
 
     def error_code(self, reset=False) -> int:
@@ -128,7 +133,7 @@ class OverlappedFusedDP(FusedDP):
         b1, b2 = o.betas
         C.dp_fused_adamw(self.grads_dev, self.shadows_dev, f.master, o.exp_avg[moff:moff + n],
                          o.exp_avg_sq[moff:moff + n], lo, n, o.lr_t, o.step_t, b1, b2, o.eps, o.weight_decay,
-                         o.grad_scale, self.world, self.max_blocks)
+                         o.grad_scale, self.world, self.max_blocks, clear=self.clear_grads)
 
     def bucket_ready(self, b):
         """Called (from the backward's hooks) when bucket b's gradients have all been issued."""

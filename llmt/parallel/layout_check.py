@@ -31,6 +31,8 @@ def main():
     p.add_argument("--dp-mode", default="nccl", choices=["nccl", "fused"])
     p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"])
     p.add_argument("--graph", action="store_true")
+    p.add_argument("--seq", type=int, default=128, help="sequence length (peer-memory tensor parallelism fuses "
+                   "its all-gathers into the GEMMs when a micro-batch gives each rank whole 128-row blocks)")
     args = p.parse_args()
     from llmt.config import get_config
     from llmt.models.llama import make_batch
@@ -44,7 +46,7 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     cfg = get_config("tiny256", kv_heads=2)
-    B, T = args.microbatches, 128
+    B, T = args.microbatches, args.seq
     batches = [make_batch(B, T, cfg.vocab, "cpu", seed=d) for d in range(args.dp)]
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     tr = ParallelTrainer(cfg, B, T, lay, microbatches=args.microbatches, device=f"cuda:{local}",

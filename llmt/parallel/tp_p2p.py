@@ -16,10 +16,25 @@ directly through NVSwitch (no NCCL, no multicast):
   pad            barrier flags; a flag barrier (bounded wait, error code on timeout) follows
                  every collective, so a buffer is rewritten only after every rank is done
                  with its previous contents
+  gather flags   one counter per 128-row block of every gather buffer (fused gathers)
 
 Alternating sets are safe because between two uses of one set every rank passes the
 barrier of the other set's collective, which it reaches only after its kernels that read the
 first set have completed (same stream).
+
+Fused all-gathers (fuse_gather, on when every rank's rows are whole 128-row blocks): the
+gather is not run when it is asked for. The returned buffer carries it as a pending gather, and
+the GEMM that consumes the buffer (qkv, w1||w3 in the forward; the w2 / wo dgrads on the
+backward's gathered dy) performs it: its epilogue warps store this rank's rows into every
+rank's buffer in 16-row pieces before their first tile, counting each piece in the
+destination's flag of that 128-row block, and its TMA producer loads a tile of A only once the
+flag of the tile's block has reached this call's count (this rank's own blocks are loaded
+first). No barrier follows a fused gather. Its buffers are still rewritten only after every
+rank is done with them: a forward site is next written in the next step, after the backward's
+reduce-scatter barrier of the same site, which every rank passes only after its weight-gradient
+GEMM read the site; between two uses of one backward gather buffer every rank passes a
+reduce-scatter barrier (each block's backward runs one between its two gathers). The flag
+counts grow by a fixed amount per call on every rank, so they are never reset.
 """
 from __future__ import annotations
 
@@ -31,8 +46,29 @@ from llmt.ops import native as N
 EPI_PEER_RS = 7
 
 
+AG_PIECES = 8  # 16-row pieces per 128-row block: each adds one to the block's flag (kAgPieces)
+
+
+class PendingGather:
+    """An all-gather owed by a gather buffer: run by the consuming GEMM (kwargs) or, when the
+    first consumer cannot fuse it, on its own (run_unfused)."""
+
+    def __init__(self, comm, x_l, index, dst_ptrs, flag_ptrs):
+        self.comm, self.x_l, self.index = comm, x_l, index
+        self.dst_ptrs, self.flag_ptrs = dst_ptrs, flag_ptrs
+
+    def kwargs(self):
+        c = self.comm
+        c.ag_calls[self.index] += 1
+        return dict(ag_src=self.x_l, ag_dst=self.dst_ptrs, ag_flags=self.flag_ptrs,
+                    ag_expect=c.ag_calls[self.index] * AG_PIECES, ag_tp=c.tp, tp_rank=c.rank, rows_per_rank=c.nl)
+
+    def run_unfused(self):
+        self.comm._gather(self.x_l, self.dst_ptrs, 700)
+
+
 class TPPeerComm:
-    def __init__(self, group, rows: int, d: int, sites: int, device):
+    def __init__(self, group, rows: int, d: int, sites: int, device, fuse_gather: bool = True):
         C = N.ext()
         self.group = group
         self.tp = dist.get_world_size(group)
@@ -45,24 +81,30 @@ class TPPeerComm:
         mat = rows * d * 2  # bytes of one (N, d) bf16 buffer
         self.n_sites = sites
         total = (sites + 2 + 2) * mat  # gather sites, 2 slot sets, 2 backward gathers
+        self.fuse_gather = fuse_gather and self.nl % 128 == 0 and d % 8 == 0
+        self.blocks = rows // 128
+        fbytes = max(4096, (sites + 2) * self.blocks * 4)  # flags of the forward sites, 2 backward gathers
         ptr, h = C.ipc_alloc(total)
         pad, ph = C.ipc_alloc(4096)
-        self._own = [ptr, pad]
-        mine = torch.tensor(list(h + ph), dtype=torch.uint8, device=dev)
+        flg, fh = C.ipc_alloc(fbytes)
+        self._own = [ptr, pad, flg]
+        mine = torch.tensor(list(h + ph + fh), dtype=torch.uint8, device=dev)
         allh = [torch.empty_like(mine) for _ in range(self.tp)]
         dist.all_gather(allh, mine, group=group)
-        bases, pads = [], []
+        bases, pads, flags = [], [], []
         self._peers = []
         for p, hh in enumerate(allh):
             if p == self.rank:
                 bases.append(ptr)
                 pads.append(pad)
+                flags.append(flg)
                 continue
             b = bytes(hh.cpu().tolist())
-            bp, pp = C.ipc_open(b[0:64]), C.ipc_open(b[64:128])
-            self._peers += [bp, pp]
+            bp, pp, fp = C.ipc_open(b[0:64]), C.ipc_open(b[64:128]), C.ipc_open(b[128:192])
+            self._peers += [bp, pp, fp]
             bases.append(bp)
             pads.append(pp)
+            flags.append(fp)
 
         def ptrs(off):
             return torch.tensor([b + off for b in bases], dtype=torch.int64, device=dev)
@@ -79,6 +121,10 @@ class TPPeerComm:
         self.slot_local = [local((sites + k) * mat, (rows, d)) for k in range(2)]
         self.bwd_ptrs = [ptrs((sites + 2 + k) * mat) for k in range(2)]
         self.bwd_local = [local((sites + 2 + k) * mat, (rows, d)) for k in range(2)]
+        fl = self.blocks * 4
+        self.site_flag_ptrs = [torch.tensor([f + s * fl for f in flags], dtype=torch.int64, device=dev)
+                               for s in range(sites + 2)]  # forward sites, then the 2 backward buffers
+        self.ag_calls = [0] * (sites + 2)
         self.pads_dev = torch.tensor(pads, dtype=torch.int64, device=dev)
         self.my_pad = pad
         self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -95,14 +141,24 @@ class TPPeerComm:
         N.ext().tp_allgather_rows(x_l.contiguous(), dst_ptrs, self.tp, self.rank * self.nl)
         self.barrier(code)
 
+    def _pending(self, x_l, buf, index, dst_ptrs):
+        out = buf.view_as(buf)
+        out._llmt_pending_ag = PendingGather(self, x_l.contiguous(), index, dst_ptrs, self.site_flag_ptrs[index])
+        return out
+
     def all_gather_site(self, x_l, site):
-        """(N/tp, d) rows of every rank -> this rank's (N, d) buffer of the site (returned)."""
+        """(N/tp, d) rows of every rank -> this rank's (N, d) buffer of the site (returned; with
+        fused gathers the consuming GEMM fills it)."""
+        if self.fuse_gather:
+            return self._pending(x_l, self.site_local[site], site, self.site_ptrs[site])
         self._gather(x_l, self.site_ptrs[site], 300)
         return self.site_local[site]
 
     def all_gather_bwd(self, x_l):
         k = self._bwd
         self._bwd ^= 1
+        if self.fuse_gather:
+            return self._pending(x_l, self.bwd_local[k], self.n_sites + k, self.bwd_ptrs[k])
         self._gather(x_l, self.bwd_ptrs[k], 600)
         return self.bwd_local[k]
 

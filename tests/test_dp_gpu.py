@@ -27,7 +27,8 @@ def _multicast():
     return pick_mode("auto", 0) == "nvls"
 
 
-@pytest.mark.parametrize("mode,graph", [("nccl", False), ("nvls", False), ("nvls", True), ("nvls-overlap", True)])
+@pytest.mark.parametrize("mode,graph", [("nccl", False), ("nvls", False), ("nvls", True), ("nvls-overlap", True),
+                                        ("fused", False)])
 def test_dp2_matches_single_gpu(mode, graph):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

@@ -63,3 +63,34 @@ def test_rank_layout_matches_reference_order():
                 seen.add(r)
     assert seen == set(range(8))
     assert lay.tp_ranks(1, 0) == [4, 5] and lay.pp_ranks(0, 1) == [1, 3] and lay.dp_ranks(1, 1) == [3, 7]
+
+
+def test_pending_gather_is_consumed_once():
+    """A gather buffer that owes its all-gather hands it to the first GEMM that reads it with a
+    K-major A, once; a consumer that reads it MN-major (a weight gradient) first runs it alone."""
+    from llmt.ops import native as N
+    from llmt.parallel.tp_p2p import AG_PIECES, PendingGather
+
+    class Comm:
+        tp, rank, nl = 2, 1, 128
+
+        def __init__(self):
+            self.ag_calls = [0, 0, 0]
+            self.unfused = []
+
+        def _gather(self, x_l, dst, code):
+            self.unfused.append((x_l, dst, code))
+
+    c = Comm()
+    x_l, dst, flags = torch.zeros(128, 8), torch.zeros(2), torch.zeros(2)
+    buf = torch.zeros(256, 8)
+    a = buf.view_as(buf)
+    a._llmt_pending_ag = PendingGather(c, x_l, 2, dst, flags)
+    kw = N._take_ag(a)
+    assert kw["ag_expect"] == AG_PIECES and kw["ag_tp"] == 2 and kw["tp_rank"] == 1 and kw["rows_per_rank"] == 128
+    assert kw["ag_src"] is x_l and kw["ag_dst"] is dst and kw["ag_flags"] is flags
+    assert N._take_ag(a) == {} and c.ag_calls == [0, 0, 1]
+    a._llmt_pending_ag = PendingGather(c, x_l, 2, dst, flags)
+    assert N._take_ag(a, ta=True) == {} and len(c.unfused) == 1 and c.ag_calls == [0, 0, 1]
+    a._llmt_pending_ag = PendingGather(c, x_l, 2, dst, flags)
+    assert N._take_ag(a)["ag_expect"] == 2 * AG_PIECES
