@@ -39,7 +39,10 @@ def main():
     p.add_argument("--graph", action="store_true", help="capture the step in a CUDA graph (pp = 1 only)")
     p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"],
                    help="tensor-parallel row collectives: NCCL, or NVLink peer memory fused with the GEMMs")
+    p.add_argument("--tp-gather", default="fused", choices=["fused", "separate"],
+                   help="peer-memory all-gathers inside the consuming GEMMs, or as their own kernel + barrier")
     args = p.parse_args()
+    os.environ["LLMT_TP_FUSE_GATHER"] = "1" if args.tp_gather == "fused" else "0"
     from llmt.config import get_config, model_flops_per_token
     from llmt.parallel.engine import ParallelTrainer
     from llmt.parallel.groups import Layout
@@ -76,6 +79,7 @@ def main():
     res = {"model": args.model, "seq": args.seq, "global_batch": args.global_batch,
            "layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches, "n_gpus": world,
            "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm, "dp_mode": dp_mode,
+           "tp_gather": args.tp_gather if args.tp_comm == "p2p" else None,
            "ms_per_step": round(ms.item(), 3), "tokens_per_s": round(tokens / step_s, 1),
            "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2), "dtype": "bf16",
            "data": "synthetic uniform-random tokens, random-init weights", "timing": "CUDA events, max over ranks"}

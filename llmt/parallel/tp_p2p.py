@@ -38,6 +38,8 @@ counts grow by a fixed amount per call on every rank, so they are never reset.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -81,6 +83,7 @@ class TPPeerComm:
         mat = rows * d * 2  # bytes of one (N, d) bf16 buffer
         self.n_sites = sites
         total = (sites + 2 + 2) * mat  # gather sites, 2 slot sets, 2 backward gathers
+        fuse_gather = fuse_gather and os.environ.get("LLMT_TP_FUSE_GATHER", "1") != "0"
         self.fuse_gather = fuse_gather and self.nl % 128 == 0 and d % 8 == 0
         self.blocks = rows // 128
         fbytes = max(4096, (sites + 2) * self.blocks * 4)  # flags of the forward sites, 2 backward gathers
