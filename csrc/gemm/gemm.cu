@@ -147,6 +147,9 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
   memset(&mp, 0, sizeof(mp));
   const bool ok_a = ta ? make_tmap_2d(&mp.a, a, dt, 2, M, K, lda, 64, kGemmBK)
                        : make_tmap_2d(&mp.a, a, dt, 2, K, M, lda, kGemmBK, kGemmBM);
+  if (g.ag_src)
+    LLMT_REQUIRE(make_tmap_2d(&mp.a2, g.ag_src, dt, 2, K, g.rows_per_rank, g.ag_lds, kGemmBK, kGemmBM),
+                 "gemm: fused all-gather: tensor map of this rank's rows rejected");
   const int code_a = last_tmap_result();
   bool ok_b;
   if (tb) {

@@ -41,6 +41,7 @@ constexpr int kEpiStageBytes = 4 * 2 * 4096;
 // Host launchers, one translation unit per operand layout (keeps the build parallel).
 struct GemmMaps {
   CUtensorMap a, b, c, c2;  // operands, main output, auxiliary output
+  CUtensorMap a2;           // fused all-gather: this rank's own rows of A (GemmArgs::ag_src)
 };
 // pair: 256 x 256 tiles on CTA pairs (cta_group::2), BN must be 256
 cudaError_t gemm_launch_kk(int bn, int epi, const GemmMaps& m, const GemmArgs& g, cudaStream_t st, bool pair);  // fwd
@@ -420,46 +421,48 @@ __device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Epilogue warps of every CTA (t = 0..127): this rank's rows into every rank's gather buffer,
-// own buffer first, then the peers in rank order, in 16-row pieces strided over the grid.
+// Epilogue warps of every CTA (t = 0..127): this rank's rows into every rank's gather buffer, in
+// 16-row pieces strided over the grid. A piece is loaded once and stored to every destination:
+// first the rank that needs it soonest (rank p walks its row blocks from its own onwards, p, p+1,
+// ..., so this rank's rows are wanted next by rank - 1, then rank - 2, ...), this rank's own
+// buffer last (only later kernels read it; this GEMM loads its own blocks from ag_src). Thread t
+// owns row t / 8 of the piece and its 16-byte columns t % 8, t % 8 + 8, ...: no index division in
+// the copy loop, 16 loads in flight per thread.
 __device__ __forceinline__ void ag_store_rows(const GemmArgs& a, int t) {
-  constexpr int PR = 128 / kAgPieces;  // rows per piece
-  constexpr int U = 8;                 // 16-byte loads in flight per thread
+  constexpr int PR = 128 / kAgPieces;  // rows per piece (16: 8 threads per row)
+  constexpr int U = 16;
+  constexpr int kMaxTp = 8;
   const int k16 = a.K / 8;
   const int blocks = a.rows_per_rank / 128;
-  const int per_dest = blocks * kAgPieces;
-  const int units = per_dest * a.ag_tp;
-  const int n16 = PR * k16;
+  const int pieces = blocks * kAgPieces;
   const int64_t ls = a.ag_lds / 8, ld = a.ag_ldd / 8;
-  const int gblk0 = a.tp_rank * blocks;  // this rank's first 128-row block of A
-  for (int u = blockIdx.x; u < units; u += gridDim.x) {
-    const int j = u / per_dest, r = u - j * per_dest;
-    const int p = (a.tp_rank + j) % a.ag_tp;
-    const int lrow0 = r * PR;
-    const uint4* src = reinterpret_cast<const uint4*>(a.ag_src) + (int64_t)lrow0 * ls;
-    uint4* dst = reinterpret_cast<uint4*>(a.ag_dst[p]) + ((int64_t)a.tp_rank * a.rows_per_rank + lrow0) * ld;
-    for (int i0 = t; i0 < n16; i0 += 128 * U) {
+  const int gblk0 = a.tp_rank * blocks;
+  const int rr = t >> 3, c0 = t & 7;
+  uint4* dst[kMaxTp];
+#pragma unroll
+  for (int j = 0; j < kMaxTp; ++j)
+    dst[j] = j < a.ag_tp ? reinterpret_cast<uint4*>(a.ag_dst[(a.tp_rank + 2 * a.ag_tp - 1 - j) % a.ag_tp]) : nullptr;
+  for (int u = blockIdx.x; u < pieces; u += gridDim.x) {
+    const int64_t lrow = (int64_t)u * PR + rr;
+    const uint4* src = reinterpret_cast<const uint4*>(a.ag_src) + lrow * ls;
+    const int64_t doff = ((int64_t)a.tp_rank * a.rows_per_rank + lrow) * ld;
+    for (int q0 = c0; q0 < k16; q0 += 8 * U) {
       uint4 v[U];
 #pragma unroll
-      for (int e = 0; e < U; ++e) {
-        const int i = i0 + e * 128;
-        if (i < n16) {
-          const int rr = i / k16;
-          v[e] = __ldg(src + rr * ls + (i - rr * k16));
-        }
-      }
+      for (int e = 0; e < U; ++e)
+        if (q0 + 8 * e < k16) v[e] = __ldg(src + q0 + 8 * e);
 #pragma unroll
-      for (int e = 0; e < U; ++e) {
-        const int i = i0 + e * 128;
-        if (i < n16) {
-          const int rr = i / k16;
-          __stcg(dst + rr * ld + (i - rr * k16), v[e]);
+      for (int j = 0; j < kMaxTp; ++j) {
+        if (j < a.ag_tp) {
+#pragma unroll
+          for (int e = 0; e < U; ++e)
+            if (q0 + 8 * e < k16) __stcg(dst[j] + doff + q0 + 8 * e, v[e]);
         }
       }
     }
-    __threadfence_system();  // this thread's stores are visible system-wide before the count
+    __threadfence_system();  // this thread's stores are visible system-wide before the counts
     named_bar_sync(1, 128);  // every epilogue thread has stored and fenced its part of the piece
-    if (t == 0) red_release_sys_add(a.ag_flags[p] + gblk0 + r / kAgPieces, 1u);
+    if (t < a.ag_tp) red_release_sys_add(a.ag_flags[t] + gblk0 + u / kAgPieces, 1u);
   }
 }
 
@@ -497,7 +500,8 @@ __device__ __forceinline__ void tile_mn(const GemmArgs& g, int rest, int rot, in
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int KIND = 0, bool PAIR = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
+            const __grid_constant__ CUtensorMap tmA2, const GemmArgs args) {
   constexpr int BM = kGemmBM, BK = kGemmBK;
   constexpr bool F8 = KIND != 0, BS = KIND >= 2;
   static_assert(!F8 || (!A_MN && !B_MN), "8-bit operands are K-major only");
@@ -540,6 +544,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (KIND == 0 && args.ag_src) prefetch_tmap(&tmA2);
   }
   if (warp == 1) {
     if constexpr (PAIR) tmem_alloc_pair<TMEM_COLS>(tmem_slot);
@@ -578,9 +583,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         int mb, nb;
         tile_mn(args, rest, ag_rot, mb, nb);
         const int k_lo = ks * kpb, k_hi = min(args.k_blocks, k_lo + kpb);
+        // fused all-gather: this rank's own row blocks come straight from its rows (tmA2, no
+        // wait); another rank's block is loaded from the gather buffer once its pieces arrived
+        const CUtensorMap* tma = &tmA;
+        int arow0 = 0;  // row of tma where this tile's A rows start, minus the tile's own offset
         if constexpr (KIND == 0) {
           const int arow = mb * TM + (int)rank * BM;  // first row of this CTA's A tile
-          if (ag && arow < args.M && arow / BM != ag_ready) {
+          const int own0 = args.tp_rank * args.rows_per_rank;
+          if (ag && arow >= own0 && arow < own0 + args.rows_per_rank) {
+            tma = &tmA2;
+            arow0 = own0;
+          } else if (ag && arow < args.M && arow / BM != ag_ready) {
             ag_wait_block(args, ag_my_flags, arow / BM, ag_give_up);
             ag_ready = arow / BM;
           }
@@ -599,7 +612,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int k0 = kb * KX;
             const int row = mb * TM + (int)rank * BM;
             if constexpr (!A_MN) {
-              tma_load_2d_pair(sa, &tmA, fb, k0, row);
+              tma_load_2d_pair(sa, tma, fb, k0, row - arow0);
             } else {
               tma_load_2d_pair(sa, &tmA, fb, row, k0);
               tma_load_2d_pair(sa + 8192, &tmA, fb, row + 64, k0);
@@ -630,7 +643,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             bulk_load(sfs + NCH * 512, args.sfb + ((int64_t)nb * args.sf_chunks + ck) * 512, NCH * 512, &full[stage]);
           }
           if constexpr (!A_MN) {
-            tma_load_2d(sa, &tmA, &full[stage], k0, mb * BM);
+            tma_load_2d(sa, tma, &full[stage], k0, mb * BM - arow0);
           } else {
             tma_load_2d(sa, &tmA, &full[stage], mb * BM, k0);
             tma_load_2d(sa + 8192, &tmA, &full[stage], mb * BM + 64, k0);
@@ -807,12 +820,12 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
       pairs = std::min(pairs, fit);
       cfg.gridDim = dim3(2 * pairs);
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp.a, mp.b, mp.c, mp.c2, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mp.a, mp.b, mp.c, mp.c2, mp.a2, args);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
   const int grid = std::min(tiles, persistent_sms());
-  launch_pdl_if(pdl_gemm_enabled(), kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, args);
+  launch_pdl_if(pdl_gemm_enabled(), kern, grid, kGemmThreads, smem, st, mp.a, mp.b, mp.c, mp.c2, mp.a2, args);
   return cudaGetLastError();
 }
 
