@@ -37,7 +37,8 @@ class ParallelTrainer:
         self.stage = build_stage(cfg, seq, layout.pp, g.pp_rank, layout.tp, g.tp_rank, seed=seed, device=self.device,
                                  init=init)
         if impl == "native":
-            self.x = NativeStage(self.stage, g.tp_group, pad_to=layout.dp, ce_chunk=ce_chunk, comm=tp_comm)
+            self.x = NativeStage(self.stage, g.tp_group, pad_to=layout.dp, ce_chunk=ce_chunk, comm=tp_comm,
+                                 in_flight=layout.pp)
             flat = self.x.flat
             if layout.dp > 1:
                 from llmt.parallel.dp import DataParallel

@@ -144,10 +144,15 @@ class NativeStage:
     """Stage on the native kernels (flat fp32 master / grad, bf16 shadow; every weight gradient
     into main_grad). Boundary activation: (pending branch output bf16, fp32 residual)."""
 
-    def __init__(self, stage: StageModel, tp_group=None, pad_to: int = 1, ce_chunk: int = 8192, comm: str = "nccl"):
+    def __init__(self, stage: StageModel, tp_group=None, pad_to: int = 1, ce_chunk: int = 8192, comm: str = "nccl",
+                 in_flight: int = 1):
         from llmt.models.native import FlatParams
         self.m, self.g, self.ce_chunk = stage, tp_group, ce_chunk
         self.comm_kind, self.comm = comm, None
+        # micro-batches between their forward and their backward at once (the pipeline depth):
+        # peer-memory gathers keep one set of site buffers per such micro-batch
+        self.in_flight = in_flight
+        self.micro = 0
         self.flat = FlatParams(stage, stage.rope_cos.device if stage.emb is None else stage.emb.weight.device,
                                pad_to=pad_to)
         self.tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
@@ -167,6 +172,8 @@ class NativeStage:
         cos = m.rope_cos[:T].contiguous()
         sin = m.rope_sin[:T].contiguous()
         comm = self._peer_comm(B * T)
+        if comm is not None:
+            comm.select_set(self.micro)
         for i, blk in enumerate(m.blocks):
             a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i)
         return (a, r)
@@ -178,7 +185,8 @@ class NativeStage:
             from llmt.parallel.tp_p2p import TPPeerComm
             if self.comm is not None:
                 self.comm.close()
-            self.comm = TPPeerComm(self.g, rows, self.m.cfg.d, 2 * len(self.m.blocks), self.flat.master.device)
+            self.comm = TPPeerComm(self.g, rows, self.m.cfg.d, 2 * len(self.m.blocks), self.flat.master.device,
+                                   sets=self.in_flight)
         return self.comm
 
     def close(self):
@@ -249,6 +257,7 @@ class Pipeline1F1B:
         inputs, outputs, losses = [None] * m_count, [None] * m_count, []
 
         def fwd(i, acts_in):
+            self.x.micro = i  # the executor's per-micro-batch buffers (peer-memory gathers)
             if self.first:
                 acts = self.x.forward_blocks(self.x.forward_first(idx[i]), mb, T)
             else:

@@ -7,7 +7,11 @@ directly through NVSwitch (no NCCL, no multicast):
 
   gather sites   one (N, d) bf16 buffer per all-gather site of the forward (two per block):
                  each rank stores its N/tp rows into every peer's buffer; the gathered
-                 tensor handed to the next GEMM is this rank's buffer (kept for the backward)
+                 tensor handed to the next GEMM is this rank's buffer (kept for the backward).
+                 Under pipeline parallelism several micro-batches are between their forward
+                 and their backward at once: `sets` copies of the site buffers, micro-batch i
+                 uses set i % sets (select_set), so a later forward never overwrites rows an
+                 earlier micro-batch's backward still reads
   slots          (tp, N/tp, d) bf16, two sets used alternately: the row-parallel GEMMs (wo,
                  w2) store each output row straight into slot `rank` of the row's owner from
                  their epilogue (GEMM -> reduce-scatter in one kernel, the transfer overlapping
@@ -70,7 +74,7 @@ class PendingGather:
 
 
 class TPPeerComm:
-    def __init__(self, group, rows: int, d: int, sites: int, device, fuse_gather: bool = True):
+    def __init__(self, group, rows: int, d: int, sites: int, device, fuse_gather: bool = True, sets: int = 1):
         C = N.ext()
         self.group = group
         self.tp = dist.get_world_size(group)
@@ -82,6 +86,8 @@ class TPPeerComm:
         self.device = dev
         mat = rows * d * 2  # bytes of one (N, d) bf16 buffer
         self.n_sites = sites
+        self.sets, self.set = sets, 0
+        sites = sites * sets  # forward site buffers of every set, set-major
         total = (sites + 2 + 2) * mat  # gather sites, 2 slot sets, 2 backward gathers
         fuse_gather = fuse_gather and os.environ.get("LLMT_TP_FUSE_GATHER", "1") != "0"
         self.fuse_gather = fuse_gather and self.nl % 128 == 0 and d % 8 == 0
@@ -144,6 +150,10 @@ class TPPeerComm:
         N.ext().tp_allgather_rows(x_l.contiguous(), dst_ptrs, self.tp, self.rank * self.nl)
         self.barrier(code)
 
+    def select_set(self, k: int):
+        """Forward gathers from now on use site-buffer set k (the micro-batch's)."""
+        self.set = k % self.sets
+
     def _pending(self, x_l, buf, index, dst_ptrs):
         out = buf.view_as(buf)
         out._llmt_pending_ag = PendingGather(self, x_l.contiguous(), index, dst_ptrs, self.site_flag_ptrs[index])
@@ -152,6 +162,7 @@ class TPPeerComm:
     def all_gather_site(self, x_l, site):
         """(N/tp, d) rows of every rank -> this rank's (N, d) buffer of the site (returned; with
         fused gathers the consuming GEMM fills it)."""
+        site += self.set * self.n_sites
         if self.fuse_gather:
             return self._pending(x_l, self.site_local[site], site, self.site_ptrs[site])
         self._gather(x_l, self.site_ptrs[site], 300)
@@ -161,7 +172,7 @@ class TPPeerComm:
         k = self._bwd
         self._bwd ^= 1
         if self.fuse_gather:
-            return self._pending(x_l, self.bwd_local[k], self.n_sites + k, self.bwd_ptrs[k])
+            return self._pending(x_l, self.bwd_local[k], self.n_sites * self.sets + k, self.bwd_ptrs[k])
         self._gather(x_l, self.bwd_ptrs[k], 600)
         return self.bwd_local[k]
 
