@@ -129,7 +129,7 @@ cudaError_t gemm(const void* a, int64_t lda, const void* b, int64_t ldb, bool ta
     g.ag_ldd = lda;
   }
   // 256 x 256 tiles on CTA pairs wherever the planner picked 256-wide tiles and M fills them
-  const bool pair = BN == 256 && M > kGemmBM && epi != EPI_PEER_RS && gemm_pairs_enabled();
+  const bool pair = BN == 256 && M > kGemmBM && gemm_pairs_enabled();
   g.M = M;
   g.N = N;
   g.K = K;

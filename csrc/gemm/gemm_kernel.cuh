@@ -242,33 +242,44 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int row, int wrow,
       st.store3d(tmC2, b, col0, 1, wrow);
     }
   } else if constexpr (EPI == EPI_PEER_RS) {
-    // bf16 rows straight into the owner rank's reduce-scatter slot through NVLink
-    bf16* dst = nullptr;
-    if (rv) {
-      const int q = row / a.rows_per_rank;
-      dst = static_cast<bf16*>(a.peer[q]) +
-            ((int64_t)a.tp_rank * a.rows_per_rank + (row - q * a.rows_per_rank)) * a.ldo;
-    }
+    // bf16 rows straight into their owner rank's reduce-scatter slot through NVLink. A thread
+    // holds one accumulator row, so a per-thread store would write 16-byte pieces of 32 rows;
+    // instead each 32 x 64 chunk is staged in the warp's shared-memory buffer (128B swizzle) and
+    // leaves row by row: lanes 8k .. 8k + 7 write one row's 128 contiguous bytes, four rows per
+    // store instruction.
+    const int rpr = a.rows_per_rank;
+    const int sub = st.lane >> 3, u = st.lane & 7;
+    uint8_t* b = st.base;  // the warp's first 4 KB buffer (this epilogue issues no TMA stores)
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col0 = nb * BN + c * 32;
+    for (int c = 0; c < BN / 64; ++c) {
+      const int col0 = nb * BN + c * 64;
       if (col0 >= a.N) break;  // uniform across the warp
-      uint32_t r[32];
-      tmem_ld32(taddr + c * 32, r);
+      uint32_t r0[32], r1[32];
+      tmem_ld32(taddr + c * 64, r0);
+      tmem_ld32(taddr + c * 64 + 32, r1);
       tmem_wait_ld();
-      if (rv) {
-        float v[32];
+      float v[64];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = cvt(r[j]);
-        uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
+      for (int j = 0; j < 32; ++j) {
+        v[j] = cvt(r0[j]);
+        v[32 + j] = cvt(r1[j]);
+      }
+      __syncwarp();  // every lane has read the previous chunk out of the buffer
+      st.put_bf16x64(b, v);
+      __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const BF16x8 o = float_to_bf16x8(v + 8 * u);
-          __stcg(d4 + u, *reinterpret_cast<const uint4*>(&o));
+      for (int it = 0; it < 8; ++it) {
+        const int rl = it * 4 + sub;  // row within the warp's 32
+        const int grow = wrow + rl;
+        if (grow < a.M && col0 + 8 * u < a.N) {
+          const int q = grow / rpr;
+          bf16* dst = static_cast<bf16*>(a.peer[q]) + ((int64_t)a.tp_rank * rpr + (grow - q * rpr)) * a.ldo + col0 +
+                      8 * u;
+          __stcg(reinterpret_cast<uint4*>(dst), *reinterpret_cast<const uint4*>(b + rl * 128 + ((u ^ (rl & 7)) << 4)));
         }
       }
     }
-    __threadfence_system();  // this tile's rows are visible to their owners before the barrier
+    (void)row;  // (the rows are made visible to their owners once, after the last tile)
   } else if constexpr (EPI == EPI_SWIGLU_BWD) {
     // g and u arrive by TMA (3D map over the saved [g | u] rows) one chunk ahead, into the
     // warp's two 4 KB buffers; dg and du are written back in place and leave by TMA.
@@ -765,6 +776,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       buf ^= 1;
       if (buf == 0) aphase ^= 1;
     }
+    // PEER_RS: every row this thread stored to a peer is visible system-wide before the flag
+    // barrier that follows the GEMM releases the owners
+    if constexpr (EPI == EPI_PEER_RS) __threadfence_system();
     st.drain();
   }
   pdl_trigger();  // this CTA is done: the next kernel in the stream may be scheduled

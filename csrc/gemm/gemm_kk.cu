@@ -30,6 +30,7 @@ static cudaError_t run_kk_pair(int epi, const GemmMaps& mp, const GemmArgs& g, c
     case EPI_ROPE: return launch<256, S, false, false, EPI_ROPE, 0, true>(mp, g, st);
     case EPI_CE_FWD: return launch<256, S, false, false, EPI_CE_FWD, 0, true>(mp, g, st);
     case EPI_CE_BWD: return launch<256, S, false, false, EPI_CE_BWD, 0, true>(mp, g, st);
+    case EPI_PEER_RS: return launch<256, S, false, false, EPI_PEER_RS, 0, true>(mp, g, st);
     default: set_last_error("gemm: epilogue not built for CTA pairs"); return cudaErrorInvalidValue;
   }
 }

@@ -154,3 +154,27 @@ def test_fused_allgather_wait_runs_out(nat):
     R.check_stores(1)  # this rank's own pieces were stored and counted all the same
     x = torch.randn(256, K, device="cuda").bfloat16()
     assert rel_err(nat.gemm(x, w), x.float() @ w.float().t()) < 1e-2
+
+
+@pytest.mark.parametrize("tp,rank,rows,N,bn", [(2, 1, 256, 512, 0), (4, 2, 128, 1024, 0), (2, 0, 200, 96, 0),
+                                               (2, 1, 512, 1024, 256), (4, 3, 256, 768, 256)])
+def test_peer_rs_epilogue_stand_in(nat, tp, rank, rows, N, bn):
+    """GEMM -> reduce-scatter in one kernel (the wo / w2 GEMMs): output row r goes to slot `rank`
+    of its owner r // rows; the owners' slot buffers are local stand-ins here. bn = 256 runs the
+    256 x 256 tiles on CTA pairs."""
+    from llmt.parallel.tp_p2p import EPI_PEER_RS
+    K = 384
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(tp * rows, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    slots = [torch.full((tp * rows, N), 7.0, device="cuda", dtype=torch.bfloat16) for _ in range(tp)]
+    ptrs = torch.tensor([s.data_ptr() for s in slots], dtype=torch.int64, device="cuda")
+    nat.ext().gemm(x, w, False, True, EPI_PEER_RS, slots[rank], peer=ptrs, tp_rank=rank, rows_per_rank=rows, bn=bn)
+    torch.cuda.synchronize()
+    assert nat.gemm_error_code() == 0
+    ref = x.float() @ w.float().t()
+    for q in range(tp):
+        mine = slots[q][rank * rows:(rank + 1) * rows]
+        assert rel_err(mine, ref[q * rows:(q + 1) * rows]) < 1e-2
+        other = torch.cat([slots[q][:rank * rows], slots[q][(rank + 1) * rows:]])
+        assert (other == 7.0).all(), "rows written outside this rank's slot"
