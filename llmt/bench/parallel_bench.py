@@ -39,6 +39,8 @@ def main():
     p.add_argument("--graph", action="store_true", help="capture the step in a CUDA graph (pp = 1 only)")
     p.add_argument("--tp-comm", default="nccl", choices=["nccl", "p2p"],
                    help="tensor-parallel row collectives: NCCL, or NVLink peer memory fused with the GEMMs")
+    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"],
+                   help="block linears (low precision with NCCL tensor-parallel collectives only)")
     p.add_argument("--tp-gather", default="fused", choices=["fused", "separate"],
                    help="peer-memory all-gathers inside the consuming GEMMs, or as their own kernel + barrier")
     args = p.parse_args()
@@ -54,7 +56,8 @@ def main():
     lay = Layout(dp=args.dp, tp=args.tp, pp=args.pp)
     B = args.global_batch // args.dp
     tr = ParallelTrainer(cfg, B, args.seq, lay, microbatches=args.microbatches, device=f"cuda:{local}",
-                         init="local", dp_mode=args.dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm)
+                         init="local", dp_mode=args.dp_mode, cuda_graph=args.graph, tp_comm=args.tp_comm,
+                         linear=args.linear)
     dp_mode = tr.dp.mode if tr.dp is not None else None  # what "auto" resolved to
     g = torch.Generator().manual_seed(1 + tr.groups.dp_rank)
     idx = torch.randint(0, cfg.vocab, (B, args.seq), generator=g).pin_memory()
@@ -79,9 +82,10 @@ def main():
     res = {"model": args.model, "seq": args.seq, "global_batch": args.global_batch,
            "layout": f"dp{args.dp} tp{args.tp} pp{args.pp}", "microbatches": args.microbatches, "n_gpus": world,
            "cuda_graph": bool(tr.use_graph), "tp_comm": args.tp_comm, "dp_mode": dp_mode,
-           "tp_gather": args.tp_gather if args.tp_comm == "p2p" else None,
+           "tp_gather": args.tp_gather if args.tp_comm == "p2p" else None, "linear": args.linear,
            "ms_per_step": round(ms.item(), 3), "tokens_per_s": round(tokens / step_s, 1),
-           "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2), "dtype": "bf16",
+           "mfu_vs_measured_bf16": None, "peak_mem_gb": round(mem.item(), 2),
+           "dtype": "bf16" if args.linear == "bf16" else f"{args.linear} block linears, bf16 rest",
            "data": "synthetic uniform-random tokens, random-init weights", "timing": "CUDA events, max over ranks"}
     if rank == 0:
         try:

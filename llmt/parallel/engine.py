@@ -27,7 +27,8 @@ from llmt.parallel.tp import sync_replicated_grads
 class ParallelTrainer:
     def __init__(self, cfg: ModelConfig, batch: int, seq: int, layout: Layout, microbatches: int = 1,
                  device="cuda", seed: int = 0, lr: float = 3e-4, impl: str = "native", dp_mode: str = "nccl",
-                 init: str = "full", ce_chunk: int = 8192, cuda_graph: bool = False, tp_comm: str = "nccl"):
+                 init: str = "full", ce_chunk: int = 8192, cuda_graph: bool = False, tp_comm: str = "nccl",
+                 linear: str = "bf16"):
         self.cfg, self.batch, self.seq, self.layout, self.m = cfg, batch, seq, layout, microbatches
         if batch % microbatches:
             raise ValueError("batch must be a multiple of microbatches")
@@ -38,7 +39,7 @@ class ParallelTrainer:
                                  init=init)
         if impl == "native":
             self.x = NativeStage(self.stage, g.tp_group, pad_to=layout.dp, ce_chunk=ce_chunk, comm=tp_comm,
-                                 in_flight=layout.pp)
+                                 in_flight=layout.pp, linear=linear)
             flat = self.x.flat
             if layout.dp > 1:
                 from llmt.parallel.dp import DataParallel

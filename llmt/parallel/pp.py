@@ -145,7 +145,7 @@ class NativeStage:
     into main_grad). Boundary activation: (pending branch output bf16, fp32 residual)."""
 
     def __init__(self, stage: StageModel, tp_group=None, pad_to: int = 1, ce_chunk: int = 8192, comm: str = "nccl",
-                 in_flight: int = 1):
+                 in_flight: int = 1, linear: str = "bf16"):
         from llmt.models.native import FlatParams
         self.m, self.g, self.ce_chunk = stage, tp_group, ce_chunk
         self.comm_kind, self.comm = comm, None
@@ -153,6 +153,11 @@ class NativeStage:
         # peer-memory gathers keep one set of site buffers per such micro-batch
         self.in_flight = in_flight
         self.micro = 0
+        if linear not in ("bf16", "fp8", "mxfp8", "nvfp4"):
+            raise ValueError(f"linear must be bf16, fp8, mxfp8 or nvfp4, not {linear!r}")
+        if linear != "bf16" and comm == "p2p" and tp_group is not None:
+            raise ValueError("low-precision block linears run with NCCL tensor-parallel collectives (tp_comm='nccl')")
+        self.linear = linear  # block linears of the stage's blocks (the head stays bf16)
         self.flat = FlatParams(stage, stage.rope_cos.device if stage.emb is None else stage.emb.weight.device,
                                pad_to=pad_to)
         self.tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
@@ -175,7 +180,7 @@ class NativeStage:
         if comm is not None:
             comm.select_set(self.micro)
         for i, blk in enumerate(m.blocks):
-            a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i)
+            a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i, self.linear)
         return (a, r)
 
     def _peer_comm(self, rows):

@@ -211,12 +211,45 @@ class TPTorchLlama(torch.nn.Module):
 
 
 # ---------------------------------------------------------------- native path (sm_100a kernels)
-def native_tp_block(blk, a, r, cos, sin, B, T, cfg, group, comm=None, i=0):
+def _lowp_regions(linear, cos, sin, B, T, cfg):
+    """The block's three linear regions (qkv + attention, wo, SwiGLU MLP) with low-precision
+    block linears: tensorwise e4m3 (fp8) or block-scaled MXFP8 / NVFP4, the same functions the
+    single-shard model uses. Returns (qkv_attention(x, w), linear(x, w), mlp(x, w1, w2))."""
+    if linear == "fp8":
+        from llmt.ops import fp8 as F8
+        return (lambda x, w: F8.QKVAttentionFP8.apply(x, w, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd),
+                F8.LinearFP8.apply,
+                lambda x, w1, w2: F8.SwiGLUMLPFP8.apply(x, w1, w2, cfg.ffn))
+    from llmt.ops import mx as MX
+    from llmt.ops import native as N
+    kind = N.MXFP8 if linear == "mxfp8" else N.NVFP4
+    return (lambda x, w: MX.QKVAttentionMX.apply(x, w, cos, sin, B, T, cfg.H, cfg.kvh, cfg.hd, kind),
+            lambda x, w: MX.LinearMX.apply(x, w, kind),
+            lambda x, w1, w2: MX.SwiGLUMLPMX.apply(x, w1, w2, cfg.ffn, kind))
+
+
+def native_tp_block(blk, a, r, cos, sin, B, T, cfg, group, comm=None, i=0, linear="bf16"):
     """One block on the native kernels over a tensor-parallel group: NCCL row collectives
     (comm None), or peer-memory ones with the row-parallel GEMMs storing to their owners
-    (comm = TPPeerComm; all-gather sites 2i and 2i+1). group None: no tensor parallelism."""
+    (comm = TPPeerComm; all-gather sites 2i and 2i+1). group None: no tensor parallelism.
+    linear: "bf16", or "fp8" / "mxfp8" / "nvfp4" block linears (NCCL collectives only: the
+    peer-memory collectives are fused into the bf16 GEMMs). Each rank quantizes its own shards;
+    NVFP4's per-tensor scale and tensorwise fp8's scale then come from the shard's amax."""
+    if linear != "bf16" and comm is not None:
+        raise ValueError("low-precision block linears run with NCCL tensor-parallel collectives "
+                         "(tp_comm='nccl'); the peer-memory collectives are fused into the bf16 GEMMs")
     from llmt.ops import functions as Fn
     from llmt.parallel.tp_p2p import AllGatherP2P, RowLinearRS
+    if linear != "bf16":
+        qkv_attn, lin, mlp = _lowp_regions(linear, cos, sin, B, T, cfg)
+        if a is None:
+            n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
+        else:
+            n1, s1 = Fn.AddRMSNormFn.apply(a, r, blk.norm1.weight, cfg.eps)
+        o = qkv_attn(gather_rows(n1, group), blk.attn.qkv.weight)
+        att = scatter_rows(lin(o, blk.attn.wo.weight), group)
+        n2, s2 = Fn.AddRMSNormFn.apply(att, s1, blk.norm2.weight, cfg.eps)
+        return scatter_rows(mlp(gather_rows(n2, group), blk.mlp.w1.weight, blk.mlp.w2.weight), group), s2
     if a is None:
         n1, s1 = Fn.RMSNormFn.apply(r, blk.norm1.weight, cfg.eps), r
     else:
@@ -243,7 +276,7 @@ class TPNativeLlama:
     accumulated into its parameter's main_grad."""
 
     def __init__(self, local: LlamaModel, group, ce_chunk: int = 8192, pad_to: int = 1, ckpt: bool = False,
-                 comm: str = "nccl"):
+                 comm: str = "nccl", linear: str = "bf16"):
         from llmt.models.native import FlatParams
         self.model = local
         self.cfg = local.cfg
@@ -258,6 +291,11 @@ class TPNativeLlama:
         self.r = dist.get_rank(group) if group is not None else 0
         self.comm_kind = comm
         self.comm = None  # TPPeerComm, built on the first forward (needs the token count)
+        if linear not in ("bf16", "fp8", "mxfp8", "nvfp4"):
+            raise ValueError(f"linear must be bf16, fp8, mxfp8 or nvfp4, not {linear!r}")
+        if linear != "bf16" and comm == "p2p":
+            raise ValueError("low-precision block linears run with NCCL tensor-parallel collectives (comm='nccl')")
+        self.linear = linear
 
     def _peer_comm(self, rows):
         if self.comm_kind != "p2p" or self.group is None:
@@ -285,9 +323,9 @@ class TPNativeLlama:
         for i, blk in enumerate(m.blocks):
             if self.ckpt and torch.is_grad_enabled():
                 a, r = torch.utils.checkpoint.checkpoint(native_tp_block, blk, a, r, cos, sin, B, T, cfg, g, comm, i,
-                                                      use_reentrant=False, preserve_rng_state=False)
+                                                      self.linear, use_reentrant=False, preserve_rng_state=False)
             else:
-                a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i)
+                a, r = native_tp_block(blk, a, r, cos, sin, B, T, cfg, g, comm, i, self.linear)
         h = Fn.FinalNormFn.apply(a, r, m.norm_f.weight, cfg.eps)
         return Fn.HeadCEVP.apply(gather_rows(h, g), m.head.weight, targets.reshape(-1), v0, g, self.ce_chunk)
 

@@ -24,6 +24,9 @@ def main():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--graph", action="store_true")
     p.add_argument("--kv-heads", type=int, default=None)
+    p.add_argument("--ffn", type=int, default=None, help="override the model's ffn width")
+    p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"],
+                   help="block linears of both the sharded and the single-GPU model")
     p.add_argument("--size", default=None, help="model size (default: tiny256 up to tp 2, tiny beyond: its"
                    " ffn splits into GEMM-aligned shards)")
     args = p.parse_args()
@@ -37,11 +40,11 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     size = args.size or ("tiny256" if world <= 2 else "tiny")
-    cfg = get_config(size, kv_heads=args.kv_heads)
+    cfg = get_config(size, kv_heads=args.kv_heads, **({"ffn": args.ffn} if args.ffn else {}))
     B, T = 2, 128
     idx, tgt = make_batch(B, T, cfg.vocab, "cpu", seed=0)
     group = dist.new_group(list(range(world)))
-    tr = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=args.graph, tp_group=group)
+    tr = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=args.graph, tp_group=group, linear=args.linear)
     losses = [tr.train_step(idx, tgt) for _ in range(args.steps)]
     torch.cuda.synchronize()
     codes = {"gemm": native.gemm_error_code(), "attn": native.attn_error_code()}
@@ -51,15 +54,20 @@ def main():
     ok = True
     if rank == 0:
         full = unshard_state(gathered, cfg)
-        ref = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=False)
+        ref = Trainer(cfg, B, T, device=f"cuda:{local}", cuda_graph=False, linear=args.linear)
         ref_losses = [ref.train_step(idx, tgt) for _ in range(args.steps)]
         rsd = ref.model.state_dict()
         num = sum(float((full[k].to(rsd[k].device) - rsd[k].float()).norm() ** 2) for k in rsd)
         den = sum(float(rsd[k].float().norm() ** 2) for k in rsd)
         rel = (num / den) ** 0.5
         loss_gap = max(abs(a - b) for a, b in zip(losses, ref_losses))
-        ok = rel < 2e-3 and loss_gap < 2e-2 and all(v == 0 for v in codes.values())
-        print(json.dumps({"tp": world, "graph": args.graph, "kv_heads": cfg.kvh, "rel_err_master": rel,
+        # low-precision linears: the shards' partial sums are rounded to bf16 before the next
+        # quantization, which can flip the sign of a tiny gradient element, and AdamW's first
+        # steps move a weight by about lr whatever its gradient's size (2 lr for a flipped sign)
+        bound = 2e-3 if args.linear == "bf16" else 1e-2
+        ok = rel < bound and loss_gap < 2e-2 and all(v == 0 for v in codes.values())
+        print(json.dumps({"tp": world, "graph": args.graph, "kv_heads": cfg.kvh, "linear": args.linear,
+                          "rel_err_master": rel,
                           "losses": losses, "ref_losses": ref_losses, "error_codes": codes, "ok": ok}), flush=True)
     tr.release()
     dist.barrier()

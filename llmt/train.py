@@ -41,13 +41,11 @@ class Trainer:
         self.tp_group = tp_group
         pad_to = dp.world_size if dp is not None else 1
         if tp_group is not None:
-            if linear != "bf16":
-                raise ValueError("fp8 linears are built for the single-shard model only")
             import torch.distributed as dist
             from llmt.parallel.tp import TPNativeLlama, build_local_model
             tp, r = dist.get_world_size(tp_group), dist.get_rank(tp_group)
             self.model = build_local_model(cfg, seq, tp, r, seed=seed, device=self.device, init=init)
-            self.net = TPNativeLlama(self.model, tp_group, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt)
+            self.net = TPNativeLlama(self.model, tp_group, ce_chunk=ce_chunk, pad_to=pad_to, ckpt=ckpt, linear=linear)
         else:
             self.model = build_model(cfg, seq, seed=seed, device=self.device)
             overlap = dp is not None and getattr(dp, "overlap", False)

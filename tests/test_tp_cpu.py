@@ -94,3 +94,11 @@ def test_pending_gather_is_consumed_once():
     assert N._take_ag(a, ta=True) == {} and len(c.unfused) == 1 and c.ag_calls == [0, 0, 1]
     a._llmt_pending_ag = PendingGather(c, x_l, 2, dst, flags)
     assert N._take_ag(a)["ag_expect"] == 2 * AG_PIECES
+
+
+def test_low_precision_tp_block_needs_nccl_collectives():
+    """Low-precision block linears are not fused with the peer-memory collectives: asking for both
+    is refused before any kernel runs."""
+    from llmt.parallel.tp import native_tp_block
+    with pytest.raises(ValueError, match="NCCL"):
+        native_tp_block(None, None, None, None, None, 1, 128, None, None, comm=object(), i=0, linear="mxfp8")
