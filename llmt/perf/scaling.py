@@ -152,6 +152,17 @@ def evaluate(cfg, seq, G, n, dp, tp, pp, mb, comp: StageCompute, links, system, 
 RUN_KW = dict(fused_tp=False, overlap_dp=False)
 
 
+def run_kw(run):
+    """How a measured run's collectives are modeled: exposed (RUN_KW), except the peer-memory
+    tensor-parallel collectives of a run whose all-gathers ran inside the GEMMs (tp_comm "p2p",
+    tp_gather "fused": both the gather and the reduce-scatter are fused into GEMMs, so the
+    transfer overlaps the tiles)."""
+    kw = dict(RUN_KW)
+    if run.get("tp_comm") == "p2p" and run.get("tp_gather") == "fused":
+        kw["fused_tp"] = True
+    return kw
+
+
 def run_layout(run):
     """(dp, tp, pp, micro-batch size, global batch) of a parallel-bench result."""
     kv = {p[:2]: int(p[2:]) for p in run["layout"].split()}
@@ -162,7 +173,7 @@ def run_layout(run):
 def _terms(run, comp, links, system):
     cfg, seq = comp.cfg, comp.seq
     dp, tp, pp, mb, G = run_layout(run)
-    r = evaluate(cfg, seq, G, dp * tp * pp, dp, tp, pp, mb, comp, links, system, **RUN_KW)
+    r = evaluate(cfg, seq, G, dp * tp * pp, dp, tp, pp, mb, comp, links, system, **run_kw(run))
     b = r["breakdown_s"]
     scaled_c = b["compute"] + b["pipeline bubble"]
     scaled_t = b["tp comm (exposed)"]
@@ -193,7 +204,7 @@ def calibrate(fit_runs, comp, links, system):
 def predict_run(run, comp, links, system, compute_scale=1.0, comm_scale=1.0):
     dp, tp, pp, mb, G = run_layout(run)
     r = evaluate(comp.cfg, comp.seq, G, dp * tp * pp, dp, tp, pp, mb, comp, links, system,
-                 compute_scale=compute_scale, comm_scale=comm_scale, **RUN_KW)
+                 compute_scale=compute_scale, comm_scale=comm_scale, **run_kw(run))
     return r["step_s"] * 1e3
 
 

@@ -34,3 +34,16 @@ def test_search_with_calibration_matches_validation():
     r = evaluate(SIZES["llama3-8b"], 4096, 16, 8, 2, 2, 2, 2, comp, links, "b200_nvl8_ib",
                  compute_scale=res["compute_scale"], comm_scale=res["comm_scale"], **RUN_KW)
     assert abs(r["step_s"] * 1e3 - res["holdout"][0]["calibrated_ms"]) < 0.01
+
+
+def test_fused_tensor_parallel_runs_are_modeled_overlapped():
+    """Runs whose tensor-parallel collectives ran inside the GEMMs (peer memory, fused gathers)
+    are predicted with the collectives overlapped, from scales fitted on the NCCL runs only."""
+    import json
+    from llmt.perf.scaling import run_kw
+    fused = str(R / "par_8b_tp2_p2p_fused.json")
+    assert run_kw(json.load(open(fused)))["fused_tp"]
+    assert not run_kw(json.load(open(R / "par_8b_tp2_p2p_separate.json")))["fused_tp"]
+    fit = [str(R / f) for f in ("par_8b_tp2_nccl.json", "par_8b_tp4.json", "par_8b_tp8_nccl.json")]
+    res = validate(fit, [fused], Machine.from_peaks(), load_links())
+    assert abs(res["holdout"][0]["error"]) < 0.05, res["holdout"]
