@@ -825,11 +825,15 @@ cudaError_t launch(const GemmMaps& mp, const GemmArgs& args, cudaStream_t st) {
     if (args.ag_src) {
       // a fused all-gather needs every pair resident at once (the producers wait for rows that
       // other CTAs' epilogue warps store): no more pairs than the clusters that fit together
-      static int fit = 0;
+      // (one value per instantiation: every GPU of a job is a B200; atomic, since host threads
+      // may launch concurrently)
+      static std::atomic<int> fit_cache{0};
+      int fit = fit_cache.load(std::memory_order_relaxed);
       if (!fit) {
         cfg.gridDim = dim3(2 * pairs);
         cudaError_t e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
         if (e != cudaSuccess || fit < 1) return e != cudaSuccess ? e : cudaErrorLaunchOutOfResources;
+        fit_cache.store(fit, std::memory_order_relaxed);
       }
       pairs = std::min(pairs, fit);
       cfg.gridDim = dim3(2 * pairs);
