@@ -102,3 +102,74 @@ def test_low_precision_tp_block_needs_nccl_collectives():
     from llmt.parallel.tp import native_tp_block
     with pytest.raises(ValueError, match="NCCL"):
         native_tp_block(None, None, None, None, None, 1, 128, None, None, comm=object(), i=0, linear="mxfp8")
+
+
+class _FakeExt:
+    """The parts of the extension TPPeerComm uses, over CPU memory: "pointers" are integers into
+    per-allocation byte buffers, an opened peer handle maps to a distinct fake base."""
+
+    def __init__(self, rank):
+        self.bufs, self.next = {}, (rank + 1) << 40
+
+    def _new(self, nbytes):
+        base = self.next
+        self.next += max(nbytes, 1 << 12) + (1 << 20)
+        self.bufs[base] = torch.zeros(nbytes, dtype=torch.uint8)
+        return base
+
+    def ipc_alloc(self, nbytes):
+        base = self._new(nbytes)
+        return base, list(base.to_bytes(8, "little")) + [0] * 56
+
+    def ipc_open(self, handle):
+        return self._new(16) + (1 << 36)  # a peer's mapping: never dereferenced here
+
+    def tensor_from_ptr(self, ptr, n, dtype, dev):
+        base = max(b for b in self.bufs if b <= ptr)
+        es = torch.empty((), dtype=dtype).element_size()
+        return self.bufs[base][ptr - base: ptr - base + n * es].view(dtype)
+
+    def ipc_close(self, p):
+        pass
+
+    def ipc_free(self, p):
+        pass
+
+
+def _peer_comm_layout(rank, world):
+    import torch.distributed as dist
+    from llmt.ops import native as N
+    from llmt.parallel import tp_p2p
+    fake = _FakeExt(rank)
+    N.ext = lambda: fake
+    tp_p2p.torch.cuda.synchronize = lambda *a, **k: None
+    rows, d, sites, sets = 512, 64, 4, 2
+    c = tp_p2p.TPPeerComm(dist.new_group([0, 1]), rows, d, sites, "cpu", sets=sets)
+    blocks, mat = rows // 128, rows * d * 2
+    assert c.fuse_gather and c.nl == 256 and len(c.site_local) == sites * sets
+    x_l = torch.randn(c.nl, d).bfloat16()
+    for k in range(sets):
+        c.select_set(k + sets)  # micro-batch k + sets reuses set k
+        out = c.all_gather_site(x_l, 3)
+        pend = out._llmt_pending_ag
+        idx = k * sites + 3
+        assert pend.index == idx and out.data_ptr() == c.site_local[idx].data_ptr()
+        # this rank's entry of the pointer arrays is its own buffer, the other rank's is the mapping
+        assert int(pend.dst_ptrs[rank]) == c._own[0] + idx * mat
+        assert int(pend.flag_ptrs[rank]) == c._own[2] + idx * blocks * 4
+        assert int(pend.dst_ptrs[1 - rank]) != int(pend.dst_ptrs[rank])
+        kw = pend.kwargs()
+        assert kw["ag_expect"] == 8 and kw["rows_per_rank"] == 256 and kw["tp_rank"] == rank
+    # distinct sets never share a buffer; the backward gathers come after every set's sites
+    ptrs = {t.data_ptr() for t in c.site_local} | {t.data_ptr() for t in c.bwd_local}
+    assert len(ptrs) == sites * sets + 2
+    b = c.all_gather_bwd(x_l)._llmt_pending_ag
+    assert b.index == sites * sets and int(b.flag_ptrs[rank]) == c._own[2] + sites * sets * blocks * 4
+    assert len(c.ag_calls) == sites * sets + 2
+
+
+def test_peer_comm_buffer_sets_and_flags():
+    """Peer-memory tensor parallelism under pipeline parallelism: every in-flight micro-batch has
+    its own forward gather buffers and flag counters, and the pointer arrays a fused gather hands
+    the GEMM point at the right buffer of every rank (CPU stand-in for the extension)."""
+    run_ranks(_peer_comm_layout, 2)
