@@ -101,7 +101,11 @@ def _split_inventory(cfg, mb, seq, tp):
     return per_layer, first, last, opt
 
 
-def build_rank(cfg, mb, seq, dp, tp, pp, m, dp_i, pp_i, tp_i, machine, kinds):
+def build_rank(cfg, mb, seq, dp, tp, pp, m, dp_i, pp_i, tp_i, machine, kinds, fused_tp=False):
+    """One rank's graph. fused_tp: the tensor-parallel collectives run inside the GEMMs (the
+    peer-memory path): an all-gather and the GEMM that consumes it both start from the GEMM's
+    input and run concurrently, a reduce-scatter starts with the GEMM that produces its rows, and
+    the next operator waits for both (its inputs include the collective's output)."""
     rank = rank_of(dp_i, pp_i, tp_i, tp, pp)
     g = Graph(rank, machine)
     per_layer, first, last, opt = _split_inventory(cfg, mb, seq, tp)
@@ -127,24 +131,37 @@ def build_rank(cfg, mb, seq, dp, tp, pp, m, dp_i, pp_i, tp_i, machine, kinds):
                 for o, k in first:
                     if o.phase == "fwd":
                         g.add(o.name, "comp", o.cat, "fwd", (), (x,), o.flops * k, o.bytes * k, mb=i)
+            join = ()  # outputs of fused collectives the next operator also waits for
             for li in layers:
                 for o, k in per_layer:
                     if o.phase != "fwd":
                         continue
-                    ins = (x,)
+                    ins = (x,) + join
+                    join = ()
                     if tp > 1 and ("qkv" in o.name or "w1||w3" in o.name):
-                        coll(f"SP all-gather before {o.name} L{li}", ck.ALL_GATHER, act, tpg, "fwd", li, i, (x,), (x + ".ag",))
-                        ins = (x + ".ag",)
+                        coll(f"SP all-gather before {o.name} L{li}", ck.ALL_GATHER, act, tpg, "fwd", li, i, ins, (x + ".ag",))
+                        if fused_tp:
+                            join = (x + ".ag",)
+                        else:
+                            ins = (x + ".ag",)
+                    rs = tp > 1 and (o.name.startswith("wo") or o.name.startswith("w2"))
+                    if rs and fused_tp:
+                        coll(f"SP reduce-scatter in {o.name} L{li}", ck.REDUCE_SCATTER, act, tpg, "fwd", li, i, ins,
+                             (x + ".rs",))
+                        join = (x + ".rs",)
                     g.add(f"{o.name} L{li} mb{i}", "comp", o.cat, "fwd", ins, (x,), o.flops * k, o.bytes * k, li, i)
-                    if tp > 1 and (o.name.startswith("wo") or o.name.startswith("w2")):
+                    if rs and not fused_tp:
                         coll(f"SP reduce-scatter after {o.name} L{li}", ck.REDUCE_SCATTER, act, tpg, "fwd", li, i, (x,), (x,))
+            x_out = (x,) + join
             if next_r is not None:
-                g.add(f"send act mb{i}", "send", "communication", "fwd", (x,), (), nbytes=act, mb=i,
+                g.add(f"send act mb{i}", "send", "communication", "fwd", x_out, (), nbytes=act, mb=i,
                       comm={"src": rank, "dst": next_r, "tag": 2 * i, "bytes": act})
             else:
                 for o, k in last:
                     if o.phase == "fwd":
-                        g.add(f"{o.name} mb{i}", "comp", o.cat, "fwd", (x,), (f"loss.mb{i}",), o.flops * k, o.bytes * k, mb=i)
+                        g.add(f"{o.name} mb{i}", "comp", o.cat, "fwd", x_out, (f"loss.mb{i}",), o.flops * k, o.bytes * k,
+                              mb=i)
+                        x_out = (x,)
         else:
             gx = f"grad.mb{i}"
             if next_r is not None:
@@ -154,15 +171,23 @@ def build_rank(cfg, mb, seq, dp, tp, pp, m, dp_i, pp_i, tp_i, machine, kinds):
                 for o, k in last:
                     if o.phase == "bwd":
                         g.add(f"{o.name} mb{i}", "comp", o.cat, "bwd", (f"loss.mb{i}",), (gx,), o.flops * k, o.bytes * k, mb=i)
+            join = ()
             for li in reversed(layers):
                 for o, k in per_layer:
                     if o.phase != "bwd":
                         continue
-                    ins = (gx,)
+                    ins = (gx,) + (join if "wgrad" not in o.name else ())
+                    if "wgrad" not in o.name:
+                        join = ()
                     if tp > 1 and ("w2 dgrad" in o.name or o.name.startswith("wo dgrad")):
-                        coll(f"SP all-gather before {o.name} L{li}", ck.ALL_GATHER, act, tpg, "bwd", li, i, (gx,), (gx + ".ag",))
-                        ins = (gx + ".ag",)
+                        coll(f"SP all-gather before {o.name} L{li}", ck.ALL_GATHER, act, tpg, "bwd", li, i, ins, (gx + ".ag",))
+                        if fused_tp:  # the dgrad GEMM gathers dy itself
+                            join = (gx + ".ag",)
+                        else:
+                            ins = (gx + ".ag",)
                     wout = (f"wgrad.L{li}",) if "wgrad" in o.name else (gx,)
+                    if "wgrad" in o.name and fused_tp:
+                        ins = ins + tuple(t for t in join if t.endswith(".ag"))  # reads the gathered dy
                     g.add(f"{o.name} L{li} mb{i}", "comp", o.cat, "bwd", ins, wout, o.flops * k, o.bytes * k, li, i)
                     if tp > 1 and (o.name.startswith("qkv dgrad") or o.name.startswith("w1||w3 dgrad")):
                         coll(f"SP reduce-scatter after {o.name} L{li}", ck.REDUCE_SCATTER, act, tpg, "bwd", li, i, (gx,), (gx,))
@@ -211,14 +236,14 @@ def to_chakra(n) -> dict:
             "attrs": attrs}
 
 
-def export(cfg, mb, seq, dp, tp, pp, m, outdir=None, machine=None):
+def export(cfg, mb, seq, dp, tp, pp, m, outdir=None, machine=None, fused_tp=False):
     machine = machine or Machine.from_peaks()
     table, kinds = make_groups(dp, tp, pp)
     graphs = {}
     for a in range(dp):
         for b in range(pp):
             for t in range(tp):
-                gr = build_rank(cfg, mb, seq, dp, tp, pp, m, a, b, t, machine, kinds)
+                gr = build_rank(cfg, mb, seq, dp, tp, pp, m, a, b, t, machine, kinds, fused_tp)
                 graphs[gr.rank] = gr
     if outdir:
         os.makedirs(outdir, exist_ok=True)
@@ -312,9 +337,13 @@ def main():
     ap.add_argument("--pp", type=int, default=2)
     ap.add_argument("--microbatches", type=int, default=4)
     ap.add_argument("--out", default="traces")
+    ap.add_argument("--fused-tp", action="store_true",
+                    help="tensor-parallel collectives inside the GEMMs (the peer-memory path): each runs "
+                         "concurrently with its GEMM instead of before / after it")
     args = ap.parse_args()
     cfg = SIZES[args.size]
-    graphs, table = export(cfg, args.batch, args.seq, args.dp, args.tp, args.pp, args.microbatches, args.out)
+    graphs, table = export(cfg, args.batch, args.seq, args.dp, args.tp, args.pp, args.microbatches, args.out,
+                           fused_tp=args.fused_tp)
     res = {"graph": check_graphs(graphs, table),
            "cross_check": cross_check(cfg, args.batch, args.seq, args.dp, args.tp, args.pp, args.microbatches, graphs),
            "roundtrip": check_roundtrip(graphs, args.out)}

@@ -153,3 +153,27 @@ def test_official_chakra_decoder_check_skips_or_passes(tmp_path):
     export(get_config("tiny256"), 1, 64, 2, 1, 2, 2, outdir=str(tmp_path))
     res = official_decode(str(tmp_path))
     assert res["status"] in ("skipped", "pass"), res
+
+
+def test_export_fused_tensor_parallel_collectives(tmp_path):
+    """With the collectives inside the GEMMs (--fused-tp) every gather and reduce-scatter still
+    appears once per site (same group sequences, checks pass), but no GEMM waits for its gather:
+    the gather and the GEMM start from the same input, and the next operator waits for both."""
+    from llmt.config import get_config
+    from llmt.export import trace
+    cfg = get_config("tiny256")
+    plain, _ = trace.export(cfg, 2, 256, 1, 2, 2, 2)
+    graphs, table = trace.export(cfg, 2, 256, 1, 2, 2, 2, str(tmp_path / "fused"), fused_tp=True)
+    assert trace.check_graphs(graphs, table)["pass"]
+    assert trace.check_roundtrip(graphs, str(tmp_path / "fused"))["pass"]
+    for r, gr in graphs.items():
+        colls = [n for n in gr.nodes if n["kind"] == "coll"]
+        assert len(colls) == len([n for n in plain[r].nodes if n["kind"] == "coll"])
+        ag = {n["id"] for n in colls if n["name"].startswith("SP all-gather")}
+        rs = {n["id"] for n in colls if n["name"].startswith("SP reduce-scatter in")}
+        assert ag and rs
+        consumers = [n for n in gr.nodes if n["kind"] == "comp" and n["phase"] == "fwd"
+                     and n["name"].startswith(("qkv", "w1||w3"))]
+        assert consumers and not any(ag & set(n["data_deps"]) for n in consumers)
+        # every gather and every fused reduce-scatter is waited for by a later node
+        assert all(any(i in n["data_deps"] for n in gr.nodes) for i in ag | rs)
