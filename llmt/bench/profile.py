@@ -77,11 +77,15 @@ def clean_ms(step, warmup=3, steps=10):
     return statistics.median(ev[i].elapsed_time(ev[i + 1]) for i in range(steps))
 
 
-def profile_step(step, prof_steps=3, top=25):
+def profile_step(step, prof_steps=3, top=25, trace=None):
+    """Kernel shares of `prof_steps` profiled steps; trace: also write the profiler timeline as a
+    Chrome trace (JSON, viewable in chrome://tracing or Perfetto)."""
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
         for _ in range(prof_steps):
             step()
         torch.cuda.synchronize()
+    if trace:
+        prof.export_chrome_trace(trace)
     kern = [e for e in prof.events() if e.device_type == DeviceType.CUDA and not e.name.startswith(WRAPPER_PREFIXES)]
     per = defaultdict(lambda: [0, 0.0])
     buckets = defaultdict(float)
@@ -130,6 +134,7 @@ def main():
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--ref-row", default="5 + torch.compile", help="reference ladder row for --impl reference")
     p.add_argument("--linear", default="bf16", choices=["bf16", "fp8", "mxfp8", "nvfp4"])
+    p.add_argument("--trace", default=None, help="write the profiled steps' timeline as a Chrome trace (JSON)")
     p.add_argument("--once", action="store_true",
                    help="run one warm-up step and one step, then exit (a short program for ncu launch lists)")
     args = p.parse_args()
@@ -151,7 +156,7 @@ def main():
         print("two steps done")
         return
     ms = clean_ms(step)
-    res = profile_step(step, args.prof_steps, args.top)
+    res = profile_step(step, args.prof_steps, args.top, trace=args.trace)
     res["clean_ms_per_step"] = ms
     res["idle_pct"] = round(100.0 * (1 - res["busy_ms_per_step"] / ms), 2) if ms > 0 else None
     res["config"] = {"size": args.size, "batch": args.batch, "seq": args.seq, "graph": args.graph,
