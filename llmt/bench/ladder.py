@@ -82,6 +82,9 @@ def main():
     ap.add_argument("--rows", default="ref,native")
     ap.add_argument("--ref-rows", default="1,2,3,4,5,6,7,8,9")
     ap.add_argument("--out", default=None)
+    ap.add_argument("--mem-cap", type=float, default=0.97,
+                    help="fraction of the GPU's memory the native rows may allocate (like the reference's runs: "
+                         "a row that does not fit is recorded as oom instead of spilling)")
     args = ap.parse_args()
     from llmt.bench.calibrate import env_info, matmul_tflops
     from llmt.perf.roofline import Machine
@@ -107,6 +110,8 @@ def main():
     if "native" in args.rows:
         from llmt.config import SIZES, model_flops_per_token
         cfg = SIZES[args.size]
+        if 0 < args.mem_cap < 1:
+            torch.cuda.set_per_process_memory_fraction(args.mem_cap)  # this process's allocator only
         for name, opts in native_rows():
             print(f"running {name} ...", flush=True)
             row = run_native(args.size, args.batch, args.seq, opts, args.warmup, args.steps)
