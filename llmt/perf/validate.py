@@ -93,6 +93,31 @@ def fit_alpha(rows):
     return num / den if den > 0 else 1.0
 
 
+def mfu_gap(row, peak_tflops, alpha=1.0):
+    """Where the measured step's time goes relative to the MFU ideal, in ms (sums to measured_ms).
+
+    ideal: the model FLOPs (the MFU numerator: 6 x matmul params + 12 L d T per token) at the bf16
+    peak. The GEMM and attention terms are their calibrated times (scaled by the fitted L2 factor
+    alpha) minus their share of the ideal: the GEMMs' share is the 6 x params part, attention's
+    the 12 L d T part (counted as full, non-causal attention, as the MFU formula does). The
+    memory-bound, optimizer and launch-gap terms are the calibrated prediction's; whatever the
+    model does not place (idle time, cache effects across kernels) is the residual."""
+    cfg = SIZES[row["size"]]
+    tok = row["batch"] * row["seq"]
+    peak = peak_tflops * 1e12
+    attn_flops = 12 * cfg.L * cfg.d * row["seq"] * tok
+    all_flops = model_flops_per_token(cfg, row["seq"]) * tok
+    cats = row["calibrated_by_cat_ms"]
+    gap = {"model FLOPs at the bf16 peak": all_flops / peak * 1e3,
+           "GEMMs below peak": alpha * cats["matmul"] - (all_flops - attn_flops) / peak * 1e3,
+           "attention below peak": alpha * cats["attention"] - attn_flops / peak * 1e3,
+           "memory-bound ops (norms, elementwise, loss)": cats["elementwise"] + cats["copy/cast"] + cats["loss"],
+           "optimizer": cats["optimizer"],
+           "kernel launch gaps": row["gap_ms"]}
+    gap["residual (not placed by the model)"] = row["measured_ms"] - sum(gap.values())
+    return {k: round(v, 3) for k, v in gap.items()}
+
+
 def run(configs, machine, cache, out_rows, tag):
     for size, B, T in configs:
         cfg = SIZES[size]
@@ -118,7 +143,19 @@ def main():
     ap.add_argument("--out", default=None)
     ap.add_argument("--cache", default="/tmp/llmt_shape_times.json")
     ap.add_argument("--no-holdout", action="store_true")
+    ap.add_argument("--gap-from", default=None,
+                    help="a results file of this script: add the MFU-gap breakdown to its rows (no GPU needed)")
     args = ap.parse_args()
+    if args.gap_from:
+        with open(args.gap_from) as f:
+            res = json.load(f)
+        alpha = res["summary"]["alpha"]
+        for r in res["rows"]:
+            r["mfu_gap_ms"] = mfu_gap(r, res["machine"]["bf16_tflops"], alpha)
+            print(r["size"], r["batch"], r["seq"], json.dumps(r["mfu_gap_ms"]))
+        with open(args.out or args.gap_from, "w") as f:
+            json.dump(res, f, indent=1)
+        return
     gap = measure_gap_us()
     m = Machine.from_peaks(sustained=True, gpu_gap_us=gap)
     rows = []
@@ -129,6 +166,7 @@ def main():
     for r in rows:
         r["fitted_ms"] = round(fitted_ms(r, alpha), 3)
         r["fitted_err"] = round((r["fitted_ms"] - r["measured_ms"]) / r["measured_ms"], 4)
+        r["mfu_gap_ms"] = mfu_gap(r, m.bf16_tflops, alpha)
     summ = {"alpha": round(alpha, 4)}
     for tag in ("fit", "holdout"):
         rs = [r for r in rows if r["set"] == tag]

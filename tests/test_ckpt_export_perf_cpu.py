@@ -177,3 +177,18 @@ def test_export_fused_tensor_parallel_collectives(tmp_path):
         assert consumers and not any(ag & set(n["data_deps"]) for n in consumers)
         # every gather and every fused reduce-scatter is waited for by a later node
         assert all(any(i in n["data_deps"] for n in gr.nodes) for i in ag | rs)
+
+
+def test_mfu_gap_breakdown_sums_to_measured_step():
+    """The MFU-gap breakdown of each measured step in the committed validation results places
+    every millisecond: its terms sum to the measured step time, the ideal term is the MFU share."""
+    import json
+    import pathlib
+    from llmt.perf.validate import mfu_gap
+    res = json.loads((pathlib.Path(__file__).resolve().parents[1] / "results" / "perf_model_validation.json").read_text())
+    peak = res["machine"]["bf16_tflops"]
+    for r in res["rows"]:
+        gap = mfu_gap(r, peak, res["summary"]["alpha"])
+        assert abs(sum(gap.values()) - r["measured_ms"]) < 0.01
+        assert abs(gap["model FLOPs at the bf16 peak"] / r["measured_ms"] - r["mfu"]) < 0.01
+        assert gap["GEMMs below peak"] > 0 and gap["optimizer"] > 0
