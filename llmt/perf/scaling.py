@@ -242,6 +242,24 @@ def validate(fit_paths, holdout_paths, machine, links, system="b200_nvl8_ib", sh
     return res
 
 
+def no_layout_reason(cfg, seq, G, n, links, system):
+    """Why no dp x tp x pp layout of n GPUs works (evaluate() rejected them all): the first of
+    a too-small global batch, weights and optimizer state too large even when split as widely as
+    the model allows, or divisibility (the remaining case: some split would fit, none divides)."""
+    sysd = links["systems"][system]
+    widest_tp = max(t for t in (1, 2, 4, 8) if t <= sysd["gpus_per_node"] and cfg.H % t == 0 and cfg.kvh % t == 0)
+    widest = widest_tp * cfg.L  # model-parallel GPUs: tp inside a node, one layer per stage
+    if G * widest < n:
+        return (f"global batch of {G} sequences is too small: at most {widest} model-parallel GPUs per "
+                f"replica and one sequence per replica give {G * widest} < {n} GPUs")
+    total, _ = count_params(cfg)
+    split = min(widest, n)
+    if total * (4 + 4 + 2) / split + total * 8 / n > 0.9 * sysd["gpu_memory_gb"] * 1e9:
+        return (f"fp32 master + gradient, bf16 weights and the ZeRO-1 Adam state do not fit in "
+                f"{sysd['gpu_memory_gb']} GB per GPU even split {split} ways")
+    return "no split of the GPUs divides the heads, layers and global batch while fitting in memory"
+
+
 def divisors(x, cap):
     return [d for d in range(1, min(x, cap) + 1) if x % d == 0]
 
@@ -331,7 +349,7 @@ def main():
                       f"{r['tokens_per_s'] / 1e6:8.3f} M tok/s  MFU {100 * r['mfu']:5.1f}%  mem {r['mem_gb']:.1f} GB")
                 res.append({"model": name, "gpus": n, **r})
             if not rows:
-                print(f"{name:10s} {n:5d} GPUs  no layout fits")
+                print(f"{name:10s} {n:5d} GPUs  no layout fits: {no_layout_reason(cfg, seq, G, n, links, args.system)}")
     if args.json:
         with open(args.json, "w") as f:
             json.dump(res, f, indent=1)

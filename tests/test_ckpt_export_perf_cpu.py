@@ -192,3 +192,16 @@ def test_mfu_gap_breakdown_sums_to_measured_step():
         assert abs(sum(gap.values()) - r["measured_ms"]) < 0.01
         assert abs(gap["model FLOPs at the bf16 peak"] / r["measured_ms"] - r["mfu"]) < 0.01
         assert gap["GEMMs below peak"] > 0 and gap["optimizer"] > 0
+
+
+def test_scaling_model_explains_missing_layouts():
+    """When no layout of n GPUs works the scaling model says why: batch too small, or weights and
+    optimizer state too large even at the widest split."""
+    from llmt.config import SIZES
+    from llmt.perf.roofline import Machine
+    from llmt.perf.scaling import StageCompute, all_layouts, load_links, no_layout_reason
+    links, m = load_links(), Machine.from_peaks()
+    for name, G, n, word in (("llama3-8b", 1, 4096, "too small"), ("llama3-70b", 8, 2, "do not fit")):
+        cfg = SIZES[name]
+        assert not all_layouts(cfg, 4096, G, n, StageCompute(cfg, 4096, m), links, "b200_nvl8_ib")
+        assert word in no_layout_reason(cfg, 4096, G, n, links, "b200_nvl8_ib")
