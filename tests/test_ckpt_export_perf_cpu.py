@@ -205,3 +205,12 @@ def test_scaling_model_explains_missing_layouts():
         cfg = SIZES[name]
         assert not all_layouts(cfg, 4096, G, n, StageCompute(cfg, 4096, m), links, "b200_nvl8_ib")
         assert word in no_layout_reason(cfg, 4096, G, n, links, "b200_nvl8_ib")
+
+
+def test_scaling_chart_svg():
+    """The scaling model's JSON renders as a plain-SVG MFU-vs-GPUs chart, one line per model."""
+    from llmt.bench.charts import scaling_chart
+    rows = [{"model": m, "gpus": n, "tokens_per_s": 1e6 * n, "mfu": 0.5 - 0.01 * n.bit_length()}
+            for m in ("medium", "llama3-8b") for n in (8, 64, 1024)]
+    svg = scaling_chart(rows)
+    assert svg.startswith("<svg") and svg.count("<polyline") == 2 and "llama3-8b" in svg
