@@ -132,6 +132,15 @@ def test_astra_inputs_and_acceptance(tmp_path):
     assert ok and ticks == {0: 100, 1: 100}
     ok, _ = accept("sys[0] finished, 100 cycles\nsys[1] finished, 90 cycles", 2)
     assert not ok
+    # pipeline stages finish at different ticks; the ranks of one stage agree (tp innermost)
+    log = "\n".join(f"sys[{r}] finished, {t} cycles, exposed communication 7 cycles"
+                     for r, t in ((0, 500), (1, 500), (2, 480), (3, 480)))
+    ok, ticks = accept(log, 4, tp=2, pp=2)
+    assert ok and max(ticks.values()) == 500
+    ok, _ = accept(log.replace("sys[3] finished, 480", "sys[3] finished, 470"), 4, tp=2, pp=2)
+    assert not ok
+    ok, _ = accept("\n".join(log.splitlines()[:3]), 4, tp=2, pp=2)  # one rank's line lost, both stages seen
+    assert ok
 
 
 def test_execution_trace_cross_check_matches_inventory(tmp_path):
