@@ -250,16 +250,36 @@ class Prediction:
     ops: list = field(default_factory=list)
 
 
+def gemm_efficiency(shape_times: dict, peak_flops: float, min_gflop: float = 20.0) -> float:
+    """Achieved / peak of the timed GEMM shapes of at least min_gflop, FLOP-weighted (total FLOPs
+    over total time): the derating applied to GEMM shapes that were not timed (shapes too large
+    for one GPU, or a model whose shapes were never measured)."""
+    flops = secs = 0.0
+    for k, t in shape_times.items():
+        f = k.split("|")
+        if f[0] != "gemm" or t <= 0:
+            continue
+        fl = 2.0 * int(f[1]) * int(f[2]) * int(f[3])
+        if fl >= min_gflop * 1e9:
+            flops += fl
+            secs += t
+    return min(1.0, flops / secs / peak_flops) if secs > 0 else 1.0
+
+
 def predict(ops, machine: Machine, shape_times: dict | None = None, graph: bool = True) -> Prediction:
     """Step time: sum over ops of max(compute, memory) (or the measured shape time), plus the
-    GPU gap per launch; with graph=False the CPU issue time can bound the step instead."""
+    GPU gap per launch; with graph=False the CPU issue time can bound the step instead. With
+    shape times, a GEMM whose shape was not timed runs at the timed GEMMs' efficiency."""
     peak = machine.bf16_tflops * 1e12
     bw = machine.hbm_gbs * 1e9
     p = Prediction(0.0, {c: 0.0 for c in CATEGORIES})
+    eff = gemm_efficiency(shape_times, peak) if shape_times else 1.0
     for op in ops:
         tc, tm = op.flops / peak, op.bytes / bw
         if shape_times and op.key is not None and _key(op.key) in shape_times:
             t, bound = shape_times[_key(op.key)], "measured"
+        elif shape_times and op.key is not None and op.key[0] == "gemm" and eff < 1.0:
+            t, bound = max(tc / eff, tm), "derated"
         else:
             t, bound = max(tc, tm), ("compute" if tc >= tm else "memory")
         p.by_cat[op.cat] += t * op.count * 1e3

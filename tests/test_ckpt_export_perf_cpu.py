@@ -223,3 +223,19 @@ def test_scaling_chart_svg():
             for m in ("medium", "llama3-8b") for n in (8, 64, 1024)]
     svg = scaling_chart(rows)
     assert svg.startswith("<svg") and svg.count("<polyline") == 2 and "llama3-8b" in svg
+
+
+def test_untimed_gemm_shapes_run_at_the_timed_efficiency():
+    """Shapes without a measured time (too large for one GPU, or never timed) are derated by the
+    FLOP-weighted efficiency of the timed GEMMs instead of running at the peak."""
+    from llmt.perf.roofline import Machine, gemm_efficiency, gemm_op, predict
+    m = Machine.from_peaks()
+    peak = m.bf16_tflops * 1e12
+    timed = gemm_op("timed", 4096, 4096, 4096, "fwd", 1, "nt")
+    st = {"|".join(str(x) for x in timed.key): 2.0 * timed.flops / peak}  # at half the peak
+    assert abs(gemm_efficiency(st, peak) - 0.5) < 1e-9
+    big = gemm_op("untimed", 8192, 8192, 8192, "fwd", 1, "nt")
+    p = predict([timed, big], m, st)
+    assert [o["bound"] for o in p.ops] == ["measured", "derated"]
+    assert abs(p.ops[1]["ms"] - 2e3 * big.flops / peak) < 1e-3
+    assert predict([big], m).ops[0]["bound"] == "compute"  # no shape times: plain roofline
