@@ -173,3 +173,29 @@ def test_peer_comm_buffer_sets_and_flags():
     its own forward gather buffers and flag counters, and the pointer arrays a fused gather hands
     the GEMM point at the right buffer of every rank (CPU stand-in for the extension)."""
     run_ranks(_peer_comm_layout, 2)
+
+
+def test_mxfp8_shards_quantize_like_the_whole_tensor():
+    """Under tensor parallelism each rank quantizes its own shards. For MXFP8 (one scale per 32
+    elements along the contraction) that gives the same bytes and scales as quantizing the whole
+    tensor, for row shards (qkv, w1||w3: output rows) and for column shards whose width is a
+    multiple of 32 (wo, w2: the contraction itself), so the sharded model multiplies the same
+    numbers as the single-GPU one."""
+    from llmt.config import get_config
+    from llmt.ops.lowp_ref import mxfp8_quant_ref
+    from llmt.parallel.tp import shard_tensor
+    cfg = get_config("tiny256", ffn=768)
+    g = torch.Generator().manual_seed(0)
+    tp = 2
+    for name, shape in (("blocks.0.attn.qkv.weight", (3 * cfg.d, cfg.d)), ("blocks.0.mlp.w1.weight", (cfg.ffn, cfg.d)),
+                        ("blocks.0.attn.wo.weight", (cfg.d, cfg.d)), ("blocks.0.mlp.w2.weight", (cfg.d, cfg.ffn))):
+        w = torch.randn(*shape, generator=g) * 0.02
+        q, s = mxfp8_quant_ref(w)
+        for r in range(tp):
+            qs, ss = mxfp8_quant_ref(shard_tensor(name, w, cfg, tp, r).contiguous())
+            assert torch.equal(qs.view(torch.uint8), shard_tensor(name, q.view(torch.uint8), cfg, tp, r)), name
+            if name.endswith(("wo.weight", "w2.weight")):  # column shard: the scales split by 32-blocks
+                n = ss.shape[1]
+                assert torch.equal(ss, s[:, r * n:(r + 1) * n]), name
+            else:
+                assert torch.equal(ss, shard_tensor(name, s, cfg, tp, r)), name
