@@ -232,9 +232,11 @@ class Pipeline1F1B:
 
     def _batch(self, sends, recvs, peer_send, peer_recv):
         """One NCCL group of sends to peer_send and receives from peer_recv. A group with receives
-        is waited for (the compute stream needs their data next); a send-only group is not: the
-        compute stream goes on with the next micro-batch while the transfer runs, and the group
-        is waited for at the end of the step (its tensors are kept alive until then)."""
+        is waited for, which with NCCL is a dependency of the compute stream on the transfer (the
+        host does not block: it goes on queuing the consumer's kernels, which run when the data
+        has arrived); a send-only group is not waited for at all: the compute stream goes on with
+        the next micro-batch while the transfer runs, and the group is waited for at the end of
+        the step (its tensors are kept alive until then)."""
         sends = [t.contiguous() for t in sends]
         ops = [dist.P2POp(dist.isend, t, peer_send, self.group) for t in sends]
         ops += [dist.P2POp(dist.irecv, t, peer_recv, self.group) for t in recvs]
